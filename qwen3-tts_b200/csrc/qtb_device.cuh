@@ -1,0 +1,176 @@
+// qtb_device.cuh -- device-side helpers shared by every sm_100a kernel of the
+// decode engine: PTX wrappers (streaming loads, mma.sync, bulk copies,
+// mbarriers), bf16/fp16 bit tricks, warp reductions and the bounded grid
+// barrier used by the persistent decode kernel.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define QTB_DEV __device__ __forceinline__
+
+namespace qtb {
+
+// ---------------------------------------------------------------- loads ----
+// Weights, norm gains, RoPE tables, embedding tables and page tables are
+// read-only for a kernel's lifetime: non-coherent path, no L1 allocation.
+QTB_DEV uint4 ld_stream(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+// Same, with an L2 eviction-priority policy (created once per thread).
+QTB_DEV uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+QTB_DEV uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+QTB_DEV uint4 ld_stream_hint(const void *p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(pol));
+  return r;
+}
+QTB_DEV uint2 ld_nc_u2(const void *p) {
+  uint2 r;
+  asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+QTB_DEV uint4 ld_nc_u4(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+// Activations, partial sums and KV pages are produced by other CTAs inside the
+// same persistent launch: read them at L2 (".cg") so a stale L1 line is never
+// used.
+QTB_DEV float ld_cg(const float *p) { return __ldcg(p); }
+QTB_DEV float4 ld_cg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+QTB_DEV uint4 ld_cg_u4(const void *p) { return __ldcg(reinterpret_cast<const uint4 *>(p)); }
+
+// ------------------------------------------------------------- numerics ----
+QTB_DEV float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+QTB_DEV float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+// f32 -> bf16 by truncation (the reference's KV store semantics, bits >> 16).
+QTB_DEV uint32_t f32_to_bf16_trunc(float f) { return __float_as_uint(f) >> 16; }
+// f32 -> bf16 round-to-nearest-even (used only to split activations into
+// hi + lo bf16 parts for the tensor-core GEMV).
+QTB_DEV uint32_t f32_to_bf16_rn(float f) {
+  uint32_t u = __float_as_uint(f);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return u >> 16;
+}
+QTB_DEV float half_bits_to_f32(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
+
+// Orderable key for a float: larger float <=> larger unsigned key.
+QTB_DEV uint32_t float_order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <typename T>
+QTB_DEV T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+QTB_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------- tensor cores ---
+// D(16x8,f32) += A(16x16) * B(16x8); A row-major fragment (4 regs), B column
+// fragment (2 regs).  The GEMV keeps weights as A and the activation (split
+// into hi and lo halves, one per column) as B.
+QTB_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+QTB_DEV void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Two signed int8 weights (selected bytes of w, already XOR 0x80) -> f16x2
+// holding exactly their values: 0x64XX is 1024 + XX in fp16.
+QTB_DEV uint32_t i8x2_to_f16x2(uint32_t w_xor80, uint32_t sel) {
+  uint32_t h = __byte_perm(w_xor80, 0x00006464u, sel);
+  const uint32_t bias = 0x64806480u;  // (1024 + 128, 1024 + 128)
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(bias));
+  return r;
+}
+// Two 4-bit codes (bits [0,4) and [16,20) of w) -> f16x2 holding the codes.
+QTB_DEV uint32_t u4x2_to_f16x2(uint32_t w) {
+  uint32_t h = (w & 0x000f000fu) | 0x64006400u;
+  const uint32_t bias = 0x64006400u;  // (1024, 1024)
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(bias));
+  return r;
+}
+
+// -------------------------------------------------- bulk copies (TMA 1D) ---
+QTB_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+QTB_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+QTB_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+QTB_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+QTB_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+QTB_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+QTB_DEV void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Bounded wait on an mbarrier phase. Returns false after ~`limit_cycles`.
+QTB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit_cycles) {
+  uint32_t done = 0;
+  long long t0 = clock64();
+  while (true) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > limit_cycles) return false;
+  }
+}
+
+// ------------------------------------------------------------ grid sync ----
+QTB_DEV unsigned ld_acquire_gpu(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+QTB_DEV unsigned atom_add_release_gpu(unsigned *p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+QTB_DEV void st_release_gpu(unsigned *p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+}  // namespace qtb

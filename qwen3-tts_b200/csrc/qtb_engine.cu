@@ -1,0 +1,1237 @@
+// qtb_engine.cu -- host runtime of the B200 decode engine: weight upload and
+// repacking into tensor-core fragment order, KV page pools, stage-program
+// construction, cooperative launches and the qtb_* C ABI.
+//
+// Build: nvcc -gencode arch=compute_100a,code=sm_100a (see the package
+// Makefile).  No PyTorch, no CPU fallback: every compute path runs the
+// decode_kernel in qtb_kernels.cuh.
+#include "qtb_kernels.cuh"
+#include "../../include/qwen3tts_b200.h"
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+#include <algorithm>
+#include <functional>
+
+using namespace qtb;
+
+// ------------------------------------------------------------ errors -------
+static thread_local std::string g_err;
+static int set_err(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+#define CUDA_TRY(call)                                                                          \
+  do {                                                                                          \
+    cudaError_t e_ = (call);                                                                    \
+    if (e_ != cudaSuccess)                                                                      \
+      return set_err(QTB_E_CUDA, "%s:%d %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+extern "C" const char *qtb_last_error(void) { return g_err.c_str(); }
+
+extern "C" int qtb_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+// ------------------------------------------------------ device arena -------
+struct Arena {
+  std::vector<void *> ptrs;
+  int alloc(void **p, size_t bytes) {
+    *p = nullptr;
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) return set_err(QTB_E_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    ptrs.push_back(*p);
+    return 0;
+  }
+  template <typename T>
+  int upload(T **dst, const void *src, size_t bytes) {
+    int rc = alloc((void **)dst, bytes);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return set_err(QTB_E_CUDA, "cudaMemcpy: %s", cudaGetErrorString(e));
+    return 0;
+  }
+  void release() {
+    for (void *p : ptrs) cudaFree(p);
+    ptrs.clear();
+  }
+};
+
+static void parallel_for(int n, const std::function<void(int, int)> &fn) {
+  unsigned hw = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
+  int nt = std::min<int>((int)hw, std::max(1, n / 16));
+  if (nt <= 1) { fn(0, n); return; }
+  std::vector<std::thread> th;
+  for (int i = 0; i < nt; i++) {
+    int a = (int)((long long)n * i / nt), b = (int)((long long)n * (i + 1) / nt);
+    th.emplace_back(fn, a, b);
+  }
+  for (auto &t : th) t.join();
+}
+
+// ------------------------------------------- fragment-order repacking ------
+// Tile t = 16 rows; lane l (gid = l/4, tig = l%4) of the warp holds, for each
+// 16-column k-step, rows r0 = 16t+gid and r1 = r0+8 at columns c = 16s+2tig,
+// c+1, c+8, c+9 (the m16n8k16 A-fragment).  The layouts below put those
+// values in the lane's 16 contiguous bytes of each 512-byte warp chunk.
+static inline uint16_t host_nib_q4_0(const uint8_t *blocks, int K, int r, int k) {
+  const uint8_t *blk = blocks + ((size_t)r * (K / 32) + k / 32) * 18;
+  const uint8_t byte = blk[2 + (k % 32) / 2];
+  return (k & 1) ? (byte >> 4) : (byte & 0xf);
+}
+static inline uint16_t host_scale_q4_0(const uint8_t *blocks, int K, int r, int g) {
+  const uint8_t *blk = blocks + ((size_t)r * (K / 32) + g) * 18;
+  return (uint16_t)(blk[0] | (blk[1] << 8));
+}
+static inline uint16_t host_nib_i4g(const uint8_t *codes, int K, int r, int k) {
+  const uint8_t byte = codes[(size_t)r * (K / 2) + k / 2];
+  return (k & 1) ? (byte >> 4) : (byte & 0xf);
+}
+
+static void repack_bf16(const uint16_t *W, int rows, int K, std::vector<uint8_t> &out) {
+  out.resize((size_t)rows * K * 2);
+  uint16_t *o = (uint16_t *)out.data();
+  const int T = rows / 16, ST = K / 16;
+  parallel_for(T, [&](int t0, int t1) {
+    for (int t = t0; t < t1; t++)
+      for (int s = 0; s < ST; s++)
+        for (int l = 0; l < 32; l++) {
+          const int gid = l >> 2, tig = l & 3;
+          const size_t r0 = 16 * t + gid, r1 = r0 + 8, c = 16 * s + 2 * tig;
+          uint16_t *d = o + (((size_t)t * ST + s) * 32 + l) * 8;
+          d[0] = W[r0 * K + c]; d[1] = W[r0 * K + c + 1];
+          d[2] = W[r1 * K + c]; d[3] = W[r1 * K + c + 1];
+          d[4] = W[r0 * K + c + 8]; d[5] = W[r0 * K + c + 9];
+          d[6] = W[r1 * K + c + 8]; d[7] = W[r1 * K + c + 9];
+        }
+  });
+}
+
+static void repack_int8(const int8_t *W, int rows, int K, std::vector<uint8_t> &out) {
+  out.resize((size_t)rows * K);
+  uint8_t *o = out.data();
+  const int T = rows / 16, CT = K / 32;
+  parallel_for(T, [&](int t0, int t1) {
+    for (int t = t0; t < t1; t++)
+      for (int c = 0; c < CT; c++)
+        for (int l = 0; l < 32; l++) {
+          const int gid = l >> 2, tig = l & 3;
+          const size_t r0 = 16 * t + gid, r1 = r0 + 8;
+          uint8_t *d = o + (((size_t)t * CT + c) * 32 + l) * 16;
+          for (int q = 0; q < 2; q++) {
+            const size_t k = 32 * c + 16 * q + 2 * tig;
+            uint8_t *dq = d + 8 * q;
+            dq[0] = (uint8_t)W[r0 * K + k]; dq[1] = (uint8_t)W[r0 * K + k + 1];
+            dq[2] = (uint8_t)W[r1 * K + k]; dq[3] = (uint8_t)W[r1 * K + k + 1];
+            dq[4] = (uint8_t)W[r0 * K + k + 8]; dq[5] = (uint8_t)W[r0 * K + k + 9];
+            dq[6] = (uint8_t)W[r1 * K + k + 8]; dq[7] = (uint8_t)W[r1 * K + k + 9];
+          }
+        }
+  });
+}
+
+// int4 (q4_0 or asymmetric g32): nibble getter + per-group scale/zero getters.
+template <typename NibF, typename SclF, typename ZeroF>
+static void repack_int4(int rows, int K, bool with_zero, NibF nib, SclF scl, ZeroF zero,
+                        std::vector<uint8_t> &wout, std::vector<uint8_t> &gout) {
+  wout.resize((size_t)rows * K / 2);
+  const int GSZ = with_zero ? 16 : 8;
+  const int T = rows / 16, CT = K / 64;
+  gout.resize((size_t)T * CT * 8 * GSZ);
+  uint8_t *o = wout.data();
+  uint8_t *go = gout.data();
+  parallel_for(T, [&](int t0, int t1) {
+    for (int t = t0; t < t1; t++)
+      for (int c = 0; c < CT; c++) {
+        for (int l = 0; l < 32; l++) {
+          const int gid = l >> 2, tig = l & 3;
+          const int r0 = 16 * t + gid, r1 = r0 + 8;
+          uint32_t *d = (uint32_t *)(o + (((size_t)t * CT + c) * 32 + l) * 16);
+          for (int q = 0; q < 4; q++) {
+            const int k = 64 * c + 16 * q + 2 * tig;
+            uint32_t w = 0;
+            w |= (uint32_t)nib(r0, k) << 0;      w |= (uint32_t)nib(r0, k + 1) << 16;
+            w |= (uint32_t)nib(r1, k) << 4;      w |= (uint32_t)nib(r1, k + 1) << 20;
+            w |= (uint32_t)nib(r0, k + 8) << 8;  w |= (uint32_t)nib(r0, k + 9) << 24;
+            w |= (uint32_t)nib(r1, k + 8) << 12; w |= (uint32_t)nib(r1, k + 9) << 28;
+            d[q] = w;
+          }
+        }
+        for (int gid = 0; gid < 8; gid++) {
+          const int r0 = 16 * t + gid, r1 = r0 + 8, g0 = 2 * c, g1 = 2 * c + 1;
+          uint16_t *gd = (uint16_t *)(go + (((size_t)t * CT + c) * 8 + gid) * GSZ);
+          gd[0] = scl(r0, g0); gd[1] = scl(r0, g1); gd[2] = scl(r1, g0); gd[3] = scl(r1, g1);
+          if (with_zero) { gd[4] = zero(r0, g0); gd[5] = zero(r0, g1); gd[6] = zero(r1, g0); gd[7] = zero(r1, g1); }
+        }
+      }
+  });
+}
+
+// ------------------------------------------------------- device matrix -----
+struct DMat {
+  const uint8_t *w = nullptr;
+  const float *row_scale = nullptr;
+  const uint8_t *gsz = nullptr;
+  int fmt = 0, rows = 0, K = 0;
+  int64_t alg_bytes = 0;   // stored bytes of the reference format (weights + scales/zeros)
+};
+
+static int64_t fmt_alg_bytes(int fmt, int rows, int K) {
+  switch (fmt) {
+    case FMT_BF16: return (int64_t)rows * K * 2;
+    case FMT_INT8: return (int64_t)rows * K + (int64_t)rows * 4;
+    case FMT_Q4_0: return (int64_t)rows * (K / 32) * 18;
+    case FMT_INT4G: return (int64_t)rows * (K / 32) * 20;
+  }
+  return 0;
+}
+
+static int check_dims(int fmt, int rows, int K) {
+  if (rows <= 0 || K <= 0 || rows % 128 != 0 || K % 64 != 0)
+    return set_err(QTB_E_INVALID, "matrix %dx%d: rows must be a multiple of 128 and cols of 64", rows, K);
+  if (fmt < 0 || fmt > 3) return set_err(QTB_E_INVALID, "bad weight format %d", fmt);
+  return 0;
+}
+
+// Upload `n` host matrices stacked along rows (same K and format) as one.
+static int upload_matrix(Arena &ar, int fmt, const qtb_matrix_t *const *ms, const int *rows_each, int n, int K,
+                         DMat &out) {
+  int rows = 0;
+  for (int i = 0; i < n; i++) {
+    if (!ms[i] || !ms[i]->data) return set_err(QTB_E_INVALID, "missing weight data");
+    if (rows_each[i] % 16) return set_err(QTB_E_INVALID, "row block %d not a multiple of 16", rows_each[i]);
+    rows += rows_each[i];
+  }
+  int rc = check_dims(fmt, rows, K);
+  if (rc) return rc;
+  out.fmt = fmt; out.rows = rows; out.K = K;
+  out.alg_bytes = fmt_alg_bytes(fmt, rows, K);
+  std::vector<uint8_t> wf, gf;
+  if (fmt == FMT_BF16) {
+    std::vector<uint16_t> W((size_t)rows * K);
+    size_t off = 0;
+    for (int i = 0; i < n; i++) {
+      memcpy(W.data() + off, ms[i]->data, (size_t)rows_each[i] * K * 2);
+      off += (size_t)rows_each[i] * K;
+    }
+    repack_bf16(W.data(), rows, K, wf);
+  } else if (fmt == FMT_INT8) {
+    std::vector<int8_t> W((size_t)rows * K);
+    std::vector<float> sc(rows);
+    size_t off = 0, ro = 0;
+    for (int i = 0; i < n; i++) {
+      if (!ms[i]->row_scale) return set_err(QTB_E_INVALID, "int8 matrix without row_scale");
+      memcpy(W.data() + off, ms[i]->data, (size_t)rows_each[i] * K);
+      memcpy(sc.data() + ro, ms[i]->row_scale, (size_t)rows_each[i] * 4);
+      off += (size_t)rows_each[i] * K;
+      ro += rows_each[i];
+    }
+    repack_int8(W.data(), rows, K, wf);
+    float *dsc;
+    if ((rc = ar.upload(&dsc, sc.data(), sc.size() * 4))) return rc;
+    out.row_scale = dsc;
+  } else if (fmt == FMT_Q4_0) {
+    std::vector<uint8_t> Bk((size_t)rows * (K / 32) * 18);
+    size_t off = 0;
+    for (int i = 0; i < n; i++) {
+      const size_t nb = (size_t)rows_each[i] * (K / 32) * 18;
+      memcpy(Bk.data() + off, ms[i]->data, nb);
+      off += nb;
+    }
+    const uint8_t *bp = Bk.data();
+    repack_int4(rows, K, false, [&](int r, int k) { return host_nib_q4_0(bp, K, r, k); },
+                [&](int r, int g) { return host_scale_q4_0(bp, K, r, g); }, [&](int, int) { return (uint16_t)0; }, wf, gf);
+  } else {
+    std::vector<uint8_t> C((size_t)rows * K / 2);
+    std::vector<uint16_t> S((size_t)rows * (K / 32)), Z((size_t)rows * (K / 32));
+    size_t off = 0, go = 0;
+    for (int i = 0; i < n; i++) {
+      if (!ms[i]->group_scale || !ms[i]->group_zero) return set_err(QTB_E_INVALID, "int4g32 matrix without scale/zero");
+      memcpy(C.data() + off, ms[i]->data, (size_t)rows_each[i] * K / 2);
+      memcpy(S.data() + go, ms[i]->group_scale, (size_t)rows_each[i] * (K / 32) * 2);
+      memcpy(Z.data() + go, ms[i]->group_zero, (size_t)rows_each[i] * (K / 32) * 2);
+      off += (size_t)rows_each[i] * K / 2;
+      go += (size_t)rows_each[i] * (K / 32);
+    }
+    const uint8_t *cp = C.data();
+    const uint16_t *sp = S.data(), *zp = Z.data();
+    repack_int4(rows, K, true, [&](int r, int k) { return host_nib_i4g(cp, K, r, k); },
+                [&](int r, int g) { return sp[(size_t)r * (K / 32) + g]; },
+                [&](int r, int g) { return zp[(size_t)r * (K / 32) + g]; }, wf, gf);
+  }
+  uint8_t *dw;
+  if ((rc = ar.upload(&dw, wf.data(), wf.size()))) return rc;
+  out.w = dw;
+  if (!gf.empty()) {
+    uint8_t *dg;
+    if ((rc = ar.upload(&dg, gf.data(), gf.size()))) return rc;
+    out.gsz = dg;
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------- the engine -----
+struct DLayer {
+  DMat qkv, o, gu, down;
+  const float *in_norm, *post_norm, *q_norm, *k_norm;
+};
+struct DStack {
+  int hidden = 0, n_layers = 0, n_heads = 0, n_kv = 0, head_dim = 0, inter = 0, fmt = 0;
+  float eps = 1e-6f;
+  std::vector<DLayer> layers;
+  const float *rope_cos = nullptr, *rope_sin = nullptr;
+  int rope_len = 0;
+  const float *final_norm = nullptr;
+  int64_t weight_bytes = 0;
+  int q_dim() const { return n_heads * head_dim; }
+  int kv_dim() const { return n_kv * head_dim; }
+  int qkv_dim() const { return q_dim() + 2 * kv_dim(); }
+};
+
+struct qtb_engine {
+  int device = 0;
+  int n_sm = 0;
+  Arena ar;
+  DStack talker, cp;
+  int has_talker = 0, has_cp = 0;
+  DMat codec_head;                 // [codebook rows used][hidden] bf16
+  const uint16_t *codec_emb = nullptr;
+  int codec_vocab = 0, codebook = 0;
+  const float *cp_norm = nullptr;
+  DMat lm_head[15];
+  const uint16_t *cp_emb[15] = {};
+  int cp_emb_dim = 0;
+  DMat mtp;
+  const float *mtp_bias = nullptr;
+  int has_mtp = 0;
+};
+
+static int upload_stack(qtb_engine *e, const qtb_stack_desc_t &d, DStack &s) {
+  s.hidden = d.hidden; s.n_layers = d.n_layers; s.n_heads = d.n_heads; s.n_kv = d.n_kv_heads;
+  s.head_dim = d.head_dim; s.inter = d.inter; s.fmt = d.fmt; s.eps = d.eps;
+  if (d.head_dim != HD) return set_err(QTB_E_UNSUPPORTED, "head_dim %d (engine supports 128)", d.head_dim);
+  if (d.n_kv_heads <= 0 || d.n_heads != 2 * d.n_kv_heads)
+    return set_err(QTB_E_UNSUPPORTED, "GQA group %d/%d (engine supports 2 query heads per KV head)", d.n_heads, d.n_kv_heads);
+  if (!d.layers) return set_err(QTB_E_INVALID, "no layers");
+  int rc;
+  Arena &ar = e->ar;
+  s.layers.resize(d.n_layers);
+  const int H = d.hidden, qd = s.q_dim(), kvd = s.kv_dim(), I = d.inter;
+  for (int l = 0; l < d.n_layers; l++) {
+    const qtb_layer_t &L = d.layers[l];
+    DLayer &D = s.layers[l];
+    const qtb_matrix_t *qkv[3] = {&L.wq, &L.wk, &L.wv};
+    const int rq[3] = {qd, kvd, kvd};
+    if ((rc = upload_matrix(ar, d.fmt, qkv, rq, 3, H, D.qkv))) return rc;
+    const qtb_matrix_t *o[1] = {&L.wo};
+    const int ro[1] = {H};
+    if ((rc = upload_matrix(ar, d.fmt, o, ro, 1, qd, D.o))) return rc;
+    const qtb_matrix_t *gu[1] = {&L.gate_up};
+    const int rg[1] = {2 * I};
+    if ((rc = upload_matrix(ar, d.fmt, gu, rg, 1, H, D.gu))) return rc;
+    const qtb_matrix_t *dn[1] = {&L.down};
+    const int rd[1] = {H};
+    if ((rc = upload_matrix(ar, d.fmt, dn, rd, 1, I, D.down))) return rc;
+    if (!L.input_norm || !L.post_attn_norm || !L.q_norm || !L.k_norm) return set_err(QTB_E_INVALID, "layer %d: missing norm", l);
+    float *p;
+    if ((rc = ar.upload(&p, L.input_norm, H * 4))) return rc; D.in_norm = p;
+    if ((rc = ar.upload(&p, L.post_attn_norm, H * 4))) return rc; D.post_norm = p;
+    if ((rc = ar.upload(&p, L.q_norm, HD * 4))) return rc; D.q_norm = p;
+    if ((rc = ar.upload(&p, L.k_norm, HD * 4))) return rc; D.k_norm = p;
+    s.weight_bytes += D.qkv.alg_bytes + D.o.alg_bytes + D.gu.alg_bytes + D.down.alg_bytes;
+  }
+  // RoPE tables: as given (bit-exact with the caller) or computed here.
+  const int half = HD / 2;
+  int len = d.rope_len > 0 ? d.rope_len : 8192;
+  std::vector<float> cs((size_t)len * half), sn((size_t)len * half);
+  if (d.rope_cos && d.rope_sin) {
+    memcpy(cs.data(), d.rope_cos, cs.size() * 4);
+    memcpy(sn.data(), d.rope_sin, sn.size() * 4);
+  } else {
+    for (int i = 0; i < half; i++) {
+      const float inv = 1.0f / powf(d.rope_theta, (float)(2 * i) / (float)HD);
+      for (int p = 0; p < len; p++) {
+        const float ang = (float)p * inv;
+        cs[(size_t)p * half + i] = cosf(ang);
+        sn[(size_t)p * half + i] = sinf(ang);
+      }
+    }
+  }
+  float *pc, *ps;
+  if ((rc = ar.upload(&pc, cs.data(), cs.size() * 4))) return rc;
+  if ((rc = ar.upload(&ps, sn.data(), sn.size() * 4))) return rc;
+  s.rope_cos = pc; s.rope_sin = ps; s.rope_len = len;
+  if (d.final_norm) {
+    float *p;
+    if ((rc = ar.upload(&p, d.final_norm, H * 4))) return rc;
+    s.final_norm = p;
+  }
+  return 0;
+}
+
+extern "C" void qtb_engine_destroy(qtb_engine_t *e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  e->ar.release();
+  delete e;
+}
+
+extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_engine_t **out) {
+  if (!d || !out) return set_err(QTB_E_INVALID, "null argument");
+  *out = nullptr;
+  int ndev = 0;
+  CUDA_TRY(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return set_err(QTB_E_INVALID, "device %d of %d", device, ndev);
+  CUDA_TRY(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return set_err(QTB_E_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", device, prop.major, prop.minor);
+  int coop = 0;
+  CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
+  if (!coop) return set_err(QTB_E_UNSUPPORTED, "device lacks cooperative launch");
+  CUDA_TRY(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  int per_sm = 0;
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, NTHREADS, SMEM_BYTES));
+  if (per_sm < 1) return set_err(QTB_E_UNSUPPORTED, "decode kernel does not fit on an SM");
+
+  qtb_engine *e = new qtb_engine();
+  e->device = device;
+  e->n_sm = prop.multiProcessorCount;
+  int rc = 0;
+  e->has_talker = d->talker.n_layers > 0;
+  if (e->has_talker) {
+    if ((rc = upload_stack(e, d->talker, e->talker))) goto fail;
+    if (d->codec_head && d->codebook > 0) {
+      qtb_matrix_t ch = {d->codec_head, nullptr, nullptr, nullptr};
+      const qtb_matrix_t *m[1] = {&ch};
+      const int r[1] = {d->codebook};
+      if ((rc = upload_matrix(e->ar, FMT_BF16, m, r, 1, d->talker.hidden, e->codec_head))) goto fail;
+    }
+  }
+  if (d->codec_embedding && d->codec_vocab > 0) {
+    const int th = e->has_talker ? d->talker.hidden : d->cp_emb_dim;
+    uint16_t *p;
+    if ((rc = e->ar.upload(&p, d->codec_embedding, (size_t)d->codec_vocab * th * 2))) goto fail;
+    e->codec_emb = p;
+  }
+  e->codec_vocab = d->codec_vocab;
+  e->codebook = d->codebook;
+  e->has_cp = d->has_cp;
+  if (e->has_cp) {
+    if ((rc = upload_stack(e, d->cp, e->cp))) goto fail;
+    if (!d->cp_norm) { rc = set_err(QTB_E_INVALID, "cp_norm missing"); goto fail; }
+    {
+      float *p;
+      if ((rc = e->ar.upload(&p, d->cp_norm, d->cp.hidden * 4))) goto fail;
+      e->cp_norm = p;
+    }
+    e->cp_emb_dim = d->cp_emb_dim;
+    for (int g = 0; g < 15; g++) {
+      if (d->cp_lm_head[g].data) {
+        const qtb_matrix_t *m[1] = {&d->cp_lm_head[g]};
+        const int r[1] = {d->codebook};
+        if ((rc = upload_matrix(e->ar, d->cp.fmt, m, r, 1, d->cp.hidden, e->lm_head[g]))) goto fail;
+      }
+      if (d->cp_codec_emb[g]) {
+        uint16_t *p;
+        if ((rc = e->ar.upload(&p, d->cp_codec_emb[g], (size_t)d->codebook * d->cp_emb_dim * 2))) goto fail;
+        e->cp_emb[g] = p;
+      }
+    }
+    if (d->cp_mtp_proj.data) {
+      const qtb_matrix_t *m[1] = {&d->cp_mtp_proj};
+      const int r[1] = {d->cp.hidden};
+      if ((rc = upload_matrix(e->ar, d->cp_mtp_fmt, m, r, 1, d->cp_emb_dim, e->mtp))) goto fail;
+      e->has_mtp = 1;
+      if (d->cp_mtp_bias) {
+        float *p;
+        if ((rc = e->ar.upload(&p, d->cp_mtp_bias, d->cp.hidden * 4))) goto fail;
+        e->mtp_bias = p;
+      }
+    }
+  }
+  *out = e;
+  return 0;
+fail:
+  qtb_engine_destroy(e);
+  return rc;
+}
+
+extern "C" int64_t qtb_engine_talker_weight_bytes(const qtb_engine_t *e) { return e ? e->talker.weight_bytes : 0; }
+extern "C" int64_t qtb_engine_cp_pass_weight_bytes(const qtb_engine_t *e) {
+  return e ? e->cp.weight_bytes + (e->has_mtp ? e->mtp.alg_bytes : 0) : 0;
+}
+extern "C" int64_t qtb_engine_cp_head_weight_bytes(const qtb_engine_t *e) { return e ? e->lm_head[0].alg_bytes : 0; }
+
+// --------------------------------------------------------- the session -----
+enum { PROG_TALKER = 0, PROG_CP_PASS = 1, PROG_CP_FRAME = 2, PROG_FRAME = 3, PROG_N = 4 };
+
+struct StackBufs {
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *hidden = nullptr, *tmp = nullptr;
+  uint16_t *kpool = nullptr, *vpool = nullptr;  // [layer][n_pages][n_kv][16][128]
+  int n_pages = 0;
+  int *page_table = nullptr;                    // [B][pt_stride]
+  int pt_stride = 0;
+  int max_splits = 1;
+  size_t layer_pool_elems() const { return 0; }
+};
+
+struct qtb_session {
+  qtb_engine *e = nullptr;
+  int B = 0, max_ctx = 0;
+  Arena ar;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  StackBufs tk, cp;
+  size_t tk_layer_elems = 0, cp_layer_elems = 0;
+  int *pos = nullptr;        // talker positions [B]
+  int *cp_pos = nullptr;     // CP positions [B] (single-pass API)
+  int *codes = nullptr;      // [B][16]
+  float *cp_in = nullptr;    // [B][talker hidden] input of qtb_cp_frame
+  float *pad = nullptr;      // [hidden]
+  float *ws = nullptr; size_t ws_floats = 0;
+  unsigned *sem = nullptr; int sem_n = 0;
+  unsigned long long *amax_ws = nullptr;
+  unsigned *amax_sem = nullptr;
+  float *att_ws = nullptr;
+  unsigned *att_sem = nullptr;
+  Ctl *ctl = nullptr;
+  Stage *prog[PROG_N] = {};
+  int prog_n[PROG_N] = {};
+  int has_pad = 0;
+  double last_ms = 0;
+  int last_launches = 0;
+  // pinned staging
+  float *h_in = nullptr, *h_out = nullptr;
+  int *h_pos = nullptr, *h_codes = nullptr;
+  size_t h_in_floats = 0, h_out_floats = 0;
+};
+
+static int nch_for(int B) {
+  const int c = (2 * B + 7) / 8;
+  int n = 1;
+  while (n < c) n <<= 1;
+  return n;
+}
+
+// Choose the k-slice count: minimise the per-warp load (rounds x slice) with
+// the staged activation slice within shared memory.
+static int choose_S(int T, int K, int B, int W, int fmt) {
+  const int nch = nch_for(B), ent = 4 * std::min(8, 2 * B);
+  int best = -1;
+  double best_cost = 1e30;
+  for (int S = 1; S <= 64; S <<= 1) {
+    if (K % S) break;
+    const int ks = K / S;
+    if (ks % 64 || ks < 64) break;
+    const size_t xbytes = (size_t)(ks / 16) * nch * ent * 8 + (size_t)B * (ks / 32) * 4 + 256 + 16;
+    if (xbytes > (size_t)SMEM_X_BYTES) continue;
+    const long long U = (long long)T * S;
+    const double cost = (double)((U + W - 1) / W) * ks * (S > 1 ? 1.05 : 1.0);
+    if (cost < best_cost - 1e-9) { best_cost = cost; best = S; }
+  }
+  (void)fmt;
+  return best;
+}
+
+struct ProgBuilder {
+  qtb_session *s;
+  std::vector<Stage> st;
+  int err = 0;
+  int W() const { return s->e->n_sm * NWARPS; }
+
+  void gemv(const DMat &m, int B, const float *x, int ldx, const float *norm_w, float eps, float *y, int ldy,
+            int epi, int evict_last, const float *bias = nullptr) {
+    Stage S;
+    memset(&S, 0, sizeof S);
+    S.kind = ST_GEMV;
+    S.B = B;
+    GemvArgs &g = S.g;
+    g.w = m.w; g.row_scale = m.row_scale; g.gsz = m.gsz; g.bias = bias;
+    g.fmt = m.fmt; g.rows = m.rows; g.K = m.K;
+    g.S = choose_S(m.rows / 16, m.K, B, W(), m.fmt);
+    if (g.S < 1) { err = set_err(QTB_E_UNSUPPORTED, "no k-slicing fits shared memory (K=%d, B=%d)", m.K, B); return; }
+    g.nch = nch_for(B);
+    g.evict_last = evict_last;
+    g.x = x; g.ldx = ldx; g.norm_w = norm_w; g.eps = eps;
+    g.y = y; g.ldy = ldy; g.epi = epi;
+    g.ws = s->ws; g.sem = s->sem;
+    g.amax_ws = s->amax_ws; g.amax_sem = s->amax_sem;
+    const size_t need = (size_t)(m.rows / 16) * g.S * 16 * B;
+    if (g.S > 1 && need > s->ws_floats) { err = set_err(QTB_E_INVALID, "split-K workspace too small"); return; }
+    if (m.rows / 16 > s->sem_n) { err = set_err(QTB_E_INVALID, "semaphore array too small"); return; }
+    st.push_back(S);
+  }
+  void argmax(const DMat &m, int B, const float *x, int ldx, const float *norm_w, float eps, int *codes,
+              int code_stride, const uint16_t *emb, int emb_ld, int emb_rows, float *emb_out, int emb_out_ld,
+              int evict_last) {
+    gemv(m, B, x, ldx, norm_w, eps, nullptr, 0, EPI_ARGMAX, evict_last);
+    if (err) return;
+    GemvArgs &g = st.back().g;
+    g.codes = codes; g.code_stride = code_stride;
+    g.emb_table = emb; g.emb_ld = emb_ld; g.emb_rows = emb_rows; g.emb_out = emb_out; g.emb_out_ld = emb_out_ld;
+  }
+  void attn(const DStack &k, const StackBufs &b, int layer, int B, const int *pos_ptr, int pos_const, size_t layer_elems) {
+    Stage S;
+    memset(&S, 0, sizeof S);
+    S.kind = ST_ATTN;
+    S.B = B;
+    AttnArgs &a = S.a;
+    a.qkv = b.qkv; a.ld_qkv = k.qkv_dim();
+    a.out = b.attn; a.ld_out = k.q_dim();
+    a.q_norm = k.layers[layer].q_norm; a.k_norm = k.layers[layer].k_norm;
+    a.rope_cos = k.rope_cos; a.rope_sin = k.rope_sin; a.rope_len = k.rope_len;
+    a.pos_ptr = pos_ptr; a.pos_const = pos_const;
+    a.page_table = b.page_table; a.pt_stride = b.pt_stride;
+    a.kpool = b.kpool + (size_t)layer * layer_elems;
+    a.vpool = b.vpool + (size_t)layer * layer_elems;
+    a.n_pages = b.n_pages;
+    a.n_heads = k.n_heads; a.n_kv = k.n_kv;
+    a.eps = k.eps; a.scale = 1.0f / sqrtf((float)HD);
+    a.max_splits = b.max_splits; a.min_pps = 4;
+    a.ws = s->att_ws; a.sem = s->att_sem;
+    st.push_back(S);
+  }
+  void layers(const DStack &k, const StackBufs &b, int B, const int *pos_ptr, int pos_const, size_t layer_elems, int evict_last) {
+    const int H = k.hidden;
+    for (int l = 0; l < k.n_layers && !err; l++) {
+      const DLayer &L = k.layers[l];
+      gemv(L.qkv, B, b.x, H, L.in_norm, k.eps, b.qkv, k.qkv_dim(), EPI_STORE, evict_last);
+      attn(k, b, l, B, pos_ptr, pos_const, layer_elems);
+      gemv(L.o, B, b.attn, k.q_dim(), nullptr, k.eps, b.x, H, EPI_RESID, evict_last);
+      gemv(L.gu, B, b.x, H, L.post_norm, k.eps, b.h, k.inter, EPI_SWIGLU, evict_last);
+      gemv(L.down, B, b.h, k.inter, nullptr, k.eps, b.x, H, EPI_RESID, evict_last);
+    }
+  }
+  void norm(const float *x, int ldx, const float *w, float *y, int ldy, int dim, float eps, int B) {
+    Stage S;
+    memset(&S, 0, sizeof S);
+    S.kind = ST_NORM; S.B = B;
+    S.n.x = x; S.n.ldx = ldx; S.n.w = w; S.n.y = y; S.n.ldy = ldy; S.n.dim = dim; S.n.eps = eps;
+    st.push_back(S);
+  }
+  Stage &embed(float *dst, int ld, int dim, int B, const float *fsrc, int fsrc_ld) {
+    Stage S;
+    memset(&S, 0, sizeof S);
+    S.kind = ST_EMBED; S.B = B;
+    S.e.dst = dst; S.e.ld_dst = ld; S.e.dim = dim; S.e.fsrc = fsrc; S.e.fsrc_ld = fsrc_ld;
+    st.push_back(S);
+    return st.back();
+  }
+  static void add_tab(Stage &S, const uint16_t *tab, int ld, int rows, const int *code, int stride) {
+    const int i = S.e.ntab++;
+    S.e.tab[i] = tab; S.e.tab_ld[i] = ld; S.e.tab_rows[i] = rows; S.e.code[i] = code; S.e.code_stride[i] = stride;
+  }
+  void pos_inc(int *pos, int B) {
+    Stage S;
+    memset(&S, 0, sizeof S);
+    S.kind = ST_POS_INC; S.B = B; S.p.pos = pos;
+    st.push_back(S);
+  }
+};
+
+// The code-predictor frame (qwen_cp_predict, qwen_tts_code_predictor.c:926-1045):
+// pos 0 = projected talker hidden, pos 1 = projected codec embedding of code0,
+// then codebooks 1..15 with the embedding of the previous code as input.
+static void build_cp_frame(ProgBuilder &pb, qtb_session *s, const float *talker_hidden) {
+  qtb_engine *e = s->e;
+  const DStack &k = e->cp;
+  StackBufs &b = s->cp;
+  const int B = s->B, CH = k.hidden;
+  const int TH = e->has_talker ? e->talker.hidden : e->cp_emb_dim;
+  auto project = [&](const float *src, int src_ld) {
+    if (e->has_mtp) pb.gemv(e->mtp, B, src, src_ld, nullptr, k.eps, b.x, CH, EPI_STORE, 1, e->mtp_bias);
+    else pb.embed(b.x, CH, CH, B, src, src_ld);
+  };
+  // pos 0
+  project(talker_hidden, TH);
+  pb.layers(k, b, B, nullptr, 0, s->cp_layer_elems, 1);
+  // pos 1: the talker's codec embedding of code0
+  {
+    float *dst = e->has_mtp ? b.tmp : b.x;
+    const int dim = e->has_mtp ? TH : CH;
+    Stage &S = pb.embed(dst, dim, dim, B, nullptr, 0);
+    ProgBuilder::add_tab(S, e->codec_emb, TH, e->codec_vocab, s->codes, 16);
+    if (e->has_mtp) pb.gemv(e->mtp, B, b.tmp, TH, nullptr, k.eps, b.x, CH, EPI_STORE, 1, e->mtp_bias);
+  }
+  pb.layers(k, b, B, nullptr, 1, s->cp_layer_elems, 1);
+  for (int g = 0; g < 15 && !pb.err; g++) {
+    const bool last = (g == 14);
+    float *emb_out = e->has_mtp ? b.tmp : b.x;
+    const int emb_ld = e->cp_emb_dim;
+    pb.argmax(e->lm_head[g], B, b.x, CH, e->cp_norm, k.eps, s->codes + 1 + g, 16,
+              last ? nullptr : e->cp_emb[g], emb_ld, e->codebook, emb_out, emb_ld, 1);
+    if (last) break;
+    if (e->has_mtp) pb.gemv(e->mtp, B, b.tmp, TH, nullptr, k.eps, b.x, CH, EPI_STORE, 1, e->mtp_bias);
+    pb.layers(k, b, B, nullptr, g + 2, s->cp_layer_elems, 1);
+  }
+}
+
+static int upload_prog(qtb_session *s, int which, ProgBuilder &pb) {
+  if (pb.err) return pb.err;
+  if (pb.st.empty()) return 0;
+  Stage *d;
+  int rc = s->ar.upload(&d, pb.st.data(), pb.st.size() * sizeof(Stage));
+  if (rc) return rc;
+  s->prog[which] = d;
+  s->prog_n[which] = (int)pb.st.size();
+  return 0;
+}
+
+static int build_programs(qtb_session *s) {
+  qtb_engine *e = s->e;
+  const int B = s->B;
+  int rc;
+  if (e->has_talker) {
+    const DStack &k = e->talker;
+    ProgBuilder pb{s};
+    pb.layers(k, s->tk, B, s->pos, 0, s->tk_layer_elems, 0);
+    pb.norm(s->tk.x, k.hidden, k.final_norm, s->tk.hidden, k.hidden, k.hidden, k.eps, B);
+    if ((rc = upload_prog(s, PROG_TALKER, pb))) return rc;
+  }
+  if (e->has_cp) {
+    const DStack &k = e->cp;
+    ProgBuilder pb{s};
+    pb.layers(k, s->cp, B, s->cp_pos, 0, s->cp_layer_elems, 1);
+    if ((rc = upload_prog(s, PROG_CP_PASS, pb))) return rc;
+    ProgBuilder pf{s};
+    build_cp_frame(pf, s, s->cp_in);
+    if ((rc = upload_prog(s, PROG_CP_FRAME, pf))) return rc;
+  }
+  if (e->has_talker && e->codec_head.w && e->codec_emb) {
+    const DStack &k = e->talker;
+    ProgBuilder pb{s};
+    pb.layers(k, s->tk, B, s->pos, 0, s->tk_layer_elems, 0);
+    pb.norm(s->tk.x, k.hidden, k.final_norm, s->tk.hidden, k.hidden, k.hidden, k.eps, B);
+    // greedy code0 over the first `codebook` rows of the codec head
+    pb.argmax(e->codec_head, B, s->tk.x, k.hidden, k.final_norm, k.eps, s->codes, 16, nullptr, 0, 0, nullptr, 0, 0);
+    if (e->has_cp) build_cp_frame(pb, s, s->tk.hidden);
+    Stage &S = pb.embed(s->tk.x, k.hidden, k.hidden, B, nullptr, 0);
+    ProgBuilder::add_tab(S, e->codec_emb, k.hidden, e->codec_vocab, s->codes, 16);
+    if (e->has_cp)
+      for (int g = 0; g < 15; g++) ProgBuilder::add_tab(S, e->cp_emb[g], e->cp_emb_dim, e->codebook, s->codes + 1 + g, 16);
+    S.e.add = s->pad;
+    pb.pos_inc(s->pos, B);
+    if ((rc = upload_prog(s, PROG_FRAME, pb))) return rc;
+  }
+  return 0;
+}
+
+static int alloc_stack_bufs(qtb_session *s, const DStack &k, StackBufs &b, int B, int max_ctx, int n_pages,
+                            size_t &layer_elems, int extra_tmp) {
+  Arena &ar = s->ar;
+  int rc;
+  const size_t H = k.hidden;
+  if ((rc = ar.alloc((void **)&b.x, B * H * 4))) return rc;
+  if ((rc = ar.alloc((void **)&b.hidden, B * H * 4))) return rc;
+  if ((rc = ar.alloc((void **)&b.qkv, (size_t)B * k.qkv_dim() * 4))) return rc;
+  if ((rc = ar.alloc((void **)&b.attn, (size_t)B * k.q_dim() * 4))) return rc;
+  if ((rc = ar.alloc((void **)&b.h, (size_t)B * k.inter * 4))) return rc;
+  if ((rc = ar.alloc((void **)&b.tmp, (size_t)B * std::max<int>(extra_tmp, 16) * 4))) return rc;
+  cudaMemset(b.x, 0, B * H * 4);
+  b.pt_stride = (max_ctx + PAGE - 1) / PAGE;
+  b.n_pages = n_pages > 0 ? n_pages : B * b.pt_stride;
+  layer_elems = (size_t)b.n_pages * k.n_kv * PAGE * HD;
+  const size_t pool = layer_elems * k.n_layers * 2;
+  if ((rc = ar.alloc((void **)&b.kpool, pool))) return rc;
+  if ((rc = ar.alloc((void **)&b.vpool, pool))) return rc;
+  cudaMemset(b.kpool, 0, pool);
+  cudaMemset(b.vpool, 0, pool);
+  std::vector<int> pt((size_t)B * b.pt_stride);
+  for (int i = 0; i < B; i++)
+    for (int j = 0; j < b.pt_stride; j++) pt[(size_t)i * b.pt_stride + j] = (n_pages > 0) ? -1 : i * b.pt_stride + j;
+  if ((rc = ar.upload(&b.page_table, pt.data(), pt.size() * 4))) return rc;
+  b.max_splits = std::max(1, std::min(32, (2 * s->e->n_sm + B * k.n_kv - 1) / (B * k.n_kv)));
+  return 0;
+}
+
+extern "C" void qtb_session_destroy(qtb_session_t *s) {
+  if (!s) return;
+  cudaSetDevice(s->e->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  s->ar.release();
+  if (s->ev0) cudaEventDestroy(s->ev0);
+  if (s->ev1) cudaEventDestroy(s->ev1);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  cudaFreeHost(s->h_in);
+  cudaFreeHost(s->h_out);
+  cudaFreeHost(s->h_pos);
+  cudaFreeHost(s->h_codes);
+  delete s;
+}
+
+extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n_pages, qtb_session_t **out) {
+  if (!e || !out) return set_err(QTB_E_INVALID, "null argument");
+  *out = nullptr;
+  if (batch < 1 || batch > 64) return set_err(QTB_E_INVALID, "batch %d outside 1..64", batch);
+  CUDA_TRY(cudaSetDevice(e->device));
+  qtb_session *s = new qtb_session();
+  s->e = e;
+  s->B = batch;
+  int rc = 0;
+  const int B = batch;
+  if (e->has_talker) {
+    if (max_ctx <= 0) max_ctx = e->talker.rope_len;
+    if (max_ctx > e->talker.rope_len) max_ctx = e->talker.rope_len;
+  }
+  s->max_ctx = max_ctx;
+  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreate(&s->ev0) != cudaSuccess || cudaEventCreate(&s->ev1) != cudaSuccess) {
+    rc = set_err(QTB_E_CUDA, "stream/event creation failed");
+    goto fail;
+  }
+  {
+    // workspaces sized for the largest GEMV stage of either stack
+    const int W = e->n_sm * NWARPS;
+    size_t ws = 16;
+    int sem_n = 16;
+    auto acc = [&](const DMat &m) {
+      if (!m.w) return;
+      const int T = m.rows / 16;
+      const int S = choose_S(T, m.K, B, W, m.fmt);
+      if (S > 0) ws = std::max(ws, (size_t)T * S * 16 * B);
+      sem_n = std::max(sem_n, T);
+    };
+    auto acc_stack = [&](const DStack &k) {
+      for (const DLayer &L : k.layers) { acc(L.qkv); acc(L.o); acc(L.gu); acc(L.down); }
+    };
+    acc_stack(e->talker);
+    acc_stack(e->cp);
+    acc(e->codec_head);
+    for (int g = 0; g < 15; g++) acc(e->lm_head[g]);
+    acc(e->mtp);
+    s->ws_floats = ws;
+    s->sem_n = sem_n;
+    if ((rc = s->ar.alloc((void **)&s->ws, ws * 4))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->sem, (size_t)sem_n * 4))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->amax_ws, (size_t)sem_n * B * 8))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->amax_sem, 64))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->ctl, sizeof(Ctl)))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->pos, B * 4))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->cp_pos, B * 4))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->codes, (size_t)B * 16 * 4))) goto fail;
+    cudaMemset(s->sem, 0, (size_t)sem_n * 4);
+    cudaMemset(s->amax_sem, 0, 64);
+    cudaMemset(s->ctl, 0, sizeof(Ctl));
+    cudaMemset(s->pos, 0, B * 4);
+    cudaMemset(s->cp_pos, 0, B * 4);
+    cudaMemset(s->codes, 0, (size_t)B * 16 * 4);
+  }
+  {
+    int att_splits = 1, nkv = 8;
+    if (e->has_talker) {
+      const int mtmp = e->has_cp ? std::max(e->cp_emb_dim, e->talker.hidden) : 16;
+      if ((rc = alloc_stack_bufs(s, e->talker, s->tk, B, max_ctx, n_pages, s->tk_layer_elems, mtmp))) goto fail;
+      att_splits = std::max(att_splits, s->tk.max_splits);
+      nkv = e->talker.n_kv;
+      if ((rc = s->ar.alloc((void **)&s->pad, (size_t)e->talker.hidden * 4))) goto fail;
+      cudaMemset(s->pad, 0, (size_t)e->talker.hidden * 4);
+    }
+    if (e->has_cp) {
+      const int th = e->has_talker ? e->talker.hidden : e->cp_emb_dim;
+      if ((rc = s->ar.alloc((void **)&s->cp_in, (size_t)B * th * 4))) goto fail;
+      const int cp_ctx = std::min(64, e->cp.rope_len);
+      if ((rc = alloc_stack_bufs(s, e->cp, s->cp, B, cp_ctx, 0, s->cp_layer_elems, e->cp_emb_dim + e->talker.hidden))) goto fail;
+      s->cp.max_splits = 1;
+      nkv = std::max(nkv, e->cp.n_kv);
+    }
+    if ((rc = s->ar.alloc((void **)&s->att_ws, (size_t)B * nkv * att_splits * 2 * (HD + 2) * 4))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->att_sem, (size_t)B * nkv * 4))) goto fail;
+    cudaMemset(s->att_sem, 0, (size_t)B * nkv * 4);
+  }
+  {
+    const int H = e->has_talker ? e->talker.hidden : e->cp.hidden;
+    s->h_in_floats = (size_t)B * std::max(std::max(H, e->has_cp ? e->cp.hidden : 0), e->cp_emb_dim) + 16;
+    s->h_out_floats = s->h_in_floats;
+    if (cudaMallocHost(&s->h_in, s->h_in_floats * 4) != cudaSuccess ||
+        cudaMallocHost(&s->h_out, s->h_out_floats * 4) != cudaSuccess ||
+        cudaMallocHost(&s->h_pos, (size_t)B * 4) != cudaSuccess ||
+        cudaMallocHost(&s->h_codes, (size_t)B * 16 * 4) != cudaSuccess) {
+      rc = set_err(QTB_E_OOM, "pinned host allocation failed");
+      goto fail;
+    }
+  }
+  if ((rc = build_programs(s))) goto fail;
+  if (cudaDeviceSynchronize() != cudaSuccess) { rc = set_err(QTB_E_CUDA, "session init sync failed"); goto fail; }
+  *out = s;
+  return 0;
+fail:
+  qtb_session_destroy(s);
+  return rc;
+}
+
+extern "C" int qtb_session_batch(const qtb_session_t *s) { return s ? s->B : 0; }
+extern "C" int qtb_session_n_pages(const qtb_session_t *s) { return s ? s->tk.n_pages : 0; }
+extern "C" double qtb_session_last_ms(const qtb_session_t *s) { return s ? s->last_ms : 0.0; }
+extern "C" int qtb_session_last_launches(const qtb_session_t *s) { return s ? s->last_launches : 0; }
+
+extern "C" int qtb_session_max_ctx(const qtb_session_t *s) { return s ? s->max_ctx : 0; }
+extern "C" qtb_engine_t *qtb_session_engine(qtb_session_t *s) { return s ? s->e : nullptr; }
+extern "C" int qtb_session_get_dec_x(qtb_session_t *s, float *out) {
+  if (!s || !out || !s->e->has_talker) return set_err(QTB_E_INVALID, "bad argument");
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemcpy(out, s->tk.x, (size_t)s->B * s->e->talker.hidden * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+extern "C" int qtb_session_set_pages(qtb_session_t *s, int b, const int32_t *pages, int n) {
+  if (!s || !pages || b < 0 || b >= s->B) return set_err(QTB_E_INVALID, "bad slot");
+  if (n < 0 || n > s->tk.pt_stride) return set_err(QTB_E_INVALID, "page count %d > %d", n, s->tk.pt_stride);
+  for (int i = 0; i < n; i++)
+    if (pages[i] < 0 || pages[i] >= s->tk.n_pages) return set_err(QTB_E_INVALID, "page id %d out of pool [0,%d)", pages[i], s->tk.n_pages);
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemcpy(s->tk.page_table + (size_t)b * s->tk.pt_stride, pages, (size_t)n * 4, cudaMemcpyHostToDevice));
+  return 0;
+}
+
+extern "C" int qtb_session_set_pos(qtb_session_t *s, const int32_t *pos) {
+  if (!s || !pos) return set_err(QTB_E_INVALID, "null argument");
+  for (int b = 0; b < s->B; b++)
+    if (pos[b] < 0 || pos[b] >= s->max_ctx) return set_err(QTB_E_INVALID, "position %d outside [0,%d)", pos[b], s->max_ctx);
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemcpy(s->pos, pos, (size_t)s->B * 4, cudaMemcpyHostToDevice));
+  return 0;
+}
+extern "C" int qtb_session_get_pos(qtb_session_t *s, int32_t *pos) {
+  if (!s || !pos) return set_err(QTB_E_INVALID, "null argument");
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemcpy(pos, s->pos, (size_t)s->B * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+// Clear the device error flag at the start of every API call.
+static int begin_call(qtb_session *s) {
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemsetAsync(s->ctl, 0, sizeof(Ctl), s->stream));
+  return 0;
+}
+
+// Launch program `which` n_iters times as ONE cooperative persistent kernel.
+static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
+  if (!s->prog[which]) return set_err(QTB_E_UNSUPPORTED, "program %d not available for this engine", which);
+  if ((long long)n_iters * s->prog_n[which] * s->e->n_sm > 0x3fffffffLL)
+    return set_err(QTB_E_INVALID, "too many iterations for one launch");
+  CUDA_TRY(cudaMemsetAsync(&s->ctl->bar_count, 0, sizeof(unsigned), s->stream));
+  const Stage *prog = s->prog[which];
+  int n_st = s->prog_n[which];
+  Ctl *ctl = s->ctl;
+  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_iters, (void *)&ctl};
+  if (timed) CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
+  CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(s->e->n_sm), dim3(NTHREADS), args,
+                                       SMEM_BYTES, s->stream));
+  if (timed) CUDA_TRY(cudaEventRecord(s->ev1, s->stream));
+  s->last_launches = 1;
+  return 0;
+}
+
+static int finish(qtb_session *s, bool timed) {
+  CUDA_TRY(cudaStreamSynchronize(s->stream));
+  if (timed) {
+    float ms = 0;
+    cudaEventElapsedTime(&ms, s->ev0, s->ev1);
+    s->last_ms = ms;
+  }
+  Ctl h;
+  CUDA_TRY(cudaMemcpy(&h, s->ctl, sizeof(Ctl), cudaMemcpyDeviceToHost));
+  if (h.err)
+    return set_err(QTB_E_DEVICE, "decode kernel error %d at stage %d (info %d)", h.err, h.err_stage, h.err_info);
+  return 0;
+}
+
+extern "C" int qtb_talker_step(qtb_session_t *s, const float *embeds, const int32_t *pos, float *hidden_out,
+                               float *dec_x_out) {
+  if (!s || !embeds) return set_err(QTB_E_INVALID, "null argument");
+  if (!s->e->has_talker) return set_err(QTB_E_UNSUPPORTED, "engine has no talker");
+  const int B = s->B, H = s->e->talker.hidden;
+  { int rc0 = begin_call(s); if (rc0) return rc0; }
+  if (pos) {
+    for (int b = 0; b < B; b++)
+      if (pos[b] < 0 || pos[b] >= s->max_ctx) return set_err(QTB_E_INVALID, "position %d outside [0,%d)", pos[b], s->max_ctx);
+    memcpy(s->h_pos, pos, (size_t)B * 4);
+    CUDA_TRY(cudaMemcpyAsync(s->pos, s->h_pos, (size_t)B * 4, cudaMemcpyHostToDevice, s->stream));
+  }
+  memcpy(s->h_in, embeds, (size_t)B * H * 4);
+  CUDA_TRY(cudaMemcpyAsync(s->tk.x, s->h_in, (size_t)B * H * 4, cudaMemcpyHostToDevice, s->stream));
+  int rc = launch_prog(s, PROG_TALKER, 1, true);
+  if (rc) return rc;
+  if (hidden_out) CUDA_TRY(cudaMemcpyAsync(hidden_out, s->tk.hidden, (size_t)B * H * 4, cudaMemcpyDeviceToHost, s->stream));
+  if (dec_x_out) CUDA_TRY(cudaMemcpyAsync(dec_x_out, s->tk.x, (size_t)B * H * 4, cudaMemcpyDeviceToHost, s->stream));
+  return finish(s, true);
+}
+
+extern "C" int qtb_cp_pass(qtb_session_t *s, float *x, const int32_t *pos) {
+  if (!s || !x || !pos) return set_err(QTB_E_INVALID, "null argument");
+  if (!s->e->has_cp) return set_err(QTB_E_UNSUPPORTED, "engine has no code predictor");
+  const int B = s->B, CH = s->e->cp.hidden;
+  for (int b = 0; b < B; b++)
+    if (pos[b] < 0 || pos[b] >= 64 || pos[b] >= s->e->cp.rope_len) return set_err(QTB_E_INVALID, "CP position %d outside [0,64)", pos[b]);
+  { int rc0 = begin_call(s); if (rc0) return rc0; }
+  memcpy(s->h_pos, pos, (size_t)B * 4);
+  CUDA_TRY(cudaMemcpyAsync(s->cp_pos, s->h_pos, (size_t)B * 4, cudaMemcpyHostToDevice, s->stream));
+  memcpy(s->h_in, x, (size_t)B * CH * 4);
+  CUDA_TRY(cudaMemcpyAsync(s->cp.x, s->h_in, (size_t)B * CH * 4, cudaMemcpyHostToDevice, s->stream));
+  int rc = launch_prog(s, PROG_CP_PASS, 1, true);
+  if (rc) return rc;
+  CUDA_TRY(cudaMemcpyAsync(s->h_out, s->cp.x, (size_t)B * CH * 4, cudaMemcpyDeviceToHost, s->stream));
+  rc = finish(s, true);
+  if (rc) return rc;
+  memcpy(x, s->h_out, (size_t)B * CH * 4);
+  return 0;
+}
+
+extern "C" int qtb_cp_frame(qtb_session_t *s, const float *talker_hidden, const int32_t *code0, int32_t *codes_out) {
+  if (!s || !talker_hidden || !code0 || !codes_out) return set_err(QTB_E_INVALID, "null argument");
+  qtb_engine *e = s->e;
+  if (!e->has_cp || !s->prog[PROG_CP_FRAME]) return set_err(QTB_E_UNSUPPORTED, "engine has no code predictor");
+  if (!e->codec_emb) return set_err(QTB_E_UNSUPPORTED, "engine has no talker codec embedding (needed for code0)");
+  const int B = s->B;
+  const int TH = e->has_talker ? e->talker.hidden : e->cp_emb_dim;
+  for (int b = 0; b < B; b++)
+    if (code0[b] < 0 || code0[b] >= e->codec_vocab) return set_err(QTB_E_INVALID, "code0 %d outside the codec vocabulary", code0[b]);
+  { int rc0 = begin_call(s); if (rc0) return rc0; }
+  memcpy(s->h_in, talker_hidden, (size_t)B * TH * 4);
+  CUDA_TRY(cudaMemcpyAsync(s->cp_in, s->h_in, (size_t)B * TH * 4, cudaMemcpyHostToDevice, s->stream));
+  for (int b = 0; b < B; b++) s->h_codes[b * 16] = code0[b];
+  CUDA_TRY(cudaMemcpy2DAsync(s->codes, 16 * 4, s->h_codes, 16 * 4, 4, B, cudaMemcpyHostToDevice, s->stream));
+  int rc = launch_prog(s, PROG_CP_FRAME, 1, true);
+  if (rc) return rc;
+  CUDA_TRY(cudaMemcpyAsync(s->h_codes, s->codes, (size_t)B * 16 * 4, cudaMemcpyDeviceToHost, s->stream));
+  rc = finish(s, true);
+  if (rc) return rc;
+  for (int b = 0; b < B; b++) memcpy(codes_out + (size_t)b * 15, s->h_codes + (size_t)b * 16 + 1, 15 * 4);
+  return 0;
+}
+
+extern "C" int qtb_decode_frames(qtb_session_t *s, const float *embeds, const float *pad, int n_frames,
+                                 int32_t *codes_out, float *last_hidden_out) {
+  if (!s || n_frames < 1) return set_err(QTB_E_INVALID, "bad argument");
+  qtb_engine *e = s->e;
+  if (!s->prog[PROG_FRAME]) return set_err(QTB_E_UNSUPPORTED, "engine lacks codec head / embeddings for whole frames");
+  const int B = s->B, H = e->talker.hidden;
+  { int rc0 = begin_call(s); if (rc0) return rc0; }
+  int32_t hp[64];
+  CUDA_TRY(cudaMemcpy(hp, s->pos, (size_t)B * 4, cudaMemcpyDeviceToHost));
+  for (int b = 0; b < B; b++)
+    if (hp[b] + n_frames > s->max_ctx) return set_err(QTB_E_INVALID, "slot %d would pass max_ctx %d", b, s->max_ctx);
+  if (embeds) {
+    memcpy(s->h_in, embeds, (size_t)B * H * 4);
+    CUDA_TRY(cudaMemcpyAsync(s->tk.x, s->h_in, (size_t)B * H * 4, cudaMemcpyHostToDevice, s->stream));
+  }
+  if (pad) CUDA_TRY(cudaMemcpyAsync(s->pad, pad, (size_t)H * 4, cudaMemcpyHostToDevice, s->stream));
+  int rc = 0;
+  if (codes_out) {
+    // one launch per frame so every frame's codes can be read back
+    CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
+    for (int f = 0; f < n_frames; f++) {
+      if ((rc = launch_prog(s, PROG_FRAME, 1, false))) return rc;
+      CUDA_TRY(cudaMemcpyAsync(codes_out + (size_t)f * B * 16, s->codes, (size_t)B * 16 * 4, cudaMemcpyDeviceToHost, s->stream));
+    }
+    CUDA_TRY(cudaEventRecord(s->ev1, s->stream));
+    s->last_launches = n_frames;
+  } else {
+    if ((rc = launch_prog(s, PROG_FRAME, n_frames, true))) return rc;
+  }
+  if (last_hidden_out)
+    CUDA_TRY(cudaMemcpyAsync(last_hidden_out, s->tk.hidden, (size_t)B * H * 4, cudaMemcpyDeviceToHost, s->stream));
+  return finish(s, true);
+}
+
+// ------------------------------------------------ KV scatter / gather ------
+__global__ void kv_copy_kernel(uint16_t *pool, const int *pt, int pt_stride, int n_kv, size_t layer_elems,
+                               uint16_t *host_layout, int layer_stride, int len, int n_layers, int to_pool) {
+  const int kvd = n_kv * HD;
+  const size_t total = (size_t)n_layers * len * kvd;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % kvd);
+    const size_t lp = i / kvd;
+    const int p = (int)(lp % len), l = (int)(lp / len);
+    const int page = pt[p / PAGE];
+    const int g = c / HD, d = c % HD;
+    uint16_t *pp = pool + (size_t)l * layer_elems + (((size_t)page * n_kv + g) * PAGE + p % PAGE) * HD + d;
+    uint16_t *hp = host_layout + ((size_t)l * layer_stride + p) * kvd + c;
+    if (to_pool) *pp = *hp; else *hp = *pp;
+  }
+}
+
+static int kv_transfer(qtb_session *s, StackBufs &b, const DStack &k, size_t layer_elems, int slot, uint16_t *kh,
+                       uint16_t *vh, int layer_stride, int len, int to_pool) {
+  if (slot < 0 || slot >= s->B || !kh || !vh) return set_err(QTB_E_INVALID, "bad slot/pointer");
+  if (len < 0 || len > b.pt_stride * PAGE || len > layer_stride) return set_err(QTB_E_INVALID, "length %d out of range", len);
+  if (len == 0) return 0;
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  std::vector<int> pt(b.pt_stride);
+  CUDA_TRY(cudaMemcpy(pt.data(), b.page_table + (size_t)slot * b.pt_stride, pt.size() * 4, cudaMemcpyDeviceToHost));
+  for (int i = 0; i < (len + PAGE - 1) / PAGE; i++)
+    if (pt[i] < 0 || pt[i] >= b.n_pages) return set_err(QTB_E_INVALID, "slot %d has no page for positions %d..", slot, i * PAGE);
+  const size_t n = (size_t)k.n_layers * layer_stride * k.kv_dim();
+  uint16_t *dh = nullptr;
+  CUDA_TRY(cudaMalloc(&dh, n * 2));
+  int rc = 0;
+  const int *dpt = b.page_table + (size_t)slot * b.pt_stride;
+  for (int kvsel = 0; kvsel < 2 && !rc; kvsel++) {
+    uint16_t *host = kvsel ? vh : kh;
+    uint16_t *pool = kvsel ? b.vpool : b.kpool;
+    if (to_pool && cudaMemcpy(dh, host, n * 2, cudaMemcpyHostToDevice) != cudaSuccess) { rc = set_err(QTB_E_CUDA, "kv upload"); break; }
+    kv_copy_kernel<<<512, 256, 0, s->stream>>>(pool, dpt, b.pt_stride, k.n_kv, layer_elems, dh, layer_stride, len,
+                                                k.n_layers, to_pool);
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess) { rc = set_err(QTB_E_CUDA, "kv copy kernel: %s", cudaGetErrorString(cudaGetLastError())); break; }
+    if (!to_pool && cudaMemcpy(host, dh, n * 2, cudaMemcpyDeviceToHost) != cudaSuccess) { rc = set_err(QTB_E_CUDA, "kv download"); break; }
+  }
+  cudaFree(dh);
+  return rc;
+}
+
+extern "C" int qtb_session_upload_kv(qtb_session_t *s, int b, const uint16_t *k, const uint16_t *v, int layer_stride, int len) {
+  if (!s || !s->e->has_talker) return set_err(QTB_E_INVALID, "no talker");
+  return kv_transfer(s, s->tk, s->e->talker, s->tk_layer_elems, b, (uint16_t *)k, (uint16_t *)v, layer_stride, len, 1);
+}
+extern "C" int qtb_session_download_kv(qtb_session_t *s, int b, uint16_t *k, uint16_t *v, int layer_stride, int len) {
+  if (!s || !s->e->has_talker) return set_err(QTB_E_INVALID, "no talker");
+  return kv_transfer(s, s->tk, s->e->talker, s->tk_layer_elems, b, k, v, layer_stride, len, 0);
+}
+extern "C" int qtb_session_download_cp_kv(qtb_session_t *s, int b, uint16_t *k, uint16_t *v, int layer_stride, int len) {
+  if (!s || !s->e->has_cp) return set_err(QTB_E_INVALID, "no code predictor");
+  return kv_transfer(s, s->cp, s->e->cp, s->cp_layer_elems, b, k, v, layer_stride, len, 0);
+}
+
+// ---------------------------------------------- standalone kernel entries --
+struct MiniRun {
+  Arena ar;
+  cudaStream_t st = nullptr;
+  ~MiniRun() {
+    if (st) cudaStreamDestroy(st);
+    ar.release();
+  }
+};
+
+static int run_single_stage(MiniRun &mr, const Stage &S) {
+  int rc;
+  Stage *dp;
+  Ctl *ctl;
+  if ((rc = mr.ar.upload(&dp, &S, sizeof S))) return rc;
+  if ((rc = mr.ar.alloc((void **)&ctl, sizeof(Ctl)))) return rc;
+  CUDA_TRY(cudaMemset(ctl, 0, sizeof(Ctl)));
+  int dev = 0, nsm = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  CUDA_TRY(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  const Stage *prog = dp;
+  int n_st = 1, n_it = 1;
+  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_it, (void *)&ctl};
+  CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(nsm), dim3(NTHREADS), args, SMEM_BYTES, mr.st));
+  CUDA_TRY(cudaStreamSynchronize(mr.st));
+  Ctl h;
+  CUDA_TRY(cudaMemcpy(&h, ctl, sizeof h, cudaMemcpyDeviceToHost));
+  if (h.err) return set_err(QTB_E_DEVICE, "kernel error %d (info %d)", h.err, h.err_info);
+  return 0;
+}
+
+extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols, const float *x, int batch, float *y) {
+  if (!w || !x || !y || batch < 1 || batch > 64) return set_err(QTB_E_INVALID, "bad argument");
+  MiniRun mr;
+  CUDA_TRY(cudaStreamCreateWithFlags(&mr.st, cudaStreamNonBlocking));
+  int dev = 0, nsm = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  DMat m;
+  const qtb_matrix_t *ms[1] = {w};
+  const int re[1] = {rows};
+  int rc = upload_matrix(mr.ar, fmt, ms, re, 1, cols, m);
+  if (rc) return rc;
+  float *dx, *dy, *ws;
+  unsigned *sem;
+  const int T = rows / 16;
+  const int S = choose_S(T, cols, batch, nsm * NWARPS, fmt);
+  if (S < 1) return set_err(QTB_E_UNSUPPORTED, "no k-slicing fits");
+  if ((rc = mr.ar.upload(&dx, x, (size_t)batch * cols * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&dy, (size_t)batch * rows * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&ws, (size_t)T * S * 16 * batch * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&sem, (size_t)T * 4))) return rc;
+  CUDA_TRY(cudaMemset(sem, 0, (size_t)T * 4));
+  Stage st;
+  memset(&st, 0, sizeof st);
+  st.kind = ST_GEMV;
+  st.B = batch;
+  GemvArgs &g = st.g;
+  g.w = m.w; g.row_scale = m.row_scale; g.gsz = m.gsz;
+  g.fmt = fmt; g.rows = rows; g.K = cols; g.S = S; g.nch = nch_for(batch);
+  g.x = dx; g.ldx = cols; g.y = dy; g.ldy = rows; g.epi = EPI_STORE; g.ws = ws; g.sem = sem;
+  if ((rc = run_single_stage(mr, st))) return rc;
+  CUDA_TRY(cudaMemcpy(y, dy, (size_t)batch * rows * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+extern "C" int qtb_attention_host(const float *qkv, int batch, int n_heads, int n_kv, int head_dim, const float *q_norm,
+                                  const float *k_norm, float eps, const float *rope_cos, const float *rope_sin, int rope_len,
+                                  uint16_t *kpages, uint16_t *vpages, int n_pages, const int32_t *page_table, int pt_stride,
+                                  const int32_t *pos, int max_splits, float *out) {
+  if (!qkv || !q_norm || !k_norm || !rope_cos || !rope_sin || !kpages || !vpages || !page_table || !pos || !out)
+    return set_err(QTB_E_INVALID, "null argument");
+  if (head_dim != HD || n_heads != 2 * n_kv || batch < 1 || batch > 64 || max_splits < 1 || max_splits > 64)
+    return set_err(QTB_E_UNSUPPORTED, "shape not supported");
+  for (int b = 0; b < batch; b++) {
+    if (pos[b] < 0 || pos[b] >= rope_len || pos[b] >= pt_stride * PAGE) return set_err(QTB_E_INVALID, "position out of range");
+    for (int i = 0; i <= pos[b] / PAGE; i++) {
+      const int p = page_table[(size_t)b * pt_stride + i];
+      if (p < 0 || p >= n_pages) return set_err(QTB_E_INVALID, "page table entry %d out of pool", p);
+    }
+  }
+  MiniRun mr;
+  CUDA_TRY(cudaStreamCreateWithFlags(&mr.st, cudaStreamNonBlocking));
+  const int qd = n_heads * HD, kvd = n_kv * HD, qkvd = qd + 2 * kvd;
+  const size_t pool = (size_t)n_pages * n_kv * PAGE * HD;
+  int rc;
+  float *dqkv, *dqn, *dkn, *dcos, *dsin, *dout, *ws;
+  uint16_t *dk, *dv;
+  int *dpt, *dpos;
+  unsigned *sem;
+  if ((rc = mr.ar.upload(&dqkv, qkv, (size_t)batch * qkvd * 4))) return rc;
+  if ((rc = mr.ar.upload(&dqn, q_norm, HD * 4))) return rc;
+  if ((rc = mr.ar.upload(&dkn, k_norm, HD * 4))) return rc;
+  if ((rc = mr.ar.upload(&dcos, rope_cos, (size_t)rope_len * (HD / 2) * 4))) return rc;
+  if ((rc = mr.ar.upload(&dsin, rope_sin, (size_t)rope_len * (HD / 2) * 4))) return rc;
+  if ((rc = mr.ar.upload(&dk, kpages, pool * 2))) return rc;
+  if ((rc = mr.ar.upload(&dv, vpages, pool * 2))) return rc;
+  if ((rc = mr.ar.upload(&dpt, page_table, (size_t)batch * pt_stride * 4))) return rc;
+  if ((rc = mr.ar.upload(&dpos, pos, (size_t)batch * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&dout, (size_t)batch * qd * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&ws, (size_t)batch * n_kv * max_splits * 2 * (HD + 2) * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&sem, (size_t)batch * n_kv * 4))) return rc;
+  CUDA_TRY(cudaMemset(sem, 0, (size_t)batch * n_kv * 4));
+  Stage st;
+  memset(&st, 0, sizeof st);
+  st.kind = ST_ATTN;
+  st.B = batch;
+  AttnArgs &a = st.a;
+  a.qkv = dqkv; a.ld_qkv = qkvd; a.out = dout; a.ld_out = qd;
+  a.q_norm = dqn; a.k_norm = dkn; a.rope_cos = dcos; a.rope_sin = dsin; a.rope_len = rope_len;
+  a.pos_ptr = dpos; a.page_table = dpt; a.pt_stride = pt_stride;
+  a.kpool = dk; a.vpool = dv; a.n_pages = n_pages; a.n_heads = n_heads; a.n_kv = n_kv;
+  a.eps = eps; a.scale = 1.0f / sqrtf((float)HD); a.max_splits = max_splits; a.min_pps = 1;
+  a.ws = ws; a.sem = sem;
+  if ((rc = run_single_stage(mr, st))) return rc;
+  CUDA_TRY(cudaMemcpy(out, dout, (size_t)batch * qd * 4, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(kpages, dk, pool * 2, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(vpages, dv, pool * 2, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+extern "C" int qtb_engine_talker_layers(const qtb_engine_t *e) { return e ? e->talker.n_layers : 0; }
+extern "C" int qtb_engine_talker_kv_dim(const qtb_engine_t *e) { return e ? e->talker.kv_dim() : 0; }

@@ -1,0 +1,893 @@
+// qtb_kernels.cuh -- the decode engine's device code.
+//
+// One persistent, cooperative kernel (decode_kernel) executes a "stage
+// program": a flat list of stages separated by grid-wide barriers.  A talker
+// step is 5 stages per layer (qwen_tts_talker.c:537-699):
+//   GEMV qkv   (RMSNorm prologue, [q;k;v] rows fused into one matrix)
+//   ATTN       (per-head QK RMSNorm + NeoX RoPE + bf16-truncating paged KV
+//               append + split-K GQA attention + in-stage split combine)
+//   GEMV o     (residual-add epilogue)
+//   GEMV gu    (RMSNorm prologue, SwiGLU epilogue on the interleaved rows)
+//   GEMV down  (residual-add epilogue)
+// and a code-predictor frame is 16 such 5-layer passes with a greedy lm_head
+// (GEMV with an argmax epilogue that also gathers the next pass's input
+// embedding) between them (qwen_tts_code_predictor.c:926-1045).
+//
+// GEMV = weights x activations on the tensor cores (mma.sync m16n8k16).  At
+// host upload every weight matrix is permuted into "fragment order": for each
+// 16-row tile and each k-chunk, lane l's 16 bytes are exactly its A-fragment
+// registers, so a warp streams 512 contiguous bytes per load and dequantizes
+// in registers (bf16: none; int8: 1 PRMT + 1 HSUB2 per 2 weights; int4: 1 LOP3
+// + 1 HSUB2 per 2 weights).  The f32 activation is split into hi + lo halves
+// (bf16 or fp16, matching the weight operand type) which occupy two MMA
+// columns, so the product keeps ~16-22 bits of activation precision with f32
+// accumulation -- the reference's f32-activation semantics
+// (qwen_tts_cuda_talker.cu:9-21) within a few 1e-6 relative.
+#pragma once
+#include "qtb_device.cuh"
+
+namespace qtb {
+
+constexpr int NTHREADS = 256;
+constexpr int NWARPS = NTHREADS / 32;
+constexpr int HD = 128;       // head_dim (Qwen3-TTS talker and CP)
+constexpr int PAGE = 16;      // KV positions per page
+constexpr int ATT_NBUF = 4;   // K/V page buffers in flight per CTA
+constexpr int SMEM_X_BYTES = 96 * 1024;
+constexpr int SMEM_MISC_BYTES = 8 * 1024;
+constexpr int SMEM_BYTES = SMEM_X_BYTES + SMEM_MISC_BYTES;
+constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
+
+enum StageKind { ST_GEMV = 1, ST_ATTN = 2, ST_EMBED = 3, ST_NORM = 4, ST_POS_INC = 5 };
+enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+enum Fmt { FMT_BF16 = 0, FMT_INT8 = 1, FMT_Q4_0 = 2, FMT_INT4G = 3 };
+enum ErrCode {
+  ERR_NONE = 0, ERR_BARRIER_TIMEOUT = 1, ERR_MBAR_TIMEOUT = 2, ERR_BAD_PAGE = 3,
+  ERR_BAD_POS = 4, ERR_BAD_CODE = 5, ERR_BAD_STAGE = 6
+};
+
+struct GemvArgs {
+  const uint8_t *w;          // fragment-ordered weights
+  const float *row_scale;    // int8: [rows]
+  const uint8_t *gsz;        // int4: per (tile, 64-col chunk, group-of-4-lanes) scale(/zero)
+  const float *bias;         // [rows] or null
+  int fmt, rows, K, S;       // S = k-slices; units = rows/16 * S
+  int nch;                   // MMA column chunks = ceil(2B/8)
+  int evict_last;            // keep these weights in L2 (code-predictor)
+  const float *x; int ldx;   // activation [B][ldx]
+  const float *norm_w;       // RMSNorm gain [K] or null
+  float eps;
+  float *y; int ldy;
+  int epi;
+  float *ws; unsigned *sem;  // split-K partials [units][16][B] and per-tile counters
+  // argmax epilogue
+  unsigned long long *amax_ws; unsigned *amax_sem;
+  int *codes; int code_stride;
+  const uint16_t *emb_table; int emb_ld; int emb_rows; float *emb_out; int emb_out_ld;
+};
+
+struct AttnArgs {
+  const float *qkv; int ld_qkv;
+  float *out; int ld_out;
+  const float *q_norm, *k_norm;
+  const float *rope_cos, *rope_sin; int rope_len;
+  const int *pos_ptr; int pos_const;
+  const int *page_table; int pt_stride;
+  uint16_t *kpool, *vpool; int n_pages;
+  int n_heads, n_kv;
+  float eps, scale;
+  int max_splits, min_pps;
+  float *ws; unsigned *sem;
+};
+
+struct EmbedArgs {
+  float *dst; int ld_dst; int dim;
+  const float *fsrc; int fsrc_ld;
+  int ntab;
+  const uint16_t *tab[16]; int tab_ld[16]; int tab_rows[16];
+  const int *code[16]; int code_stride[16];
+  const float *add;
+};
+
+struct NormArgs { const float *x; int ldx; const float *w; float *y; int ldy; int dim; float eps; };
+struct PosArgs { int *pos; };
+
+struct Stage {
+  int kind;
+  int B;
+  union {
+    GemvArgs g;
+    AttnArgs a;
+    EmbedArgs e;
+    NormArgs n;
+    PosArgs p;
+  };
+};
+
+struct Ctl {
+  unsigned bar_count;   // monotonic grid-barrier counter (zeroed before each launch)
+  int pad0[31];
+  int err;              // first error code
+  int err_stage;        // stage index that raised it
+  int err_info;
+  int pad1[29];
+};
+
+struct KCtx {
+  unsigned epoch;
+  unsigned page_ctr;    // K/V page buffers consumed so far (mbarrier phase source)
+  uint64_t pol_first, pol_last;
+  uint64_t *bars;
+  Ctl *ctl;
+  int stage;
+};
+
+// CTA-uniform read of the launch's error flag.
+QTB_DEV bool cta_err(KCtx &kc) {
+  __shared__ int s_e;
+  __syncthreads();
+  if (threadIdx.x == 0) s_e = *(volatile int *)&kc.ctl->err;
+  __syncthreads();
+  return s_e != 0;
+}
+
+QTB_DEV void raise_err(KCtx &kc, int code, int info) {
+  if (atomicCAS(&kc.ctl->err, 0, code) == 0) {
+    kc.ctl->err_stage = kc.stage;
+    kc.ctl->err_info = info;
+  }
+}
+
+// Grid-wide barrier on a monotonic counter.  Bounded: gives up (and raises
+// ERR_BARRIER_TIMEOUT) after WAIT_LIMIT_CYCLES, or as soon as any CTA has
+// raised an error, so a failing launch always returns.
+QTB_DEV bool grid_barrier(KCtx &kc) {
+  __shared__ int s_ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    __threadfence();
+    unsigned target = (kc.epoch + 1u) * gridDim.x;
+    atom_add_release_gpu(&kc.ctl->bar_count, 1u);
+    long long t0 = clock64();
+    while ((int)(ld_acquire_gpu(&kc.ctl->bar_count) - target) < 0) {
+      if (*(volatile int *)&kc.ctl->err) { ok = 0; break; }
+      if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_err(kc, ERR_BARRIER_TIMEOUT, (int)kc.epoch); ok = 0; break; }
+    }
+    __threadfence();
+    s_ok = ok && (*(volatile int *)&kc.ctl->err == 0);
+  }
+  __syncthreads();
+  kc.epoch++;
+  return s_ok != 0;
+}
+
+// =========================================================== GEMV stage ====
+
+// Split f32 pair into the hi or lo operand (fp16 or bf16) and pack 2 values.
+template <bool F16>
+QTB_DEV uint32_t split_pack(float v0, float v1, int lo) {
+  if (F16) {
+    __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+    if (lo) {
+      h0 = __float2half_rn(v0 - __half2float(h0));
+      h1 = __float2half_rn(v1 - __half2float(h1));
+    }
+    return (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+  } else {
+    uint32_t b0 = f32_to_bf16_rn(v0), b1 = f32_to_bf16_rn(v1);
+    if (lo) {
+      b0 = f32_to_bf16_rn(v0 - __uint_as_float(b0 << 16));
+      b1 = f32_to_bf16_rn(v1 - __uint_as_float(b1 << 16));
+    }
+    return b0 | (b1 << 16);
+  }
+}
+
+// Per-batch 1/rms of the stage input (every CTA recomputes it; x is small).
+QTB_DEV void stage_inv_rms(const GemvArgs &a, int B, float *s_inv) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int b = warp; b < B; b += NWARPS) {
+    const float *xb = a.x + (size_t)b * a.ldx;
+    float ss = 0.f;
+    for (int i = lane * 4; i < a.K; i += 128) {
+      float4 v = ld_cg4(xb + i);
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) s_inv[b] = 1.0f / sqrtf(ss / (float)a.K + a.eps);
+  }
+}
+
+QTB_DEV float norm_in(const GemvArgs &a, const float *s_inv, int b, int k, float v) {
+  return a.norm_w ? (v * s_inv[b]) * __ldg(a.norm_w + k) : v;
+}
+
+// Stage the activation slice [k0, k0 + kslice) of every batch row into shared
+// memory in B-fragment order (entry e = (kstep * nch + chunk) * ent + lane).
+template <bool F16>
+QTB_DEV void stage_x(const GemvArgs &a, int B, int ent, int k0, int kslice, const float *s_inv,
+                     float *s_xsum, uint2 *s_xf, bool want_xsum) {
+  const int nch = a.nch;
+  const int ksteps = kslice >> 4;
+  const int total = ksteps * nch * ent;
+  for (int e = threadIdx.x; e < total; e += NTHREADS) {
+    const int l = e % ent;
+    const int qj = e / ent;
+    const int j = qj % nch, q = qj / nch;
+    const int gid = l >> 2, tig = l & 3;
+    const int b = 4 * j + (gid >> 1), lo = gid & 1;
+    uint32_t r0 = 0, r1 = 0;
+    if (b < B) {
+      const int k = k0 + 16 * q + 2 * tig;
+      const float *xb = a.x + (size_t)b * a.ldx;
+      float2 p0 = __ldcg(reinterpret_cast<const float2 *>(xb + k));
+      float2 p1 = __ldcg(reinterpret_cast<const float2 *>(xb + k + 8));
+      float v0 = norm_in(a, s_inv, b, k, p0.x), v1 = norm_in(a, s_inv, b, k + 1, p0.y);
+      float v2 = norm_in(a, s_inv, b, k + 8, p1.x), v3 = norm_in(a, s_inv, b, k + 9, p1.y);
+      r0 = split_pack<F16>(v0, v1, lo);
+      r1 = split_pack<F16>(v2, v3, lo);
+    }
+    s_xf[e] = make_uint2(r0, r1);
+  }
+  if (want_xsum) {
+    const int ng = kslice >> 5;
+    for (int idx = threadIdx.x; idx < B * ng; idx += NTHREADS) {
+      const int b = idx / ng, gl = idx - b * ng;
+      const float *xb = a.x + (size_t)b * a.ldx;
+      const int kb = k0 + gl * 32;
+      float s = 0.f;
+#pragma unroll 4
+      for (int i = 0; i < 32; i += 2) {
+        float2 p = __ldcg(reinterpret_cast<const float2 *>(xb + kb + i));
+        s += norm_in(a, s_inv, b, kb + i, p.x);
+        s += norm_in(a, s_inv, b, kb + i + 1, p.y);
+      }
+      s_xsum[idx] = s;
+    }
+  }
+}
+
+template <int FMT> struct FmtTraits;
+template <> struct FmtTraits<FMT_BF16> { static constexpr int CK = 1; static constexpr int GSZ = 0; };
+template <> struct FmtTraits<FMT_INT8> { static constexpr int CK = 2; static constexpr int GSZ = 0; };
+template <> struct FmtTraits<FMT_Q4_0> { static constexpr int CK = 4; static constexpr int GSZ = 8; };
+template <> struct FmtTraits<FMT_INT4G> { static constexpr int CK = 4; static constexpr int GSZ = 16; };
+
+// One warp computes one unit: 16 rows x kslice columns, all batch columns.
+// res[j][0] / res[j][1] = rows (16t + gid) / (16t + gid + 8) for b = 4j + tig.
+template <int FMT, int NCH>
+QTB_DEV void gemv_unit(const GemvArgs &a, int B, int t, int s, int kslice, const uint2 *s_xf,
+                       int ent, const float *s_xsum, float (&res)[NCH][2], const KCtx &kc) {
+  using Tr = FmtTraits<FMT>;
+  constexpr int CK = Tr::CK;
+  // loads in flight per lane: deep for small batches (bandwidth-bound), shallow
+  // for large ones (tensor-bound, and the accumulators need the registers)
+  constexpr int PD = NCH >= 8 ? 2 : (NCH >= 4 ? 4 : 8);
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int nck_total = a.K / (16 * CK);
+  const int nck = kslice / (16 * CK);
+  const size_t cbase = (size_t)t * nck_total + (size_t)s * nck;
+  const uint8_t *wp = a.w + cbase * 512 + lane * 16;
+  const uint8_t *gp = Tr::GSZ ? a.gsz + cbase * (8 * Tr::GSZ) + gid * Tr::GSZ : nullptr;
+  const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
+  const bool has_x = lane < ent;
+
+  float acc[NCH][4];
+#pragma unroll
+  for (int j = 0; j < NCH; j++) { acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f; res[j][0] = res[j][1] = 0.f; }
+
+  uint4 wbuf[PD];
+  uint4 gbuf[PD];
+#pragma unroll
+  for (int i = 0; i < PD; i++) {
+    if (i < nck) {
+      wbuf[i] = ld_stream_hint(wp + (size_t)i * 512, pol);
+      if (Tr::GSZ == 8) { uint2 g = ld_nc_u2(gp + (size_t)i * 64); gbuf[i] = make_uint4(g.x, g.y, 0, 0); }
+      if (Tr::GSZ == 16) gbuf[i] = ld_nc_u4(gp + (size_t)i * 128);
+    }
+  }
+  for (int c0 = 0; c0 < nck; c0 += PD) {
+#pragma unroll
+    for (int i = 0; i < PD; i++) {
+      const int c = c0 + i;
+      if (c < nck) {
+        const uint4 wv = wbuf[i];
+        const uint4 gv = gbuf[i];
+        if (c + PD < nck) {
+          wbuf[i] = ld_stream_hint(wp + (size_t)(c + PD) * 512, pol);
+          if (Tr::GSZ == 8) { uint2 g = ld_nc_u2(gp + (size_t)(c + PD) * 64); gbuf[i] = make_uint4(g.x, g.y, 0, 0); }
+          if (Tr::GSZ == 16) gbuf[i] = ld_nc_u4(gp + (size_t)(c + PD) * 128);
+        }
+        if (FMT == FMT_BF16) {
+          const uint32_t A[4] = {wv.x, wv.y, wv.z, wv.w};
+          const uint2 *xf = s_xf + (size_t)c * NCH * ent;
+#pragma unroll
+          for (int j = 0; j < NCH; j++) {
+            uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
+            mma_bf16(acc[j], A, bx.x, bx.y);
+          }
+        } else if (FMT == FMT_INT8) {
+          const uint32_t wd[4] = {wv.x ^ 0x80808080u, wv.y ^ 0x80808080u, wv.z ^ 0x80808080u, wv.w ^ 0x80808080u};
+#pragma unroll
+          for (int q = 0; q < 2; q++) {
+            const uint32_t A[4] = {i8x2_to_f16x2(wd[2 * q], 0x4140), i8x2_to_f16x2(wd[2 * q], 0x4342),
+                                   i8x2_to_f16x2(wd[2 * q + 1], 0x4140), i8x2_to_f16x2(wd[2 * q + 1], 0x4342)};
+            const uint2 *xf = s_xf + (size_t)(2 * c + q) * NCH * ent;
+#pragma unroll
+            for (int j = 0; j < NCH; j++) {
+              uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
+              mma_f16(acc[j], A, bx.x, bx.y);
+            }
+          }
+        } else {
+          // int4: two groups of 32 columns per chunk.
+          const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int gh = 0; gh < 2; gh++) {
+            float sc0, sc1, z0, z1;
+            if (FMT == FMT_Q4_0) {
+              sc0 = half_bits_to_f32(gh ? (gv.x >> 16) : (gv.x & 0xffffu));
+              sc1 = half_bits_to_f32(gh ? (gv.y >> 16) : (gv.y & 0xffffu));
+              z0 = 8.f; z1 = 8.f;
+            } else {
+              sc0 = half_bits_to_f32(gh ? (gv.x >> 16) : (gv.x & 0xffffu));
+              sc1 = half_bits_to_f32(gh ? (gv.y >> 16) : (gv.y & 0xffffu));
+              z0 = half_bits_to_f32(gh ? (gv.z >> 16) : (gv.z & 0xffffu));
+              z1 = half_bits_to_f32(gh ? (gv.w >> 16) : (gv.w & 0xffffu));
+            }
+            const int gl = 2 * c + gh;   // group index within the slice
+#pragma unroll
+            for (int j = 0; j < NCH; j++) {
+              float cg[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+              for (int qq = 0; qq < 2; qq++) {
+                const uint32_t w = wd[2 * gh + qq];
+                const uint32_t A[4] = {u4x2_to_f16x2(w), u4x2_to_f16x2(w >> 4), u4x2_to_f16x2(w >> 8),
+                                       u4x2_to_f16x2(w >> 12)};
+                const uint2 *xf = s_xf + (size_t)(4 * c + 2 * gh + qq) * NCH * ent;
+                uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
+                mma_f16(cg, A, bx.x, bx.y);
+              }
+              const int b = 4 * j + tig;
+              const float xs = (b < B) ? s_xsum[b * (kslice >> 5) + gl] : 0.f;
+              res[j][0] += sc0 * ((cg[0] + cg[1]) - z0 * xs);
+              res[j][1] += sc1 * ((cg[2] + cg[3]) - z1 * xs);
+            }
+          }
+        }
+      }
+    }
+  }
+  if (FMT == FMT_BF16 || FMT == FMT_INT8) {
+#pragma unroll
+    for (int j = 0; j < NCH; j++) {
+      res[j][0] = acc[j][0] + acc[j][1];
+      res[j][1] = acc[j][2] + acc[j][3];
+    }
+  }
+}
+
+QTB_DEV unsigned long long amax_key(float v, int row) {
+  return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xffffffffu - (unsigned)row);
+}
+QTB_DEV unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+  unsigned lo = (unsigned)v, hi = (unsigned)(v >> 32);
+  lo = __shfl_xor_sync(0xffffffffu, lo, m);
+  hi = __shfl_xor_sync(0xffffffffu, hi, m);
+  return ((unsigned long long)hi << 32) | lo;
+}
+
+// Epilogue for the 16 final rows of tile t (called by exactly one warp).
+template <int NCH>
+QTB_DEV void gemv_epilogue(const GemvArgs &a, int B, int t, int T, float (&res)[NCH][2], KCtx &kc) {
+  const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int j = 0; j < NCH; j++) {
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const int row = 16 * t + gid + 8 * r;
+      float v = res[j][r];
+      if (a.row_scale) v = __ldg(a.row_scale + row) * v;
+      if (a.bias) v += __ldg(a.bias + row);
+      res[j][r] = v;
+    }
+  }
+  if (a.epi == EPI_ARGMAX) {
+#pragma unroll
+    for (int j = 0; j < NCH; j++) {
+      unsigned long long k0 = amax_key(res[j][0], 16 * t + gid), k1 = amax_key(res[j][1], 16 * t + gid + 8);
+      unsigned long long k = k0 > k1 ? k0 : k1;
+#pragma unroll
+      for (int m = 4; m < 32; m <<= 1) {
+        unsigned long long o = shfl_xor_u64(k, m);
+        k = o > k ? o : k;
+      }
+      const int b = 4 * j + tig;
+      if (gid == 0 && b < B) a.amax_ws[(size_t)t * B + b] = k;
+    }
+    __syncwarp();
+    unsigned old = 0;
+    if (lane == 0) { __threadfence(); old = atomicAdd(a.amax_sem, 1u); }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != (unsigned)(T - 1)) return;
+    __threadfence();
+    for (int b0 = 0; b0 < B; b0 += 32) {
+      const int b = b0 + lane;
+      int code = 0;
+      if (b < B) {
+        unsigned long long best = 0ull;
+        for (int tt = 0; tt < T; tt++) {
+          unsigned long long k = __ldcg(a.amax_ws + (size_t)tt * B + b);
+          best = k > best ? k : best;
+        }
+        code = (int)(0xffffffffu - (unsigned)(best & 0xffffffffull));
+        a.codes[(size_t)b * a.code_stride] = code;
+      }
+      if (a.emb_table) {
+        const int nb = min(32, B - b0);
+        for (int bb = 0; bb < nb; bb++) {
+          int cb = __shfl_sync(0xffffffffu, code, bb);
+          if (cb < 0 || cb >= a.emb_rows) { if (lane == 0) raise_err(kc, ERR_BAD_CODE, cb); cb = 0; }
+          const uint16_t *row = a.emb_table + (size_t)cb * a.emb_ld;
+          float *dst = a.emb_out + (size_t)(b0 + bb) * a.emb_out_ld;
+          for (int i = lane * 8; i < a.emb_ld; i += 256) {
+            uint4 v = ld_nc_u4(row + i);
+            float4 lo4 = make_float4(bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y));
+            float4 hi4 = make_float4(bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w));
+            __stcg(reinterpret_cast<float4 *>(dst + i), lo4);
+            __stcg(reinterpret_cast<float4 *>(dst + i + 4), hi4);
+          }
+        }
+      }
+    }
+    if (lane == 0) *a.amax_sem = 0u;
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < NCH; j++) {
+    const int b = 4 * j + tig;
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const int row = 16 * t + gid + 8 * r;
+      const float v = res[j][r];
+      if (a.epi == EPI_SWIGLU) {
+        const float up = __shfl_xor_sync(0xffffffffu, v, 4);
+        if ((gid & 1) == 0 && b < B) {
+          const float g = v;
+          __stcg(a.y + (size_t)b * a.ldy + (row >> 1), g / (1.0f + expf(-g)) * up);
+        }
+      } else if (b < B) {
+        float *yp = a.y + (size_t)b * a.ldy + row;
+        if (a.epi == EPI_RESID) __stcg(yp, __ldcg(yp) + v);
+        else __stcg(yp, v);
+      }
+    }
+  }
+}
+
+template <int FMT, int NCH>
+__device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  const int T = a.rows >> 4;
+  const int S = a.S;
+  const int U = T * S;
+  const int kslice = a.K / S;
+  const int W = gridDim.x * NWARPS;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int ent = 4 * min(8, 2 * B);
+  constexpr bool F16 = (FMT != FMT_BF16);
+  constexpr bool XSUM = (FMT == FMT_Q4_0 || FMT == FMT_INT4G);
+
+  float *s_inv = reinterpret_cast<float *>(smem);                 // 64 floats
+  float *s_xsum = s_inv + 64;                                     // B * kslice/32 (int4)
+  const int xsum_n = XSUM ? ((B * (kslice >> 5) + 3) & ~3) : 0;
+  uint2 *s_xf = reinterpret_cast<uint2 *>(s_xsum + xsum_n);
+
+  bool inv_done = false;
+  for (int base = blockIdx.x * NWARPS; base < U; base += W) {
+    if (a.norm_w && !inv_done) { stage_inv_rms(a, B, s_inv); __syncthreads(); inv_done = true; }
+    const int s = base / T;
+    stage_x<F16>(a, B, ent, s * kslice, kslice, s_inv, s_xsum, s_xf, XSUM);
+    __syncthreads();
+    const int u = base + warp;
+    if (u < U) {
+      const int t = u - s * T;
+      float res[NCH][2];
+      gemv_unit<FMT, NCH>(a, B, t, s, kslice, s_xf, ent, s_xsum, res, kc);
+      bool finish = true;
+      if (S > 1) {
+#pragma unroll
+        for (int j = 0; j < NCH; j++) {
+          const int b = 4 * j + tig;
+          if (b < B) {
+            __stcg(a.ws + ((size_t)u * 16 + gid) * B + b, res[j][0]);
+            __stcg(a.ws + ((size_t)u * 16 + gid + 8) * B + b, res[j][1]);
+          }
+        }
+        __syncwarp();
+        unsigned old = 0;
+        if (lane == 0) { __threadfence(); old = atomicAdd(a.sem + t, 1u); }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        finish = (old == (unsigned)(S - 1));
+        if (finish) {
+          __threadfence();
+#pragma unroll
+          for (int j = 0; j < NCH; j++) {
+            const int b = 4 * j + tig;
+            float v0 = 0.f, v1 = 0.f;
+            if (b < B) {
+              for (int ss = 0; ss < S; ss++) {
+                const size_t uu = (size_t)ss * T + t;
+                v0 += __ldcg(a.ws + (uu * 16 + gid) * B + b);
+                v1 += __ldcg(a.ws + (uu * 16 + gid + 8) * B + b);
+              }
+            }
+            res[j][0] = v0;
+            res[j][1] = v1;
+          }
+          if (lane == 0) a.sem[t] = 0u;
+        }
+      }
+      if (finish) gemv_epilogue<NCH>(a, B, t, T, res, kc);
+    }
+    __syncthreads();
+  }
+}
+
+template <int FMT>
+QTB_DEV void gemv_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  switch (a.nch) {
+    case 1: gemv_stage_t<FMT, 1>(a, B, smem, kc); break;
+    case 2: gemv_stage_t<FMT, 2>(a, B, smem, kc); break;
+    case 4: gemv_stage_t<FMT, 4>(a, B, smem, kc); break;
+    case 8: gemv_stage_t<FMT, 8>(a, B, smem, kc); break;
+    case 16: gemv_stage_t<FMT, 16>(a, B, smem, kc); break;
+    default: if (threadIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, a.nch); break;
+  }
+}
+
+QTB_DEV void gemv_stage(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  switch (a.fmt) {
+    case FMT_BF16: gemv_stage_f<FMT_BF16>(a, B, smem, kc); break;
+    case FMT_INT8: gemv_stage_f<FMT_INT8>(a, B, smem, kc); break;
+    case FMT_Q4_0: gemv_stage_f<FMT_Q4_0>(a, B, smem, kc); break;
+    case FMT_INT4G: gemv_stage_f<FMT_INT4G>(a, B, smem, kc); break;
+    default: if (threadIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, a.fmt); break;
+  }
+}
+
+// =========================================================== ATTN stage ====
+//
+// Work item = (slot b, kv head g, split sp).  Every CTA of an item recomputes
+// the normed + roped query heads 2g, 2g+1 (qwen_rms_norm_per_head,
+// qwen_tts_kernels.c:486-577; apply_rope_neox_inplace, qwen_tts_talker.c:
+// 203-251) and the new K/V of head g; the CTA whose split holds the newest
+// page also appends K/V (bf16 by truncation, qwen_tts_talker.c:612-615) into
+// the slot's page with 16-byte stores.  Pages are staged into shared memory
+// by 1D bulk copies (cp.async.bulk, mbarrier completion) through a 4-deep
+// ring.  Scores use the reference's order (dot, then * scale); the softmax is
+// the same online recurrence as qwen_causal_attention_bf16kv
+// (qwen_tts_kernels.c:3704-3846) applied per page.  When an item has several
+// splits the last finishing CTA combines them (deterministic order).
+
+struct AttnSmem {
+  float q[2][HD];
+  float sc[2][PAGE];
+  float p[2][PAGE];
+  float corr[2];
+  float l[2];
+  float m[2];
+  int flag;
+  uint16_t knew[HD];
+  uint16_t vnew[HD];
+};
+
+__device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KCtx &kc) {
+  AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem);
+  uint16_t *kvbuf = reinterpret_cast<uint16_t *>(smem + 2048);   // ATT_NBUF x [K 16x128 | V 16x128]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q_dim = a.n_heads * HD, kv_dim = a.n_kv * HD;
+  const int n_items = B * a.n_kv * a.max_splits;
+
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const int sp = item % a.max_splits;
+    const int bg = item / a.max_splits;
+    const int g = bg % a.n_kv, b = bg / a.n_kv;
+    int pos = a.pos_ptr ? __ldcg(a.pos_ptr + b) : a.pos_const;
+    if (pos < 0 || pos >= a.rope_len || pos >= a.pt_stride * PAGE) {
+      if (threadIdx.x == 0) raise_err(kc, ERR_BAD_POS, pos);
+      return;
+    }
+    const int L = pos + 1;
+    const int npages = (L + PAGE - 1) / PAGE;
+    int nsp = min(a.max_splits, (npages + a.min_pps - 1) / a.min_pps);
+    const int pps = (npages + nsp - 1) / nsp;
+    nsp = (npages + pps - 1) / pps;
+    if (sp >= nsp) continue;
+    const int p_begin = sp * pps, p_end = min(npages, p_begin + pps);
+    const bool owns_new = (p_end == npages);
+    const int *pt = a.page_table + (size_t)b * a.pt_stride;
+
+    // ---- prologue: QK RMSNorm + RoPE (+ KV append) ----
+    if (warp < 4) {
+      const float *src;
+      const float *nw = nullptr;
+      if (warp < 2) { src = a.qkv + (size_t)b * a.ld_qkv + (2 * g + warp) * HD; nw = a.q_norm; }
+      else if (warp == 2) { src = a.qkv + (size_t)b * a.ld_qkv + q_dim + g * HD; nw = a.k_norm; }
+      else src = a.qkv + (size_t)b * a.ld_qkv + q_dim + kv_dim + g * HD;
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) v[i] = __ldcg(src + lane + 32 * i);
+      if (nw) {
+        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = (v[i] * inv) * __ldg(nw + lane + 32 * i);
+        const float *cp = a.rope_cos + (size_t)pos * (HD / 2);
+        const float *snp = a.rope_sin + (size_t)pos * (HD / 2);
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+          const int d = lane + 32 * i;
+          const float c = __ldg(cp + d), s = __ldg(snp + d);
+          const float x1 = v[i], x2 = v[i + 2];
+          v[i] = fmaf(x1, c, -(x2 * s));
+          v[i + 2] = fmaf(x2, c, x1 * s);
+        }
+      }
+      if (warp < 2) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) sm->q[warp][lane + 32 * i] = v[i];
+      } else {
+        uint16_t *dst = (warp == 2) ? sm->knew : sm->vnew;
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[lane + 32 * i] = (uint16_t)f32_to_bf16_trunc(v[i]);
+      }
+    }
+    if (threadIdx.x == 0) {
+      sm->m[0] = sm->m[1] = -INFINITY;
+      sm->l[0] = sm->l[1] = 0.f;
+    }
+    __syncthreads();
+    if (owns_new && threadIdx.x < 32) {
+      const int page = __ldg(pt + pos / PAGE);
+      if (page < 0 || page >= a.n_pages) {
+        if (threadIdx.x == 0) raise_err(kc, ERR_BAD_PAGE, page);
+      } else {
+        const int half = threadIdx.x >> 4, part = threadIdx.x & 15;   // 16 x 16 B per K / V row
+        uint16_t *pool = half ? a.vpool : a.kpool;
+        const uint16_t *srcv = half ? sm->vnew : sm->knew;
+        uint4 val = *reinterpret_cast<const uint4 *>(srcv + part * 8);
+        uint16_t *dst = pool + (((size_t)page * a.n_kv + g) * PAGE + (pos % PAGE)) * HD + part * 8;
+        __stcg(reinterpret_cast<uint4 *>(dst), val);
+      }
+    }
+    if (cta_err(kc)) return;
+
+    // ---- main loop over this split's pages ----
+    const int n = p_end - p_begin;
+    const int tid = threadIdx.x;
+    const int hh = tid >> 7, d = tid & 127;
+    float acc = 0.f;
+    if (tid == 0) {
+      fence_proxy_async();
+      for (int i = 0; i < min(n, ATT_NBUF); i++) {
+        const unsigned ctr = kc.page_ctr + i;
+        const int buf = ctr % ATT_NBUF;
+        int page = __ldg(pt + p_begin + i);
+        if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
+        uint16_t *dstk = kvbuf + (size_t)buf * 2 * PAGE * HD;
+        const size_t off = (((size_t)page * a.n_kv + g) * PAGE) * HD;
+        mbar_arrive_expect_tx(kc.bars + buf, 2 * PAGE * HD * 2);
+        bulk_g2s(dstk, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
+        bulk_g2s(dstk + PAGE * HD, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
+      }
+    }
+    for (int i = 0; i < n; i++) {
+      const unsigned ctr = kc.page_ctr + i;
+      const int buf = ctr % ATT_NBUF;
+      const uint32_t parity = (ctr / ATT_NBUF) & 1u;
+      if (tid == 0) {
+        if (!mbar_wait(kc.bars + buf, parity, WAIT_LIMIT_CYCLES)) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+      }
+      if (cta_err(kc)) {
+        // leave no bulk copy in flight: wait (bounded) for the ones issued after this page
+        if (tid == 0)
+          for (int j = i + 1; j < min(n, i + ATT_NBUF); j++) {
+            const unsigned c2 = kc.page_ctr + j;
+            mbar_wait(kc.bars + (c2 % ATT_NBUF), (c2 / ATT_NBUF) & 1u, 100000000LL);
+          }
+        __syncthreads();
+        return;
+      }
+      uint16_t *kb = kvbuf + (size_t)buf * 2 * PAGE * HD;
+      uint16_t *vb = kb + PAGE * HD;
+      const int pg = p_begin + i;
+      const int ntok = min(PAGE, L - pg * PAGE);
+      if (pg == npages - 1 && owns_new) {
+        // The newest token is taken from registers/smem, not from the copy.
+        const int slot = pos % PAGE;
+        if (tid < HD) { kb[slot * HD + tid] = sm->knew[tid]; vb[slot * HD + tid] = sm->vnew[tid]; }
+        __syncthreads();
+      }
+      // scores: warp w -> tokens 2w, 2w+1; lane -> dims 4*lane .. 4*lane+3
+      {
+        float part[2][2];
+#pragma unroll
+        for (int tt = 0; tt < 2; tt++) {
+          const int tok = 2 * warp + tt;
+          const uint2 kv = *reinterpret_cast<const uint2 *>(kb + tok * HD + lane * 4);
+          const float k0 = bf16lo(kv.x), k1 = bf16hi(kv.x), k2 = bf16lo(kv.y), k3 = bf16hi(kv.y);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; h2++) {
+            const float *qq = sm->q[h2] + lane * 4;
+            part[tt][h2] = qq[0] * k0 + qq[1] * k1 + qq[2] * k2 + qq[3] * k3;
+          }
+        }
+#pragma unroll
+        for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+          for (int h2 = 0; h2 < 2; h2++) part[tt][h2] = warp_sum(part[tt][h2]);
+        if (lane == 0) {
+#pragma unroll
+          for (int tt = 0; tt < 2; tt++) {
+            const int tok = 2 * warp + tt;
+#pragma unroll
+            for (int h2 = 0; h2 < 2; h2++) sm->sc[h2][tok] = (tok < ntok) ? part[tt][h2] * a.scale : -INFINITY;
+          }
+        }
+      }
+      __syncthreads();
+      if (tid < 32) {
+        const int h2 = tid >> 4, tok = tid & 15;
+        const float s = sm->sc[h2][tok];
+        float mx = s;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float m_old = sm->m[h2];
+        const float m_new = fmaxf(m_old, mx);
+        const float p = (tok < ntok) ? expf(s - m_new) : 0.f;
+        float ps = p;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        sm->p[h2][tok] = p;
+        __syncwarp();
+        if (tok == 0) {
+          const float corr = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+          sm->corr[h2] = corr;
+          sm->l[h2] = sm->l[h2] * corr + ps;
+          sm->m[h2] = m_new;
+        }
+      }
+      __syncthreads();
+      {
+        float s = 0.f;
+#pragma unroll
+        for (int tok = 0; tok < PAGE; tok++) {
+          const float vv = __uint_as_float(((uint32_t)vb[tok * HD + d]) << 16);
+          s = fmaf(sm->p[hh][tok], vv, s);
+        }
+        acc = acc * sm->corr[hh] + s;
+      }
+      __syncthreads();
+      if (tid == 0 && i + ATT_NBUF < n) {
+        int page = __ldg(pt + p_begin + i + ATT_NBUF);
+        if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
+        const size_t off = (((size_t)page * a.n_kv + g) * PAGE) * HD;
+        mbar_arrive_expect_tx(kc.bars + buf, 2 * PAGE * HD * 2);
+        bulk_g2s(kb, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
+        bulk_g2s(vb, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
+      }
+    }
+    kc.page_ctr += n;
+
+    // ---- output / split combine ----
+    const int head = 2 * g + hh;
+    if (nsp == 1) {
+      __stcg(a.out + (size_t)b * a.ld_out + head * HD + d, acc * (1.0f / sm->l[hh]));
+    } else {
+      float *wsi = a.ws + ((((size_t)b * a.n_kv + g) * a.max_splits + sp) * 2 + hh) * (HD + 2);
+      __stcg(wsi + d, acc);
+      if (d == 0) { __stcg(wsi + HD, sm->m[hh]); __stcg(wsi + HD + 1, sm->l[hh]); }
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) sm->flag = (atomicAdd(a.sem + (size_t)b * a.n_kv + g, 1u) == (unsigned)(nsp - 1));
+      __syncthreads();
+      if (sm->flag) {
+        __threadfence();
+        const float *w0 = a.ws + ((((size_t)b * a.n_kv + g) * a.max_splits) * 2 + hh) * (HD + 2);
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < nsp; s2++) M = fmaxf(M, __ldcg(w0 + (size_t)s2 * 2 * (HD + 2) + HD));
+        float Ls = 0.f, O = 0.f;
+        for (int s2 = 0; s2 < nsp; s2++) {
+          const float *wsp = w0 + (size_t)s2 * 2 * (HD + 2);
+          const float e = expf(__ldcg(wsp + HD) - M);
+          Ls += __ldcg(wsp + HD + 1) * e;
+          O += __ldcg(wsp + d) * e;
+        }
+        __stcg(a.out + (size_t)b * a.ld_out + head * HD + d, O * (1.0f / Ls));
+        if (tid == 0) a.sem[(size_t)b * a.n_kv + g] = 0u;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ============================================================ misc stages ==
+__device__ __noinline__ void embed_stage(const EmbedArgs &e, int B, KCtx &kc) {
+  const int total = B * e.dim;
+  for (int idx = blockIdx.x * NTHREADS + threadIdx.x; idx < total; idx += gridDim.x * NTHREADS) {
+    const int b = idx / e.dim, i = idx - b * e.dim;
+    float v = e.fsrc ? __ldcg(e.fsrc + (size_t)b * e.fsrc_ld + i) : 0.f;
+    for (int t = 0; t < e.ntab; t++) {
+      int c = __ldcg(e.code[t] + (size_t)b * e.code_stride[t]);
+      if (c < 0 || c >= e.tab_rows[t]) { if (i == 0) raise_err(kc, ERR_BAD_CODE, c); c = 0; }
+      v += __uint_as_float(((uint32_t)__ldg(e.tab[t] + (size_t)c * e.tab_ld[t] + i)) << 16);
+    }
+    if (e.add) v += __ldg(e.add + i);
+    __stcg(e.dst + (size_t)b * e.ld_dst + i, v);
+  }
+}
+
+__device__ __noinline__ void norm_stage(const NormArgs &n, int B) {
+  __shared__ float s_red[NWARPS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    const float *xb = n.x + (size_t)b * n.ldx;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n.dim; i += NTHREADS) { const float v = __ldcg(xb + i); ss += v * v; }
+    ss = warp_sum(ss);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARPS; w++) tot += s_red[w];
+    const float inv = 1.0f / sqrtf(tot / (float)n.dim + n.eps);
+    for (int i = threadIdx.x; i < n.dim; i += NTHREADS)
+      __stcg(n.y + (size_t)b * n.ldy + i, (__ldcg(xb + i) * inv) * __ldg(n.w + i));
+    __syncthreads();
+  }
+}
+
+// ====================================================== persistent kernel ==
+__global__ void __launch_bounds__(NTHREADS, 1)
+decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ctl) {
+  extern __shared__ __align__(128) char smem[];
+  __shared__ __align__(8) uint64_t bars[ATT_NBUF];
+  KCtx kc;
+  kc.epoch = 0;
+  kc.page_ctr = 0;
+  kc.pol_first = policy_evict_first();
+  kc.pol_last = policy_evict_last();
+  kc.bars = bars;
+  kc.ctl = ctl;
+  kc.stage = 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ATT_NBUF; i++) mbar_init(bars + i, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  for (int it = 0; it < n_iters; it++) {
+    for (int si = 0; si < n_stages; si++) {
+      const Stage *st = prog + si;
+      kc.stage = si;
+      const int B = st->B;
+      switch (st->kind) {
+        case ST_GEMV: gemv_stage(st->g, B, smem, kc); break;
+        case ST_ATTN: attn_stage(st->a, B, smem, kc); break;
+        case ST_EMBED: embed_stage(st->e, B, kc); break;
+        case ST_NORM: norm_stage(st->n, B); break;
+        case ST_POS_INC:
+          if (blockIdx.x == 0) for (int b = threadIdx.x; b < B; b += NTHREADS) st->p.pos[b] += 1;
+          break;
+        default:
+          if (threadIdx.x == 0 && blockIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, st->kind);
+          break;
+      }
+      if (!grid_barrier(kc)) return;
+    }
+  }
+}
+
+}  // namespace qtb

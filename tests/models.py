@@ -1,0 +1,69 @@
+"""Synthetic model fixtures shared by the CPU and GPU tests (seeded; the shapes
+of the Qwen3-TTS 0.6B / 1.7B talker and code predictor, or smaller stacks)."""
+import os
+import tempfile
+
+import numpy as np
+
+import qtts_b200 as Q
+import refbind
+
+
+def tiny_cfg(layers=2, cp_layers=2, hidden=1024, inter=3072):
+    return Q.ModelCfg(hidden=hidden, layers=layers, inter=inter, cp_layers=cp_layers)
+
+
+_cache = {}
+
+
+def build(cfg, seed=0, norm_gain="random", with_cp=True, tmpdir=None):
+    """(HostModel, safetensors path) for cfg; cached per process."""
+    key = (tuple(sorted(cfg.__dict__.items())), seed, norm_gain, with_cp)
+    if key in _cache:
+        return _cache[key]
+    m = Q.synth_model(cfg, seed=seed, with_cp=with_cp, norm_gain=norm_gain)
+    d = tmpdir or tempfile.mkdtemp(prefix="qtb_st_")
+    path = os.path.join(d, f"model_{abs(hash(key)) % 10**8}.safetensors")
+    refbind.write_safetensors(path, refbind.model_tensors(m))
+    _cache[key] = (m, path)
+    return m, path
+
+
+def ref_quantized(ref, cfg, fmt, cp=False, n_layers=None):
+    """The reference's own quantized bytes for every matrix (so the engine is
+    given byte-identical INT8 / q4_0 weights), keyed like Engine(quantized=)."""
+    out = {}
+    if fmt == "bf16":
+        return out
+    H = cfg.cp_hidden if cp else cfg.hidden
+    I = cfg.cp_inter if cp else cfg.inter
+    nh, nkv, hd = (cfg.cp_heads, cfg.cp_kv_heads, cfg.cp_head_dim) if cp else (cfg.heads, cfg.kv_heads, cfg.head_dim)
+    L = n_layers if n_layers is not None else (cfg.cp_layers if cp else cfg.layers)
+    shapes = {"wq": (nh * hd, H), "wk": (nkv * hd, H), "wv": (nkv * hd, H), "wo": (H, nh * hd),
+              "gate_up": (2 * I, H), "down": (H, I)}
+    which = {"wq": 0, "wk": 1, "wv": 2, "wo": 3, "gate_up": 4, "down": 5}
+    pre = "c" if cp else "t"
+    for l in range(L):
+        for nm, (r, c) in shapes.items():
+            if fmt == "int8":
+                q = ref.weight(cp, l, which[nm], 1, r * c, np.int8).reshape(r, c)
+                s = ref.weight(cp, l, which[nm], 2, r * 4, np.float32)
+                out[f"{pre}{l}.{nm}"] = {"data": q, "row_scale": s}
+            elif fmt == "q4_0":
+                b = ref.weight(cp, l, which[nm], 3, r * (c // 32) * 18, np.uint8).reshape(r, c // 32 * 18)
+                out[f"{pre}{l}.{nm}"] = {"data": b}
+    if cp:
+        for g in range(15):
+            r, c = cfg.codebook, cfg.cp_hidden
+            if fmt == "int8":
+                out[f"lm{g}"] = {"data": ref.lm_head(g, 1, r * c, np.int8).reshape(r, c),
+                                 "row_scale": ref.lm_head(g, 2, r * 4, np.float32)}
+            elif fmt == "q4_0":
+                out[f"lm{g}"] = {"data": ref.lm_head(g, 3, r * (c // 32) * 18, np.uint8).reshape(r, c // 32 * 18)}
+    return out
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))

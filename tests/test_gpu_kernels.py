@@ -1,0 +1,121 @@
+"""Per-kernel parity on the B200: the engine's tensor-core GEMV (all weight
+formats, batch 1..64) and the fused QK-norm + RoPE + paged KV append + split-K
+attention, against the numpy oracle (itself pinned to the reference in
+test_oracle_pin.py).  Tolerances are far tighter than the 1e-2 relative L2
+the reference's CPU kernels allow: f32 activations are carried as hi+lo
+halves, so the GEMV error is ~1e-6 relative."""
+import numpy as np
+import pytest
+
+import qtts_b200 as Q
+import qtts_oracle as O
+from models import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+GEMV_TOL = 2e-5
+
+
+def rand_w(rng, rows, cols):
+    return Q.bf16_from_f32(rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
+
+
+def oracle_gemv(fmt, q, W, x):
+    rows, cols = W.shape
+    if fmt == Q.FMT_BF16:
+        return O.matvec_bf16(W, x)
+    if fmt == Q.FMT_INT8:
+        return O.matvec_int8(q["data"], q["row_scale"], x)
+    if fmt == Q.FMT_Q4_0:
+        return O.matvec_q4_0(q["data"], rows, cols, x)
+    return O.matvec_int4g(q["data"], q["group_scale"], q["group_zero"], rows, cols, x)
+
+
+@pytest.mark.parametrize("fmt", [Q.FMT_BF16, Q.FMT_INT8, Q.FMT_Q4_0, Q.FMT_INT4G32])
+@pytest.mark.parametrize("rows,cols", [(256, 1024), (1024, 3072), (4096, 1024), (2048, 2048), (1024, 6144)])
+@pytest.mark.parametrize("batch", [1, 2, 5, 8, 17, 64])
+def test_gemv_matches_oracle(have_gpu, fmt, rows, cols, batch):
+    rng = np.random.default_rng(rows * 7 + cols + batch + fmt)
+    W = rand_w(rng, rows, cols)
+    q = Q.quantize(W, fmt)
+    x = rng.standard_normal((batch, cols), dtype=np.float32)
+    y = Q.gemv(fmt, q, rows, cols, x)
+    ref = oracle_gemv(fmt, q, W, x)
+    for b in range(batch):
+        assert rel_l2(y[b], ref[b]) < GEMV_TOL, (b, rel_l2(y[b], ref[b]))
+
+
+def test_gemv_large_activations_and_zero_rows(have_gpu):
+    rng = np.random.default_rng(9)
+    W = rand_w(rng, 256, 1024)
+    W[17] = 0
+    x = (rng.standard_normal((3, 1024)) * 300).astype(np.float32)
+    for fmt in (Q.FMT_BF16, Q.FMT_INT8, Q.FMT_Q4_0, Q.FMT_INT4G32):
+        q = Q.quantize(W, fmt)
+        y = Q.gemv(fmt, q, 256, 1024, x)
+        ref = oracle_gemv(fmt, q, W, x)
+        assert np.all(y[:, 17] == 0)
+        assert rel_l2(y, ref) < GEMV_TOL
+
+
+def make_attention_case(rng, B, pos, n_pages, nh=16, nkv=8, permute=True):
+    hd = 128
+    pt_stride = max(p // 16 + 1 for p in pos) + 2
+    pool = rng.permutation(n_pages) if permute else np.arange(n_pages)
+    pt = np.full((B, pt_stride), -1, np.int32)
+    nxt = 0
+    for b in range(B):
+        for i in range(pos[b] // 16 + 1):
+            pt[b, i] = pool[nxt]
+            nxt += 1
+    kp = Q.bf16_from_f32(rng.standard_normal((n_pages, nkv, 16, hd), dtype=np.float32))
+    vp = Q.bf16_from_f32(rng.standard_normal((n_pages, nkv, 16, hd), dtype=np.float32))
+    qkv = rng.standard_normal((B, (nh + 2 * nkv) * hd), dtype=np.float32)
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    cs, sn = Q.rope_tables(1e6, hd, 8192)
+    return qkv, kp, vp, pt, qn, kn, cs, sn
+
+
+@pytest.mark.parametrize("pos,max_splits", [([0, 15, 16, 37], 4), ([200, 1, 513, 2047], 8), ([4095], 32),
+                                            ([63, 64], 1)])
+def test_attention_append_matches_oracle(have_gpu, pos, max_splits):
+    rng = np.random.default_rng(sum(pos) + max_splits)
+    B, nh, nkv, hd, eps = len(pos), 16, 8, 128, 1e-6
+    n_pages = sum(p // 16 + 1 for p in pos) + 5
+    qkv, kp, vp, pt, qn, kn, cs, sn = make_attention_case(rng, B, pos, n_pages)
+    kp0, vp0 = kp.copy(), vp.copy()
+    out = Q.attention(qkv, nh, nkv, qn, kn, eps, cs, sn, kp, vp, pt, np.array(pos, np.int32), max_splits)
+    for b in range(B):
+        p = pos[b]
+        q = O.rope_neox(O.rms_norm_per_head(qkv[b, :nh * hd], qn, nh, hd, eps), nh, hd, cs, sn, p)
+        k = O.rope_neox(O.rms_norm_per_head(qkv[b, nh * hd:(nh + nkv) * hd], kn, nkv, hd, eps), nkv, hd, cs, sn, p)
+        v = qkv[b, (nh + nkv) * hd:]
+        page, slot = pt[b, p // 16], p % 16
+        got_k = kp[page, :, slot, :].reshape(-1)
+        got_v = vp[page, :, slot, :].reshape(-1)
+        # V append is a pure bf16 truncation: bit-exact
+        assert np.array_equal(got_v, O.bf16_trunc(v))
+        # K passes through QK-norm + RoPE first: equal up to one bf16 ulp
+        dk = np.abs(got_k.astype(np.int32) - O.bf16_trunc(k).astype(np.int32))
+        assert dk.max() <= 1 and np.mean(dk == 0) > 0.98
+        K, V = O.gather_pages(kp, vp, pt[b], p + 1)
+        ref = O.attention_bf16kv(q, K, V, nh, nkv, hd, p + 1)
+        assert rel_l2(out[b], ref) < 1e-5, (b, rel_l2(out[b], ref))
+    # nothing but the appended slots changed
+    touched = np.zeros(kp.shape[:1] + kp.shape[2:3], bool)
+    for b in range(B):
+        touched[pt[b, pos[b] // 16], pos[b] % 16] = True
+    for page in range(n_pages):
+        for slot in range(16):
+            if not touched[page, slot]:
+                assert np.array_equal(kp[page, :, slot], kp0[page, :, slot])
+                assert np.array_equal(vp[page, :, slot], vp0[page, :, slot])
+
+
+def test_attention_rejects_bad_page_table(have_gpu):
+    rng = np.random.default_rng(4)
+    qkv, kp, vp, pt, qn, kn, cs, sn = make_attention_case(rng, 1, [40], 8)
+    pt[0, 1] = 99  # outside the pool: refused on the host before launch
+    with pytest.raises(RuntimeError, match="page table"):
+        Q.attention(qkv, 16, 8, qn, kn, 1e-6, cs, sn, kp, vp, pt, np.array([40], np.int32), 4)

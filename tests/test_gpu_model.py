@@ -1,0 +1,240 @@
+"""Whole-step parity on the B200 against the reference's own CPU decode path
+(oracle/_ref), on seeded synthetic weights:
+
+- talker steps (bf16 / int8 / q4_0 with the reference's quantized bytes),
+  hidden states within tolerance and KV caches within one bf16 ulp;
+- the code-predictor frame: identical greedy codes;
+- paged KV (random page permutation) == identity pages, bit for bit;
+- batched slots == single-slot runs;
+- whole greedy frames on the device == the reference's frame loop;
+- 0.6B BF16: identical greedy codec tokens over 256 steps after a 64-token
+  prefill (the BASELINE config-1 workload).
+"""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import qtts_b200 as Q
+import qtts_oracle as O
+import refbind
+from models import build, ref_quantized, rel_l2, tiny_cfg
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+FMT = {"bf16": Q.FMT_BF16, "int8": Q.FMT_INT8, "q4_0": Q.FMT_Q4_0}
+
+
+def engine_from_ref(ref, m, cfg, fmt, with_cp=True, talker=True):
+    q = ref_quantized(ref, cfg, fmt)
+    if with_cp:
+        q.update(ref_quantized(ref, cfg, fmt, cp=True))
+    model = m
+    if not talker:
+        model = Q.HostModel(cfg, Q.HostStack([]), m.codec_head, m.codec_embedding, m.cp, m.cp_norm, m.cp_lm_head,
+                            m.cp_codec_emb, m.mtp_w, m.mtp_b)
+    if not with_cp:
+        model = Q.HostModel(cfg, m.talker, m.codec_head, m.codec_embedding)
+    return Q.Engine(model, FMT[fmt], FMT[fmt], rope=ref.rope(False), cp_rope=ref.rope(True), quantized=q)
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    cfg = tiny_cfg(layers=3, cp_layers=2)
+    m, path = build(cfg)
+    return cfg, m, path
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "int8", "q4_0"])
+def test_talker_steps_match_reference(have_gpu, tiny, fmt):
+    cfg, m, path = tiny
+    ref = refbind.RefModel(path, cfg, use_int8=(fmt == "int8"), use_int4=(fmt == "q4_0"), threads=8)
+    eng = engine_from_ref(ref, m, cfg, fmt, with_cp=False)
+    ses = Q.Session(eng, 1, 256)
+    rng = np.random.default_rng(3)
+    worst = 0.0
+    for pos in range(40):
+        e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+        h_ref = ref.talker_step(e)
+        h_gpu, dx = ses.talker_step(e, pos, want_dec_x=True)
+        worst = max(worst, rel_l2(h_gpu[0], h_ref))
+    assert worst < 1e-4, worst
+    kgpu, vgpu = ses.download_kv(0, cfg.layers, cfg.kv_heads * 128, 40)
+    for l in range(cfg.layers):
+        k, v = ref.kv(l, 40)
+        for a, b in ((kgpu[l], k), (vgpu[l], v)):
+            d = np.abs(a.astype(np.int32) - b.astype(np.int32))
+            assert d.max() <= 1 and np.mean(d == 0) > 0.98
+    ref.close()
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "int8"])
+def test_cp_frame_codes_match_reference(have_gpu, tiny, fmt):
+    cfg, m, path = tiny
+    ref = refbind.RefModel(path, cfg, use_int8=(fmt == "int8"), threads=8)
+    eng = engine_from_ref(ref, m, cfg, fmt, with_cp=True, talker=False)
+    ses = Q.Session(eng, 1)
+    rng = np.random.default_rng(4)
+    agree = 0
+    n = 6
+    for it in range(n):
+        hidden = rng.standard_normal(cfg.hidden).astype(np.float32)
+        code0 = int(rng.integers(0, 2048))
+        codes_ref = ref.cp_predict(hidden, code0)
+        codes_gpu = ses.cp_frame(hidden, code0)[0]
+        agree += int(np.array_equal(codes_ref, codes_gpu))
+    assert agree == n, f"{agree}/{n} frames identical"
+    # the single-pass entry point (qwen_cuda_cp_step semantics): residual out, no norm
+    x = rng.standard_normal(cfg.cp_hidden).astype(np.float32)
+    y = ses.cp_pass(x, 0)[0]
+    ccs, csn = ref.rope(True)
+    qd = ref_quantized(ref, cfg, fmt, cp=True)
+    qs = {k[1:]: v for k, v in qd.items() if k.startswith("c")} if fmt != "bf16" else None
+    st = O.Stack(m.cp.layers, cfg.cp_hidden, cfg.cp_heads, cfg.cp_kv_heads, 128, cfg.cp_inter, cfg.eps, ccs, csn,
+                 None, fmt, qs)
+    ref_y = O.stack_step(st, x, O.new_caches(st, 64), 0)
+    assert rel_l2(y, ref_y) < 1e-4
+    ref.close()
+
+
+def test_paged_equals_identity_pages_and_batch_equals_single(have_gpu, tiny):
+    cfg, m, path = tiny
+    eng = Q.Engine(Q.HostModel(cfg, m.talker, m.codec_head, m.codec_embedding), Q.FMT_BF16)
+    B, steps = 4, 40
+    rng = np.random.default_rng(5)
+    E = (0.1 * rng.standard_normal((steps, B, cfg.hidden))).astype(np.float32)
+    ident = Q.Session(eng, B, 256)
+    pool_pages = B * 16 + 7
+    paged = Q.Session(eng, B, 256, n_pages=pool_pages)
+    perm = rng.permutation(pool_pages)
+    for b in range(B):
+        paged.set_pages(b, perm[b * 16:(b + 1) * 16])
+    singles = [Q.Session(eng, 1, 256) for _ in range(B)]
+    for t in range(steps):
+        pos = np.full(B, t, np.int32)
+        a = ident.talker_step(E[t], pos)
+        bb = paged.talker_step(E[t], pos)
+        assert np.array_equal(a, bb), t
+        for b in range(B):
+            s = singles[b].talker_step(E[t, b], t)
+            assert rel_l2(s[0], a[b]) < 1e-5
+    k1, v1 = ident.download_kv(2, cfg.layers, 1024, steps)
+    k2, v2 = paged.download_kv(2, cfg.layers, 1024, steps)
+    assert np.array_equal(k1, k2) and np.array_equal(v1, v2)
+
+
+def test_kv_upload_download_roundtrip(have_gpu, tiny):
+    cfg, m, path = tiny
+    eng = Q.Engine(Q.HostModel(cfg, m.talker, m.codec_head, m.codec_embedding), Q.FMT_BF16)
+    ses = Q.Session(eng, 2, 512, n_pages=70)
+    rng = np.random.default_rng(6)
+    ses.set_pages(1, rng.permutation(70)[:20])
+    n = 300
+    k = rng.integers(0, 65535, (cfg.layers, 333, 1024), dtype=np.uint16)
+    v = rng.integers(0, 65535, (cfg.layers, 333, 1024), dtype=np.uint16)
+    ses.upload_kv(1, k, v, 333, n)
+    k2, v2 = ses.download_kv(1, cfg.layers, 1024, n)
+    assert np.array_equal(k2, k[:, :n]) and np.array_equal(v2, v[:, :n])
+
+
+def frame_loop_reference(ref, m, cfg, embed0, n_frames, with_cp):
+    """The reference's greedy frame loop (qwen_tts.c:1648-1816, greedy sampling,
+    pad = 0): hidden -> code0 -> CP codes -> next embedding."""
+    emb = embed0
+    out = []
+    cpe = [O.f32_from_bf16(t) for t in m.cp_codec_emb] if with_cp else None
+    for _ in range(n_frames):
+        h = ref.talker_step(emb)
+        c0 = ref.codec_argmax(h, cfg.codebook)
+        codes = ref.cp_predict(h, c0) if with_cp else np.zeros(15, np.int32)
+        out.append([c0] + list(codes))
+        nxt = ref.codec_embed(c0)
+        if with_cp:
+            for g in range(15):
+                nxt = (nxt + cpe[g][codes[g]]).astype(np.float32)
+        emb = nxt
+    return np.array(out, np.int32), h
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "int8"])
+def test_decode_frames_match_reference_loop(have_gpu, tiny, fmt):
+    cfg, m, path = tiny
+    ref = refbind.RefModel(path, cfg, use_int8=(fmt == "int8"), threads=8)
+    eng = engine_from_ref(ref, m, cfg, fmt, with_cp=True)
+    ses = Q.Session(eng, 1, 512)
+    rng = np.random.default_rng(7)
+    for pos in range(8):   # prefill
+        e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+        h = ref.talker_step(e)
+        ses.talker_step(e, pos)
+    ses.set_pos([8])
+    e0 = ref.codec_embed(ref.codec_argmax(h, cfg.codebook))
+    want, h_ref = frame_loop_reference(ref, m, cfg, e0, 12, True)
+    got, h_gpu = ses.decode_frames(e0, 12)
+    assert np.array_equal(got[:, 0, :], want), (got[:, 0, :], want)
+    assert rel_l2(h_gpu[0], h_ref) < 1e-3
+    assert ses.get_pos()[0] == 20
+    ref.close()
+
+
+@pytest.mark.slow
+def test_06b_bf16_greedy_256_steps_identical(have_gpu):
+    """0.6B BF16 talker, 64-token prefill of N(0,1)*0.1
+    embeddings, 256 greedy decode steps (next input = codec_embedding[code0])."""
+    cfg = Q.CFG_06B
+    m, path = build(cfg, seed=0, norm_gain="ones", with_cp=False)
+    ref = refbind.RefModel(path, cfg, threads=os.cpu_count(), cp=False)
+    eng = Q.Engine(m, Q.FMT_BF16, rope=ref.rope(False))
+    ses = Q.Session(eng, 1, 512)
+    rng = np.random.default_rng(0)
+    for pos in range(64):
+        e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+        h = ref.talker_step(e)
+        hg = ses.talker_step(e, pos)
+    assert rel_l2(hg[0], h) < 1e-3
+    ses.set_pos([64])
+    e0 = ref.codec_embed(ref.codec_argmax(h, cfg.codebook))
+    want, h_ref = frame_loop_reference(ref, m, cfg, e0, 256, False)
+    got, h_gpu = ses.decode_frames(e0, 256)
+    same = got[:, 0, 0] == want[:, 0]
+    first_fork = int(np.argmin(same)) if not same.all() else -1
+    assert same.all(), f"greedy tokens fork at step {first_fork}"
+    ref.close()
+
+
+def test_dropin_reference_delegates_to_engine(have_gpu, tiny, tmp_path):
+    """The reference's own qwen_talker_step / qwen_cp_predict (built with
+    QWEN_HAVE_CUDA) delegating into this library through the drop-in symbols,
+    against the same reference running on its CPU path."""
+    cfg, m, path = tiny
+    script = tmp_path / "dropin.py"
+    script.write_text(f"""
+import sys, ctypes, numpy as np
+sys.path[:0] = {[os.path.join(ROOT, 'qwen3-tts_b200'), os.path.join(ROOT, 'oracle'), os.path.join(ROOT, 'tests')]!r}
+import qtts_b200 as Q
+ctypes.CDLL(Q.LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+ctypes.CDLL(Q.DROPIN_PATH, mode=ctypes.RTLD_GLOBAL)
+import refbind
+from models import tiny_cfg
+cfg = tiny_cfg(layers=3, cp_layers=2)
+cpu = refbind.RefModel({path!r}, cfg, threads=8, dropin=True)
+gpu = refbind.RefModel({path!r}, cfg, threads=8, dropin=True)
+assert gpu.L.qref_dropin_attach(gpu.h, 1, 1) == 0
+rng = np.random.default_rng(11)
+worst = 0.0
+for pos in range(24):
+    e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+    a = cpu.talker_step(e); b = gpu.talker_step(e)
+    worst = max(worst, float(np.linalg.norm(a - b) / np.linalg.norm(a)))
+codes_a = cpu.cp_predict(a, 17); codes_b = gpu.cp_predict(a, 17)
+print("WORST", worst, "CODES", list(codes_a) == list(codes_b))
+""")
+    env = dict(os.environ)
+    r = subprocess.run([sys.executable, str(script)], capture_output=True, text=True, env=env, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("WORST")][-1]
+    worst = float(line.split()[1])
+    assert worst < 1e-4 and line.endswith("True"), line
