@@ -171,6 +171,18 @@ int qtb_session_download_cp_kv(qtb_session_t *s, int b, uint16_t *k, uint16_t *v
  * the number of decode-kernel launches it made, and the per-launch kernel time
  * of the last qtb_decode_frames call. */
 double qtb_session_last_ms(const qtb_session_t *s);
+/* Stage-level profile of one iteration of program `which` (0 talker step,
+ * 1 CP pass, 2 CP frame, 3 whole frame): SM cycles per stage (between grid
+ * barriers, measured on CTA 0), the stage kind (1 GEMV, 2 attention, 3 embed,
+ * 4 norm, 5 position advance) and rows * 65536 + cols for GEMV stages.
+ * Returns the number of stages (or a negative QTB_E_* code). */
+int qtb_session_profile(qtb_session_t *s, int which, long long *cycles, int *kind, int64_t *shape, int max_stages);
+/* Intra-stage checkpoints of the last qtb_session_profile call: 8 SM-clock
+ * stamps per stage taken by CTA 0 (0 where a checkpoint was not reached). */
+int qtb_session_profile_checkpoints(qtb_session_t *s, long long *out, int max_vals);
+/* Per-CTA grid-barrier arrival times (global timer, ns) of the last
+ * qtb_session_profile call, [stage][cta]. */
+int qtb_session_profile_arrivals(qtb_session_t *s, long long *out, int max_vals);
 int    qtb_session_last_launches(const qtb_session_t *s);
 
 /* Host-side weight encoders (no device needed).  src is bf16 [rows][cols].

@@ -141,6 +141,13 @@ QTB_DEV void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint
       "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+QTB_DEV void bulk_g2s_hint(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
 // Bounded wait on an mbarrier phase. Returns false after ~`limit_cycles`.
 QTB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit_cycles) {
   uint32_t done = 0;
@@ -156,6 +163,12 @@ QTB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit_cycles) {
     if (done) return true;
     if (clock64() - t0 > limit_cycles) return false;
   }
+}
+
+QTB_DEV unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 // ------------------------------------------------------------ grid sync ----

@@ -516,6 +516,10 @@ struct qtb_session {
   Stage *prog[PROG_N] = {};
   int prog_n[PROG_N] = {};
   int has_pad = 0;
+  long long *trace = nullptr;   // per-stage clock64 trace (CTA 0), profiling only
+  int trace_n = 0, trace_on = 0;
+  std::vector<long long> last_ckpt;   // intra-stage checkpoints of the last profile
+  std::vector<long long> last_gtrace; // per-CTA arrival times (globaltimer ns) of the last profile
   double last_ms = 0;
   int last_launches = 0;
   // pinned staging
@@ -524,8 +528,12 @@ struct qtb_session {
   size_t h_in_floats = 0, h_out_floats = 0;
 };
 
-static int nch_for(int B) {
-  const int c = (2 * B + 7) / 8;
+// MMA columns per batch row: bf16 weights carry the activation as bf16
+// hi + mid + lo (+ a zero column) up to 16 rows, else hi + lo; the integer
+// formats use fp16 hi + lo.
+static int parts_for(int fmt, int B) { return (fmt == FMT_BF16 && B <= 16) ? 4 : 2; }
+static int nch_for(int fmt, int B) {
+  const int c = (parts_for(fmt, B) * B + 7) / 8;
   int n = 1;
   while (n < c) n <<= 1;
   return n;
@@ -534,7 +542,7 @@ static int nch_for(int B) {
 // Choose the k-slice count: minimise the per-warp load (rounds x slice) with
 // the staged activation slice within shared memory.
 static int choose_S(int T, int K, int B, int W, int fmt) {
-  const int nch = nch_for(B), ent = 4 * std::min(8, 2 * B);
+  const int nch = nch_for(fmt, B), ent = 4 * std::min(8, parts_for(fmt, B) * B);
   int best = -1;
   double best_cost = 1e30;
   for (int S = 1; S <= 64; S <<= 1) {
@@ -547,8 +555,20 @@ static int choose_S(int T, int K, int B, int W, int fmt) {
     const double cost = (double)((U + W - 1) / W) * ks * (S > 1 ? 1.05 : 1.0);
     if (cost < best_cost - 1e-9) { best_cost = cost; best = S; }
   }
-  (void)fmt;
   return best;
+}
+
+// Small-batch GEMV path: the whole activation is staged once and the weights
+// stream through the TMA ring (see gemv2_stage_t).
+static bool v2_ok(int fmt, int rows, int K, int B, int G) {
+  if (B > 4 || B * K > 8192) return false;   // stage_x_fused: <= 8 quads per thread
+  const int P = parts_for(fmt, B), nch = nch_for(fmt, B), ent = 4 * std::min(8, P * B);
+  if (fmt == FMT_BF16 ? nch > 2 : nch > 1) return false;
+  const bool xsum = (fmt == FMT_Q4_0 || fmt == FMT_INT4G);
+  const size_t xb = (size_t)(K / 16) * nch * ent * 8 + (xsum ? (size_t)((B * (K / 32) + 3) & ~3) * 4 : 0);
+  if (xb > (size_t)SM_X2_BYTES) return false;
+  const int T = rows / 16, nt_max = (T + G - 1) / G;
+  return 256 + (size_t)nt_max * (NWARPS + 1) * 16 * B * 4 <= (size_t)SM_R_BYTES;
 }
 
 struct ProgBuilder {
@@ -566,16 +586,18 @@ struct ProgBuilder {
     GemvArgs &g = S.g;
     g.w = m.w; g.row_scale = m.row_scale; g.gsz = m.gsz; g.bias = bias;
     g.fmt = m.fmt; g.rows = m.rows; g.K = m.K;
-    g.S = choose_S(m.rows / 16, m.K, B, W(), m.fmt);
+    g.v2 = v2_ok(m.fmt, m.rows, m.K, B, s->e->n_sm) ? 1 : 0;
+    g.S = g.v2 ? 1 : choose_S(m.rows / 16, m.K, B, W(), m.fmt);
     if (g.S < 1) { err = set_err(QTB_E_UNSUPPORTED, "no k-slicing fits shared memory (K=%d, B=%d)", m.K, B); return; }
-    g.nch = nch_for(B);
+    g.nch = nch_for(m.fmt, B);
+    g.parts = parts_for(m.fmt, B);
     g.evict_last = evict_last;
     g.x = x; g.ldx = ldx; g.norm_w = norm_w; g.eps = eps;
     g.y = y; g.ldy = ldy; g.epi = epi;
     g.ws = s->ws; g.sem = s->sem;
     g.amax_ws = s->amax_ws; g.amax_sem = s->amax_sem;
-    const size_t need = (size_t)(m.rows / 16) * g.S * 16 * B;
-    if (g.S > 1 && need > s->ws_floats) { err = set_err(QTB_E_INVALID, "split-K workspace too small"); return; }
+    const size_t need = (size_t)(m.rows / 16) * (g.v2 ? std::max(1, s->e->n_sm / std::max(1, m.rows / 16)) : g.S) * 16 * B;
+    if (need > s->ws_floats) { err = set_err(QTB_E_INVALID, "split-K workspace too small"); return; }
     if (m.rows / 16 > s->sem_n) { err = set_err(QTB_E_INVALID, "semaphore array too small"); return; }
     st.push_back(S);
   }
@@ -758,7 +780,8 @@ static int alloc_stack_bufs(qtb_session *s, const DStack &k, StackBufs &b, int B
   for (int i = 0; i < B; i++)
     for (int j = 0; j < b.pt_stride; j++) pt[(size_t)i * b.pt_stride + j] = (n_pages > 0) ? -1 : i * b.pt_stride + j;
   if ((rc = ar.upload(&b.page_table, pt.data(), pt.size() * 4))) return rc;
-  b.max_splits = std::max(1, std::min(32, (2 * s->e->n_sm + B * k.n_kv - 1) / (B * k.n_kv)));
+  // at most one attention work item per CTA: a second item would double the stage
+  b.max_splits = std::max(1, std::min(32, s->e->n_sm / (B * k.n_kv)));
   return 0;
 }
 
@@ -767,6 +790,7 @@ extern "C" void qtb_session_destroy(qtb_session_t *s) {
   cudaSetDevice(s->e->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
   s->ar.release();
+  if (s->trace) cudaFree(s->trace);
   if (s->ev0) cudaEventDestroy(s->ev0);
   if (s->ev1) cudaEventDestroy(s->ev1);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -807,6 +831,7 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
       const int T = m.rows / 16;
       const int S = choose_S(T, m.K, B, W, m.fmt);
       if (S > 0) ws = std::max(ws, (size_t)T * S * 16 * B);
+      ws = std::max(ws, (size_t)T * std::max(1, e->n_sm / std::max(1, T)) * 16 * B);
       sem_n = std::max(sem_n, T);
     };
     auto acc_stack = [&](const DStack &k) {
@@ -932,7 +957,8 @@ static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
   const Stage *prog = s->prog[which];
   int n_st = s->prog_n[which];
   Ctl *ctl = s->ctl;
-  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_iters, (void *)&ctl};
+  long long *trace = s->trace_on ? s->trace : nullptr;
+  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_iters, (void *)&ctl, (void *)&trace};
   if (timed) CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(s->e->n_sm), dim3(NTHREADS), args,
                                        SMEM_BYTES, s->stream));
@@ -1134,7 +1160,8 @@ static int run_single_stage(MiniRun &mr, const Stage &S) {
   CUDA_TRY(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   const Stage *prog = dp;
   int n_st = 1, n_it = 1;
-  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_it, (void *)&ctl};
+  long long *trace = nullptr;
+  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(nsm), dim3(NTHREADS), args, SMEM_BYTES, mr.st));
   CUDA_TRY(cudaStreamSynchronize(mr.st));
   Ctl h;
@@ -1158,7 +1185,8 @@ extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols,
   float *dx, *dy, *ws;
   unsigned *sem;
   const int T = rows / 16;
-  const int S = choose_S(T, cols, batch, nsm * NWARPS, fmt);
+  const bool v2 = v2_ok(fmt, rows, cols, batch, nsm);
+  const int S = v2 ? std::max(1, nsm / T) : choose_S(T, cols, batch, nsm * NWARPS, fmt);
   if (S < 1) return set_err(QTB_E_UNSUPPORTED, "no k-slicing fits");
   if ((rc = mr.ar.upload(&dx, x, (size_t)batch * cols * 4))) return rc;
   if ((rc = mr.ar.alloc((void **)&dy, (size_t)batch * rows * 4))) return rc;
@@ -1171,7 +1199,8 @@ extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols,
   st.B = batch;
   GemvArgs &g = st.g;
   g.w = m.w; g.row_scale = m.row_scale; g.gsz = m.gsz;
-  g.fmt = fmt; g.rows = rows; g.K = cols; g.S = S; g.nch = nch_for(batch);
+  g.fmt = fmt; g.rows = rows; g.K = cols; g.S = v2 ? 1 : S; g.nch = nch_for(fmt, batch); g.parts = parts_for(fmt, batch);
+  g.v2 = v2 ? 1 : 0;
   g.x = dx; g.ldx = cols; g.y = dy; g.ldy = rows; g.epi = EPI_STORE; g.ws = ws; g.sem = sem;
   if ((rc = run_single_stage(mr, st))) return rc;
   CUDA_TRY(cudaMemcpy(y, dy, (size_t)batch * rows * 4, cudaMemcpyDeviceToHost));
@@ -1235,3 +1264,60 @@ extern "C" int qtb_attention_host(const float *qkv, int batch, int n_heads, int 
 
 extern "C" int qtb_engine_talker_layers(const qtb_engine_t *e) { return e ? e->talker.n_layers : 0; }
 extern "C" int qtb_engine_talker_kv_dim(const qtb_engine_t *e) { return e ? e->talker.kv_dim() : 0; }
+
+// Stage-level profile of one iteration of a program (0 talker step, 1 CP pass,
+// 2 CP frame, 3 whole frame): per-stage SM clock cycles between grid barriers
+// (CTA 0's clock) and each stage's kind (1 GEMV, 2 ATTN, 3 EMBED, 4 NORM,
+// 5 POS_INC) and, for GEMV stages, rows * 65536 + K in `shape`.
+extern "C" int qtb_session_profile(qtb_session_t *s, int which, long long *cycles, int *kind, int64_t *shape, int max_stages) {
+  if (!s || which < 0 || which >= PROG_N || !s->prog[which]) return set_err(QTB_E_INVALID, "bad program");
+  const int n = s->prog_n[which];
+  if (n > max_stages) return set_err(QTB_E_INVALID, "need %d stage slots", n);
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  const int need = (n + 1) + n * 8 + 2 * n * s->e->n_sm;
+  if (!s->trace || s->trace_n < need) {
+    if (s->trace) cudaFree(s->trace);
+    s->trace = nullptr;
+    CUDA_TRY(cudaMalloc(&s->trace, (size_t)need * 8));
+    s->trace_n = need;
+  }
+  CUDA_TRY(cudaMemset(s->trace, 0, (size_t)need * 8));
+  { int rc0 = begin_call(s); if (rc0) return rc0; }
+  s->trace_on = 1;
+  int rc = launch_prog(s, which, 1, true);
+  s->trace_on = 0;
+  if (rc) return rc;
+  if ((rc = finish(s, true))) return rc;
+  std::vector<long long> t(need);
+  CUDA_TRY(cudaMemcpy(t.data(), s->trace, (size_t)need * 8, cudaMemcpyDeviceToHost));
+  s->last_ckpt.assign(t.begin() + n + 1, t.begin() + n + 1 + n * 8);
+  s->last_gtrace.assign(t.begin() + n + 1 + n * 8, t.end());
+  std::vector<Stage> st(n);
+  CUDA_TRY(cudaMemcpy(st.data(), s->prog[which], (size_t)n * sizeof(Stage), cudaMemcpyDeviceToHost));
+  long long prev = t[n];
+  for (int i = 0; i < n; i++) {
+    cycles[i] = t[i] - prev;
+    prev = t[i];
+    kind[i] = st[i].kind;
+    shape[i] = st[i].kind == ST_GEMV ? (int64_t)st[i].g.rows * 65536 + st[i].g.K : 0;
+  }
+  return n;
+}
+
+// Intra-stage checkpoints (8 per stage, CTA 0 clock64, 0 = not reached) of the
+// last qtb_session_profile call.
+extern "C" int qtb_session_profile_checkpoints(qtb_session_t *s, long long *out, int max_vals) {
+  if (!s) return set_err(QTB_E_INVALID, "null session");
+  const int n = std::min<int>((int)s->last_ckpt.size(), max_vals);
+  for (int i = 0; i < n; i++) out[i] = s->last_ckpt[i];
+  return n;
+}
+
+// Per-CTA barrier-arrival times (global timer, ns) of the last profile:
+// [stage][cta].
+extern "C" int qtb_session_profile_arrivals(qtb_session_t *s, long long *out, int max_vals) {
+  if (!s) return set_err(QTB_E_INVALID, "null session");
+  const int n = std::min<int>((int)s->last_gtrace.size(), max_vals);
+  for (int i = 0; i < n; i++) out[i] = s->last_gtrace[i];
+  return n;
+}

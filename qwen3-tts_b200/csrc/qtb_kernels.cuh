@@ -33,10 +33,26 @@ constexpr int NWARPS = NTHREADS / 32;
 constexpr int HD = 128;       // head_dim (Qwen3-TTS talker and CP)
 constexpr int PAGE = 16;      // KV positions per page
 constexpr int ATT_NBUF = 4;   // K/V page buffers in flight per CTA
-constexpr int SMEM_X_BYTES = 96 * 1024;
-constexpr int SMEM_MISC_BYTES = 8 * 1024;
-constexpr int SMEM_BYTES = SMEM_X_BYTES + SMEM_MISC_BYTES;
 constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
+
+// Dynamic shared memory map (one CTA per SM):
+//   [SM_W_OFF, +128 KB)  weight ring of the small-batch GEMV: NWSLOT slots
+//                        filled by 1D bulk copies (TMA), prefetched across
+//                        the grid barrier that precedes the stage
+//   [SM_X_OFF, +56 KB)   staged activation (small-batch GEMV) / K-V page
+//                        ring + scratch of the attention stage
+//   [SM_R_OFF, +20 KB)   1/rms, per-warp partial sums
+// The large-batch GEMV path stages its activation slice from offset 0 (at
+// most SMEM_X_BYTES) and never runs while a prefetch is in flight.
+constexpr int WSLOT_BYTES = 16384;
+constexpr int NWSLOT = 8;
+constexpr int SM_W_OFF = 0;
+constexpr int SM_X_OFF = NWSLOT * WSLOT_BYTES;
+constexpr int SM_X2_BYTES = 56 * 1024;
+constexpr int SM_R_OFF = SM_X_OFF + SM_X2_BYTES;
+constexpr int SM_R_BYTES = 20 * 1024;
+constexpr int SMEM_BYTES = SM_R_OFF + SM_R_BYTES;
+constexpr int SMEM_X_BYTES = 96 * 1024;
 
 enum StageKind { ST_GEMV = 1, ST_ATTN = 2, ST_EMBED = 3, ST_NORM = 4, ST_POS_INC = 5 };
 enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
@@ -52,8 +68,10 @@ struct GemvArgs {
   const uint8_t *gsz;        // int4: per (tile, 64-col chunk, group-of-4-lanes) scale(/zero)
   const float *bias;         // [rows] or null
   int fmt, rows, K, S;       // S = k-slices; units = rows/16 * S
-  int nch;                   // MMA column chunks = ceil(2B/8)
+  int nch;                   // MMA column chunks = ceil(P*B/8)
+  int parts;                 // MMA columns per batch row: 2 (hi, lo) or 4 (hi, mid, lo, 0)
   int evict_last;            // keep these weights in L2 (code-predictor)
+  int v2;                    // small-batch path: whole activation staged, weights TMA-streamed
   const float *x; int ldx;   // activation [B][ldx]
   const float *norm_w;       // RMSNorm gain [K] or null
   float eps;
@@ -92,7 +110,9 @@ struct EmbedArgs {
 struct NormArgs { const float *x; int ldx; const float *w; float *y; int ldy; int dim; float eps; };
 struct PosArgs { int *pos; };
 
-struct Stage {
+// One stage of a program.  16-byte aligned and sized so the kernel can bulk-copy
+// the next stage's descriptor into shared memory while the current one runs.
+struct __align__(16) Stage {
   int kind;
   int B;
   union {
@@ -103,6 +123,7 @@ struct Stage {
     PosArgs p;
   };
 };
+static_assert(sizeof(Stage) % 16 == 0, "stage descriptors are bulk-copied");
 
 struct Ctl {
   unsigned bar_count;   // monotonic grid-barrier counter (zeroed before each launch)
@@ -116,11 +137,23 @@ struct Ctl {
 struct KCtx {
   unsigned epoch;
   unsigned page_ctr;    // K/V page buffers consumed so far (mbarrier phase source)
+  unsigned wfill;       // weight-ring slot fills consumed so far (mbarrier phase source)
+  int w_pre;            // slot fills already issued for the coming GEMV stage
+  int att_pre;          // K/V pages already issued for the coming attention stage
   uint64_t pol_first, pol_last;
-  uint64_t *bars;
+  uint64_t *bars;       // ATT_NBUF page-buffer mbarriers
+  uint64_t *wbars;      // NWSLOT weight-slot mbarriers
   Ctl *ctl;
   int stage;
+  long long *trace2;    // optional intra-stage checkpoints: [stage][8] clock64 of CTA 0
+  unsigned long long *gtrace;  // optional [stage][cta] global time at arrival
+  long long t_start;    // clock64 when this CTA left the last barrier
 };
+
+// Profiling checkpoint (CTA 0, thread 0) when stage tracing is on.
+QTB_DEV void ckpt(const KCtx &kc, int i) {
+  if (kc.trace2 && blockIdx.x == 0 && threadIdx.x == 0) kc.trace2[(size_t)kc.stage * 8 + i] = clock64();
+}
 
 // CTA-uniform read of the launch's error flag.
 QTB_DEV bool cta_err(KCtx &kc) {
@@ -141,20 +174,26 @@ QTB_DEV void raise_err(KCtx &kc, int code, int info) {
 // Grid-wide barrier on a monotonic counter.  Bounded: gives up (and raises
 // ERR_BARRIER_TIMEOUT) after WAIT_LIMIT_CYCLES, or as soon as any CTA has
 // raised an error, so a failing launch always returns.
-QTB_DEV bool grid_barrier(KCtx &kc) {
-  __shared__ int s_ok;
+QTB_DEV void grid_arrive(KCtx &kc) {
   __syncthreads();
+  // release: this CTA's writes (ordered before by bar.sync) happen-before
+  // every CTA that acquires the final count
+  if (threadIdx.x == 0) atom_add_release_gpu(&kc.ctl->bar_count, 1u);
+}
+
+QTB_DEV bool grid_wait(KCtx &kc) {
+  __shared__ int s_ok;
   if (threadIdx.x == 0) {
     int ok = 1;
-    __threadfence();
-    unsigned target = (kc.epoch + 1u) * gridDim.x;
-    atom_add_release_gpu(&kc.ctl->bar_count, 1u);
-    long long t0 = clock64();
+    const unsigned target = (kc.epoch + 1u) * gridDim.x;
+    const long long t0 = clock64();
+    unsigned spins = 0;
     while ((int)(ld_acquire_gpu(&kc.ctl->bar_count) - target) < 0) {
-      if (*(volatile int *)&kc.ctl->err) { ok = 0; break; }
-      if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_err(kc, ERR_BARRIER_TIMEOUT, (int)kc.epoch); ok = 0; break; }
+      if ((++spins & 31u) == 0) {
+        if (*(volatile int *)&kc.ctl->err) { ok = 0; break; }
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_err(kc, ERR_BARRIER_TIMEOUT, (int)kc.epoch); ok = 0; break; }
+      }
     }
-    __threadfence();
     s_ok = ok && (*(volatile int *)&kc.ctl->err == 0);
   }
   __syncthreads();
@@ -164,23 +203,35 @@ QTB_DEV bool grid_barrier(KCtx &kc) {
 
 // =========================================================== GEMV stage ====
 
-// Split f32 pair into the hi or lo operand (fp16 or bf16) and pack 2 values.
+// The f32 activation is carried as a sum of narrower parts, one MMA column
+// each: fp16 hi + lo (22 mantissa bits) for the integer formats, bf16 hi +
+// mid + lo (24 bits) or hi + lo (16 bits) for bf16 weights.  Returns part
+// `part` of v0 and v1 packed as a pair.
 template <bool F16>
-QTB_DEV uint32_t split_pack(float v0, float v1, int lo) {
+QTB_DEV uint32_t split_pack(float v0, float v1, int part) {
   if (F16) {
     __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-    if (lo) {
+    if (part == 1) {
       h0 = __float2half_rn(v0 - __half2float(h0));
       h1 = __float2half_rn(v1 - __half2float(h1));
+    } else if (part > 1) {
+      return 0u;
     }
     return (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
   } else {
-    uint32_t b0 = f32_to_bf16_rn(v0), b1 = f32_to_bf16_rn(v1);
-    if (lo) {
-      b0 = f32_to_bf16_rn(v0 - __uint_as_float(b0 << 16));
-      b1 = f32_to_bf16_rn(v1 - __uint_as_float(b1 << 16));
+    uint32_t r[2];
+    const float v[2] = {v0, v1};
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      float rem = v[i];
+      uint32_t b = f32_to_bf16_rn(rem);
+      for (int k = 0; k < part && k < 3; k++) {
+        rem -= __uint_as_float(b << 16);
+        b = f32_to_bf16_rn(rem);
+      }
+      r[i] = (part > 2) ? 0u : b;
     }
-    return b0 | (b1 << 16);
+    return r[0] | (r[1] << 16);
   }
 }
 
@@ -205,10 +256,108 @@ QTB_DEV float norm_in(const GemvArgs &a, const float *s_inv, int b, int k, float
 
 // Stage the activation slice [k0, k0 + kslice) of every batch row into shared
 // memory in B-fragment order (entry e = (kstep * nch + chunk) * ent + lane).
+//
+// Small-batch variant (B <= 4, B*K <= 8192): ONE pass over global memory.
+// Thread i owns "quads" (batch b, k-step q, lane column tig): the 4 values
+// x[b][16q + 2tig + {0, 1, 8, 9}], all loaded up front.  Sums of squares are
+// reduced per batch row across the block, then every quad writes its P part
+// entries (the lanes of its column group) and, for int4 weights, the per-32
+// group sums (the 8 quads of a group sit in 8 consecutive lanes of one warp).
+template <bool F16, int P>
+QTB_DEV void stage_x_fused(const GemvArgs &a, int B, int ent, float *s_inv, float *s_xsum, uint2 *s_xf,
+                           bool want_xsum) {
+  constexpr int MAXQ = 8;  // quads per thread: B * K / 4 <= 256 * 8
+  const int K = a.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ks = K >> 4;
+  const int nq = B * ks * 4;
+  float v[MAXQ][4], nw[MAXQ][4];
+  float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < MAXQ; i++) {
+    const int t = tid + i * NTHREADS;
+    if (t < nq) {
+      const int tig = t & 3, q = (t >> 2) % ks, b = (t >> 2) / ks;
+      const float *xb = a.x + (size_t)b * a.ldx + 16 * q + 2 * tig;
+      const float2 p0 = __ldcg(reinterpret_cast<const float2 *>(xb));
+      const float2 p1 = __ldcg(reinterpret_cast<const float2 *>(xb + 8));
+      v[i][0] = p0.x; v[i][1] = p0.y; v[i][2] = p1.x; v[i][3] = p1.y;
+      if (a.norm_w) {   // gains load alongside the activation (no dependency)
+        const int k = 16 * q + 2 * tig;
+        const float2 w0 = __ldg(reinterpret_cast<const float2 *>(a.norm_w + k));
+        const float2 w1 = __ldg(reinterpret_cast<const float2 *>(a.norm_w + k + 8));
+        nw[i][0] = w0.x; nw[i][1] = w0.y; nw[i][2] = w1.x; nw[i][3] = w1.y;
+      }
+    }
+  }
+  if (a.norm_w) {
+    __shared__ float s_ss[NWARPS][4];
+#pragma unroll
+    for (int i = 0; i < MAXQ; i++) {
+      const int t = tid + i * NTHREADS;
+      if (t < nq) {
+        const int b = (t >> 2) / ks;
+        const float s2 = v[i][0] * v[i][0] + v[i][1] * v[i][1] + v[i][2] * v[i][2] + v[i][3] * v[i][3];
+        // b is warp-uniform only when a warp's 32 quads share a row; add per row
+#pragma unroll
+        for (int bb = 0; bb < 4; bb++) ss[bb] += (b == bb) ? s2 : 0.f;
+      }
+    }
+#pragma unroll
+    for (int bb = 0; bb < 4; bb++) {
+      const float w = warp_sum(ss[bb]);
+      if (lane == 0) s_ss[warp][bb] = w;
+    }
+    __syncthreads();
+    if (tid < 4) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < NWARPS; w++) tot += s_ss[w][tid];
+      s_inv[tid] = 1.0f / sqrtf(tot / (float)K + a.eps);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < MAXQ; i++) {
+    const int t = tid + i * NTHREADS;
+    float xs = 0.f;
+    if (t < nq) {
+      const int tig = t & 3, q = (t >> 2) % ks, b = (t >> 2) / ks;
+      const int k = 16 * q + 2 * tig;
+      (void)k;
+      if (a.norm_w) {
+        const float inv = s_inv[b];
+        v[i][0] = (v[i][0] * inv) * nw[i][0];
+        v[i][1] = (v[i][1] * inv) * nw[i][1];
+        v[i][2] = (v[i][2] * inv) * nw[i][2];
+        v[i][3] = (v[i][3] * inv) * nw[i][3];
+      }
+      xs = v[i][0] + v[i][1] + v[i][2] + v[i][3];
+      // entries: column = b * P + part -> chunk j = col / 8, gid = col % 8
+#pragma unroll
+      for (int part = 0; part < P; part++) {
+        const int col = b * P + part;
+        const int j = col >> 3, gid = col & 7;
+        const int e = (q * a.nch + j) * ent + gid * 4 + tig;
+        s_xf[e] = make_uint2(split_pack<F16>(v[i][0], v[i][1], part), split_pack<F16>(v[i][2], v[i][3], part));
+      }
+    }
+    if (want_xsum) {
+      // 8 consecutive quads (k-steps 2g, 2g+1 x 4 columns) form group g
+      xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+      xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+      xs += __shfl_xor_sync(0xffffffffu, xs, 4);
+      if (t < nq && (t & 7) == 0) {
+        const int q = (t >> 2) % ks, b = (t >> 2) / ks;
+        s_xsum[b * (K >> 5) + (q >> 1)] = xs;
+      }
+    }
+  }
+}
+
 template <bool F16>
 QTB_DEV void stage_x(const GemvArgs &a, int B, int ent, int k0, int kslice, const float *s_inv,
                      float *s_xsum, uint2 *s_xf, bool want_xsum) {
-  const int nch = a.nch;
+  const int nch = a.nch, P = a.parts;
   const int ksteps = kslice >> 4;
   const int total = ksteps * nch * ent;
   for (int e = threadIdx.x; e < total; e += NTHREADS) {
@@ -216,7 +365,8 @@ QTB_DEV void stage_x(const GemvArgs &a, int B, int ent, int k0, int kslice, cons
     const int qj = e / ent;
     const int j = qj % nch, q = qj / nch;
     const int gid = l >> 2, tig = l & 3;
-    const int b = 4 * j + (gid >> 1), lo = gid & 1;
+    const int col = 8 * j + gid;           // MMA column = batch * P + part
+    const int b = col / P, lo = col % P;
     uint32_t r0 = 0, r1 = 0;
     if (b < B) {
       const int k = k0 + 16 * q + 2 * tig;
@@ -254,9 +404,99 @@ template <> struct FmtTraits<FMT_INT8> { static constexpr int CK = 2; static con
 template <> struct FmtTraits<FMT_Q4_0> { static constexpr int CK = 4; static constexpr int GSZ = 8; };
 template <> struct FmtTraits<FMT_INT4G> { static constexpr int CK = 4; static constexpr int GSZ = 16; };
 
-// One warp computes one unit: 16 rows x kslice columns, all batch columns.
-// res[j][0] / res[j][1] = rows (16t + gid) / (16t + gid + 8) for b = 4j + tig.
+// Batch row held by a lane's accumulator pair in MMA column chunk j: with P
+// columns per batch row, columns (2 tig, 2 tig + 1) belong to batch
+// (8 j + 2 tig) / P.  With P = 4 two lanes (tig, tig ^ 1) share a batch row.
+template <int P> QTB_DEV int col_batch(int j, int tig) { return P == 2 ? 4 * j + tig : 2 * j + (tig >> 1); }
+template <int P> QTB_DEV bool col_owner(int tig) { return P == 2 || (tig & 1) == 0; }
+
+// One 512-byte warp chunk of fragment-ordered weights (lane's 16 bytes in wv,
+// its group scale/zero quad in gv for int4) times the staged activation.
+// c = chunk index relative to the staged activation slice; bf16 / int8
+// accumulate into acc, int4 applies its per-group scale and zero directly into
+// res (groups are 32 columns = 2 k-steps).  xsum_n = groups in the slice.
 template <int FMT, int NCH>
+QTB_DEV void mma_chunk(const uint4 wv, const uint4 gv, int c, const uint2 *s_xf, int ent, const float *s_xsum,
+                       int xsum_n, int B, float (&acc)[NCH][4], float (&res)[NCH][2]) {
+  const int lane = threadIdx.x & 31, tig = lane & 3;
+  const bool has_x = lane < ent;
+  if (FMT == FMT_BF16) {
+    const uint32_t A[4] = {wv.x, wv.y, wv.z, wv.w};
+    const uint2 *xf = s_xf + (size_t)c * NCH * ent;
+#pragma unroll
+    for (int j = 0; j < NCH; j++) {
+      uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
+      mma_bf16(acc[j], A, bx.x, bx.y);
+    }
+  } else if (FMT == FMT_INT8) {
+    const uint32_t wd[4] = {wv.x ^ 0x80808080u, wv.y ^ 0x80808080u, wv.z ^ 0x80808080u, wv.w ^ 0x80808080u};
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const uint32_t A[4] = {i8x2_to_f16x2(wd[2 * q], 0x4140), i8x2_to_f16x2(wd[2 * q], 0x4342),
+                             i8x2_to_f16x2(wd[2 * q + 1], 0x4140), i8x2_to_f16x2(wd[2 * q + 1], 0x4342)};
+      const uint2 *xf = s_xf + (size_t)(2 * c + q) * NCH * ent;
+#pragma unroll
+      for (int j = 0; j < NCH; j++) {
+        uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
+        mma_f16(acc[j], A, bx.x, bx.y);
+      }
+    }
+  } else {
+    // int4: two groups of 32 columns per chunk.
+    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int gh = 0; gh < 2; gh++) {
+      float sc0, sc1, z0, z1;
+      sc0 = half_bits_to_f32(gh ? (gv.x >> 16) : (gv.x & 0xffffu));
+      sc1 = half_bits_to_f32(gh ? (gv.y >> 16) : (gv.y & 0xffffu));
+      if (FMT == FMT_Q4_0) {
+        z0 = 8.f; z1 = 8.f;
+      } else {
+        z0 = half_bits_to_f32(gh ? (gv.z >> 16) : (gv.z & 0xffffu));
+        z1 = half_bits_to_f32(gh ? (gv.w >> 16) : (gv.w & 0xffffu));
+      }
+      const int gl = 2 * c + gh;   // group index within the slice
+#pragma unroll
+      for (int j = 0; j < NCH; j++) {
+        float cg[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int qq = 0; qq < 2; qq++) {
+          const uint32_t w = wd[2 * gh + qq];
+          const uint32_t A[4] = {u4x2_to_f16x2(w), u4x2_to_f16x2(w >> 4), u4x2_to_f16x2(w >> 8),
+                                 u4x2_to_f16x2(w >> 12)};
+          const uint2 *xf = s_xf + (size_t)(4 * c + 2 * gh + qq) * NCH * ent;
+          uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
+          mma_f16(cg, A, bx.x, bx.y);
+        }
+        const int b = 4 * j + tig;
+        const float xs = (b < B) ? s_xsum[b * xsum_n + gl] : 0.f;
+        res[j][0] += sc0 * ((cg[0] + cg[1]) - z0 * xs);
+        res[j][1] += sc1 * ((cg[2] + cg[3]) - z1 * xs);
+      }
+    }
+  }
+}
+
+// Fold the MMA accumulators into per-row results (hi + lo (+ mid) columns).
+template <int FMT, int NCH, int P>
+QTB_DEV void acc_finish(float (&acc)[NCH][4], float (&res)[NCH][2]) {
+  if (FMT == FMT_BF16 || FMT == FMT_INT8) {
+#pragma unroll
+    for (int j = 0; j < NCH; j++) {
+      res[j][0] = acc[j][0] + acc[j][1];
+      res[j][1] = acc[j][2] + acc[j][3];
+      if (P == 4) {
+        res[j][0] += __shfl_xor_sync(0xffffffffu, res[j][0], 1);
+        res[j][1] += __shfl_xor_sync(0xffffffffu, res[j][1], 1);
+      }
+    }
+  }
+}
+
+// One warp computes one unit: 16 rows x kslice columns, all batch columns.
+// res[j][0] / res[j][1] = rows (16t + gid) / (16t + gid + 8) for batch
+// col_batch<P>(j, tig).
+template <int FMT, int NCH, int P>
 QTB_DEV void gemv_unit(const GemvArgs &a, int B, int t, int s, int kslice, const uint2 *s_xf,
                        int ent, const float *s_xsum, float (&res)[NCH][2], const KCtx &kc) {
   using Tr = FmtTraits<FMT>;
@@ -299,73 +539,11 @@ QTB_DEV void gemv_unit(const GemvArgs &a, int B, int t, int s, int kslice, const
           if (Tr::GSZ == 8) { uint2 g = ld_nc_u2(gp + (size_t)(c + PD) * 64); gbuf[i] = make_uint4(g.x, g.y, 0, 0); }
           if (Tr::GSZ == 16) gbuf[i] = ld_nc_u4(gp + (size_t)(c + PD) * 128);
         }
-        if (FMT == FMT_BF16) {
-          const uint32_t A[4] = {wv.x, wv.y, wv.z, wv.w};
-          const uint2 *xf = s_xf + (size_t)c * NCH * ent;
-#pragma unroll
-          for (int j = 0; j < NCH; j++) {
-            uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
-            mma_bf16(acc[j], A, bx.x, bx.y);
-          }
-        } else if (FMT == FMT_INT8) {
-          const uint32_t wd[4] = {wv.x ^ 0x80808080u, wv.y ^ 0x80808080u, wv.z ^ 0x80808080u, wv.w ^ 0x80808080u};
-#pragma unroll
-          for (int q = 0; q < 2; q++) {
-            const uint32_t A[4] = {i8x2_to_f16x2(wd[2 * q], 0x4140), i8x2_to_f16x2(wd[2 * q], 0x4342),
-                                   i8x2_to_f16x2(wd[2 * q + 1], 0x4140), i8x2_to_f16x2(wd[2 * q + 1], 0x4342)};
-            const uint2 *xf = s_xf + (size_t)(2 * c + q) * NCH * ent;
-#pragma unroll
-            for (int j = 0; j < NCH; j++) {
-              uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
-              mma_f16(acc[j], A, bx.x, bx.y);
-            }
-          }
-        } else {
-          // int4: two groups of 32 columns per chunk.
-          const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-          for (int gh = 0; gh < 2; gh++) {
-            float sc0, sc1, z0, z1;
-            if (FMT == FMT_Q4_0) {
-              sc0 = half_bits_to_f32(gh ? (gv.x >> 16) : (gv.x & 0xffffu));
-              sc1 = half_bits_to_f32(gh ? (gv.y >> 16) : (gv.y & 0xffffu));
-              z0 = 8.f; z1 = 8.f;
-            } else {
-              sc0 = half_bits_to_f32(gh ? (gv.x >> 16) : (gv.x & 0xffffu));
-              sc1 = half_bits_to_f32(gh ? (gv.y >> 16) : (gv.y & 0xffffu));
-              z0 = half_bits_to_f32(gh ? (gv.z >> 16) : (gv.z & 0xffffu));
-              z1 = half_bits_to_f32(gh ? (gv.w >> 16) : (gv.w & 0xffffu));
-            }
-            const int gl = 2 * c + gh;   // group index within the slice
-#pragma unroll
-            for (int j = 0; j < NCH; j++) {
-              float cg[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-              for (int qq = 0; qq < 2; qq++) {
-                const uint32_t w = wd[2 * gh + qq];
-                const uint32_t A[4] = {u4x2_to_f16x2(w), u4x2_to_f16x2(w >> 4), u4x2_to_f16x2(w >> 8),
-                                       u4x2_to_f16x2(w >> 12)};
-                const uint2 *xf = s_xf + (size_t)(4 * c + 2 * gh + qq) * NCH * ent;
-                uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
-                mma_f16(cg, A, bx.x, bx.y);
-              }
-              const int b = 4 * j + tig;
-              const float xs = (b < B) ? s_xsum[b * (kslice >> 5) + gl] : 0.f;
-              res[j][0] += sc0 * ((cg[0] + cg[1]) - z0 * xs);
-              res[j][1] += sc1 * ((cg[2] + cg[3]) - z1 * xs);
-            }
-          }
-        }
+        mma_chunk<FMT, NCH>(wv, gv, c, s_xf, ent, s_xsum, kslice >> 5, B, acc, res);
       }
     }
   }
-  if (FMT == FMT_BF16 || FMT == FMT_INT8) {
-#pragma unroll
-    for (int j = 0; j < NCH; j++) {
-      res[j][0] = acc[j][0] + acc[j][1];
-      res[j][1] = acc[j][2] + acc[j][3];
-    }
-  }
+  acc_finish<FMT, NCH, P>(acc, res);
 }
 
 QTB_DEV unsigned long long amax_key(float v, int row) {
@@ -379,7 +557,7 @@ QTB_DEV unsigned long long shfl_xor_u64(unsigned long long v, int m) {
 }
 
 // Epilogue for the 16 final rows of tile t (called by exactly one warp).
-template <int NCH>
+template <int NCH, int P>
 QTB_DEV void gemv_epilogue(const GemvArgs &a, int B, int t, int T, float (&res)[NCH][2], KCtx &kc) {
   const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
 #pragma unroll
@@ -403,8 +581,8 @@ QTB_DEV void gemv_epilogue(const GemvArgs &a, int B, int t, int T, float (&res)[
         unsigned long long o = shfl_xor_u64(k, m);
         k = o > k ? o : k;
       }
-      const int b = 4 * j + tig;
-      if (gid == 0 && b < B) a.amax_ws[(size_t)t * B + b] = k;
+      const int b = col_batch<P>(j, tig);
+      if (gid == 0 && b < B && col_owner<P>(tig)) a.amax_ws[(size_t)t * B + b] = k;
     }
     __syncwarp();
     unsigned old = 0;
@@ -444,20 +622,21 @@ QTB_DEV void gemv_epilogue(const GemvArgs &a, int B, int t, int T, float (&res)[
     if (lane == 0) *a.amax_sem = 0u;
     return;
   }
+  const bool owner = col_owner<P>(tig);
 #pragma unroll
   for (int j = 0; j < NCH; j++) {
-    const int b = 4 * j + tig;
+    const int b = col_batch<P>(j, tig);
 #pragma unroll
     for (int r = 0; r < 2; r++) {
       const int row = 16 * t + gid + 8 * r;
       const float v = res[j][r];
       if (a.epi == EPI_SWIGLU) {
         const float up = __shfl_xor_sync(0xffffffffu, v, 4);
-        if ((gid & 1) == 0 && b < B) {
+        if ((gid & 1) == 0 && b < B && owner) {
           const float g = v;
           __stcg(a.y + (size_t)b * a.ldy + (row >> 1), g / (1.0f + expf(-g)) * up);
         }
-      } else if (b < B) {
+      } else if (b < B && owner) {
         float *yp = a.y + (size_t)b * a.ldy + row;
         if (a.epi == EPI_RESID) __stcg(yp, __ldcg(yp) + v);
         else __stcg(yp, v);
@@ -466,7 +645,7 @@ QTB_DEV void gemv_epilogue(const GemvArgs &a, int B, int t, int T, float (&res)[
   }
 }
 
-template <int FMT, int NCH>
+template <int FMT, int NCH, int P>
 __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
   const int T = a.rows >> 4;
   const int S = a.S;
@@ -475,7 +654,7 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
   const int W = gridDim.x * NWARPS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  const int ent = 4 * min(8, 2 * B);
+  const int ent = 4 * min(8, P * B);
   constexpr bool F16 = (FMT != FMT_BF16);
   constexpr bool XSUM = (FMT == FMT_Q4_0 || FMT == FMT_INT4G);
 
@@ -494,13 +673,13 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
     if (u < U) {
       const int t = u - s * T;
       float res[NCH][2];
-      gemv_unit<FMT, NCH>(a, B, t, s, kslice, s_xf, ent, s_xsum, res, kc);
+      gemv_unit<FMT, NCH, P>(a, B, t, s, kslice, s_xf, ent, s_xsum, res, kc);
       bool finish = true;
       if (S > 1) {
 #pragma unroll
         for (int j = 0; j < NCH; j++) {
-          const int b = 4 * j + tig;
-          if (b < B) {
+          const int b = col_batch<P>(j, tig);
+          if (b < B && col_owner<P>(tig)) {
             __stcg(a.ws + ((size_t)u * 16 + gid) * B + b, res[j][0]);
             __stcg(a.ws + ((size_t)u * 16 + gid + 8) * B + b, res[j][1]);
           }
@@ -514,7 +693,7 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
           __threadfence();
 #pragma unroll
           for (int j = 0; j < NCH; j++) {
-            const int b = 4 * j + tig;
+            const int b = col_batch<P>(j, tig);
             float v0 = 0.f, v1 = 0.f;
             if (b < B) {
               for (int ss = 0; ss < S; ss++) {
@@ -529,22 +708,315 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
           if (lane == 0) a.sem[t] = 0u;
         }
       }
-      if (finish) gemv_epilogue<NCH>(a, B, t, T, res, kc);
+      if (finish) gemv_epilogue<NCH, P>(a, B, t, T, res, kc);
     }
     __syncthreads();
   }
 }
 
+// ============================================ GEMV stage, small batches ====
+//
+// Used when the whole activation (B rows x K) fits the staging region.  Each
+// CTA owns whole 16-row tiles (T >= grid) or one k-piece of one tile (T <
+// grid, `scta` CTAs per tile); in both cases its weights are ONE contiguous
+// byte range of the fragment-ordered matrix, which thread 0 streams into the
+// NWSLOT-slot ring with 1D bulk copies.  The first ring-full is issued before
+// the grid barrier that precedes the stage (v2_prefetch), so HBM latency is
+// hidden behind the barrier.  Warps split the CTA's chunk stream evenly, keep
+// one partial per (tile, warp) in shared memory, and the CTA sums them in warp
+// order; k-pieces of one tile are combined by the last-arriving CTA in piece
+// order (deterministic).
+
+struct V2Sched {
+  int t0, nt;   // first tile and tile count of this CTA
+  int kb, kc;   // first chunk and chunk count within each tile
+  int scta, p;  // CTAs per tile and this CTA's piece
+  int L;        // chunks = nt * kc
+  int cps;      // chunks per ring slot
+  int nfill;    // slot fills = ceil(L / cps)
+};
+
+template <int FMT>
+QTB_DEV V2Sched v2_sched(const GemvArgs &a, int cta, int G) {
+  using Tr = FmtTraits<FMT>;
+  V2Sched s;
+  const int T = a.rows >> 4;
+  const int nck = a.K / (16 * Tr::CK);
+  s.cps = WSLOT_BYTES / (512 + 8 * Tr::GSZ);
+  // Whole tiles per CTA (when there are fewer tiles than CTAs the rest idle:
+  // the weights are streamed before the barrier, so a CTA holding two tiles'
+  // worth costs less than a cross-CTA reduction would).
+  s.t0 = (int)((long long)cta * T / G);
+  s.nt = (int)((long long)(cta + 1) * T / G) - s.t0;
+  s.kb = 0; s.kc = nck; s.scta = 1; s.p = 0;
+  s.L = s.nt * s.kc;
+  s.nfill = (s.L + s.cps - 1) / s.cps;
+  return s;
+}
+
+// Thread 0: bulk-copy slot fills [f0, f1) of this CTA's range into the ring.
+template <int FMT>
+QTB_DEV void v2_issue(const GemvArgs &a, const V2Sched &s, int f0, int f1, const KCtx &kc, char *smem) {
+  using Tr = FmtTraits<FMT>;
+  const int nck = a.K / (16 * Tr::CK);
+  const size_t cbase = (size_t)s.t0 * nck + s.kb;
+  const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
+  for (int f = f0; f < f1; f++) {
+    const unsigned ctr = kc.wfill + (unsigned)f;
+    const int slot = (int)(ctr % NWSLOT);
+    const int c0 = f * s.cps, n = min(s.cps, s.L - c0);
+    char *dst = smem + SM_W_OFF + slot * WSLOT_BYTES;
+    uint64_t *bar = kc.wbars + slot;
+    const uint32_t wbytes = (uint32_t)n * 512u, gbytes = (uint32_t)n * 8u * Tr::GSZ;
+    mbar_arrive_expect_tx(bar, wbytes + gbytes);
+    bulk_g2s_hint(dst, a.w + (cbase + c0) * 512, wbytes, bar, pol);
+    if (Tr::GSZ) bulk_g2s_hint(dst + s.cps * 512, a.gsz + (cbase + c0) * (8 * Tr::GSZ), gbytes, bar, pol);
+  }
+}
+
+template <int FMT>
+QTB_DEV int v2_prefetch_f(const GemvArgs &a, const KCtx &kc, char *smem) {
+  const V2Sched s = v2_sched<FMT>(a, blockIdx.x, gridDim.x);
+  const int n = min(s.nfill, NWSLOT);
+  if (n > 0) {
+    fence_proxy_async_smem();
+    v2_issue<FMT>(a, s, 0, n, kc, smem);
+  }
+  return n;
+}
+
+// Thread 0, before the grid barrier: issue the first ring-full of a coming
+// small-batch GEMV stage.  Returns the number of fills issued.
+QTB_DEV int v2_prefetch(const GemvArgs &a, const KCtx &kc, char *smem) {
+  switch (a.fmt) {
+    case FMT_BF16: return v2_prefetch_f<FMT_BF16>(a, kc, smem);
+    case FMT_INT8: return v2_prefetch_f<FMT_INT8>(a, kc, smem);
+    case FMT_Q4_0: return v2_prefetch_f<FMT_Q4_0>(a, kc, smem);
+    case FMT_INT4G: return v2_prefetch_f<FMT_INT4G>(a, kc, smem);
+  }
+  return 0;
+}
+
+// Epilogue on final row values val(tl, r, b) held in shared memory
+// (s_val[(tl * 16 + r) * sv_ld + b]) for the CTA's tiles t0 .. t0 + nt - 1.
+QTB_DEV void v2_epilogue(const GemvArgs &a, int B, int t0, int nt, const float *s_val, int sv_ld, KCtx &kc) {
+  const int tid = threadIdx.x;
+  auto val = [&](int tl, int r, int b) {
+    const int row = 16 * (t0 + tl) + r;
+    float v = s_val[(tl * 16 + r) * sv_ld + b];
+    if (a.row_scale) v = __ldg(a.row_scale + row) * v;
+    if (a.bias) v += __ldg(a.bias + row);
+    return v;
+  };
+  if (a.epi == EPI_STORE || a.epi == EPI_RESID) {
+    for (int idx = tid; idx < nt * 16 * B; idx += NTHREADS) {
+      const int b = idx % B, r = (idx / B) % 16, tl = idx / (16 * B);
+      const int row = 16 * (t0 + tl) + r;
+      const float v = val(tl, r, b);
+      float *yp = a.y + (size_t)b * a.ldy + row;
+      if (a.epi == EPI_RESID) __stcg(yp, __ldcg(yp) + v);
+      else __stcg(yp, v);
+    }
+  } else if (a.epi == EPI_SWIGLU) {
+    for (int idx = tid; idx < nt * 8 * B; idx += NTHREADS) {
+      const int b = idx % B, pr = (idx / B) % 8, tl = idx / (8 * B);
+      const float g = val(tl, 2 * pr, b), u = val(tl, 2 * pr + 1, b);
+      const int row = 16 * (t0 + tl) + 2 * pr;
+      __stcg(a.y + (size_t)b * a.ldy + (row >> 1), g / (1.0f + expf(-g)) * u);
+    }
+  } else {  // EPI_ARGMAX
+    __shared__ int s_last;
+    for (int idx = tid; idx < nt * B; idx += NTHREADS) {
+      const int b = idx % B, tl = idx / B;
+      unsigned long long best = 0ull;
+      for (int r = 0; r < 16; r++) {
+        const unsigned long long k = amax_key(val(tl, r, b), 16 * (t0 + tl) + r);
+        best = k > best ? k : best;
+      }
+      a.amax_ws[(size_t)(t0 + tl) * B + b] = best;
+    }
+    __syncthreads();
+    const int T = a.rows >> 4;
+    if (tid == 0) {
+      __threadfence();
+      const unsigned old = atomicAdd(a.amax_sem, (unsigned)nt);
+      s_last = (old + (unsigned)nt == (unsigned)T);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    __shared__ int s_code[64];
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int b = warp; b < B; b += NWARPS) {
+      unsigned long long best = 0ull;
+      for (int tt = lane; tt < T; tt += 32) {
+        const unsigned long long k = __ldcg(a.amax_ws + (size_t)tt * B + b);
+        best = k > best ? k : best;
+      }
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) {
+        const unsigned long long o = shfl_xor_u64(best, m);
+        best = o > best ? o : best;
+      }
+      const int code = (int)(0xffffffffu - (unsigned)(best & 0xffffffffull));
+      if (lane == 0) {
+        a.codes[(size_t)b * a.code_stride] = code;
+        s_code[b] = code;
+      }
+    }
+    __syncthreads();
+    if (a.emb_table) {
+      for (int idx = tid; idx < B * (a.emb_ld / 8); idx += NTHREADS) {
+        const int b = idx / (a.emb_ld / 8), i = (idx % (a.emb_ld / 8)) * 8;
+        int cb = s_code[b];
+        if (cb < 0 || cb >= a.emb_rows) { if (i == 0) raise_err(kc, ERR_BAD_CODE, cb); cb = 0; }
+        const uint4 v = ld_nc_u4(a.emb_table + (size_t)cb * a.emb_ld + i);
+        float *dst = a.emb_out + (size_t)b * a.emb_out_ld + i;
+        __stcg(reinterpret_cast<float4 *>(dst), make_float4(bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y)));
+        __stcg(reinterpret_cast<float4 *>(dst + 4), make_float4(bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w)));
+      }
+    }
+    if (tid == 0) *a.amax_sem = 0u;
+  }
+}
+
+template <int FMT, int NCH, int P>
+__device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  using Tr = FmtTraits<FMT>;
+  constexpr bool F16 = (FMT != FMT_BF16);
+  constexpr bool XSUM = (FMT == FMT_Q4_0 || FMT == FMT_INT4G);
+  const V2Sched s = v2_sched<FMT>(a, blockIdx.x, gridDim.x);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+  const int ent = 4 * min(8, P * B);
+  const int xsum_n = a.K >> 5;
+  float *s_inv = reinterpret_cast<float *>(smem + SM_R_OFF);
+  float *s_red = s_inv + 64;   // [nt][NWARPS][16][B]
+  float *s_xsum = reinterpret_cast<float *>(smem + SM_X_OFF);
+  const int xsum_floats = XSUM ? ((B * xsum_n + 3) & ~3) : 0;
+  uint2 *s_xf = reinterpret_cast<uint2 *>(s_xsum + xsum_floats);
+
+  if (tid == 0 && kc.w_pre == 0 && s.nfill > 0) {
+    fence_proxy_async_smem();
+    v2_issue<FMT>(a, s, 0, min(s.nfill, NWSLOT), kc, smem);
+  }
+  kc.w_pre = 0;
+  ckpt(kc, 0);
+  if (s.nt == 0) return;
+
+  stage_x_fused<F16, P>(a, B, ent, s_inv, s_xsum, s_xf, XSUM);
+  for (int i = tid; i < s.nt * NWARPS * 16 * B; i += NTHREADS) s_red[i] = 0.f;
+  __syncthreads();
+  ckpt(kc, 2);
+
+  const int per_wave = NWSLOT * s.cps;
+  for (int w0 = 0; w0 < s.L; w0 += per_wave) {
+    const int wl = min(per_wave, s.L - w0);
+    const int cb = w0 + (warp * wl) / NWARPS, ce = w0 + ((warp + 1) * wl) / NWARPS;
+    float acc[NCH][4], res[NCH][2];
+#pragma unroll
+    for (int j = 0; j < NCH; j++) { acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f; res[j][0] = res[j][1] = 0.f; }
+    auto flush = [&](int tl) {
+      acc_finish<FMT, NCH, P>(acc, res);
+#pragma unroll
+      for (int j = 0; j < NCH; j++) {
+        const int b = col_batch<P>(j, tig);
+        if (b < B && col_owner<P>(tig)) {
+          s_red[((tl * NWARPS + warp) * 16 + gid) * B + b] += res[j][0];
+          s_red[((tl * NWARPS + warp) * 16 + gid + 8) * B + b] += res[j][1];
+        }
+        acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        res[j][0] = res[j][1] = 0.f;
+      }
+    };
+    // walk (tile, chunk) and (fill, offset) incrementally: no divisions in the loop
+    int tl = cb / s.kc, kk = cb - tl * s.kc;
+    int f = cb / s.cps, o = cb - f * s.cps;
+    int waited = -1;
+    for (int ci = cb; ci < ce; ci++) {
+      const unsigned ctr = kc.wfill + (unsigned)f;
+      const char *slot = smem + SM_W_OFF + (ctr % NWSLOT) * WSLOT_BYTES;
+      if (f != waited) {
+        if (!mbar_wait(kc.wbars + (ctr % NWSLOT), (ctr / NWSLOT) & 1u, WAIT_LIMIT_CYCLES))
+          raise_err(kc, ERR_MBAR_TIMEOUT, f);
+        waited = f;
+      }
+      const uint4 wv = *reinterpret_cast<const uint4 *>(slot + o * 512 + lane * 16);
+      uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+      if (Tr::GSZ == 8) {
+        const uint2 g = *reinterpret_cast<const uint2 *>(slot + s.cps * 512 + o * 64 + gid * 8);
+        gv = make_uint4(g.x, g.y, 0u, 0u);
+      } else if (Tr::GSZ == 16) {
+        gv = *reinterpret_cast<const uint4 *>(slot + s.cps * 512 + o * 128 + gid * 16);
+      }
+      mma_chunk<FMT, NCH>(wv, gv, s.kb + kk, s_xf, ent, s_xsum, xsum_n, B, acc, res);
+      if (++o == s.cps) { o = 0; ++f; }
+      if (++kk == s.kc) {
+        flush(tl);
+        kk = 0;
+        ++tl;
+      }
+    }
+    if (kk != 0 && ce > cb) flush(tl);
+    __syncthreads();
+    if (tid == 0 && w0 + per_wave < s.L) {
+      const int f0 = (w0 + per_wave) / s.cps;
+      fence_proxy_async_smem();
+      v2_issue<FMT>(a, s, f0, min(s.nfill, f0 + NWSLOT), kc, smem);
+    }
+  }
+  kc.wfill += (unsigned)s.nfill;
+  ckpt(kc, 3);
+
+  // per tile: sum the warps' partials in warp order -> s_val[tl][16][B]
+  float *s_val = s_red + s.nt * NWARPS * 16 * B;
+  for (int idx = tid; idx < s.nt * 16 * B; idx += NTHREADS) {
+    const int b = idx % B, r = (idx / B) % 16, tl2 = idx / (16 * B);
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARPS; w++) v += s_red[((tl2 * NWARPS + w) * 16 + r) * B + b];
+    s_val[idx] = v;
+  }
+  __syncthreads();
+  ckpt(kc, 4);
+  v2_epilogue(a, B, s.t0, s.nt, s_val, B, kc);
+  ckpt(kc, 5);
+}
+
+template <int FMT>
+QTB_DEV void gemv2_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  if (FMT == FMT_BF16 && a.parts == 4) {
+    switch (a.nch) {
+      case 1: gemv2_stage_t<FMT, 1, 4>(a, B, smem, kc); return;
+      case 2: gemv2_stage_t<FMT, 2, 4>(a, B, smem, kc); return;
+    }
+  } else if (a.parts == 2 && FMT != FMT_BF16) {
+    switch (a.nch) {
+      case 1: gemv2_stage_t<FMT, 1, 2>(a, B, smem, kc); return;
+    }
+  }
+  if (threadIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, 1000 + a.nch * 16 + a.parts);
+}
+
 template <int FMT>
 QTB_DEV void gemv_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
-  switch (a.nch) {
-    case 1: gemv_stage_t<FMT, 1>(a, B, smem, kc); break;
-    case 2: gemv_stage_t<FMT, 2>(a, B, smem, kc); break;
-    case 4: gemv_stage_t<FMT, 4>(a, B, smem, kc); break;
-    case 8: gemv_stage_t<FMT, 8>(a, B, smem, kc); break;
-    case 16: gemv_stage_t<FMT, 16>(a, B, smem, kc); break;
-    default: if (threadIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, a.nch); break;
+  if (a.v2) { gemv2_stage_f<FMT>(a, B, smem, kc); return; }
+  if (FMT == FMT_BF16 && a.parts == 4) {
+    switch (a.nch) {
+      case 1: gemv_stage_t<FMT, 1, 4>(a, B, smem, kc); return;
+      case 2: gemv_stage_t<FMT, 2, 4>(a, B, smem, kc); return;
+      case 4: gemv_stage_t<FMT, 4, 4>(a, B, smem, kc); return;
+      case 8: gemv_stage_t<FMT, 8, 4>(a, B, smem, kc); return;
+    }
+  } else if (a.parts == 2) {
+    switch (a.nch) {
+      case 1: if (FMT != FMT_BF16) { gemv_stage_t<FMT, 1, 2>(a, B, smem, kc); return; } break;
+      case 2: if (FMT != FMT_BF16) { gemv_stage_t<FMT, 2, 2>(a, B, smem, kc); return; } break;
+      case 4: if (FMT != FMT_BF16) { gemv_stage_t<FMT, 4, 2>(a, B, smem, kc); return; } break;
+      case 8: gemv_stage_t<FMT, 8, 2>(a, B, smem, kc); return;
+      case 16: gemv_stage_t<FMT, 16, 2>(a, B, smem, kc); return;
+    }
   }
+  if (threadIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, a.nch * 16 + a.parts);
 }
 
 QTB_DEV void gemv_stage(const GemvArgs &a, int B, char *smem, KCtx &kc) {
@@ -571,7 +1043,11 @@ QTB_DEV void gemv_stage(const GemvArgs &a, int B, char *smem, KCtx &kc) {
 // (qwen_tts_kernels.c:3704-3846) applied per page.  When an item has several
 // splits the last finishing CTA combines them (deterministic order).
 
-struct AttnSmem {
+// The bf16 rows of the new token come first: they are read as 16-byte
+// vectors for the page store, so they must sit on 16-byte boundaries.
+struct __align__(16) AttnSmem {
+  uint16_t knew[HD];
+  uint16_t vnew[HD];
   float q[2][HD];
   float sc[2][PAGE];
   float p[2][PAGE];
@@ -579,9 +1055,64 @@ struct AttnSmem {
   float l[2];
   float m[2];
   int flag;
-  uint16_t knew[HD];
-  uint16_t vnew[HD];
 };
+static_assert(sizeof(AttnSmem) <= 2048, "attention scratch overlaps the page buffers");
+
+struct AttnItem {
+  int b, g, sp, pos, L, npages, nsp, p_begin, p_end;
+  bool bad_pos;
+};
+
+// Decode work item -> (slot, kv head, split) and the split's page range.
+// Returns false for items beyond the slot's split count (or a bad position).
+QTB_DEV bool attn_item(const AttnArgs &a, int item, AttnItem &it) {
+  it.bad_pos = false;
+  it.sp = item % a.max_splits;
+  const int bg = item / a.max_splits;
+  it.g = bg % a.n_kv;
+  it.b = bg / a.n_kv;
+  it.pos = a.pos_ptr ? __ldcg(a.pos_ptr + it.b) : a.pos_const;
+  if (it.pos < 0 || it.pos >= a.rope_len || it.pos >= a.pt_stride * PAGE) { it.bad_pos = true; return false; }
+  it.L = it.pos + 1;
+  it.npages = (it.L + PAGE - 1) / PAGE;
+  int nsp = min(a.max_splits, (it.npages + a.min_pps - 1) / a.min_pps);
+  const int pps = (it.npages + nsp - 1) / nsp;
+  it.nsp = (it.npages + pps - 1) / pps;
+  if (it.sp >= it.nsp) return false;
+  it.p_begin = it.sp * pps;
+  it.p_end = min(it.npages, it.p_begin + pps);
+  return true;
+}
+
+// Thread 0: bulk-copy pages [i0, i1) of the item's range into the page ring.
+QTB_DEV void attn_issue(const AttnArgs &a, const AttnItem &it, int i0, int i1, KCtx &kc, uint16_t *kvbuf) {
+  const int *pt = a.page_table + (size_t)it.b * a.pt_stride;
+  for (int i = i0; i < i1; i++) {
+    const unsigned ctr = kc.page_ctr + i;
+    const int buf = ctr % ATT_NBUF;
+    int page = __ldg(pt + it.p_begin + i);
+    if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
+    uint16_t *dstk = kvbuf + (size_t)buf * 2 * PAGE * HD;
+    const size_t off = (((size_t)page * a.n_kv + it.g) * PAGE) * HD;
+    mbar_arrive_expect_tx(kc.bars + buf, 2 * PAGE * HD * 2);
+    bulk_g2s(dstk, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
+    bulk_g2s(dstk + PAGE * HD, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
+  }
+}
+
+// Thread 0, before the grid barrier: issue the first pages of this CTA's first
+// attention item (older positions only; the newest token is patched in from
+// registers by the stage itself).  Returns the number of pages issued.
+QTB_DEV int attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem_attn) {
+  const int n_items = B * a.n_kv * a.max_splits;
+  if ((int)blockIdx.x >= n_items) return 0;
+  AttnItem it;
+  if (!attn_item(a, blockIdx.x, it)) return 0;
+  const int n = min(it.p_end - it.p_begin, ATT_NBUF);
+  fence_proxy_async();
+  attn_issue(a, it, 0, n, kc, reinterpret_cast<uint16_t *>(smem_attn + 2048));
+  return n;
+}
 
 __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KCtx &kc) {
   AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem);
@@ -590,24 +1121,30 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
   const int q_dim = a.n_heads * HD, kv_dim = a.n_kv * HD;
   const int n_items = B * a.n_kv * a.max_splits;
 
+  bool first = true;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int sp = item % a.max_splits;
-    const int bg = item / a.max_splits;
-    const int g = bg % a.n_kv, b = bg / a.n_kv;
-    int pos = a.pos_ptr ? __ldcg(a.pos_ptr + b) : a.pos_const;
-    if (pos < 0 || pos >= a.rope_len || pos >= a.pt_stride * PAGE) {
-      if (threadIdx.x == 0) raise_err(kc, ERR_BAD_POS, pos);
-      return;
+    AttnItem it;
+    if (!attn_item(a, item, it)) {
+      if (it.bad_pos) {
+        if (threadIdx.x == 0) raise_err(kc, ERR_BAD_POS, it.pos);
+        return;
+      }
+      first = false;
+      continue;
     }
-    const int L = pos + 1;
-    const int npages = (L + PAGE - 1) / PAGE;
-    int nsp = min(a.max_splits, (npages + a.min_pps - 1) / a.min_pps);
-    const int pps = (npages + nsp - 1) / nsp;
-    nsp = (npages + pps - 1) / pps;
-    if (sp >= nsp) continue;
-    const int p_begin = sp * pps, p_end = min(npages, p_begin + pps);
+    const int b = it.b, g = it.g, sp = it.sp, pos = it.pos, L = it.L, npages = it.npages, nsp = it.nsp;
+    const int p_begin = it.p_begin, p_end = it.p_end;
     const bool owns_new = (p_end == npages);
     const int *pt = a.page_table + (size_t)b * a.pt_stride;
+    // pages first (the ones prefetched before the barrier are already in flight)
+    if (threadIdx.x == 0) {
+      const int pre = first ? kc.att_pre : 0;
+      fence_proxy_async();
+      attn_issue(a, it, pre, min(p_end - p_begin, ATT_NBUF), kc, kvbuf);
+    }
+    first = false;
+    kc.att_pre = 0;
+    ckpt(kc, 0);
 
     // ---- prologue: QK RMSNorm + RoPE (+ KV append) ----
     if (warp < 4) {
@@ -616,21 +1153,27 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
       if (warp < 2) { src = a.qkv + (size_t)b * a.ld_qkv + (2 * g + warp) * HD; nw = a.q_norm; }
       else if (warp == 2) { src = a.qkv + (size_t)b * a.ld_qkv + q_dim + g * HD; nw = a.k_norm; }
       else src = a.qkv + (size_t)b * a.ld_qkv + q_dim + kv_dim + g * HD;
-      float v[4];
+      float v[4], gw[4], rc[2], rs[2];
 #pragma unroll
       for (int i = 0; i < 4; i++) v[i] = __ldcg(src + lane + 32 * i);
+      if (nw) {   // independent of the row values: issue with them
+#pragma unroll
+        for (int i = 0; i < 4; i++) gw[i] = __ldg(nw + lane + 32 * i);
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+          rc[i] = __ldg(a.rope_cos + (size_t)pos * (HD / 2) + lane + 32 * i);
+          rs[i] = __ldg(a.rope_sin + (size_t)pos * (HD / 2) + lane + 32 * i);
+        }
+      }
       if (nw) {
         float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
         ss = warp_sum(ss);
         const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
 #pragma unroll
-        for (int i = 0; i < 4; i++) v[i] = (v[i] * inv) * __ldg(nw + lane + 32 * i);
-        const float *cp = a.rope_cos + (size_t)pos * (HD / 2);
-        const float *snp = a.rope_sin + (size_t)pos * (HD / 2);
+        for (int i = 0; i < 4; i++) v[i] = (v[i] * inv) * gw[i];
 #pragma unroll
         for (int i = 0; i < 2; i++) {
-          const int d = lane + 32 * i;
-          const float c = __ldg(cp + d), s = __ldg(snp + d);
+          const float c = rc[i], s = rs[i];
           const float x1 = v[i], x2 = v[i + 2];
           v[i] = fmaf(x1, c, -(x2 * s));
           v[i + 2] = fmaf(x2, c, x1 * s);
@@ -664,33 +1207,20 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
       }
     }
     if (cta_err(kc)) return;
+    ckpt(kc, 1);
 
     // ---- main loop over this split's pages ----
     const int n = p_end - p_begin;
     const int tid = threadIdx.x;
     const int hh = tid >> 7, d = tid & 127;
     float acc = 0.f;
-    if (tid == 0) {
-      fence_proxy_async();
-      for (int i = 0; i < min(n, ATT_NBUF); i++) {
-        const unsigned ctr = kc.page_ctr + i;
-        const int buf = ctr % ATT_NBUF;
-        int page = __ldg(pt + p_begin + i);
-        if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
-        uint16_t *dstk = kvbuf + (size_t)buf * 2 * PAGE * HD;
-        const size_t off = (((size_t)page * a.n_kv + g) * PAGE) * HD;
-        mbar_arrive_expect_tx(kc.bars + buf, 2 * PAGE * HD * 2);
-        bulk_g2s(dstk, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
-        bulk_g2s(dstk + PAGE * HD, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
-      }
-    }
     for (int i = 0; i < n; i++) {
       const unsigned ctr = kc.page_ctr + i;
       const int buf = ctr % ATT_NBUF;
       const uint32_t parity = (ctr / ATT_NBUF) & 1u;
-      if (tid == 0) {
-        if (!mbar_wait(kc.bars + buf, parity, WAIT_LIMIT_CYCLES)) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-      }
+      // every thread observes the phase flip, which makes the bulk-copied
+      // bytes visible to it
+      if (!mbar_wait(kc.bars + buf, parity, WAIT_LIMIT_CYCLES)) raise_err(kc, ERR_MBAR_TIMEOUT, i);
       if (cta_err(kc)) {
         // leave no bulk copy in flight: wait (bounded) for the ones issued after this page
         if (tid == 0)
@@ -781,6 +1311,7 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
       }
     }
     kc.page_ctr += n;
+    ckpt(kc, 2);
 
     // ---- output / split combine ----
     const int head = 2 * g + hh;
@@ -819,13 +1350,25 @@ __device__ __noinline__ void embed_stage(const EmbedArgs &e, int B, KCtx &kc) {
   const int total = B * e.dim;
   for (int idx = blockIdx.x * NTHREADS + threadIdx.x; idx < total; idx += gridDim.x * NTHREADS) {
     const int b = idx / e.dim, i = idx - b * e.dim;
-    float v = e.fsrc ? __ldcg(e.fsrc + (size_t)b * e.fsrc_ld + i) : 0.f;
-    for (int t = 0; t < e.ntab; t++) {
-      int c = __ldcg(e.code[t] + (size_t)b * e.code_stride[t]);
-      if (c < 0 || c >= e.tab_rows[t]) { if (i == 0) raise_err(kc, ERR_BAD_CODE, c); c = 0; }
-      v += __uint_as_float(((uint32_t)__ldg(e.tab[t] + (size_t)c * e.tab_ld[t] + i)) << 16);
+    // all codes first, then all table rows: independent loads in flight together
+    int c[16];
+#pragma unroll
+    for (int t = 0; t < 16; t++) c[t] = (t < e.ntab) ? __ldcg(e.code[t] + (size_t)b * e.code_stride[t]) : 0;
+    const float f = e.fsrc ? __ldcg(e.fsrc + (size_t)b * e.fsrc_ld + i) : 0.f;
+    const float ad = e.add ? __ldg(e.add + i) : 0.f;
+    uint16_t r[16];
+#pragma unroll
+    for (int t = 0; t < 16; t++) {
+      if (t < e.ntab) {
+        if (c[t] < 0 || c[t] >= e.tab_rows[t]) { if (i == 0) raise_err(kc, ERR_BAD_CODE, c[t]); c[t] = 0; }
+        r[t] = __ldg(e.tab[t] + (size_t)c[t] * e.tab_ld[t] + i);
+      }
     }
-    if (e.add) v += __ldg(e.add + i);
+    float v = f;
+#pragma unroll
+    for (int t = 0; t < 16; t++)
+      if (t < e.ntab) v += __uint_as_float(((uint32_t)r[t]) << 16);
+    if (e.add) v += ad;
     __stcg(e.dst + (size_t)b * e.ld_dst + i, v);
   }
 }
@@ -833,10 +1376,19 @@ __device__ __noinline__ void embed_stage(const EmbedArgs &e, int B, KCtx &kc) {
 __device__ __noinline__ void norm_stage(const NormArgs &n, int B) {
   __shared__ float s_red[NWARPS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int MAXV = 8;   // dim <= 2048
   for (int b = blockIdx.x; b < B; b += gridDim.x) {
     const float *xb = n.x + (size_t)b * n.ldx;
+    float xv[MAXV], wv[MAXV];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < n.dim; i += NTHREADS) { const float v = __ldcg(xb + i); ss += v * v; }
+#pragma unroll
+    for (int j = 0; j < MAXV; j++) {
+      const int i = threadIdx.x + j * NTHREADS;
+      xv[j] = (i < n.dim) ? __ldcg(xb + i) : 0.f;
+      wv[j] = (i < n.dim) ? __ldg(n.w + i) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < MAXV; j++) ss += xv[j] * xv[j];
     ss = warp_sum(ss);
     if (lane == 0) s_red[warp] = ss;
     __syncthreads();
@@ -844,38 +1396,68 @@ __device__ __noinline__ void norm_stage(const NormArgs &n, int B) {
 #pragma unroll
     for (int w = 0; w < NWARPS; w++) tot += s_red[w];
     const float inv = 1.0f / sqrtf(tot / (float)n.dim + n.eps);
-    for (int i = threadIdx.x; i < n.dim; i += NTHREADS)
-      __stcg(n.y + (size_t)b * n.ldy + i, (__ldcg(xb + i) * inv) * __ldg(n.w + i));
+#pragma unroll
+    for (int j = 0; j < MAXV; j++) {
+      const int i = threadIdx.x + j * NTHREADS;
+      if (i < n.dim) __stcg(n.y + (size_t)b * n.ldy + i, (xv[j] * inv) * wv[j]);
+    }
     __syncthreads();
   }
 }
 
 // ====================================================== persistent kernel ==
 __global__ void __launch_bounds__(NTHREADS, 1)
-decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ctl) {
+decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ctl, long long *trace) {
   extern __shared__ __align__(128) char smem[];
   __shared__ __align__(8) uint64_t bars[ATT_NBUF];
+  __shared__ __align__(8) uint64_t wbars[NWSLOT];
+  __shared__ __align__(8) uint64_t sbars[2];
+  __shared__ Stage s_st[2];   // current and next stage descriptors
   KCtx kc;
   kc.epoch = 0;
   kc.page_ctr = 0;
+  kc.wfill = 0;
+  kc.w_pre = 0;
+  kc.att_pre = 0;
+  kc.wbars = wbars;
   kc.pol_first = policy_evict_first();
   kc.pol_last = policy_evict_last();
   kc.bars = bars;
   kc.ctl = ctl;
   kc.stage = 0;
+  kc.trace2 = trace ? trace + (size_t)n_iters * n_stages + 1 : nullptr;
+  kc.gtrace = trace ? reinterpret_cast<unsigned long long *>(trace + (size_t)n_iters * n_stages + 1 + (size_t)n_stages * 8)
+                    : nullptr;
   if (threadIdx.x == 0) {
     for (int i = 0; i < ATT_NBUF; i++) mbar_init(bars + i, 1);
+    for (int i = 0; i < NWSLOT; i++) mbar_init(wbars + i, 1);
+    mbar_init(sbars + 0, 1);
+    mbar_init(sbars + 1, 1);
     fence_mbar_init();
+    // stage descriptors travel through shared memory, one stage ahead
+    mbar_arrive_expect_tx(sbars + 0, sizeof(Stage));
+    bulk_g2s(s_st + 0, prog, sizeof(Stage), sbars + 0);
   }
   __syncthreads();
+  if (trace && blockIdx.x == 0 && threadIdx.x == 0) trace[(size_t)n_iters * n_stages] = clock64();
+  unsigned sctr = 0;   // descriptors consumed
+  kc.t_start = clock64();
   for (int it = 0; it < n_iters; it++) {
-    for (int si = 0; si < n_stages; si++) {
-      const Stage *st = prog + si;
+    for (int si = 0; si < n_stages; si++, sctr++) {
+      const int cur = sctr & 1;
+      const bool more = (si + 1 < n_stages) || (it + 1 < n_iters);
+      if (!mbar_wait(sbars + cur, (sctr >> 1) & 1u, WAIT_LIMIT_CYCLES)) raise_err(kc, ERR_MBAR_TIMEOUT, -1);
+      if (threadIdx.x == 0 && more) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(sbars + (cur ^ 1), sizeof(Stage));
+        bulk_g2s(s_st + (cur ^ 1), prog + ((si + 1 < n_stages) ? si + 1 : 0), sizeof(Stage), sbars + (cur ^ 1));
+      }
+      const Stage *st = s_st + cur;
       kc.stage = si;
       const int B = st->B;
       switch (st->kind) {
         case ST_GEMV: gemv_stage(st->g, B, smem, kc); break;
-        case ST_ATTN: attn_stage(st->a, B, smem, kc); break;
+        case ST_ATTN: attn_stage(st->a, B, smem + SM_X_OFF, kc); break;
         case ST_EMBED: embed_stage(st->e, B, kc); break;
         case ST_NORM: norm_stage(st->n, B); break;
         case ST_POS_INC:
@@ -885,7 +1467,35 @@ decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ct
           if (threadIdx.x == 0 && blockIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, st->kind);
           break;
       }
-      if (!grid_barrier(kc)) return;
+      ckpt(kc, 6);
+      grid_arrive(kc);
+      // issue the next stage's independent loads (weights, older KV pages)
+      // while the other CTAs finish
+      if (more) {
+        if (threadIdx.x == 0) {
+          const Stage *nx = s_st + (cur ^ 1);
+          if (mbar_wait(sbars + (cur ^ 1), ((sctr + 1) >> 1) & 1u, WAIT_LIMIT_CYCLES)) {
+            if (nx->kind == ST_GEMV && nx->g.v2) kc.w_pre = v2_prefetch(nx->g, kc, smem);
+            else if (nx->kind == ST_ATTN) kc.att_pre = attn_prefetch(nx->a, nx->B, kc, smem + SM_X_OFF);
+          } else {
+            raise_err(kc, ERR_MBAR_TIMEOUT, -2);
+          }
+        }
+      }
+      ckpt(kc, 7);
+      if (kc.gtrace && threadIdx.x == 0) {
+        // [stage][cta] = global arrival time; [n_stages + stage][cta] = this CTA's
+        // busy cycles since it left the previous barrier (same-SM clock) | smid << 48
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        kc.gtrace[(size_t)si * gridDim.x + blockIdx.x] = globaltimer();
+        kc.gtrace[(size_t)(n_stages + si) * gridDim.x + blockIdx.x] =
+            (unsigned long long)(clock64() - kc.t_start) | ((unsigned long long)smid << 48);
+      }
+      if (!grid_wait(kc)) return;
+      kc.t_start = clock64();
+      // optional stage trace: CTA 0's clock when every CTA has finished stage si
+      if (trace && blockIdx.x == 0 && threadIdx.x == 0) trace[(size_t)it * n_stages + si] = clock64();
     }
   }
 }

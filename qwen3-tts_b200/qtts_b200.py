@@ -84,6 +84,8 @@ def lib():
     L.qtb_decode_frames.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp]
     for n in ("qtb_session_upload_kv", "qtb_session_download_kv", "qtb_session_download_cp_kv"):
         getattr(L, n).argtypes = [_vp, C.c_int, _vp, _vp, C.c_int, C.c_int]
+    L.qtb_session_profile.argtypes = [_vp, C.c_int, _vp, _vp, _vp, C.c_int]
+    L.qtb_session_profile_checkpoints.argtypes = [_vp, _vp, C.c_int]
     L.qtb_quantize_int8.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp]
     L.qtb_quantize_q4_0.argtypes = [_vp, C.c_int, C.c_int, _vp]
     L.qtb_quantize_int4g32.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp, _vp]
@@ -407,6 +409,20 @@ class Session:
         hid = np.empty((self.B, cfg.hidden), np.float32)
         check(lib().qtb_decode_frames(self.h, ptr(e), ptr(pd), n_frames, ptr(codes), ptr(hid)))
         return codes, hid
+
+    def profile(self, which=3, max_stages=4096):
+        """Per-stage SM cycles of one iteration of a program (see
+        qtb_session_profile); returns (cycles, kind, shape) arrays."""
+        cyc = np.zeros(max_stages, np.int64)
+        kind = np.zeros(max_stages, np.int32)
+        shape = np.zeros(max_stages, np.int64)
+        n = lib().qtb_session_profile(self.h, which, ptr(cyc), ptr(kind), ptr(shape), max_stages)
+        if n < 0:
+            check(n)
+        ck = np.zeros(n * 8, np.int64)
+        lib().qtb_session_profile_checkpoints(self.h, ptr(ck), n * 8)
+        self.checkpoints = ck.reshape(n, 8)
+        return cyc[:n], kind[:n], shape[:n]
 
     def last_ms(self):
         return lib().qtb_session_last_ms(self.h)

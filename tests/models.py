@@ -67,3 +67,19 @@ def rel_l2(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def kv_close(a, b, min_equal=0.98):
+    """bf16 KV caches computed from nearly equal f32 values: most bytes equal,
+    and every element within one bf16 ulp of its magnitude or a tiny absolute
+    floor (elements near zero after cancellation may differ by many ulps in bit
+    pattern while differing by ~1e-7 absolute)."""
+    fa = (np.asarray(a).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    fb = (np.asarray(b).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    rms = np.sqrt(np.mean(fb ** 2)) + 1e-30
+    tol = 2.0 ** -6 * np.maximum(np.abs(fa), np.abs(fb)) + 2e-3 * rms
+    ok = bool(np.all(np.abs(fa - fb) <= tol)) and float(np.mean(np.asarray(a) == np.asarray(b))) > min_equal
+    if not ok:
+        i = np.unravel_index(np.argmax(np.abs(fa - fb) - tol), fa.shape)
+        print("kv_close: worst", i, fa[i], fb[i], "tol", tol[i], "equal", float(np.mean(np.asarray(a) == np.asarray(b))))
+    return ok
