@@ -271,10 +271,13 @@ def argmax_first(y):
     return int(np.argmax(y))
 
 
-def cp_predict(cp: Stack, cp_norm, lm_heads, cp_emb, codec_emb, talker_hidden, code0, mtp=None):
+def cp_predict(cp: Stack, cp_norm, lm_heads, cp_emb, codec_emb, talker_hidden, code0, mtp=None, force=None,
+               margins=None):
     """qwen_cp_predict (qwen_tts_code_predictor.c:926-1045), greedy heads.
     lm_heads: f32 [2048][cp_h] x 15; cp_emb / codec_emb: f32 tables;
-    mtp: (W f32, b f32) or None."""
+    mtp: (W f32, b f32) or None.  force: codes to feed back instead of the
+    argmax (teacher forcing); margins: list receiving (top1 - top2, logit std)
+    per head."""
     def proj(v):
         if mtp is None:
             return np.asarray(v, np.float32)[: cp.H].copy()
@@ -287,6 +290,11 @@ def cp_predict(cp: Stack, cp_norm, lm_heads, cp_emb, codec_emb, talker_hidden, c
     for g in range(15):
         logits = mv(lm_heads[g], rms_norm(x, cp_norm, cp.eps))
         c = argmax_first(logits)
+        if margins is not None:
+            top = np.sort(np.asarray(logits, np.float64))[-2:]
+            margins.append((float(top[1] - top[0]), float(np.std(logits))))
+        if force is not None:
+            c = int(force[g])
         codes.append(c)
         if g == 14:
             break

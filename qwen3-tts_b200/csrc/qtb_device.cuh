@@ -165,6 +165,25 @@ QTB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit_cycles) {
   }
 }
 
+// Non-blocking probe of an mbarrier phase (true once the phase of the given
+// parity has completed).
+QTB_DEV bool mbar_test(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Ask L2 to fetch [p, p + bytes) (16-byte aligned, multiple of 16 bytes);
+// nothing waits for it.
+QTB_DEV void prefetch_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 QTB_DEV unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -176,6 +195,17 @@ QTB_DEV unsigned ld_acquire_gpu(const unsigned *p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+// Two adjacent 32-bit words (8-byte aligned) read by one acquire load.
+QTB_DEV uint2 ld_acquire_gpu_v2(const unsigned *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return make_uint2((unsigned)v, (unsigned)(v >> 32));
+}
+QTB_DEV unsigned atom_add_acq_rel_gpu(unsigned *p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 QTB_DEV unsigned atom_add_release_gpu(unsigned *p, unsigned v) {
   unsigned old;

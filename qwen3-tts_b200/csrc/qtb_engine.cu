@@ -407,6 +407,15 @@ extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_eng
   CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
   if (!coop) return set_err(QTB_E_UNSUPPORTED, "device lacks cooperative launch");
   CUDA_TRY(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  {
+    // the smallest shared-memory carveout that holds the kernel leaves the
+    // rest of the SM's unified array to L1 (stack frames of the stage calls)
+    cudaFuncAttributes fa;
+    CUDA_TRY(cudaFuncGetAttributes(&fa, decode_kernel));
+    const size_t need = (size_t)SMEM_BYTES + fa.sharedSizeBytes + 1024;
+    const int pct = (int)((need * 100 + prop.sharedMemPerMultiprocessor - 1) / prop.sharedMemPerMultiprocessor);
+    CUDA_TRY(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, std::min(100, pct)));
+  }
   int per_sm = 0;
   CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, NTHREADS, SMEM_BYTES));
   if (per_sm < 1) return set_err(QTB_E_UNSUPPORTED, "decode kernel does not fit on an SM");
@@ -1274,7 +1283,7 @@ extern "C" int qtb_session_profile(qtb_session_t *s, int which, long long *cycle
   const int n = s->prog_n[which];
   if (n > max_stages) return set_err(QTB_E_INVALID, "need %d stage slots", n);
   CUDA_TRY(cudaSetDevice(s->e->device));
-  const int need = (n + 1) + n * 8 + 2 * n * s->e->n_sm;
+  const int need = (n + 1) + n * NCKPT + 2 * n * s->e->n_sm;
   if (!s->trace || s->trace_n < need) {
     if (s->trace) cudaFree(s->trace);
     s->trace = nullptr;
@@ -1290,8 +1299,8 @@ extern "C" int qtb_session_profile(qtb_session_t *s, int which, long long *cycle
   if ((rc = finish(s, true))) return rc;
   std::vector<long long> t(need);
   CUDA_TRY(cudaMemcpy(t.data(), s->trace, (size_t)need * 8, cudaMemcpyDeviceToHost));
-  s->last_ckpt.assign(t.begin() + n + 1, t.begin() + n + 1 + n * 8);
-  s->last_gtrace.assign(t.begin() + n + 1 + n * 8, t.end());
+  s->last_ckpt.assign(t.begin() + n + 1, t.begin() + n + 1 + n * NCKPT);
+  s->last_gtrace.assign(t.begin() + n + 1 + n * NCKPT, t.end());
   std::vector<Stage> st(n);
   CUDA_TRY(cudaMemcpy(st.data(), s->prog[which], (size_t)n * sizeof(Stage), cudaMemcpyDeviceToHost));
   long long prev = t[n];
@@ -1304,7 +1313,7 @@ extern "C" int qtb_session_profile(qtb_session_t *s, int which, long long *cycle
   return n;
 }
 
-// Intra-stage checkpoints (8 per stage, CTA 0 clock64, 0 = not reached) of the
+// Intra-stage checkpoints (NCKPT per stage, CTA 0 clock64, 0 = not reached) of the
 // last qtb_session_profile call.
 extern "C" int qtb_session_profile_checkpoints(qtb_session_t *s, long long *out, int max_vals) {
   if (!s) return set_err(QTB_E_INVALID, "null session");

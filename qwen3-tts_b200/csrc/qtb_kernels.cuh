@@ -33,25 +33,35 @@ constexpr int NWARPS = NTHREADS / 32;
 constexpr int HD = 128;       // head_dim (Qwen3-TTS talker and CP)
 constexpr int PAGE = 16;      // KV positions per page
 constexpr int ATT_NBUF = 4;   // K/V page buffers in flight per CTA
-constexpr long long WAIT_LIMIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
+constexpr long long WAIT_LIMIT_CYCLES = 500000000LL;  // ~0.25 s at 1.9 GHz
 
 // Dynamic shared memory map (one CTA per SM):
-//   [SM_W_OFF, +128 KB)  weight ring of the small-batch GEMV: NWSLOT slots
-//                        filled by 1D bulk copies (TMA), prefetched across
-//                        the grid barrier that precedes the stage
-//   [SM_X_OFF, +56 KB)   staged activation (small-batch GEMV) / K-V page
+//   [SM_W_OFF, +96 KB)   weight ring of the small-batch GEMV: NWSLOT slots
+//                        filled by 1D bulk copies (TMA) by the weight streamer
+//   [SM_X_OFF, +48 KB)   staged activation (small-batch GEMV) / K-V page
 //                        ring + scratch of the attention stage
-//   [SM_R_OFF, +20 KB)   1/rms, per-warp partial sums
+//   [SM_R_OFF, +12 KB)   1/rms, per-warp partial sums
+// 156 KB in all, so with the static part the SM's unified L1/shared array can
+// run the 164 KB shared-memory configuration and keep ~90 KB of L1 for the
+// threads' stack frames (the stage functions are real calls).
 // The large-batch GEMV path stages its activation slice from offset 0 (at
-// most SMEM_X_BYTES) and never runs while a prefetch is in flight.
+// most SMEM_X_BYTES); the weight streamer never runs past such a stage, so no
+// bulk copy is in flight while it runs.
 constexpr int WSLOT_BYTES = 16384;
-constexpr int NWSLOT = 8;
+constexpr int NWSLOT = 6;
 constexpr int SM_W_OFF = 0;
 constexpr int SM_X_OFF = NWSLOT * WSLOT_BYTES;
-constexpr int SM_X2_BYTES = 56 * 1024;
+constexpr int SM_X2_BYTES = 48 * 1024;
 constexpr int SM_R_OFF = SM_X_OFF + SM_X2_BYTES;
-constexpr int SM_R_BYTES = 20 * 1024;
+constexpr int SM_R_BYTES = 12 * 1024;
 constexpr int SMEM_BYTES = SM_R_OFF + SM_R_BYTES;
+// Stage descriptors travel through a ring of NDESC shared-memory slots,
+// bulk-copied NDESC - 1 stages ahead; the weight streamer looks at most
+// STREAM_AHEAD stages past the last completed one (STREAM_AHEAD < NDESC keeps
+// every descriptor it reads landed or pending in its slot's current phase).
+constexpr int NDESC = 4;
+constexpr int NCKPT = 32;     // profiling checkpoints per stage
+constexpr int STREAM_AHEAD = NDESC - 1;
 constexpr int SMEM_X_BYTES = 96 * 1024;
 
 enum StageKind { ST_GEMV = 1, ST_ATTN = 2, ST_EMBED = 3, ST_NORM = 4, ST_POS_INC = 5 };
@@ -127,19 +137,22 @@ static_assert(sizeof(Stage) % 16 == 0, "stage descriptors are bulk-copied");
 
 struct Ctl {
   unsigned bar_count;   // monotonic grid-barrier counter (zeroed before each launch)
-  int pad0[31];
-  int err;              // first error code
+  int err;              // first error code (same 8 bytes: one load polls both)
   int err_stage;        // stage index that raised it
   int err_info;
-  int pad1[29];
+  int pad[60];
 };
 
+// Per-CTA kernel state, one copy in shared memory.  Fields are written by
+// thread 0 only (at points separated from other threads' reads by a CTA
+// barrier), except `local_err`, which any thread may set to 1.
 struct KCtx {
   unsigned epoch;
   unsigned page_ctr;    // K/V page buffers consumed so far (mbarrier phase source)
   unsigned wfill;       // weight-ring slot fills consumed so far (mbarrier phase source)
-  int w_pre;            // slot fills already issued for the coming GEMV stage
   int att_pre;          // K/V pages already issued for the coming attention stage
+  unsigned att_issued;  // thread 0: K/V page copies issued so far
+  int local_err;        // this thread has raised an error
   uint64_t pol_first, pol_last;
   uint64_t *bars;       // ATT_NBUF page-buffer mbarriers
   uint64_t *wbars;      // NWSLOT weight-slot mbarriers
@@ -148,57 +161,52 @@ struct KCtx {
   long long *trace2;    // optional intra-stage checkpoints: [stage][8] clock64 of CTA 0
   unsigned long long *gtrace;  // optional [stage][cta] global time at arrival
   long long t_start;    // clock64 when this CTA left the last barrier
+  // stage program and the weight streamer (streamer fields: thread 0 only)
+  unsigned seq;         // running stage number: iteration * n_stages + stage
+  unsigned n_total;     // stages in this launch
+  int n_stages;
+  Stage *dring;         // NDESC descriptor slots in shared memory
+  uint64_t *dbars;      // their mbarriers
+  unsigned w_issued;    // weight-ring fills issued so far
+  unsigned w_free;      // fills whose slots have been read by every warp
+  unsigned pf_seq;      // next stage the streamer looks at
+  int pf_f;             // next fill of that stage
+  int last;             // this CTA's arrival completed the current barrier
 };
 
 // Profiling checkpoint (CTA 0, thread 0) when stage tracing is on.
 QTB_DEV void ckpt(const KCtx &kc, int i) {
-  if (kc.trace2 && blockIdx.x == 0 && threadIdx.x == 0) kc.trace2[(size_t)kc.stage * 8 + i] = clock64();
+  if (kc.trace2 && blockIdx.x == 0 && threadIdx.x == 0) kc.trace2[(size_t)kc.stage * NCKPT + i] = clock64();
+}
+// Per-warp checkpoint (CTA 0, lane 0 of each warp): slot base + warp.
+QTB_DEV void ckpt_w(const KCtx &kc, int base) {
+  if (kc.trace2 && blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+    kc.trace2[(size_t)kc.stage * NCKPT + base + (threadIdx.x >> 5)] = clock64();
 }
 
-// CTA-uniform read of the launch's error flag.
-QTB_DEV bool cta_err(KCtx &kc) {
-  __shared__ int s_e;
-  __syncthreads();
-  if (threadIdx.x == 0) s_e = *(volatile int *)&kc.ctl->err;
-  __syncthreads();
-  return s_e != 0;
-}
 
 QTB_DEV void raise_err(KCtx &kc, int code, int info) {
+  kc.local_err = 1;
   if (atomicCAS(&kc.ctl->err, 0, code) == 0) {
     kc.ctl->err_stage = kc.stage;
     kc.ctl->err_info = info;
   }
 }
 
-// Grid-wide barrier on a monotonic counter.  Bounded: gives up (and raises
+// Grid-wide barrier on a monotonic counter, in two halves: grid_arrive here,
+// grid_wait (which also runs the prefetch hook while it polls) next to the
+// persistent kernel.  Bounded: the wait gives up (and raises
 // ERR_BARRIER_TIMEOUT) after WAIT_LIMIT_CYCLES, or as soon as any CTA has
 // raised an error, so a failing launch always returns.
 QTB_DEV void grid_arrive(KCtx &kc) {
   __syncthreads();
-  // release: this CTA's writes (ordered before by bar.sync) happen-before
-  // every CTA that acquires the final count
-  if (threadIdx.x == 0) atom_add_release_gpu(&kc.ctl->bar_count, 1u);
-}
-
-QTB_DEV bool grid_wait(KCtx &kc) {
-  __shared__ int s_ok;
+  // acq_rel: this CTA's writes (ordered before by bar.sync) happen-before every
+  // CTA that acquires the final count; the CTA whose increment completes the
+  // count acquires all the others' writes through the same RMW and needs no poll
   if (threadIdx.x == 0) {
-    int ok = 1;
     const unsigned target = (kc.epoch + 1u) * gridDim.x;
-    const long long t0 = clock64();
-    unsigned spins = 0;
-    while ((int)(ld_acquire_gpu(&kc.ctl->bar_count) - target) < 0) {
-      if ((++spins & 31u) == 0) {
-        if (*(volatile int *)&kc.ctl->err) { ok = 0; break; }
-        if (clock64() - t0 > WAIT_LIMIT_CYCLES) { raise_err(kc, ERR_BARRIER_TIMEOUT, (int)kc.epoch); ok = 0; break; }
-      }
-    }
-    s_ok = ok && (*(volatile int *)&kc.ctl->err == 0);
+    kc.last = (atom_add_acq_rel_gpu(&kc.ctl->bar_count, 1u) + 1u == target) ? 1 : 0;
   }
-  __syncthreads();
-  kc.epoch++;
-  return s_ok != 0;
 }
 
 // =========================================================== GEMV stage ====
@@ -263,10 +271,17 @@ QTB_DEV float norm_in(const GemvArgs &a, const float *s_inv, int b, int k, float
 // reduced per batch row across the block, then every quad writes its P part
 // entries (the lanes of its column group) and, for int4 weights, the per-32
 // group sums (the 8 quads of a group sit in 8 consecutive lanes of one warp).
-template <bool F16, int P>
-QTB_DEV void stage_x_fused(const GemvArgs &a, int B, int ent, float *s_inv, float *s_xsum, uint2 *s_xf,
-                           bool want_xsum) {
-  constexpr int MAXQ = 8;  // quads per thread: B * K / 4 <= 256 * 8
+// Functions run once per stage on the critical path are real calls: one copy
+// of their code stays in the SM's instruction cache across the stages.
+#define QTB_CALL __device__ __noinline__
+QTB_CALL void stream(KCtx &kc, char *smem, unsigned done, unsigned limit);
+
+// MAXQ = quads (4 consecutive k of one batch row) per thread, B * K / 4 <=
+// 256 * MAXQ; a separate function per MAXQ keeps the small cases' register
+// footprint (and the caller's) small.
+template <bool F16, int P, int MAXQ>
+__device__ __noinline__ void stage_x_fused(const GemvArgs &a, int B, int ent, float *s_inv, float *s_xsum,
+                                           uint2 *s_xf, bool want_xsum, KCtx &kc, char *smem) {
   const int K = a.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ks = K >> 4;
   const int nq = B * ks * 4;
@@ -289,6 +304,9 @@ QTB_DEV void stage_x_fused(const GemvArgs &a, int B, int ent, float *s_inv, floa
       }
     }
   }
+  // while the activation is in flight: the next stage's weights (issued
+  // after the loads above, so they queue behind them)
+  if (tid == 0) stream(kc, smem, kc.seq, kc.seq + 2);
   if (a.norm_w) {
     __shared__ float s_ss[NWARPS][4];
 #pragma unroll
@@ -302,6 +320,8 @@ QTB_DEV void stage_x_fused(const GemvArgs &a, int B, int ent, float *s_inv, floa
         for (int bb = 0; bb < 4; bb++) ss[bb] += (b == bb) ? s2 : 0.f;
       }
     }
+    ckpt(kc, 8);   // activation landed
+    ckpt_w(kc, 16);
 #pragma unroll
     for (int bb = 0; bb < 4; bb++) {
       const float w = warp_sum(ss[bb]);
@@ -417,7 +437,7 @@ template <int P> QTB_DEV bool col_owner(int tig) { return P == 2 || (tig & 1) ==
 // res (groups are 32 columns = 2 k-steps).  xsum_n = groups in the slice.
 template <int FMT, int NCH>
 QTB_DEV void mma_chunk(const uint4 wv, const uint4 gv, int c, const uint2 *s_xf, int ent, const float *s_xsum,
-                       int xsum_n, int B, float (&acc)[NCH][4], float (&res)[NCH][2]) {
+                       int xsum_n, int B, float (&acc)[NCH][4], float (&res)[NCH][2], float (&acc2)[NCH][4]) {
   const int lane = threadIdx.x & 31, tig = lane & 3;
   const bool has_x = lane < ent;
   if (FMT == FMT_BF16) {
@@ -438,7 +458,8 @@ QTB_DEV void mma_chunk(const uint4 wv, const uint4 gv, int c, const uint2 *s_xf,
 #pragma unroll
       for (int j = 0; j < NCH; j++) {
         uint2 bx = has_x ? xf[j * ent + lane] : make_uint2(0u, 0u);
-        mma_f16(acc[j], A, bx.x, bx.y);
+        if (q == 0) mma_f16(acc[j], A, bx.x, bx.y);   // two independent chains
+        else mma_f16(acc2[j], A, bx.x, bx.y);
       }
     }
   } else {
@@ -513,9 +534,13 @@ QTB_DEV void gemv_unit(const GemvArgs &a, int B, int t, int s, int kslice, const
   const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
   const bool has_x = lane < ent;
 
-  float acc[NCH][4];
+  float acc[NCH][4], acc2[NCH][4];
 #pragma unroll
-  for (int j = 0; j < NCH; j++) { acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f; res[j][0] = res[j][1] = 0.f; }
+  for (int j = 0; j < NCH; j++) {
+    acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    acc2[j][0] = acc2[j][1] = acc2[j][2] = acc2[j][3] = 0.f;
+    res[j][0] = res[j][1] = 0.f;
+  }
 
   uint4 wbuf[PD];
   uint4 gbuf[PD];
@@ -539,10 +564,14 @@ QTB_DEV void gemv_unit(const GemvArgs &a, int B, int t, int s, int kslice, const
           if (Tr::GSZ == 8) { uint2 g = ld_nc_u2(gp + (size_t)(c + PD) * 64); gbuf[i] = make_uint4(g.x, g.y, 0, 0); }
           if (Tr::GSZ == 16) gbuf[i] = ld_nc_u4(gp + (size_t)(c + PD) * 128);
         }
-        mma_chunk<FMT, NCH>(wv, gv, c, s_xf, ent, s_xsum, kslice >> 5, B, acc, res);
+        mma_chunk<FMT, NCH>(wv, gv, c, s_xf, ent, s_xsum, kslice >> 5, B, acc, res, acc2);
       }
     }
   }
+#pragma unroll
+  for (int j = 0; j < NCH; j++)
+#pragma unroll
+    for (int e2 = 0; e2 < 4; e2++) acc[j][e2] += acc2[j][e2];
   acc_finish<FMT, NCH, P>(acc, res);
 }
 
@@ -717,15 +746,14 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
 // ============================================ GEMV stage, small batches ====
 //
 // Used when the whole activation (B rows x K) fits the staging region.  Each
-// CTA owns whole 16-row tiles (T >= grid) or one k-piece of one tile (T <
-// grid, `scta` CTAs per tile); in both cases its weights are ONE contiguous
-// byte range of the fragment-ordered matrix, which thread 0 streams into the
-// NWSLOT-slot ring with 1D bulk copies.  The first ring-full is issued before
-// the grid barrier that precedes the stage (v2_prefetch), so HBM latency is
-// hidden behind the barrier.  Warps split the CTA's chunk stream evenly, keep
-// one partial per (tile, warp) in shared memory, and the CTA sums them in warp
-// order; k-pieces of one tile are combined by the last-arriving CTA in piece
-// order (deterministic).
+// CTA owns a run of whole 16-row tiles, so its weights are ONE contiguous byte
+// range of the fragment-ordered matrix.  Thread 0 is also the CTA's weight
+// streamer: it bulk-copies those ranges, stage after stage in program order,
+// into the NWSLOT-slot ring as slots free up -- typically while the grid
+// barriers of the stages before are still pending -- so a stage usually finds
+// its weights already in shared memory.  Warps split the CTA's chunk stream
+// evenly, keep one partial per (tile, warp) in shared memory, and the CTA sums
+// them in warp order (deterministic).
 
 struct V2Sched {
   int t0, nt;   // first tile and tile count of this CTA
@@ -746,23 +774,25 @@ QTB_DEV V2Sched v2_sched(const GemvArgs &a, int cta, int G) {
   // Whole tiles per CTA (when there are fewer tiles than CTAs the rest idle:
   // the weights are streamed before the barrier, so a CTA holding two tiles'
   // worth costs less than a cross-CTA reduction would).
-  s.t0 = (int)((long long)cta * T / G);
-  s.nt = (int)((long long)(cta + 1) * T / G) - s.t0;
+  s.t0 = cta * T / G;
+  s.nt = (cta + 1) * T / G - s.t0;
   s.kb = 0; s.kc = nck; s.scta = 1; s.p = 0;
   s.L = s.nt * s.kc;
   s.nfill = (s.L + s.cps - 1) / s.cps;
   return s;
 }
 
-// Thread 0: bulk-copy slot fills [f0, f1) of this CTA's range into the ring.
+// Thread 0: bulk-copy slot fills [f0, f1) of this CTA's range into the ring;
+// fill f0 is the launch's fill number ctr0 (slot ctr0 % NWSLOT).
 template <int FMT>
-QTB_DEV void v2_issue(const GemvArgs &a, const V2Sched &s, int f0, int f1, const KCtx &kc, char *smem) {
+QTB_DEV void v2_issue(const GemvArgs &a, const V2Sched &s, int f0, int f1, unsigned ctr0, const KCtx &kc,
+                      char *smem) {
   using Tr = FmtTraits<FMT>;
   const int nck = a.K / (16 * Tr::CK);
   const size_t cbase = (size_t)s.t0 * nck + s.kb;
   const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
   for (int f = f0; f < f1; f++) {
-    const unsigned ctr = kc.wfill + (unsigned)f;
+    const unsigned ctr = ctr0 + (unsigned)(f - f0);
     const int slot = (int)(ctr % NWSLOT);
     const int c0 = f * s.cps, n = min(s.cps, s.L - c0);
     char *dst = smem + SM_W_OFF + slot * WSLOT_BYTES;
@@ -774,32 +804,94 @@ QTB_DEV void v2_issue(const GemvArgs &a, const V2Sched &s, int f0, int f1, const
   }
 }
 
+// Streamer step for one small-batch GEMV stage: issue as many of this CTA's
+// remaining fills as the ring has free slots.  True once all are issued.  The
+// first visit also asks L2 for the stage's small operands (RMSNorm gains, the
+// CTA's row scales and bias), so the activation staging and the epilogue hit
+// L2 instead of HBM.
 template <int FMT>
-QTB_DEV int v2_prefetch_f(const GemvArgs &a, const KCtx &kc, char *smem) {
+QTB_DEV bool stream_gemv(const GemvArgs &a, KCtx &kc, char *smem) {
   const V2Sched s = v2_sched<FMT>(a, blockIdx.x, gridDim.x);
-  const int n = min(s.nfill, NWSLOT);
-  if (n > 0) {
-    fence_proxy_async_smem();
-    v2_issue<FMT>(a, s, 0, n, kc, smem);
+  if (s.nfill == 0) return true;
+  if (kc.pf_f == 0) {
+    if (a.norm_w) prefetch_l2(a.norm_w, (uint32_t)a.K * 4u);
+    if (a.row_scale) prefetch_l2(a.row_scale + 16 * s.t0, (uint32_t)s.nt * 64u);
+    if (a.bias) prefetch_l2(a.bias + 16 * s.t0, (uint32_t)s.nt * 64u);
   }
-  return n;
+  const int room = NWSLOT - (int)(kc.w_issued - kc.w_free);
+  const int n = min(s.nfill - kc.pf_f, room);
+  if (n > 0) {
+    v2_issue<FMT>(a, s, kc.pf_f, kc.pf_f + n, kc.w_issued, kc, smem);
+    kc.pf_f += n;
+    kc.w_issued += (unsigned)n;
+  }
+  return kc.pf_f >= s.nfill;
 }
 
-// Thread 0, before the grid barrier: issue the first ring-full of a coming
-// small-batch GEMV stage.  Returns the number of fills issued.
-QTB_DEV int v2_prefetch(const GemvArgs &a, const KCtx &kc, char *smem) {
-  switch (a.fmt) {
-    case FMT_BF16: return v2_prefetch_f<FMT_BF16>(a, kc, smem);
-    case FMT_INT8: return v2_prefetch_f<FMT_INT8>(a, kc, smem);
-    case FMT_Q4_0: return v2_prefetch_f<FMT_Q4_0>(a, kc, smem);
-    case FMT_INT4G: return v2_prefetch_f<FMT_INT4G>(a, kc, smem);
+// Thread 0: the weight streamer.  Walks the stage program ahead of the stage
+// being computed and bulk-copies the weights of coming small-batch GEMV stages
+// into the ring as slots free up.  Fills are issued and consumed in program
+// order, so the launch's n-th fill always lands in slot n % NWSLOT.  `done` =
+// stages this CTA has completed; stages before `limit` are looked at.  The
+// streamer stops at a descriptor that has not landed, at a large-batch GEMV
+// stage that has not run yet (that path uses the ring region for its
+// activation), and STREAM_AHEAD stages past `done`.  Callers look one stage
+// ahead only once the current stage's activation has landed, so the bulk
+// traffic never queues in front of an activation load on the critical path.
+QTB_CALL void stream(KCtx &kc, char *smem, unsigned done, unsigned limit) {
+  // A completed stage has no fills left to issue (each GEMV stage issues its
+  // own before reading them), and its descriptor slot may already hold a later
+  // stage: never look behind `done`.
+  if (kc.pf_seq < done) {
+    kc.pf_seq = done;
+    kc.pf_f = 0;
   }
-  return 0;
+  bool fenced = false;
+  while (kc.pf_seq < kc.n_total && kc.pf_seq < limit && kc.pf_seq < done + STREAM_AHEAD) {
+    const unsigned k = kc.pf_seq;
+    const int slot = (int)(k % NDESC);
+    if (!mbar_test(kc.dbars + slot, (k / NDESC) & 1u)) break;
+    const Stage *st = kc.dring + slot;
+    if (st->kind == ST_GEMV) {
+      const GemvArgs &a = st->g;
+      if (!a.v2) {
+        if (k >= done) break;
+      } else {
+        if (!fenced) {   // the slots were last read through the generic proxy
+          fence_proxy_async_smem();
+          fenced = true;
+        }
+        bool all = true;
+        switch (a.fmt) {
+          case FMT_BF16: all = stream_gemv<FMT_BF16>(a, kc, smem); break;
+          case FMT_INT8: all = stream_gemv<FMT_INT8>(a, kc, smem); break;
+          case FMT_Q4_0: all = stream_gemv<FMT_Q4_0>(a, kc, smem); break;
+          case FMT_INT4G: all = stream_gemv<FMT_INT4G>(a, kc, smem); break;
+        }
+        if (!all) break;
+      }
+    } else if (st->kind == ST_ATTN && k > done) {
+      if (st->a.q_norm) prefetch_l2(st->a.q_norm, HD * 4);
+      if (st->a.k_norm) prefetch_l2(st->a.k_norm, HD * 4);
+    }
+    kc.pf_seq++;
+    kc.pf_f = 0;
+  }
+}
+
+// Thread 0, on the way out after an error: wait (bounded) for this CTA's own
+// bulk copies still in flight, so none lands after the CTA has exited.
+QTB_CALL void drain(KCtx &kc, unsigned cur) {
+  constexpr long long LIM = 200000000LL;   // ~0.1 s per copy group
+  for (unsigned c = kc.wfill; c != kc.w_issued; c++) mbar_wait(kc.wbars + c % NWSLOT, (c / NWSLOT) & 1u, LIM);
+  for (unsigned c = kc.page_ctr; c != kc.att_issued; c++) mbar_wait(kc.bars + c % ATT_NBUF, (c / ATT_NBUF) & 1u, LIM);
+  for (unsigned k = cur + 1; k < cur + NDESC && k < kc.n_total; k++)
+    mbar_wait(kc.dbars + k % NDESC, (k / NDESC) & 1u, LIM);
 }
 
 // Epilogue on final row values val(tl, r, b) held in shared memory
 // (s_val[(tl * 16 + r) * sv_ld + b]) for the CTA's tiles t0 .. t0 + nt - 1.
-QTB_DEV void v2_epilogue(const GemvArgs &a, int B, int t0, int nt, const float *s_val, int sv_ld, KCtx &kc) {
+QTB_CALL void v2_epilogue(const GemvArgs &a, int B, int t0, int nt, const float *s_val, int sv_ld, KCtx &kc) {
   const int tid = threadIdx.x;
   auto val = [&](int tl, int r, int b) {
     const int row = 16 * (t0 + tl) + r;
@@ -895,27 +987,47 @@ __device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem,
   const int xsum_floats = XSUM ? ((B * xsum_n + 3) & ~3) : 0;
   uint2 *s_xf = reinterpret_cast<uint2 *>(s_xsum + xsum_floats);
 
-  if (tid == 0 && kc.w_pre == 0 && s.nfill > 0) {
-    fence_proxy_async_smem();
-    v2_issue<FMT>(a, s, 0, min(s.nfill, NWSLOT), kc, smem);
-  }
-  kc.w_pre = 0;
+  // this stage's first fills, unless the streamer issued them already
+  ckpt(kc, 11);
+  if (tid == 0) stream(kc, smem, kc.seq, kc.seq + 1);
   ckpt(kc, 0);
   if (s.nt == 0) return;
 
-  stage_x_fused<F16, P>(a, B, ent, s_inv, s_xsum, s_xf, XSUM);
+  {
+    const int mq = (B * (a.K >> 2) + NTHREADS - 1) / NTHREADS;
+    if (mq <= 1) stage_x_fused<F16, P, 1>(a, B, ent, s_inv, s_xsum, s_xf, XSUM, kc, smem);
+    else if (mq <= 2) stage_x_fused<F16, P, 2>(a, B, ent, s_inv, s_xsum, s_xf, XSUM, kc, smem);
+    else if (mq <= 4) stage_x_fused<F16, P, 4>(a, B, ent, s_inv, s_xsum, s_xf, XSUM, kc, smem);
+    else stage_x_fused<F16, P, 8>(a, B, ent, s_inv, s_xsum, s_xf, XSUM, kc, smem);
+  }
   for (int i = tid; i < s.nt * NWARPS * 16 * B; i += NTHREADS) s_red[i] = 0.f;
   __syncthreads();
   ckpt(kc, 2);
 
-  const int per_wave = NWSLOT * s.cps;
+  constexpr int CPS = WSLOT_BYTES / (512 + 8 * Tr::GSZ);   // chunks per ring slot (== s.cps)
+  const int per_wave = NWSLOT * CPS;
+  const unsigned wf = kc.wfill;
   for (int w0 = 0; w0 < s.L; w0 += per_wave) {
+    // Warps take equal runs of whole 4-chunk groups (tile lengths, wave
+    // lengths and tile starts are multiples of 4 chunks).
     const int wl = min(per_wave, s.L - w0);
-    const int cb = w0 + (warp * wl) / NWARPS, ce = w0 + ((warp + 1) * wl) / NWARPS;
-    float acc[NCH][4], res[NCH][2];
+    const int q4 = (wl + 3) >> 2;
+    const int cb = w0 + 4 * ((warp * q4) / NWARPS);
+    const int ce = min(w0 + wl, w0 + 4 * (((warp + 1) * q4) / NWARPS));
+    // four accumulator sets: the MMAs of a 4-chunk group are independent
+    float acc[NCH][4], acc1[NCH][4], acc2[NCH][4], acc3[NCH][4], res[NCH][2];
 #pragma unroll
-    for (int j = 0; j < NCH; j++) { acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f; res[j][0] = res[j][1] = 0.f; }
+    for (int j = 0; j < NCH; j++)
+#pragma unroll
+      for (int e2 = 0; e2 < 4; e2++) { acc[j][e2] = acc1[j][e2] = acc2[j][e2] = acc3[j][e2] = 0.f; res[j][e2 & 1] = 0.f; }
     auto flush = [&](int tl) {
+#pragma unroll
+      for (int j = 0; j < NCH; j++)
+#pragma unroll
+        for (int e2 = 0; e2 < 4; e2++) {
+          acc[j][e2] = (acc[j][e2] + acc1[j][e2]) + (acc2[j][e2] + acc3[j][e2]);
+          acc1[j][e2] = acc2[j][e2] = acc3[j][e2] = 0.f;
+        }
       acc_finish<FMT, NCH, P>(acc, res);
 #pragma unroll
       for (int j = 0; j < NCH; j++) {
@@ -928,43 +1040,61 @@ __device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem,
         res[j][0] = res[j][1] = 0.f;
       }
     };
-    // walk (tile, chunk) and (fill, offset) incrementally: no divisions in the loop
-    int tl = cb / s.kc, kk = cb - tl * s.kc;
-    int f = cb / s.cps, o = cb - f * s.cps;
-    int waited = -1;
-    for (int ci = cb; ci < ce; ci++) {
-      const unsigned ctr = kc.wfill + (unsigned)f;
-      const char *slot = smem + SM_W_OFF + (ctr % NWSLOT) * WSLOT_BYTES;
-      if (f != waited) {
-        if (!mbar_wait(kc.wbars + (ctr % NWSLOT), (ctr / NWSLOT) & 1u, WAIT_LIMIT_CYCLES))
-          raise_err(kc, ERR_MBAR_TIMEOUT, f);
-        waited = f;
-      }
-      const uint4 wv = *reinterpret_cast<const uint4 *>(slot + o * 512 + lane * 16);
-      uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+    auto load = [&](int ci, uint4 &wv, uint4 &gv) {
+      const int f = ci / CPS, o = ci - f * CPS;
+      const char *slot = smem + SM_W_OFF + ((wf + (unsigned)f) % NWSLOT) * WSLOT_BYTES;
+      wv = *reinterpret_cast<const uint4 *>(slot + o * 512 + lane * 16);
+      gv = make_uint4(0u, 0u, 0u, 0u);
       if (Tr::GSZ == 8) {
-        const uint2 g = *reinterpret_cast<const uint2 *>(slot + s.cps * 512 + o * 64 + gid * 8);
+        const uint2 g = *reinterpret_cast<const uint2 *>(slot + CPS * 512 + o * 64 + gid * 8);
         gv = make_uint4(g.x, g.y, 0u, 0u);
       } else if (Tr::GSZ == 16) {
-        gv = *reinterpret_cast<const uint4 *>(slot + s.cps * 512 + o * 128 + gid * 16);
+        gv = *reinterpret_cast<const uint4 *>(slot + CPS * 512 + o * 128 + gid * 16);
       }
-      mma_chunk<FMT, NCH>(wv, gv, s.kb + kk, s_xf, ent, s_xsum, xsum_n, B, acc, res);
-      if (++o == s.cps) { o = 0; ++f; }
-      if (++kk == s.kc) {
-        flush(tl);
-        kk = 0;
-        ++tl;
+    };
+    // the fills this warp reads (after a failed wait the CTA only runs out the stage)
+    if (cb < ce) {
+      for (int f = cb / CPS; f <= (ce - 1) / CPS; f++) {
+        const unsigned ctr = wf + (unsigned)f;
+        if (!kc.local_err && !mbar_wait(kc.wbars + (ctr % NWSLOT), (ctr / NWSLOT) & 1u, WAIT_LIMIT_CYCLES))
+          raise_err(kc, ERR_MBAR_TIMEOUT, f);
       }
     }
-    if (kk != 0 && ce > cb) flush(tl);
+    ckpt(kc, 9);   // warp 0's weights ready
+    int ci = cb;
+    while (ci < ce) {
+      const int tl = ci / s.kc;
+      const int te = min(ce, (tl + 1) * s.kc);
+      const int c0 = s.kb - tl * s.kc;   // chunk ci is column chunk c0 + ci of its tile
+      for (; ci + 4 <= te; ci += 4) {
+        uint4 wv[4], gv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) load(ci + u, wv[u], gv[u]);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          if (u & 1) mma_chunk<FMT, NCH>(wv[u], gv[u], c0 + ci + u, s_xf, ent, s_xsum, xsum_n, B, acc2, res, acc3);
+          else mma_chunk<FMT, NCH>(wv[u], gv[u], c0 + ci + u, s_xf, ent, s_xsum, xsum_n, B, acc, res, acc1);
+        }
+      }
+      for (; ci < te; ci++) {
+        uint4 wv, gv;
+        load(ci, wv, gv);
+        mma_chunk<FMT, NCH>(wv, gv, c0 + ci, s_xf, ent, s_xsum, xsum_n, B, acc, res, acc1);
+      }
+      flush(tl);
+    }
+    ckpt(kc, 10);   // warp 0 done with its chunks
+    ckpt_w(kc, 24);
     __syncthreads();
-    if (tid == 0 && w0 + per_wave < s.L) {
-      const int f0 = (w0 + per_wave) / s.cps;
-      fence_proxy_async_smem();
-      v2_issue<FMT>(a, s, f0, min(s.nfill, f0 + NWSLOT), kc, smem);
+    if (tid == 0 && w0 + per_wave < s.L) {   // this wave's slots are free again
+      kc.w_free = kc.wfill + (unsigned)((w0 + per_wave) / CPS);
+      stream(kc, smem, kc.seq, kc.seq + 2);
     }
   }
-  kc.wfill += (unsigned)s.nfill;
+  if (tid == 0) {   // every warp is past its last slot read
+    kc.wfill += (unsigned)s.nfill;
+    kc.w_free = kc.wfill;
+  }
   ckpt(kc, 3);
 
   // per tile: sum the warps' partials in warp order -> s_val[tl][16][B]
@@ -1057,6 +1187,7 @@ struct __align__(16) AttnSmem {
   int flag;
 };
 static_assert(sizeof(AttnSmem) <= 2048, "attention scratch overlaps the page buffers");
+static_assert(2048 + ATT_NBUF * 2 * PAGE * HD * 2 <= SM_X2_BYTES, "page ring exceeds the attention region");
 
 struct AttnItem {
   int b, g, sp, pos, L, npages, nsp, p_begin, p_end;
@@ -1097,13 +1228,14 @@ QTB_DEV void attn_issue(const AttnArgs &a, const AttnItem &it, int i0, int i1, K
     mbar_arrive_expect_tx(kc.bars + buf, 2 * PAGE * HD * 2);
     bulk_g2s(dstk, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
     bulk_g2s(dstk + PAGE * HD, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
+    kc.att_issued = ctr + 1u;
   }
 }
 
 // Thread 0, before the grid barrier: issue the first pages of this CTA's first
 // attention item (older positions only; the newest token is patched in from
 // registers by the stage itself).  Returns the number of pages issued.
-QTB_DEV int attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem_attn) {
+QTB_CALL int attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem_attn) {
   const int n_items = B * a.n_kv * a.max_splits;
   if ((int)blockIdx.x >= n_items) return 0;
   AttnItem it;
@@ -1141,9 +1273,9 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
       const int pre = first ? kc.att_pre : 0;
       fence_proxy_async();
       attn_issue(a, it, pre, min(p_end - p_begin, ATT_NBUF), kc, kvbuf);
+      kc.att_pre = 0;
     }
     first = false;
-    kc.att_pre = 0;
     ckpt(kc, 0);
 
     // ---- prologue: QK RMSNorm + RoPE (+ KV append) ----
@@ -1165,6 +1297,8 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
           rs[i] = __ldg(a.rope_sin + (size_t)pos * (HD / 2) + lane + 32 * i);
         }
       }
+      // while the rows are in flight: the next stage's weights
+      if (threadIdx.x == 0) stream(kc, smem - SM_X_OFF, kc.seq, kc.seq + 2);
       if (nw) {
         float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
         ss = warp_sum(ss);
@@ -1206,7 +1340,7 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
         __stcg(reinterpret_cast<uint4 *>(dst), val);
       }
     }
-    if (cta_err(kc)) return;
+    if (__syncthreads_or(kc.local_err)) return;
     ckpt(kc, 1);
 
     // ---- main loop over this split's pages ----
@@ -1220,15 +1354,9 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
       const uint32_t parity = (ctr / ATT_NBUF) & 1u;
       // every thread observes the phase flip, which makes the bulk-copied
       // bytes visible to it
-      if (!mbar_wait(kc.bars + buf, parity, WAIT_LIMIT_CYCLES)) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-      if (cta_err(kc)) {
-        // leave no bulk copy in flight: wait (bounded) for the ones issued after this page
-        if (tid == 0)
-          for (int j = i + 1; j < min(n, i + ATT_NBUF); j++) {
-            const unsigned c2 = kc.page_ctr + j;
-            mbar_wait(kc.bars + (c2 % ATT_NBUF), (c2 / ATT_NBUF) & 1u, 100000000LL);
-          }
-        __syncthreads();
+      const bool landed = mbar_wait(kc.bars + buf, parity, WAIT_LIMIT_CYCLES);
+      if (__syncthreads_or(!landed)) {   // copies still in flight are drained on the way out
+        if (tid == 0) raise_err(kc, ERR_MBAR_TIMEOUT, i);
         return;
       }
       uint16_t *kb = kvbuf + (size_t)buf * 2 * PAGE * HD;
@@ -1308,9 +1436,10 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
         mbar_arrive_expect_tx(kc.bars + buf, 2 * PAGE * HD * 2);
         bulk_g2s(kb, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
         bulk_g2s(vb, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
+        kc.att_issued = ctr + ATT_NBUF + 1u;
       }
     }
-    kc.page_ctr += n;
+    if (tid == 0) kc.page_ctr += n;   // the loop's last barrier has passed
     ckpt(kc, 2);
 
     // ---- output / split combine ----
@@ -1405,55 +1534,116 @@ __device__ __noinline__ void norm_stage(const NormArgs &n, int B) {
   }
 }
 
+// Second half of the grid barrier, thread 0 polling.  While the other CTAs
+// finish, the hook issues the independent loads of the coming stage -- the
+// older K/V pages of an attention stage, the weights of a GEMV stage -- one
+// step per poll, so a barrier that completes stops the hook within one step.
+// The CTA whose arrival completed the barrier skips both (an error raised
+// elsewhere reaches it at a later barrier, or the host at the end).  Advances
+// the stage counters.
+QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    int ok = kc.local_err ? 0 : 1;   // a CTA that raised an error leaves after arriving
+    if (ok && !kc.last) {
+      const unsigned target = (kc.epoch + 1u) * gridDim.x;
+      const unsigned nxt = kc.seq + 1;
+      int phase = (nxt < kc.n_total) ? 0 : 2;
+      const long long t0 = clock64();
+      unsigned spins = 0;
+      while (true) {
+        const uint2 w = ld_acquire_gpu_v2(&kc.ctl->bar_count);   // {count, err}
+        if (w.y != 0u) { ok = 0; break; }
+        if ((int)(w.x - target) >= 0) break;
+        if (phase == 0) {
+          const int slot = (int)(nxt % NDESC);
+          if (mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u)) {
+            const Stage *nx = kc.dring + slot;
+            if (nx->kind == ST_ATTN) kc.att_pre = attn_prefetch(nx->a, nx->B, kc, smem + SM_X_OFF);
+          }
+          phase = 1;
+        } else if (phase == 1) {
+          stream(kc, smem, nxt, nxt + 1);
+          phase = 2;
+        }
+        if ((++spins & 31u) == 0 && clock64() - t0 > WAIT_LIMIT_CYCLES) {
+          raise_err(kc, ERR_BARRIER_TIMEOUT, (int)kc.epoch);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+    kc.epoch++;
+    kc.seq++;
+    kc.stage = (kc.stage + 1 == kc.n_stages) ? 0 : kc.stage + 1;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
 // ====================================================== persistent kernel ==
 __global__ void __launch_bounds__(NTHREADS, 1)
 decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ctl, long long *trace) {
   extern __shared__ __align__(128) char smem[];
   __shared__ __align__(8) uint64_t bars[ATT_NBUF];
   __shared__ __align__(8) uint64_t wbars[NWSLOT];
-  __shared__ __align__(8) uint64_t sbars[2];
-  __shared__ Stage s_st[2];   // current and next stage descriptors
-  KCtx kc;
-  kc.epoch = 0;
-  kc.page_ctr = 0;
-  kc.wfill = 0;
-  kc.w_pre = 0;
-  kc.att_pre = 0;
-  kc.wbars = wbars;
-  kc.pol_first = policy_evict_first();
-  kc.pol_last = policy_evict_last();
-  kc.bars = bars;
-  kc.ctl = ctl;
-  kc.stage = 0;
-  kc.trace2 = trace ? trace + (size_t)n_iters * n_stages + 1 : nullptr;
-  kc.gtrace = trace ? reinterpret_cast<unsigned long long *>(trace + (size_t)n_iters * n_stages + 1 + (size_t)n_stages * 8)
-                    : nullptr;
+  __shared__ __align__(8) uint64_t dbars[NDESC];
+  __shared__ Stage dring[NDESC];   // stage descriptors, NDESC - 1 stages ahead
+  __shared__ KCtx kc;
+  if (threadIdx.x == 0) {
+    kc.epoch = 0;
+    kc.page_ctr = 0;
+    kc.wfill = 0;
+    kc.att_pre = 0;
+    kc.att_issued = 0;
+    kc.local_err = 0;
+    kc.wbars = wbars;
+    kc.pol_first = policy_evict_first();
+    kc.pol_last = policy_evict_last();
+    kc.bars = bars;
+    kc.ctl = ctl;
+    kc.stage = 0;
+    kc.trace2 = trace ? trace + (size_t)n_iters * n_stages + 1 : nullptr;
+    kc.gtrace = trace ? reinterpret_cast<unsigned long long *>(trace + (size_t)n_iters * n_stages + 1 +
+                                                               (size_t)n_stages * NCKPT)
+                      : nullptr;
+    kc.seq = 0;
+    kc.n_total = (unsigned)n_stages * (unsigned)n_iters;
+    kc.n_stages = n_stages;
+    kc.dring = dring;
+    kc.dbars = dbars;
+    kc.w_issued = 0;
+    kc.w_free = 0;
+    kc.pf_seq = 0;
+    kc.pf_f = 0;
+  }
+  auto issue_desc = [&](unsigned k) {   // thread 0: descriptor of stage k into its slot
+    const int slot = (int)(k % NDESC);
+    mbar_arrive_expect_tx(dbars + slot, sizeof(Stage));
+    bulk_g2s(dring + slot, prog + k % (unsigned)n_stages, sizeof(Stage), dbars + slot);
+  };
   if (threadIdx.x == 0) {
     for (int i = 0; i < ATT_NBUF; i++) mbar_init(bars + i, 1);
     for (int i = 0; i < NWSLOT; i++) mbar_init(wbars + i, 1);
-    mbar_init(sbars + 0, 1);
-    mbar_init(sbars + 1, 1);
+    for (int i = 0; i < NDESC; i++) mbar_init(dbars + i, 1);
     fence_mbar_init();
-    // stage descriptors travel through shared memory, one stage ahead
-    mbar_arrive_expect_tx(sbars + 0, sizeof(Stage));
-    bulk_g2s(s_st + 0, prog, sizeof(Stage), sbars + 0);
+    for (unsigned k = 0; k < NDESC - 1 && k < kc.n_total; k++) issue_desc(k);
+    kc.t_start = clock64();
   }
   __syncthreads();
   if (trace && blockIdx.x == 0 && threadIdx.x == 0) trace[(size_t)n_iters * n_stages] = clock64();
-  unsigned sctr = 0;   // descriptors consumed
-  kc.t_start = clock64();
   for (int it = 0; it < n_iters; it++) {
-    for (int si = 0; si < n_stages; si++, sctr++) {
-      const int cur = sctr & 1;
-      const bool more = (si + 1 < n_stages) || (it + 1 < n_iters);
-      if (!mbar_wait(sbars + cur, (sctr >> 1) & 1u, WAIT_LIMIT_CYCLES)) raise_err(kc, ERR_MBAR_TIMEOUT, -1);
-      if (threadIdx.x == 0 && more) {
+    for (int si = 0; si < n_stages; si++) {
+      const unsigned seq = kc.seq;
+      const int slot = (int)(seq % NDESC);
+      if (!mbar_wait(dbars + slot, (seq / NDESC) & 1u, WAIT_LIMIT_CYCLES)) raise_err(kc, ERR_MBAR_TIMEOUT, -1);
+      if (threadIdx.x == 0 && seq + NDESC - 1 < kc.n_total) {
+        // the slot of stage seq - 1 is free: every thread left that stage
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(sbars + (cur ^ 1), sizeof(Stage));
-        bulk_g2s(s_st + (cur ^ 1), prog + ((si + 1 < n_stages) ? si + 1 : 0), sizeof(Stage), sbars + (cur ^ 1));
+        issue_desc(seq + NDESC - 1);
       }
-      const Stage *st = s_st + cur;
-      kc.stage = si;
+      const Stage *st = dring + slot;
       const int B = st->B;
       switch (st->kind) {
         case ST_GEMV: gemv_stage(st->g, B, smem, kc); break;
@@ -1469,19 +1659,6 @@ decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ct
       }
       ckpt(kc, 6);
       grid_arrive(kc);
-      // issue the next stage's independent loads (weights, older KV pages)
-      // while the other CTAs finish
-      if (more) {
-        if (threadIdx.x == 0) {
-          const Stage *nx = s_st + (cur ^ 1);
-          if (mbar_wait(sbars + (cur ^ 1), ((sctr + 1) >> 1) & 1u, WAIT_LIMIT_CYCLES)) {
-            if (nx->kind == ST_GEMV && nx->g.v2) kc.w_pre = v2_prefetch(nx->g, kc, smem);
-            else if (nx->kind == ST_ATTN) kc.att_pre = attn_prefetch(nx->a, nx->B, kc, smem + SM_X_OFF);
-          } else {
-            raise_err(kc, ERR_MBAR_TIMEOUT, -2);
-          }
-        }
-      }
       ckpt(kc, 7);
       if (kc.gtrace && threadIdx.x == 0) {
         // [stage][cta] = global arrival time; [n_stages + stage][cta] = this CTA's
@@ -1492,8 +1669,11 @@ decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ct
         kc.gtrace[(size_t)(n_stages + si) * gridDim.x + blockIdx.x] =
             (unsigned long long)(clock64() - kc.t_start) | ((unsigned long long)smid << 48);
       }
-      if (!grid_wait(kc)) return;
-      kc.t_start = clock64();
+      if (!grid_wait(kc, smem)) {   // (advances kc.seq and kc.stage)
+        if (threadIdx.x == 0) drain(kc, seq);
+        return;
+      }
+      if (threadIdx.x == 0) kc.t_start = clock64();
       // optional stage trace: CTA 0's clock when every CTA has finished stage si
       if (trace && blockIdx.x == 0 && threadIdx.x == 0) trace[(size_t)it * n_stages + si] = clock64();
     }

@@ -53,6 +53,9 @@ class EngineDesc(C.Structure):
 _lib = None
 
 
+NCKPT = 32   # intra-stage profiling checkpoints per stage (kernel constant)
+
+
 def lib():
     """Load libqwen3tts_b200.so (raises when it is not built)."""
     global _lib
@@ -419,9 +422,9 @@ class Session:
         n = lib().qtb_session_profile(self.h, which, ptr(cyc), ptr(kind), ptr(shape), max_stages)
         if n < 0:
             check(n)
-        ck = np.zeros(n * 8, np.int64)
-        lib().qtb_session_profile_checkpoints(self.h, ptr(ck), n * 8)
-        self.checkpoints = ck.reshape(n, 8)
+        ck = np.zeros(n * NCKPT, np.int64)
+        lib().qtb_session_profile_checkpoints(self.h, ptr(ck), n * NCKPT)
+        self.checkpoints = ck.reshape(n, NCKPT)
         return cyc[:n], kind[:n], shape[:n]
 
     def last_ms(self):

@@ -6,6 +6,7 @@ import tempfile
 import numpy as np
 
 import qtts_b200 as Q
+import qtts_oracle as O
 import refbind
 
 
@@ -83,3 +84,32 @@ def kv_close(a, b, min_equal=0.98):
         i = np.unravel_index(np.argmax(np.abs(fa - fb) - tol), fa.shape)
         print("kv_close: worst", i, fa[i], fb[i], "tol", tol[i], "equal", float(np.mean(np.asarray(a) == np.asarray(b))))
     return ok
+
+
+def codec_margin(m, cfg, h):
+    """(top1 - top2) / std of the codec-head logits on hidden h (float64)."""
+    lg = O.f32_from_bf16(m.codec_head)[:cfg.codebook].astype(np.float64) @ np.asarray(h, np.float64)
+    top = np.sort(lg)[-2:]
+    return float((top[1] - top[0]) / lg.std())
+
+
+def cp_margins(ref, m, cfg, fmt, h, code0, codes):
+    """Relative top-2 margins ((top1 - top2) / std) of the 15 code-predictor
+    heads for talker hidden h and code0, with the given codes fed back
+    (float64 restatement on the reference's quantized bytes)."""
+    q = ref_quantized(ref, cfg, fmt, cp=True)
+    cq = {k[1:]: v for k, v in q.items() if k.startswith("c")}
+    ccs, csn = ref.rope(True)
+    cp = O.Stack(m.cp.layers, cfg.cp_hidden, cfg.cp_heads, cfg.cp_kv_heads, cfg.cp_head_dim, cfg.cp_inter, cfg.eps,
+                 ccs, csn, None, fmt, cq or None)
+    lm = [O.dequant(fmt, w, q.get(f"lm{g}")) for g, w in enumerate(m.cp_lm_head)]
+    emb = [O.f32_from_bf16(w) for w in m.cp_codec_emb]
+    margins = []
+    O.cp_predict(cp, m.cp_norm, lm, emb, O.f32_from_bf16(m.codec_embedding), h, code0, force=codes, margins=margins)
+    return [mg / sd for mg, sd in margins]
+
+
+# A greedy fork between two implementations that agree to ~1e-4 is only
+# acceptable at a near-tie: the reference's own top-2 logits closer than this
+# fraction of the logit spread.
+NEAR_TIE = 5e-3
