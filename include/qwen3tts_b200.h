@@ -216,6 +216,24 @@ int qtb_attention_host(const float *qkv, int batch, int n_heads, int n_kv, int h
                        const int32_t *page_table, int pt_stride, const int32_t *pos,
                        int max_splits, float *out);
 
+/* qtb_attention_noalloc: no counterpart in the reference.  The same stage as
+ * qtb_attention_host, but every pointer is DEVICE memory owned by the caller
+ * (same layouts), `stream` is a cudaStream_t (NULL = legacy default stream),
+ * and the call allocates nothing: the launch's scratch lives in one fixed
+ * file-scope device array (about 263 KB) that bounds batch <= 4, n_kv <= 16
+ * and max_splits <= 16; larger requests return QTB_E_INVALID untouched.  For
+ * callers that must not allocate device memory while they run -- code between
+ * a pool's reservation and its release, or code whose memory budget is fixed
+ * up front.  The array is shared: calls that overlap in time race on it.  The
+ * first call on a device (with that device current) does one-time set-up, so
+ * make it before any stream capture.  Returns after the stage has finished. */
+int qtb_attention_noalloc(const float *qkv, int batch, int n_heads, int n_kv, int head_dim,
+                          const float *q_norm, const float *k_norm, float eps,
+                          const float *rope_cos, const float *rope_sin, int rope_len,
+                          uint16_t *kpages, uint16_t *vpages, int n_pages,
+                          const int32_t *page_table, int pt_stride, const int32_t *pos,
+                          int max_splits, float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,6 +16,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <mutex>
 #include <thread>
 #include <vector>
 #include <algorithm>
@@ -1329,4 +1330,96 @@ extern "C" int qtb_session_profile_arrivals(qtb_session_t *s, long long *out, in
   const int n = std::min<int>((int)s->last_gtrace.size(), max_vals);
   for (int i = 0; i < n; i++) out[i] = s->last_gtrace[i];
   return n;
+}
+
+// ------------------------------------------------------------------------
+// qtb_attention_noalloc: the standalone attention stage of qtb_attention_host
+// on caller-owned device buffers, with the launch's own scratch (stage
+// descriptor, control block, split-combine workspace and semaphores) in one
+// fixed file-scope device array instead of fresh allocations.  Limits:
+// batch <= 4, n_kv <= 16, max_splits <= 16 (the workspace bound below).
+// The array is shared by every call on a device: calls that overlap in time
+// (two streams, two host threads) race on it.  The first call on a device
+// looks the array up and sets the kernel attributes; make it before any
+// stream capture.
+namespace {
+constexpr int NOALLOC_MAX_B = 4, NOALLOC_MAX_KV = 16, NOALLOC_MAX_SPLITS = 16;
+constexpr size_t NOALLOC_DESC_OFF = 0;                                     // Stage
+constexpr size_t NOALLOC_CTL_OFF = 1024;                                   // Ctl
+constexpr size_t NOALLOC_SEM_OFF = NOALLOC_CTL_OFF + 1024;                 // unsigned [B][n_kv]
+constexpr size_t NOALLOC_WS_OFF = NOALLOC_SEM_OFF + 1024;                  // float workspace
+constexpr size_t NOALLOC_WS_BYTES =
+    (size_t)NOALLOC_MAX_B * NOALLOC_MAX_KV * NOALLOC_MAX_SPLITS * 2 * (HD + 2) * sizeof(float);
+constexpr size_t NOALLOC_BYTES = NOALLOC_WS_OFF + NOALLOC_WS_BYTES;        // 269,312 bytes
+static_assert(sizeof(Stage) <= 1024 && sizeof(Ctl) <= 1024, "scratch layout");
+static_assert((size_t)NOALLOC_MAX_B * NOALLOC_MAX_KV * sizeof(unsigned) <= 1024, "scratch layout");
+constexpr int NOALLOC_MAX_DEV = 64;
+std::mutex g_noalloc_mu;
+unsigned char *g_noalloc_addr[NOALLOC_MAX_DEV];   // per device, looked up once
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
+
+extern "C" int qtb_attention_noalloc(const float *qkv, int batch, int n_heads, int n_kv, int head_dim,
+                                     const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
+                                     const float *rope_sin, int rope_len, uint16_t *kpages, uint16_t *vpages,
+                                     int n_pages, const int32_t *page_table, int pt_stride, const int32_t *pos,
+                                     int max_splits, float *out, void *stream) {
+  if (!qkv || !q_norm || !k_norm || !rope_cos || !rope_sin || !kpages || !vpages || !page_table || !pos || !out)
+    return set_err(QTB_E_INVALID, "null argument");
+  if (head_dim != HD || n_heads != 2 * n_kv || rope_len < 1 || n_pages < 1 || pt_stride < 1)
+    return set_err(QTB_E_UNSUPPORTED, "shape not supported");
+  if (batch < 1 || batch > NOALLOC_MAX_B || n_kv < 1 || n_kv > NOALLOC_MAX_KV || max_splits < 1 ||
+      max_splits > NOALLOC_MAX_SPLITS)
+    return set_err(QTB_E_INVALID, "beyond the fixed scratch: batch <= %d, n_kv <= %d, max_splits <= %d",
+                   NOALLOC_MAX_B, NOALLOC_MAX_KV, NOALLOC_MAX_SPLITS);
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= NOALLOC_MAX_DEV) return set_err(QTB_E_UNSUPPORTED, "device index %d", dev);
+  unsigned char *base;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {   // first call on this device (current): set-up
+      void *p = nullptr;
+      CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+      CUDA_TRY(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+      g_noalloc_addr[dev] = static_cast<unsigned char *>(p);
+    }
+    base = g_noalloc_addr[dev];
+  }
+  int nsm = 0;
+  CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Stage *dstage = reinterpret_cast<Stage *>(base + NOALLOC_DESC_OFF);
+  Ctl *ctl = reinterpret_cast<Ctl *>(base + NOALLOC_CTL_OFF);
+  unsigned *sem = reinterpret_cast<unsigned *>(base + NOALLOC_SEM_OFF);
+  float *ws = reinterpret_cast<float *>(base + NOALLOC_WS_OFF);
+  const int qd = n_heads * HD, kvd = n_kv * HD;
+  Stage s;
+  memset(&s, 0, sizeof s);
+  s.kind = ST_ATTN;
+  s.B = batch;
+  AttnArgs &a = s.a;
+  a.qkv = qkv; a.ld_qkv = qd + 2 * kvd; a.out = out; a.ld_out = qd;
+  a.q_norm = q_norm; a.k_norm = k_norm; a.rope_cos = rope_cos; a.rope_sin = rope_sin; a.rope_len = rope_len;
+  a.pos_ptr = pos; a.page_table = page_table; a.pt_stride = pt_stride;
+  a.kpool = kpages; a.vpool = vpages; a.n_pages = n_pages; a.n_heads = n_heads; a.n_kv = n_kv;
+  a.eps = eps; a.scale = 1.0f / sqrtf((float)HD); a.max_splits = max_splits; a.min_pps = 1;
+  a.ws = ws; a.sem = sem;
+  // the control block and the split semaphores must start at zero; the
+  // descriptor is copied from this stack frame (synchronously, so the frame
+  // may go away when the call returns)
+  CUDA_TRY(cudaMemsetAsync(ctl, 0, sizeof(Ctl), st));
+  CUDA_TRY(cudaMemsetAsync(sem, 0, (size_t)batch * n_kv * sizeof(unsigned), st));
+  CUDA_TRY(cudaMemcpyAsync(dstage, &s, sizeof s, cudaMemcpyHostToDevice, st));
+  const Stage *prog = dstage;
+  int n_st = 1, n_it = 1;
+  long long *trace = nullptr;
+  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
+  CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(nsm), dim3(NTHREADS), args, SMEM_BYTES, st));
+  Ctl h;
+  CUDA_TRY(cudaMemcpyAsync(&h, ctl, sizeof h, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  if (h.err) return set_err(QTB_E_DEVICE, "kernel error %d (info %d)", h.err, h.err_info);
+  return 0;
 }
