@@ -115,13 +115,14 @@ def build_engine(cfg_name, device, seed=0):
 
 
 def frame_bytes(eng, with_cp, kv_positions, batch, pages_appended=1):
-    """Algorithmic bytes of one step: stored weights (incl. scales/zeros) +
-    KV read (positions 0..pos, all 28 layers) + KV appended."""
+    """Algorithmic HBM bytes of one step: the talker's stored weights (incl.
+    scales/zeros) once, the code predictor's weights and heads once (its 16
+    passes re-read them from L2, where they stay resident by design), the
+    talker KV read (positions 0..pos, all 28 layers) and the KV appended.  The
+    code predictor's own per-frame KV (at most 16 positions) lives in L2."""
     w = eng.talker_weight_bytes()
     if with_cp:
-        w += 16 * eng.cp_pass_weight_bytes() + 15 * eng.cp_head_weight_bytes()
-        # code-predictor KV: pass p reads positions 0..p of its 5 layers and appends one
-        w += batch * (sum(p + 1 for p in range(16)) + 16) * 5 * 1024 * 2 * 2
+        w += eng.cp_pass_weight_bytes() + 15 * eng.cp_head_weight_bytes()
     return w + KV_BYTES_PER_POS * (kv_positions + batch * pages_appended)
 
 
@@ -199,11 +200,11 @@ def run_b200(args, rank, world, local_rank):
     peak, peak_kind = load_peaks()
     achieved_gbs = total_bytes / (ms * 1e-3) / 1e9
     value = world * K * B / (ms_max * 1e-3)
+    traffic = measured_traffic(cfg_name, per_frame_bytes * K, K)
     out = {
-        "metric": "codec frames/s (1 talker step + 16 code-predictor passes per frame)" if with_cp else
-                  "talker decode steps/s",
+        "metric": "talker decode steps/s",
         "value": round(value, 2),
-        "unit": "frames/s" if with_cp else "steps/s",
+        "unit": "steps/s",
         "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(ms_max / K, 4),
         "higher_is_better": True,
@@ -211,21 +212,43 @@ def run_b200(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": fmt,
         "data": "synthetic (random N(0,0.02) weights of the Qwen3-TTS shapes, seeded)",
-        "config": {"workload": f"BASELINE config {cfg_name[1]}: {desc}", "batch_per_gpu": B,
-                   "parallelism": f"request-sharded replicas x{world}, no collectives",
-                   "l2": "talker weights (0.44-1.4 GB) exceed the 126 MB L2 and stream from HBM every step; "
-                         "code-predictor weights are kept L2-resident across its 16 passes by design",
-                   "start_positions": "prefill" if B == 1 else "U[128,2048]/U[256,4096] paged"},
+        "config": config_dict(cfg_name, world),
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved_gbs / peak, 4), "traffic": None,
+                     "frac": round(achieved_gbs / peak, 4), "traffic": traffic,
                      "peak_source": peak_kind, "algorithmic_bytes_per_step": int(per_frame_bytes)},
-        "e2e": {"value": round(world * e2e_frames * B / e2e_s, 2), "unit": "frames/s" if with_cp else "steps/s",
-                "h2d_bytes_per_step": B * H * 4 + (H * 4 if True else 0),
-                "d2h_bytes_per_step": B * 16 * 4 + B * H * 4 + 8},
+        # qtb_decode_frames(embeds, n_frames=1): embeddings in, codes and the
+        # last hidden state out, through the session's pinned staging buffers
+        "e2e": {"value": round(world * e2e_frames * B / e2e_s, 2), "unit": "steps/s",
+                "h2d_bytes_per_step": B * H * 4,
+                "d2h_bytes_per_step": B * 16 * 4 + B * H * 4},
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
     return out
+
+
+def config_dict(cfg_name, world):
+    model_name, fmt, with_cp, B, prefill, desc = CONFIGS[cfg_name]
+    return {"workload": f"BASELINE config {cfg_name[1]}: {desc}"
+                        + ("; every step is a whole codec frame: 1 talker step + 16 code-predictor passes "
+                           "+ 15 greedy heads + codec-head argmax + next embedding" if with_cp else ""),
+            "batch_per_gpu": B,
+            "parallelism": f"request-sharded replicas x{world}, no collectives",
+            "l2": "inputs larger than L2: the talker weights (0.44-1.4 GB) exceed the 126 MB L2 and stream from "
+                  "HBM every step; the code-predictor weights stay L2-resident across its 16 passes by design",
+            "start_positions": f"{prefill}-token prefill" if B == 1 else "U[128,2048]/U[256,4096] paged"}
+
+
+def measured_traffic(cfg_name, algorithmic_bytes, steps):
+    """DRAM bytes (read + write) of one timed launch, from the committed ncu
+    capture of the same kernel and workload (profiles/decode_kernel_<cfg>.json:
+    bytes per frame measured on a short launch, scaled to `steps` frames)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", f"decode_kernel_{cfg_name}.json")) as f:
+            d = json.load(f)
+        return int(d["dram_bytes_per_frame"] * steps)
+    except Exception:
+        return None
 
 
 def cpu_baseline_sample(cfg_name, frames=None, threads=None):
@@ -304,7 +327,7 @@ def dist_max(v):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--steps", type=int, default=512)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
@@ -315,15 +338,15 @@ def main():
     rank, world, local = dist_init()
     if args.impl == "reference":
         if rank == 0:
-            cb = cpu_baseline_sample(args.config, frames=max(2, args.steps // 32))
-            unit = "frames/s" if CONFIGS[args.config][2] else "steps/s"
-            line = {"impl": "reference", "metric": "codec frames/s" if CONFIGS[args.config][2] else
-                    "talker decode steps/s", "value": round(cb.get("value", 0.0), 3), "unit": unit,
+            cb = cpu_baseline_sample(args.config)   # a ~12 s sample of the same workload
+            unit = "steps/s"
+            line = {"impl": "reference", "metric": "talker decode steps/s", "value": round(cb.get("value", 0.0), 3),
+                    "unit": unit,
                     "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                    "config": {"workload": f"BASELINE config {args.config[1]} (reference CPU path)"},
+                    "config": config_dict(args.config, world),
                     "cpu_baseline": {"value": cb.get("value"), "unit": unit, "cores": cb.get("cores"),
-                                     "kind": "reference", "sample": f"{cb.get('frames')} frames after an 8-step prefill, "
-                                     f"default dispatch ({cb.get('isa')})"},
+                                     "kind": "reference", "sample": f"{cb.get('frames')} steps (~12 s) after an 8-step "
+                                     f"prefill, default dispatch ({cb.get('isa')}), all host threads"},
                     "e2e": {"value": round(cb.get("value", 0.0), 3), "unit": unit, "h2d_bytes_per_step": 0,
                             "d2h_bytes_per_step": 0}}
             if "error" in cb:
