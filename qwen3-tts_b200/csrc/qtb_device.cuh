@@ -104,6 +104,16 @@ QTB_DEV void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D(16x8,s32) += A(16x32,s8) * B(32x8,s8), exact integer accumulation.
+// A: 4 regs (rows gid / gid+8, k 4tig..4tig+3 and 16+4tig..), B: 2 regs
+// (k 4tig..4tig+3 and 16+4tig.., column gid).
+QTB_DEV void mma_s8(int (&d)[4], const uint4 &a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
 // Two signed int8 weights (selected bytes of w, already XOR 0x80) -> f16x2
 // holding exactly their values: 0x64XX is 1024 + XX in fp16.
 QTB_DEV uint32_t i8x2_to_f16x2(uint32_t w_xor80, uint32_t sel) {

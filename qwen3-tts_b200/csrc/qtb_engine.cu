@@ -133,16 +133,17 @@ static void repack_int8(const int8_t *W, int rows, int K, std::vector<uint8_t> &
     for (int t = t0; t < t1; t++)
       for (int c = 0; c < CT; c++)
         for (int l = 0; l < 32; l++) {
+          // the A fragment of mma m16n8k32 s8: (row gid, k 4tig..4tig+3),
+          // (row gid+8, same k), then the same two at k + 16
           const int gid = l >> 2, tig = l & 3;
           const size_t r0 = 16 * t + gid, r1 = r0 + 8;
           uint8_t *d = o + (((size_t)t * CT + c) * 32 + l) * 16;
-          for (int q = 0; q < 2; q++) {
-            const size_t k = 32 * c + 16 * q + 2 * tig;
-            uint8_t *dq = d + 8 * q;
-            dq[0] = (uint8_t)W[r0 * K + k]; dq[1] = (uint8_t)W[r0 * K + k + 1];
-            dq[2] = (uint8_t)W[r1 * K + k]; dq[3] = (uint8_t)W[r1 * K + k + 1];
-            dq[4] = (uint8_t)W[r0 * K + k + 8]; dq[5] = (uint8_t)W[r0 * K + k + 9];
-            dq[6] = (uint8_t)W[r1 * K + k + 8]; dq[7] = (uint8_t)W[r1 * K + k + 9];
+          for (int h = 0; h < 2; h++) {
+            const size_t k = 32 * c + 16 * h + 4 * tig;
+            for (int i = 0; i < 4; i++) {
+              d[8 * h + i] = (uint8_t)W[r0 * K + k + i];
+              d[8 * h + 4 + i] = (uint8_t)W[r1 * K + k + i];
+            }
           }
         }
   });
@@ -541,9 +542,14 @@ struct qtb_session {
 // MMA columns per batch row: bf16 weights carry the activation as bf16
 // hi + mid + lo (+ a zero column) up to 16 rows, else hi + lo; the integer
 // formats use fp16 hi + lo.
-static int parts_for(int fmt, int B) { return (fmt == FMT_BF16 && B <= 16) ? 4 : 2; }
-static int nch_for(int fmt, int B) {
-  const int c = (parts_for(fmt, B) * B + 7) / 8;
+// MMA columns per batch row: bf16 hi/mid/lo (+0) for B <= 16; four s8 parts
+// on the small-batch int8 path; f16 hi/lo otherwise.
+static int parts_for(int fmt, int B, bool v2 = false) {
+  if (v2 && fmt == FMT_INT8) return 4;
+  return (fmt == FMT_BF16 && B <= 16) ? 4 : 2;
+}
+static int nch_for(int fmt, int B, bool v2 = false) {
+  const int c = (parts_for(fmt, B, v2) * B + 7) / 8;
   int n = 1;
   while (n < c) n <<= 1;
   return n;
@@ -571,11 +577,14 @@ static int choose_S(int T, int K, int B, int W, int fmt) {
 // Small-batch GEMV path: the whole activation is staged once and the weights
 // stream through the TMA ring (see gemv2_stage_t).
 static bool v2_ok(int fmt, int rows, int K, int B, int G) {
-  if (B > 4 || B * K > 8192) return false;   // stage_x_fused: <= 8 quads per thread
-  const int P = parts_for(fmt, B), nch = nch_for(fmt, B), ent = 4 * std::min(8, P * B);
-  if (fmt == FMT_BF16 ? nch > 2 : nch > 1) return false;
+  if (B > 4 || B * K > 8192) return false;   // activation staging: <= 8 quads per thread
+  const int P = parts_for(fmt, B, true), nch = nch_for(fmt, B, true), ent = 4 * std::min(8, P * B);
+  if (fmt == FMT_BF16 || fmt == FMT_INT8 ? nch > 2 : nch > 1) return false;
   const bool xsum = (fmt == FMT_Q4_0 || fmt == FMT_INT4G);
-  const size_t xb = (size_t)(K / 16) * nch * ent * 8 + (xsum ? (size_t)((B * (K / 32) + 3) & ~3) * 4 : 0);
+  // int8: one (b0, b1) pair per lane per k32 chunk and column chunk
+  const size_t xb = fmt == FMT_INT8 ? (size_t)(K / 32) * nch * 32 * 8
+                                    : (size_t)(K / 16) * nch * ent * 8 +
+                                          (xsum ? (size_t)((B * (K / 32) + 3) & ~3) * 4 : 0);
   if (xb > (size_t)SM_X2_BYTES) return false;
   const int T = rows / 16, nt_max = (T + G - 1) / G;
   return 256 + (size_t)nt_max * (NWARPS + 1) * 16 * B * 4 <= (size_t)SM_R_BYTES;
@@ -599,8 +608,8 @@ struct ProgBuilder {
     g.v2 = v2_ok(m.fmt, m.rows, m.K, B, s->e->n_sm) ? 1 : 0;
     g.S = g.v2 ? 1 : choose_S(m.rows / 16, m.K, B, W(), m.fmt);
     if (g.S < 1) { err = set_err(QTB_E_UNSUPPORTED, "no k-slicing fits shared memory (K=%d, B=%d)", m.K, B); return; }
-    g.nch = nch_for(m.fmt, B);
-    g.parts = parts_for(m.fmt, B);
+    g.nch = nch_for(m.fmt, B, g.v2);
+    g.parts = parts_for(m.fmt, B, g.v2);
     g.evict_last = evict_last;
     g.x = x; g.ldx = ldx; g.norm_w = norm_w; g.eps = eps;
     g.y = y; g.ldy = ldy; g.epi = epi;
@@ -1209,7 +1218,7 @@ extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols,
   st.B = batch;
   GemvArgs &g = st.g;
   g.w = m.w; g.row_scale = m.row_scale; g.gsz = m.gsz;
-  g.fmt = fmt; g.rows = rows; g.K = cols; g.S = v2 ? 1 : S; g.nch = nch_for(fmt, batch); g.parts = parts_for(fmt, batch);
+  g.fmt = fmt; g.rows = rows; g.K = cols; g.S = v2 ? 1 : S; g.nch = nch_for(fmt, batch, v2); g.parts = parts_for(fmt, batch, v2);
   g.v2 = v2 ? 1 : 0;
   g.x = dx; g.ldx = cols; g.y = dy; g.ldy = rows; g.epi = EPI_STORE; g.ws = ws; g.sem = sem;
   if ((rc = run_single_stage(mr, st))) return rc;

@@ -375,8 +375,12 @@ __device__ __noinline__ void stage_x_fused(const GemvArgs &a, int B, int ent, fl
 }
 
 template <bool F16>
+// perm4: the int8 weight layout holds, per lane, 4 consecutive k of a 16-k
+// step (the s8 MMA fragment); as an f16 MMA operand its logical k pairs
+// (2tig, 2tig+1) and (8+2tig, 8+2tig+1) are physical k 4tig+{0,1} and
+// 4tig+{2,3}, so the activation is staged in the same order.
 QTB_DEV void stage_x(const GemvArgs &a, int B, int ent, int k0, int kslice, const float *s_inv,
-                     float *s_xsum, uint2 *s_xf, bool want_xsum) {
+                     float *s_xsum, uint2 *s_xf, bool want_xsum, bool perm4) {
   const int nch = a.nch, P = a.parts;
   const int ksteps = kslice >> 4;
   const int total = ksteps * nch * ent;
@@ -389,12 +393,12 @@ QTB_DEV void stage_x(const GemvArgs &a, int B, int ent, int k0, int kslice, cons
     const int b = col / P, lo = col % P;
     uint32_t r0 = 0, r1 = 0;
     if (b < B) {
-      const int k = k0 + 16 * q + 2 * tig;
+      const int k = k0 + 16 * q + (perm4 ? 4 : 2) * tig, k2 = k + (perm4 ? 2 : 8);
       const float *xb = a.x + (size_t)b * a.ldx;
       float2 p0 = __ldcg(reinterpret_cast<const float2 *>(xb + k));
-      float2 p1 = __ldcg(reinterpret_cast<const float2 *>(xb + k + 8));
+      float2 p1 = __ldcg(reinterpret_cast<const float2 *>(xb + k2));
       float v0 = norm_in(a, s_inv, b, k, p0.x), v1 = norm_in(a, s_inv, b, k + 1, p0.y);
-      float v2 = norm_in(a, s_inv, b, k + 8, p1.x), v3 = norm_in(a, s_inv, b, k + 9, p1.y);
+      float v2 = norm_in(a, s_inv, b, k2, p1.x), v3 = norm_in(a, s_inv, b, k2 + 1, p1.y);
       r0 = split_pack<F16>(v0, v1, lo);
       r1 = split_pack<F16>(v2, v3, lo);
     }
@@ -449,11 +453,13 @@ QTB_DEV void mma_chunk(const uint4 wv, const uint4 gv, int c, const uint2 *s_xf,
       mma_bf16(acc[j], A, bx.x, bx.y);
     }
   } else if (FMT == FMT_INT8) {
+    // s8 MMA layout (words: row gid k0..3, row gid+8 k0..3, then k16..19),
+    // read as two f16 MMAs over the perm4 k order
     const uint32_t wd[4] = {wv.x ^ 0x80808080u, wv.y ^ 0x80808080u, wv.z ^ 0x80808080u, wv.w ^ 0x80808080u};
 #pragma unroll
     for (int q = 0; q < 2; q++) {
-      const uint32_t A[4] = {i8x2_to_f16x2(wd[2 * q], 0x4140), i8x2_to_f16x2(wd[2 * q], 0x4342),
-                             i8x2_to_f16x2(wd[2 * q + 1], 0x4140), i8x2_to_f16x2(wd[2 * q + 1], 0x4342)};
+      const uint32_t A[4] = {i8x2_to_f16x2(wd[2 * q], 0x4140), i8x2_to_f16x2(wd[2 * q + 1], 0x4140),
+                             i8x2_to_f16x2(wd[2 * q], 0x4342), i8x2_to_f16x2(wd[2 * q + 1], 0x4342)};
       const uint2 *xf = s_xf + (size_t)(2 * c + q) * NCH * ent;
 #pragma unroll
       for (int j = 0; j < NCH; j++) {
@@ -696,7 +702,7 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
   for (int base = blockIdx.x * NWARPS; base < U; base += W) {
     if (a.norm_w && !inv_done) { stage_inv_rms(a, B, s_inv); __syncthreads(); inv_done = true; }
     const int s = base / T;
-    stage_x<F16>(a, B, ent, s * kslice, kslice, s_inv, s_xsum, s_xf, XSUM);
+    stage_x<F16>(a, B, ent, s * kslice, kslice, s_inv, s_xsum, s_xf, XSUM, FMT == FMT_INT8);
     __syncthreads();
     const int u = base + warp;
     if (u < U) {
@@ -1112,14 +1118,246 @@ __device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem,
   ckpt(kc, 5);
 }
 
+// ------------------------------------------ small-batch int8: s8 tensor cores
+//
+// The activation (after the fused RMSNorm) is carried as four signed 8-bit
+// parts per value, x = sx * (a0 + a1 / 2^7 + a2 / 2^14 + a3 / 2^21), sx =
+// max|x| / 127 per batch row (a0 = rint(x / sx), then each part the rounded
+// remainder times 2^7), which represents x to ~2^-29 of max|x|.  The int8
+// weights then feed the integer MMA (m16n8k32, s8 x s8 -> s32, exact) as they
+// are stored: no per-weight conversion instructions at all.  The parts of batch
+// row b are MMA columns 4b .. 4b+3; per k32 chunk c and column chunk j the
+// staged activation holds one (b0, b1) register pair per lane.
+template <int MAXQ>
+__device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float *s_scl, uint32_t *s_xw, KCtx &kc,
+                                        char *smem) {
+  const int K = a.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nk4 = K >> 2;
+  const int nq = B * nk4;
+  float v[MAXQ][4], g[MAXQ][4];
+  float ss[4] = {0.f, 0.f, 0.f, 0.f}, mx[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < MAXQ; i++) {
+    const int t = tid + i * NTHREADS;
+    if (t < nq) {
+      const int b = t / nk4, k = 4 * (t - b * nk4);
+      const float4 x4 = __ldcg(reinterpret_cast<const float4 *>(a.x + (size_t)b * a.ldx + k));
+      v[i][0] = x4.x; v[i][1] = x4.y; v[i][2] = x4.z; v[i][3] = x4.w;
+      if (a.norm_w) {
+        const float4 g4 = __ldg(reinterpret_cast<const float4 *>(a.norm_w + k));
+        g[i][0] = g4.x; g[i][1] = g4.y; g[i][2] = g4.z; g[i][3] = g4.w;
+      } else {
+        g[i][0] = g[i][1] = g[i][2] = g[i][3] = 1.f;
+      }
+    }
+  }
+  // while the activation is in flight: the next stage's weights
+  if (tid == 0) stream(kc, smem, kc.seq, kc.seq + 2);
+  __shared__ float s_red2[NWARPS][8];
+#pragma unroll
+  for (int i = 0; i < MAXQ; i++) {
+    const int t = tid + i * NTHREADS;
+    if (t < nq) {
+      const int b = t / nk4;
+      float s2 = 0.f, m2 = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        s2 += v[i][e] * v[i][e];
+        m2 = fmaxf(m2, fabsf(v[i][e] * g[i][e]));
+      }
+#pragma unroll
+      for (int bb = 0; bb < 4; bb++)
+        if (b == bb) { ss[bb] += s2; mx[bb] = fmaxf(mx[bb], m2); }
+    }
+  }
+  ckpt(kc, 8);
+#pragma unroll
+  for (int bb = 0; bb < 4; bb++) {
+    if (bb < B) {   // warp-uniform
+      const float w = warp_sum(ss[bb]), m = warp_max(mx[bb]);
+      if (lane == 0) { s_red2[warp][bb] = w; s_red2[warp][4 + bb] = m; }
+    }
+  }
+  __syncthreads();
+  if (tid < B) {
+    float tot = 0.f, m = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARPS; w++) { tot += s_red2[w][tid]; m = fmaxf(m, s_red2[w][4 + tid]); }
+    const float inv = a.norm_w ? 1.0f / sqrtf(tot / (float)K + a.eps) : 1.0f;
+    const float sx = fmaxf(m * inv, 1e-30f) * (1.0f / 127.0f);
+    s_scl[tid] = inv;          // [0, 4): 1/rms (1 without a norm)
+    s_scl[4 + tid] = sx;       // [4, 8): part scale
+    s_scl[8 + tid] = 1.0f / sx;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < MAXQ; i++) {
+    const int t = tid + i * NTHREADS;
+    if (t < nq) {
+      const int b = t / nk4, k = 4 * (t - b * nk4);
+      const float inv = s_scl[b], rsx = s_scl[8 + b];
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float xn = a.norm_w ? (v[i][e] * inv) * g[i][e] : v[i][e];
+        float r = fminf(fmaxf(xn * rsx, -127.f), 127.f);
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+          const float q = rintf(r);
+          w[p] |= ((uint32_t)(int)q & 0xffu) << (8 * e);
+          r = (r - q) * 128.f;
+        }
+      }
+      const int c = k >> 5, half = (k >> 4) & 1, tq = (k >> 2) & 3;
+#pragma unroll
+      for (int p = 0; p < 4; p++) {
+        const int col = 4 * b + p, j = col >> 3, gid = col & 7;
+        s_xw[(((c * nch + j) * 32) + gid * 4 + tq) * 2 + half] = w[p];
+      }
+    }
+  }
+}
+
+template <int NCH>
+__device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  const V2Sched s = v2_sched<FMT_INT8>(a, blockIdx.x, gridDim.x);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+  float *s_scl = reinterpret_cast<float *>(smem + SM_R_OFF);
+  float *s_red = s_scl + 64;   // [nt][NWARPS][16][B]
+  uint32_t *s_xw = reinterpret_cast<uint32_t *>(smem + SM_X_OFF);
+  const uint2 *s_xf = reinterpret_cast<const uint2 *>(s_xw);
+
+  ckpt(kc, 11);
+  if (tid == 0) stream(kc, smem, kc.seq, kc.seq + 1);   // this stage's first fills, if not issued yet
+  ckpt(kc, 0);
+  if (s.nt == 0) return;
+  {
+    const int mq = (B * (a.K >> 2) + NTHREADS - 1) / NTHREADS;
+    if (mq <= 1) stage_x_s8<1>(a, B, NCH, s_scl, s_xw, kc, smem);
+    else if (mq <= 2) stage_x_s8<2>(a, B, NCH, s_scl, s_xw, kc, smem);
+    else if (mq <= 4) stage_x_s8<4>(a, B, NCH, s_scl, s_xw, kc, smem);
+    else stage_x_s8<8>(a, B, NCH, s_scl, s_xw, kc, smem);
+  }
+  for (int i = tid; i < s.nt * NWARPS * 16 * B; i += NTHREADS) s_red[i] = 0.f;
+  __syncthreads();
+  ckpt(kc, 2);
+
+  constexpr int CPS = WSLOT_BYTES / 512;
+  const int per_wave = NWSLOT * CPS;
+  const unsigned wf = kc.wfill;
+  // column pair (2 tig, 2 tig + 1) of chunk j = parts (2 (tig & 1), +1) of
+  // batch row 2 j + tig / 2
+  const float wlo = (tig & 1) ? (1.0f / 16384.0f) : 1.0f, whi = (tig & 1) ? (1.0f / 2097152.0f) : (1.0f / 128.0f);
+  for (int w0 = 0; w0 < s.L; w0 += per_wave) {
+    const int wl = min(per_wave, s.L - w0);
+    const int q4 = (wl + 3) >> 2;
+    const int cb = w0 + 4 * ((warp * q4) / NWARPS);
+    const int ce = min(w0 + wl, w0 + 4 * (((warp + 1) * q4) / NWARPS));
+    int acc[4][NCH][4];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int j = 0; j < NCH; j++) acc[u][j][0] = acc[u][j][1] = acc[u][j][2] = acc[u][j][3] = 0;
+    auto flush = [&](int tl) {
+#pragma unroll
+      for (int j = 0; j < NCH; j++) {
+        const int i0 = acc[0][j][0] + acc[1][j][0] + acc[2][j][0] + acc[3][j][0];
+        const int i1 = acc[0][j][1] + acc[1][j][1] + acc[2][j][1] + acc[3][j][1];
+        const int i2 = acc[0][j][2] + acc[1][j][2] + acc[2][j][2] + acc[3][j][2];
+        const int i3 = acc[0][j][3] + acc[1][j][3] + acc[2][j][3] + acc[3][j][3];
+        float r0 = (float)i0 * wlo + (float)i1 * whi;   // row gid
+        float r1 = (float)i2 * wlo + (float)i3 * whi;   // row gid + 8
+        r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+        r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+        const int b = 2 * j + (tig >> 1);
+        if ((tig & 1) == 0 && b < B) {
+          const float sx = s_scl[4 + b];
+          s_red[((tl * NWARPS + warp) * 16 + gid) * B + b] += r0 * sx;
+          s_red[((tl * NWARPS + warp) * 16 + gid + 8) * B + b] += r1 * sx;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) acc[u][j][0] = acc[u][j][1] = acc[u][j][2] = acc[u][j][3] = 0;
+      }
+    };
+    auto load = [&](int ci) -> uint4 {
+      const int f = ci / CPS, o = ci - f * CPS;
+      const char *slot = smem + SM_W_OFF + ((wf + (unsigned)f) % NWSLOT) * WSLOT_BYTES;
+      return *reinterpret_cast<const uint4 *>(slot + o * 512 + lane * 16);
+    };
+    if (cb < ce) {   // the fills this warp reads (after a failed wait the CTA only runs out the stage)
+      for (int f = cb / CPS; f <= (ce - 1) / CPS; f++) {
+        const unsigned ctr = wf + (unsigned)f;
+        if (!kc.local_err && !mbar_wait(kc.wbars + (ctr % NWSLOT), (ctr / NWSLOT) & 1u, WAIT_LIMIT_CYCLES))
+          raise_err(kc, ERR_MBAR_TIMEOUT, f);
+      }
+    }
+    ckpt(kc, 9);
+    int ci = cb;
+    while (ci < ce) {
+      const int tl = ci / s.kc;
+      const int te = min(ce, (tl + 1) * s.kc);
+      const int c0 = s.kb - tl * s.kc;
+      for (; ci + 4 <= te; ci += 4) {
+        uint4 wv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) wv[u] = load(ci + u);
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+          for (int j = 0; j < NCH; j++) {
+            const uint2 bx = s_xf[((c0 + ci + u) * NCH + j) * 32 + lane];
+            mma_s8(acc[u][j], wv[u], bx.x, bx.y);
+          }
+      }
+      for (; ci < te; ci++) {
+        const uint4 wv = load(ci);
+#pragma unroll
+        for (int j = 0; j < NCH; j++) {
+          const uint2 bx = s_xf[((c0 + ci) * NCH + j) * 32 + lane];
+          mma_s8(acc[0][j], wv, bx.x, bx.y);
+        }
+      }
+      flush(tl);
+    }
+    ckpt(kc, 10);
+    __syncthreads();
+    if (tid == 0 && w0 + per_wave < s.L) {   // this wave's slots are free again
+      kc.w_free = kc.wfill + (unsigned)((w0 + per_wave) / CPS);
+      stream(kc, smem, kc.seq, kc.seq + 2);
+    }
+  }
+  if (tid == 0) {
+    kc.wfill += (unsigned)s.nfill;
+    kc.w_free = kc.wfill;
+  }
+  ckpt(kc, 3);
+  float *s_val = s_red + s.nt * NWARPS * 16 * B;
+  for (int idx = tid; idx < s.nt * 16 * B; idx += NTHREADS) {
+    const int b = idx % B, r = (idx / B) % 16, tl2 = idx / (16 * B);
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARPS; w++) v += s_red[((tl2 * NWARPS + w) * 16 + r) * B + b];
+    s_val[idx] = v;
+  }
+  __syncthreads();
+  ckpt(kc, 4);
+  v2_epilogue(a, B, s.t0, s.nt, s_val, B, kc);
+  ckpt(kc, 5);
+}
+
 template <int FMT>
 QTB_DEV void gemv2_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
-  if (FMT == FMT_BF16 && a.parts == 4) {
+  if (FMT == FMT_INT8 && a.parts == 4) {
+    switch (a.nch) {
+      case 1: gemv2_s8_t<1>(a, B, smem, kc); return;
+      case 2: gemv2_s8_t<2>(a, B, smem, kc); return;
+    }
+  } else if (FMT == FMT_BF16 && a.parts == 4) {
     switch (a.nch) {
       case 1: gemv2_stage_t<FMT, 1, 4>(a, B, smem, kc); return;
       case 2: gemv2_stage_t<FMT, 2, 4>(a, B, smem, kc); return;
     }
-  } else if (a.parts == 2 && FMT != FMT_BF16) {
+  } else if (a.parts == 2 && FMT != FMT_BF16 && FMT != FMT_INT8) {
     switch (a.nch) {
       case 1: gemv2_stage_t<FMT, 1, 2>(a, B, smem, kc); return;
     }
