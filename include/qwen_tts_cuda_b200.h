@@ -79,6 +79,22 @@ void  qwen_cuda_cp_batch_free(void *state);
 /* replaces qwen_tts_cuda_talker.cu:657 */
 int   qwen_cuda_batch_selftest(struct qwen_tts_ctx *ctx, int B, int frames);
 
+/* ---- per-op backend (the CUDA entries of the backend vtable,
+ * qwen_tts_backend.h:34-49): host bf16 W [rows][cols], host f32 x [cols] /
+ * X [cols][B] (row-major), y [rows] / Y [rows][B]; B <= 64.  Each weight is
+ * uploaded once and kept resident, cached by its host pointer (as in the
+ * reference); the device is QWEN_CUDA_DEVICE (default 0). */
+/* replaces qwen_tts_cuda.c:67 (decl qwen_tts_cuda.h:23) */
+int   qwen_cuda_available(void);
+/* replaces qwen_tts_cuda.c:73 (decl qwen_tts_cuda.h:24) */
+void *qwen_cuda_init(void);
+/* replaces qwen_tts_cuda.c:84 (decl qwen_tts_cuda.h:25) */
+void  qwen_cuda_free(void *ctx);
+/* replaces qwen_tts_cuda.c:138 (decl qwen_tts_cuda.h:28) */
+void  qwen_cuda_matvec_bf16(void *ctx, float *y, const uint16_t *W, const float *x, int rows, int cols);
+/* replaces qwen_tts_cuda.c:119 (decl qwen_tts_cuda.h:33) */
+void  qwen_cuda_matmat_bf16(void *ctx, float *Y, const uint16_t *W, const float *X, int rows, int cols, int B);
+
 /* ---- additions -------------------------------------------------------------- */
 /* Last failure of any entry point above on this thread: 0 or a QTB_E_* code;
  * qtb_last_error() (qwen3tts_b200.h) has the message. */

@@ -7,6 +7,7 @@
 // decode_kernel in qtb_kernels.cuh.
 #include "qtb_kernels.cuh"
 #include "../../include/qwen3tts_b200.h"
+#include "../../include/qwen_tts_cuda_b200.h"
 
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -1431,4 +1432,163 @@ extern "C" int qtb_attention_noalloc(const float *qkv, int batch, int n_heads, i
   CUDA_TRY(cudaStreamSynchronize(st));
   if (h.err) return set_err(QTB_E_DEVICE, "kernel error %d (info %d)", h.err, h.err_info);
   return 0;
+}
+
+// ------------------------------------------------------------------------
+// The reference's per-op CUDA backend (qwen_tts_cuda.h:23-35, defined in
+// qwen_tts_cuda.c:67-141): y = W x and Y = W X for host bf16 weights and host
+// f32 activations, behind the backend vtable (qwen_tts_backend.h:34-49).
+// Like the reference, each weight is uploaded once and kept resident, cached
+// by its host pointer; here it is stored in the engine's bf16 fragment order
+// (rows padded to 128, columns to 64 with zeros) and the product runs as one
+// GEMV stage of the decode kernel.  X and Y are row-major [cols][B] and
+// [rows][B] as in the reference; B <= 64.
+namespace {
+struct OpWeight {
+  const void *key;
+  int rows, cols;
+  DMat m;
+};
+struct OpCtx {
+  int device = 0, nsm = 0;
+  Arena weights;
+  std::vector<OpWeight> cache;
+  cudaStream_t st = nullptr;
+  float *dx = nullptr, *dy = nullptr, *ws = nullptr;
+  unsigned *sem = nullptr;
+  Ctl *ctl = nullptr;
+  Stage *dstage = nullptr;
+  size_t x_cap = 0, y_cap = 0, ws_cap = 0, sem_cap = 0;
+};
+
+int op_grow(void **p, size_t *cap, size_t need) {
+  if (*cap >= need) return 0;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  cudaError_t e = cudaMalloc(p, need);
+  if (e != cudaSuccess) return set_err(QTB_E_OOM, "cudaMalloc(%zu): %s", need, cudaGetErrorString(e));
+  *cap = need;
+  return 0;
+}
+
+int op_matmat(OpCtx *c, float *Y, const uint16_t *W, const float *X, int rows, int cols, int B) {
+  if (!c || !Y || !W || !X || rows < 1 || cols < 1 || B < 1 || B > 64) return set_err(QTB_E_INVALID, "bad argument");
+  CUDA_TRY(cudaSetDevice(c->device));
+  const int rp = (rows + 127) / 128 * 128, cp = (cols + 63) / 64 * 64;   // upload_matrix granularity
+  const OpWeight *ow = nullptr;
+  for (const OpWeight &o : c->cache)
+    if (o.key == W && o.rows == rows && o.cols == cols) { ow = &o; break; }
+  if (!ow) {
+    std::vector<uint16_t> pad((size_t)rp * cp, 0);
+    for (int r = 0; r < rows; r++) memcpy(pad.data() + (size_t)r * cp, W + (size_t)r * cols, (size_t)cols * 2);
+    qtb_matrix_t hm;
+    memset(&hm, 0, sizeof hm);
+    hm.data = pad.data();
+    const qtb_matrix_t *ms[1] = {&hm};
+    const int re[1] = {rp};
+    OpWeight o;
+    o.key = W; o.rows = rows; o.cols = cols;
+    int rc = upload_matrix(c->weights, FMT_BF16, ms, re, 1, cp, o.m);
+    if (rc) return rc;
+    c->cache.push_back(o);
+    ow = &c->cache.back();
+  }
+  const int T = rp / 16;
+  const bool v2 = v2_ok(FMT_BF16, rp, cp, B, c->nsm);
+  const int S = v2 ? std::max(1, c->nsm / T) : choose_S(T, cp, B, c->nsm * NWARPS, FMT_BF16);
+  if (S < 1) return set_err(QTB_E_UNSUPPORTED, "no k-slicing fits (cols %d, B %d)", cols, B);
+  int rc;
+  if ((rc = op_grow((void **)&c->dx, &c->x_cap, (size_t)B * cp * 4))) return rc;
+  if ((rc = op_grow((void **)&c->dy, &c->y_cap, (size_t)B * rp * 4))) return rc;
+  if ((rc = op_grow((void **)&c->ws, &c->ws_cap, (size_t)T * S * 16 * B * 4))) return rc;
+  if ((rc = op_grow((void **)&c->sem, &c->sem_cap, (size_t)T * 4))) return rc;
+  // X [cols][B] -> [B][cp] (zero-padded columns)
+  std::vector<float> xt((size_t)B * cp, 0.f), yt((size_t)B * rp);
+  for (int k = 0; k < cols; k++)
+    for (int b = 0; b < B; b++) xt[(size_t)b * cp + k] = X[(size_t)k * B + b];
+  CUDA_TRY(cudaMemcpyAsync(c->dx, xt.data(), xt.size() * 4, cudaMemcpyHostToDevice, c->st));
+  CUDA_TRY(cudaMemsetAsync(c->sem, 0, (size_t)T * 4, c->st));
+  CUDA_TRY(cudaMemsetAsync(c->ctl, 0, sizeof(Ctl), c->st));
+  Stage s;
+  memset(&s, 0, sizeof s);
+  s.kind = ST_GEMV;
+  s.B = B;
+  GemvArgs &g = s.g;
+  g.w = ow->m.w; g.fmt = FMT_BF16; g.rows = rp; g.K = cp; g.S = v2 ? 1 : S;
+  g.nch = nch_for(FMT_BF16, B, v2); g.parts = parts_for(FMT_BF16, B, v2); g.v2 = v2 ? 1 : 0;
+  g.x = c->dx; g.ldx = cp; g.y = c->dy; g.ldy = rp; g.epi = EPI_STORE; g.ws = c->ws; g.sem = c->sem;
+  CUDA_TRY(cudaMemcpyAsync(c->dstage, &s, sizeof s, cudaMemcpyHostToDevice, c->st));
+  const Stage *prog = c->dstage;
+  int n_st = 1, n_it = 1;
+  long long *trace = nullptr;
+  Ctl *ctl = c->ctl;
+  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
+  CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(c->nsm), dim3(NTHREADS), args, SMEM_BYTES, c->st));
+  Ctl h;
+  CUDA_TRY(cudaMemcpyAsync(&h, c->ctl, sizeof h, cudaMemcpyDeviceToHost, c->st));
+  CUDA_TRY(cudaMemcpyAsync(yt.data(), c->dy, yt.size() * 4, cudaMemcpyDeviceToHost, c->st));
+  CUDA_TRY(cudaStreamSynchronize(c->st));
+  if (h.err) return set_err(QTB_E_DEVICE, "kernel error %d (info %d)", h.err, h.err_info);
+  for (int r = 0; r < rows; r++)
+    for (int b = 0; b < B; b++) Y[(size_t)r * B + b] = yt[(size_t)b * rp + r];
+  return 0;
+}
+}  // namespace
+
+extern "C" int qwen_cuda_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n < 1) return 0;
+  int dev = 0;
+  if (const char *d = getenv("QWEN_CUDA_DEVICE")) dev = atoi(d);
+  cudaDeviceProp p;
+  if (dev < 0 || dev >= n || cudaGetDeviceProperties(&p, dev) != cudaSuccess) return 0;
+  return p.major == 10 ? 1 : 0;
+}
+
+extern "C" void *qwen_cuda_init(void) {
+  OpCtx *c = new OpCtx();
+  if (const char *d = getenv("QWEN_CUDA_DEVICE")) c->device = atoi(d);
+  int rc = 0;
+  cudaDeviceProp p;
+  if (cudaSetDevice(c->device) != cudaSuccess || cudaGetDeviceProperties(&p, c->device) != cudaSuccess || p.major != 10) {
+    set_err(QTB_E_UNSUPPORTED, "no sm_100 device %d", c->device);
+    rc = 1;
+  } else {
+    c->nsm = p.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
+        c->weights.alloc((void **)&c->ctl, sizeof(Ctl)) || c->weights.alloc((void **)&c->dstage, sizeof(Stage)))
+      rc = 1;
+  }
+  if (rc) {
+    fprintf(stderr, "qwen3tts_b200: qwen_cuda_init failed: %s\n", qtb_last_error());
+    if (c->st) cudaStreamDestroy(c->st);
+    c->weights.release();
+    delete c;
+    return nullptr;
+  }
+  return c;
+}
+
+extern "C" void qwen_cuda_free(void *ctx) {
+  OpCtx *c = static_cast<OpCtx *>(ctx);
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->st) cudaStreamSynchronize(c->st);
+  for (void *p : {(void *)c->dx, (void *)c->dy, (void *)c->ws, (void *)c->sem})
+    if (p) cudaFree(p);
+  if (c->st) cudaStreamDestroy(c->st);
+  c->weights.release();
+  delete c;
+}
+
+extern "C" void qwen_cuda_matmat_bf16(void *ctx, float *Y, const uint16_t *W, const float *X, int rows, int cols, int B) {
+  const int rc = op_matmat(static_cast<OpCtx *>(ctx), Y, W, X, rows, cols, B);
+  qtb_ref_set_error(rc);
+  if (rc) fprintf(stderr, "qwen3tts_b200: qwen_cuda_matmat_bf16 failed (%d): %s\n", rc, qtb_last_error());
+}
+
+extern "C" void qwen_cuda_matvec_bf16(void *ctx, float *y, const uint16_t *W, const float *x, int rows, int cols) {
+  qwen_cuda_matmat_bf16(ctx, y, W, x, rows, cols, 1);
 }

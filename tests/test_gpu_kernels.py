@@ -119,3 +119,37 @@ def test_attention_rejects_bad_page_table(have_gpu):
     pt[0, 1] = 99  # outside the pool: refused on the host before launch
     with pytest.raises(RuntimeError, match="page table"):
         Q.attention(qkv, 16, 8, qn, kn, 1e-6, cs, sn, kp, vp, pt, np.array([40], np.int32), 4)
+
+
+def test_backend_vtable_matmat_bf16(have_gpu):
+    """The reference's per-op backend entries (qwen_cuda_init / _matmat_bf16 /
+    _matvec_bf16 / _free): row-major X [cols][B], Y [rows][B], shapes that are
+    not multiples of the tile sizes, and a second call that hits the resident
+    weight cache."""
+    import ctypes as C
+    L = Q.lib()
+    L.qwen_cuda_init.restype = C.c_void_p
+    L.qwen_cuda_free.argtypes = [C.c_void_p]
+    L.qwen_cuda_matmat_bf16.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]
+    L.qwen_cuda_matvec_bf16.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+    assert L.qwen_cuda_available() == 1
+    ctx = L.qwen_cuda_init()
+    assert ctx
+    rng = np.random.default_rng(31)
+    try:
+        for rows, cols, B in [(100, 200, 1), (256, 1024, 3), (72, 640, 64)]:
+            W = Q.bf16_from_f32(rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
+            Wf = O.f32_from_bf16(W).astype(np.float64)
+            for call in range(2):
+                X = rng.standard_normal((cols, B), dtype=np.float32)
+                Y = np.full((rows, B), np.nan, np.float32)
+                L.qwen_cuda_matmat_bf16(ctx, Y.ctypes.data, W.ctypes.data, X.ctypes.data, rows, cols, B)
+                assert L.qwen_cuda_last_error() == 0
+                assert rel_l2(Y, Wf @ X.astype(np.float64)) < GEMV_TOL, (rows, cols, B, call)
+        x = rng.standard_normal(200, dtype=np.float32)
+        W = Q.bf16_from_f32(rng.standard_normal((100, 200), dtype=np.float32) * np.float32(0.02))
+        y = np.empty(100, np.float32)
+        L.qwen_cuda_matvec_bf16(ctx, y.ctypes.data, W.ctypes.data, x.ctypes.data, 100, 200)
+        assert rel_l2(y, O.f32_from_bf16(W).astype(np.float64) @ x) < GEMV_TOL
+    finally:
+        L.qwen_cuda_free(ctx)
