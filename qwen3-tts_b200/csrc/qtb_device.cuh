@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #define QTB_DEV __device__ __forceinline__
+#define QTB_HOST_DEV __host__ __device__ __forceinline__
 
 namespace qtb {
 

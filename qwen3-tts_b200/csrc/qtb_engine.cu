@@ -526,6 +526,7 @@ struct qtb_session {
   unsigned *att_sem = nullptr;
   Ctl *ctl = nullptr;
   Stage *prog[PROG_N] = {};
+  V2Plan *plan[PROG_N] = {};   // [stage][CTA] shares of the small-batch GEMV stages
   int prog_n[PROG_N] = {};
   int has_pad = 0;
   long long *trace = nullptr;   // per-stage clock64 trace (CTA 0), profiling only
@@ -726,13 +727,26 @@ static void build_cp_frame(ProgBuilder &pb, qtb_session *s, const float *talker_
   }
 }
 
+// Each CTA's share of every small-batch GEMV stage of a program ([stage][G]).
+static void make_plans(const std::vector<Stage> &st, int G, std::vector<V2Plan> &out) {
+  out.assign(st.size() * (size_t)G, V2Plan{0, 0, 0, 0});
+  for (size_t i = 0; i < st.size(); i++)
+    if (st[i].kind == ST_GEMV && st[i].g.v2)
+      for (int c = 0; c < G; c++) out[i * G + c] = v2_plan(st[i].g.fmt, st[i].g.rows, st[i].g.K, c, G);
+}
+
 static int upload_prog(qtb_session *s, int which, ProgBuilder &pb) {
   if (pb.err) return pb.err;
   if (pb.st.empty()) return 0;
   Stage *d;
   int rc = s->ar.upload(&d, pb.st.data(), pb.st.size() * sizeof(Stage));
   if (rc) return rc;
+  std::vector<V2Plan> pl;
+  make_plans(pb.st, s->e->n_sm, pl);
+  V2Plan *dp;
+  if ((rc = s->ar.upload(&dp, pl.data(), pl.size() * sizeof(V2Plan)))) return rc;
   s->prog[which] = d;
+  s->plan[which] = dp;
   s->prog_n[which] = (int)pb.st.size();
   return 0;
 }
@@ -975,10 +989,11 @@ static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
     return set_err(QTB_E_INVALID, "too many iterations for one launch");
   CUDA_TRY(cudaMemsetAsync(&s->ctl->bar_count, 0, sizeof(unsigned), s->stream));
   const Stage *prog = s->prog[which];
+  const V2Plan *plan = s->plan[which];
   int n_st = s->prog_n[which];
   Ctl *ctl = s->ctl;
   long long *trace = s->trace_on ? s->trace : nullptr;
-  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_iters, (void *)&ctl, (void *)&trace};
+  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_iters, (void *)&ctl, (void *)&trace};
   if (timed) CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(s->e->n_sm), dim3(NTHREADS), args,
                                        SMEM_BYTES, s->stream));
@@ -1178,10 +1193,15 @@ static int run_single_stage(MiniRun &mr, const Stage &S) {
   CUDA_TRY(cudaGetDevice(&dev));
   CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
   CUDA_TRY(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  std::vector<V2Plan> pl;
+  make_plans(std::vector<Stage>{S}, nsm, pl);
+  V2Plan *dplan;
+  if ((rc = mr.ar.upload(&dplan, pl.data(), pl.size() * sizeof(V2Plan)))) return rc;
   const Stage *prog = dp;
+  const V2Plan *plan = dplan;
   int n_st = 1, n_it = 1;
   long long *trace = nullptr;
-  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
+  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(nsm), dim3(NTHREADS), args, SMEM_BYTES, mr.st));
   CUDA_TRY(cudaStreamSynchronize(mr.st));
   Ctl h;
@@ -1425,7 +1445,8 @@ extern "C" int qtb_attention_noalloc(const float *qkv, int batch, int n_heads, i
   const Stage *prog = dstage;
   int n_st = 1, n_it = 1;
   long long *trace = nullptr;
-  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
+  const V2Plan *plan = nullptr;   // an attention stage reads no GEMV plan
+  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(nsm), dim3(NTHREADS), args, SMEM_BYTES, st));
   Ctl h;
   CUDA_TRY(cudaMemcpyAsync(&h, ctl, sizeof h, cudaMemcpyDeviceToHost, st));
@@ -1458,6 +1479,7 @@ struct OpCtx {
   unsigned *sem = nullptr;
   Ctl *ctl = nullptr;
   Stage *dstage = nullptr;
+  V2Plan *dplan = nullptr;
   size_t x_cap = 0, y_cap = 0, ws_cap = 0, sem_cap = 0;
 };
 
@@ -1519,11 +1541,15 @@ int op_matmat(OpCtx *c, float *Y, const uint16_t *W, const float *X, int rows, i
   g.nch = nch_for(FMT_BF16, B, v2); g.parts = parts_for(FMT_BF16, B, v2); g.v2 = v2 ? 1 : 0;
   g.x = c->dx; g.ldx = cp; g.y = c->dy; g.ldy = rp; g.epi = EPI_STORE; g.ws = c->ws; g.sem = c->sem;
   CUDA_TRY(cudaMemcpyAsync(c->dstage, &s, sizeof s, cudaMemcpyHostToDevice, c->st));
+  std::vector<V2Plan> pl;
+  make_plans(std::vector<Stage>{s}, c->nsm, pl);
+  CUDA_TRY(cudaMemcpyAsync(c->dplan, pl.data(), pl.size() * sizeof(V2Plan), cudaMemcpyHostToDevice, c->st));
   const Stage *prog = c->dstage;
+  const V2Plan *plan = c->dplan;
   int n_st = 1, n_it = 1;
   long long *trace = nullptr;
   Ctl *ctl = c->ctl;
-  void *args[] = {(void *)&prog, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
+  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(c->nsm), dim3(NTHREADS), args, SMEM_BYTES, c->st));
   Ctl h;
   CUDA_TRY(cudaMemcpyAsync(&h, c->ctl, sizeof h, cudaMemcpyDeviceToHost, c->st));
@@ -1558,7 +1584,8 @@ extern "C" void *qwen_cuda_init(void) {
     c->nsm = p.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess ||
         cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
-        c->weights.alloc((void **)&c->ctl, sizeof(Ctl)) || c->weights.alloc((void **)&c->dstage, sizeof(Stage)))
+        c->weights.alloc((void **)&c->ctl, sizeof(Ctl)) || c->weights.alloc((void **)&c->dstage, sizeof(Stage)) ||
+        c->weights.alloc((void **)&c->dplan, (size_t)c->nsm * sizeof(V2Plan)))
       rc = 1;
   }
   if (rc) {

@@ -146,6 +146,8 @@ struct Ctl {
 // Per-CTA kernel state, one copy in shared memory.  Fields are written by
 // thread 0 only (at points separated from other threads' reads by a CTA
 // barrier), except `local_err`, which any thread may set to 1.
+struct V2Plan;
+
 struct KCtx {
   unsigned epoch;
   unsigned page_ctr;    // K/V page buffers consumed so far (mbarrier phase source)
@@ -166,6 +168,7 @@ struct KCtx {
   unsigned n_total;     // stages in this launch
   int n_stages;
   Stage *dring;         // NDESC descriptor slots in shared memory
+  V2Plan *pring;        // this CTA's plan entry for each descriptor slot
   uint64_t *dbars;      // their mbarriers
   unsigned w_issued;    // weight-ring fills issued so far
   unsigned w_free;      // fills whose slots have been read by every warp
@@ -304,9 +307,6 @@ __device__ __noinline__ void stage_x_fused(const GemvArgs &a, int B, int ent, fl
       }
     }
   }
-  // while the activation is in flight: the next stage's weights (issued
-  // after the loads above, so they queue behind them)
-  if (tid == 0) stream(kc, smem, kc.seq, kc.seq + 2);
   if (a.norm_w) {
     __shared__ float s_ss[NWARPS][4];
 #pragma unroll
@@ -332,7 +332,7 @@ __device__ __noinline__ void stage_x_fused(const GemvArgs &a, int B, int ent, fl
       float tot = 0.f;
 #pragma unroll
       for (int w = 0; w < NWARPS; w++) tot += s_ss[w][tid];
-      s_inv[tid] = 1.0f / sqrtf(tot / (float)K + a.eps);
+      s_inv[tid] = rsqrtf(tot * __frcp_rn((float)K) + a.eps);   // within 2 ulp of 1 / sqrtf
     }
     __syncthreads();
   }
@@ -764,32 +764,55 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
 struct V2Sched {
   int t0, nt;   // first tile and tile count of this CTA
   int kb, kc;   // first chunk and chunk count within each tile
-  int scta, p;  // CTAs per tile and this CTA's piece
   int L;        // chunks = nt * kc
   int cps;      // chunks per ring slot
   int nfill;    // slot fills = ceil(L / cps)
 };
 
+// A CTA's share of a small-batch GEMV stage, computed on the host for every
+// (stage, CTA) and bulk-copied with the stage descriptor, so the kernel does
+// no integer division to find it: whole 16-row tiles t0 .. t0+nt-1 (when
+// there are fewer tiles than CTAs the rest idle -- the weights are streamed
+// ahead, so a CTA holding two tiles' worth costs less than a cross-CTA
+// reduction would), L chunks of 512 bytes in nfill ring fills.
+struct __align__(16) V2Plan {
+  int t0, nt, L, nfill;
+};
+static_assert(sizeof(V2Plan) == 16, "plans are bulk-copied");
+
 template <int FMT>
-QTB_DEV V2Sched v2_sched(const GemvArgs &a, int cta, int G) {
+QTB_HOST_DEV constexpr int v2_cps() { return WSLOT_BYTES / (512 + 8 * FmtTraits<FMT>::GSZ); }
+
+QTB_HOST_DEV V2Plan v2_plan(int fmt, int rows, int K, int cta, int G) {
+  const int gsz = fmt == FMT_Q4_0 ? 8 : (fmt == FMT_INT4G ? 16 : 0);
+  const int ck = fmt == FMT_BF16 ? 1 : (fmt == FMT_INT8 ? 2 : 4);
+  const int T = rows >> 4, nck = K / (16 * ck), cps = WSLOT_BYTES / (512 + 8 * gsz);
+  V2Plan p;
+  p.t0 = (int)((long long)cta * T / G);
+  p.nt = (int)((long long)(cta + 1) * T / G) - p.t0;
+  p.L = p.nt * nck;
+  p.nfill = (p.L + cps - 1) / cps;
+  return p;
+}
+
+template <int FMT>
+QTB_DEV V2Sched v2_sched(const GemvArgs &a, const V2Plan &p) {
   using Tr = FmtTraits<FMT>;
   V2Sched s;
-  const int T = a.rows >> 4;
-  const int nck = a.K / (16 * Tr::CK);
-  s.cps = WSLOT_BYTES / (512 + 8 * Tr::GSZ);
-  // Whole tiles per CTA (when there are fewer tiles than CTAs the rest idle:
-  // the weights are streamed before the barrier, so a CTA holding two tiles'
-  // worth costs less than a cross-CTA reduction would).
-  s.t0 = cta * T / G;
-  s.nt = (cta + 1) * T / G - s.t0;
-  s.kb = 0; s.kc = nck; s.scta = 1; s.p = 0;
-  s.L = s.nt * s.kc;
-  s.nfill = (s.L + s.cps - 1) / s.cps;
+  s.cps = v2_cps<FMT>();
+  s.t0 = p.t0;
+  s.nt = p.nt;
+  s.kb = 0;
+  s.kc = a.K / (16 * Tr::CK);
+  s.L = p.L;
+  s.nfill = p.nfill;
   return s;
 }
 
-// Thread 0: bulk-copy slot fills [f0, f1) of this CTA's range into the ring;
-// fill f0 is the launch's fill number ctr0 (slot ctr0 % NWSLOT).
+// One warp: bulk-copy slot fills [f0, f1) (at most NWSLOT) of this CTA's range
+// into the ring, lane i issuing fill f0 + i (the copies are issued in
+// parallel: one bulk copy costs a thread ~250 cycles to issue); fill f0 is the
+// launch's fill number ctr0 (slot ctr0 % NWSLOT).
 template <int FMT>
 QTB_DEV void v2_issue(const GemvArgs &a, const V2Sched &s, int f0, int f1, unsigned ctr0, const KCtx &kc,
                       char *smem) {
@@ -797,7 +820,9 @@ QTB_DEV void v2_issue(const GemvArgs &a, const V2Sched &s, int f0, int f1, unsig
   const int nck = a.K / (16 * Tr::CK);
   const size_t cbase = (size_t)s.t0 * nck + s.kb;
   const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
-  for (int f = f0; f < f1; f++) {
+  const int f = f0 + (int)(threadIdx.x & 31);
+  if (f < f1) {
+    fence_proxy_async_smem();   // the slot was last read through the generic proxy
     const unsigned ctr = ctr0 + (unsigned)(f - f0);
     const int slot = (int)(ctr % NWSLOT);
     const int c0 = f * s.cps, n = min(s.cps, s.L - c0);
@@ -810,51 +835,62 @@ QTB_DEV void v2_issue(const GemvArgs &a, const V2Sched &s, int f0, int f1, unsig
   }
 }
 
-// Streamer step for one small-batch GEMV stage: issue as many of this CTA's
-// remaining fills as the ring has free slots.  True once all are issued.  The
-// first visit also asks L2 for the stage's small operands (RMSNorm gains, the
-// CTA's row scales and bias), so the activation staging and the epilogue hit
-// L2 instead of HBM.
+// Streamer step for one small-batch GEMV stage (one warp): issue as many of
+// this CTA's remaining fills as the ring has free slots.  True once all are
+// issued.
 template <int FMT>
-QTB_DEV bool stream_gemv(const GemvArgs &a, KCtx &kc, char *smem) {
-  const V2Sched s = v2_sched<FMT>(a, blockIdx.x, gridDim.x);
+QTB_DEV bool stream_gemv(const GemvArgs &a, const V2Plan &p, KCtx &kc, char *smem) {
+  const V2Sched s = v2_sched<FMT>(a, p);
   if (s.nfill == 0) return true;
-  if (kc.pf_f == 0) {
-    if (a.norm_w) prefetch_l2(a.norm_w, (uint32_t)a.K * 4u);
-    if (a.row_scale) prefetch_l2(a.row_scale + 16 * s.t0, (uint32_t)s.nt * 64u);
-    if (a.bias) prefetch_l2(a.bias + 16 * s.t0, (uint32_t)s.nt * 64u);
-  }
+  const int pf_f = kc.pf_f;
   const int room = NWSLOT - (int)(kc.w_issued - kc.w_free);
-  const int n = min(s.nfill - kc.pf_f, room);
-  if (n > 0) {
-    v2_issue<FMT>(a, s, kc.pf_f, kc.pf_f + n, kc.w_issued, kc, smem);
-    kc.pf_f += n;
+  const int n = min(s.nfill - pf_f, room);
+  if (n > 0) v2_issue<FMT>(a, s, pf_f, pf_f + n, kc.w_issued, kc, smem);
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0 && n > 0) {
+    kc.pf_f = pf_f + n;
     kc.w_issued += (unsigned)n;
   }
-  return kc.pf_f >= s.nfill;
+  __syncwarp();
+  return pf_f + max(n, 0) >= s.nfill;
 }
 
-// Thread 0: the weight streamer.  Walks the stage program ahead of the stage
-// being computed and bulk-copies the weights of coming small-batch GEMV stages
-// into the ring as slots free up.  Fills are issued and consumed in program
-// order, so the launch's n-th fill always lands in slot n % NWSLOT.  `done` =
-// stages this CTA has completed; stages before `limit` are looked at.  The
-// streamer stops at a descriptor that has not landed, at a large-batch GEMV
-// stage that has not run yet (that path uses the ring region for its
-// activation), and STREAM_AHEAD stages past `done`.  Callers look one stage
-// ahead only once the current stage's activation has landed, so the bulk
-// traffic never queues in front of an activation load on the critical path.
+// Ask L2 for a coming GEMV stage's small operands (RMSNorm gains, this CTA's
+// row scales and bias), so its activation staging and epilogue hit L2.
+QTB_DEV void prefetch_gemv_operands(const GemvArgs &a, const V2Plan &p) {
+  if (p.nt == 0) return;
+  if (a.norm_w) prefetch_l2(a.norm_w, (uint32_t)a.K * 4u);
+  if (a.row_scale) prefetch_l2(a.row_scale + 16 * p.t0, (uint32_t)p.nt * 64u);
+  if (a.bias) prefetch_l2(a.bias + 16 * p.t0, (uint32_t)p.nt * 64u);
+}
+
+// The weight streamer, run by all 32 lanes of one warp.  Walks the stage
+// program ahead of the stage being computed and bulk-copies the weights of
+// coming small-batch GEMV stages into the ring as slots free up.  Fills are
+// issued and consumed in program order, so the launch's n-th fill always lands
+// in slot n % NWSLOT.  `done` = stages this CTA has completed; stages before
+// `limit` are looked at.  The streamer stops at a descriptor that has not
+// landed, at a large-batch GEMV stage that has not run yet (that path uses the
+// ring region for its activation), and STREAM_AHEAD stages past `done`.
+// Callers look one stage ahead only once the current stage's activation loads
+// are in flight, so the bulk traffic queues behind them.  Only lane 0 writes
+// the streamer state; __syncwarp orders it for the other lanes.
 QTB_CALL void stream(KCtx &kc, char *smem, unsigned done, unsigned limit) {
+  const int lane = threadIdx.x & 31;
   // A completed stage has no fills left to issue (each GEMV stage issues its
   // own before reading them), and its descriptor slot may already hold a later
   // stage: never look behind `done`.
   if (kc.pf_seq < done) {
-    kc.pf_seq = done;
-    kc.pf_f = 0;
+    __syncwarp();
+    if (lane == 0) {
+      kc.pf_seq = done;
+      kc.pf_f = 0;
+    }
+    __syncwarp();
   }
-  bool fenced = false;
-  while (kc.pf_seq < kc.n_total && kc.pf_seq < limit && kc.pf_seq < done + STREAM_AHEAD) {
+  while (true) {
     const unsigned k = kc.pf_seq;
+    if (!(k < kc.n_total && k < limit && k < done + STREAM_AHEAD)) break;
     const int slot = (int)(k % NDESC);
     if (!mbar_test(kc.dbars + slot, (k / NDESC) & 1u)) break;
     const Stage *st = kc.dring + slot;
@@ -863,25 +899,23 @@ QTB_CALL void stream(KCtx &kc, char *smem, unsigned done, unsigned limit) {
       if (!a.v2) {
         if (k >= done) break;
       } else {
-        if (!fenced) {   // the slots were last read through the generic proxy
-          fence_proxy_async_smem();
-          fenced = true;
-        }
+        const V2Plan &pl = kc.pring[slot];
         bool all = true;
         switch (a.fmt) {
-          case FMT_BF16: all = stream_gemv<FMT_BF16>(a, kc, smem); break;
-          case FMT_INT8: all = stream_gemv<FMT_INT8>(a, kc, smem); break;
-          case FMT_Q4_0: all = stream_gemv<FMT_Q4_0>(a, kc, smem); break;
-          case FMT_INT4G: all = stream_gemv<FMT_INT4G>(a, kc, smem); break;
+          case FMT_BF16: all = stream_gemv<FMT_BF16>(a, pl, kc, smem); break;
+          case FMT_INT8: all = stream_gemv<FMT_INT8>(a, pl, kc, smem); break;
+          case FMT_Q4_0: all = stream_gemv<FMT_Q4_0>(a, pl, kc, smem); break;
+          case FMT_INT4G: all = stream_gemv<FMT_INT4G>(a, pl, kc, smem); break;
         }
         if (!all) break;
       }
-    } else if (st->kind == ST_ATTN && k > done) {
-      if (st->a.q_norm) prefetch_l2(st->a.q_norm, HD * 4);
-      if (st->a.k_norm) prefetch_l2(st->a.k_norm, HD * 4);
     }
-    kc.pf_seq++;
-    kc.pf_f = 0;
+    __syncwarp();
+    if (lane == 0) {
+      kc.pf_seq = k + 1;
+      kc.pf_f = 0;
+    }
+    __syncwarp();
   }
 }
 
@@ -920,7 +954,7 @@ QTB_CALL void v2_epilogue(const GemvArgs &a, int B, int t0, int nt, const float 
       const int b = idx % B, pr = (idx / B) % 8, tl = idx / (8 * B);
       const float g = val(tl, 2 * pr, b), u = val(tl, 2 * pr + 1, b);
       const int row = 16 * (t0 + tl) + 2 * pr;
-      __stcg(a.y + (size_t)b * a.ldy + (row >> 1), g / (1.0f + expf(-g)) * u);
+      __stcg(a.y + (size_t)b * a.ldy + (row >> 1), __fdividef(g, 1.0f + expf(-g)) * u);
     }
   } else {  // EPI_ARGMAX
     __shared__ int s_last;
@@ -983,7 +1017,7 @@ __device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem,
   using Tr = FmtTraits<FMT>;
   constexpr bool F16 = (FMT != FMT_BF16);
   constexpr bool XSUM = (FMT == FMT_Q4_0 || FMT == FMT_INT4G);
-  const V2Sched s = v2_sched<FMT>(a, blockIdx.x, gridDim.x);
+  const V2Sched s = v2_sched<FMT>(a, kc.pring[kc.seq % NDESC]);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
   const int ent = 4 * min(8, P * B);
   const int xsum_n = a.K >> 5;
@@ -995,7 +1029,7 @@ __device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem,
 
   // this stage's first fills, unless the streamer issued them already
   ckpt(kc, 11);
-  if (tid == 0) stream(kc, smem, kc.seq, kc.seq + 1);
+  if (warp == 0 && kc.pf_seq <= kc.seq) stream(kc, smem, kc.seq, kc.seq + 1);
   ckpt(kc, 0);
   if (s.nt == 0) return;
 
@@ -1092,8 +1126,9 @@ __device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem,
     ckpt(kc, 10);   // warp 0 done with its chunks
     ckpt_w(kc, 24);
     __syncthreads();
-    if (tid == 0 && w0 + per_wave < s.L) {   // this wave's slots are free again
-      kc.w_free = kc.wfill + (unsigned)((w0 + per_wave) / CPS);
+    if (w0 + per_wave < s.L && warp == 0) {   // this wave's slots are free again
+      if (lane == 0) kc.w_free = kc.wfill + (unsigned)((w0 + per_wave) / CPS);
+      __syncwarp();
       stream(kc, smem, kc.seq, kc.seq + 2);
     }
   }
@@ -1122,15 +1157,16 @@ __device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem,
 //
 // The activation (after the fused RMSNorm) is carried as four signed 8-bit
 // parts per value, x = sx * (a0 + a1 / 2^7 + a2 / 2^14 + a3 / 2^21), sx =
-// max|x| / 127 per batch row (a0 = rint(x / sx), then each part the rounded
-// remainder times 2^7), which represents x to ~2^-29 of max|x|.  The int8
+// max|x| / 127 per batch row (the fixed-point value rint(x / sx * 2^21) split
+// into a leading part and three balanced base-128 digits), which represents x
+// to ~2^-29 of max|x|.  The int8
 // weights then feed the integer MMA (m16n8k32, s8 x s8 -> s32, exact) as they
 // are stored: no per-weight conversion instructions at all.  The parts of batch
 // row b are MMA columns 4b .. 4b+3; per k32 chunk c and column chunk j the
 // staged activation holds one (b0, b1) register pair per lane.
 template <int MAXQ>
-__device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float *s_scl, uint32_t *s_xw, KCtx &kc,
-                                        char *smem) {
+__device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float *s_scl, uint32_t *s_xw,
+                                        float *s_zero, int n_zero, KCtx &kc) {
   const int K = a.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nk4 = K >> 2;
   const int nq = B * nk4;
@@ -1151,8 +1187,6 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float
       }
     }
   }
-  // while the activation is in flight: the next stage's weights
-  if (tid == 0) stream(kc, smem, kc.seq, kc.seq + 2);
   __shared__ float s_red2[NWARPS][8];
 #pragma unroll
   for (int i = 0; i < MAXQ; i++) {
@@ -1178,35 +1212,52 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float
       if (lane == 0) { s_red2[warp][bb] = w; s_red2[warp][4 + bb] = m; }
     }
   }
+  for (int i = tid; i < n_zero; i += NTHREADS) s_zero[i] = 0.f;   // the caller's partial sums
   __syncthreads();
-  if (tid < B) {
-    float tot = 0.f, m = 0.f;
+  // every thread derives the scales itself (broadcast reads): no second barrier
+  float inv[4], rsx[4];
 #pragma unroll
-    for (int w = 0; w < NWARPS; w++) { tot += s_red2[w][tid]; m = fmaxf(m, s_red2[w][4 + tid]); }
-    const float inv = a.norm_w ? 1.0f / sqrtf(tot / (float)K + a.eps) : 1.0f;
-    const float sx = fmaxf(m * inv, 1e-30f) * (1.0f / 127.0f);
-    s_scl[tid] = inv;          // [0, 4): 1/rms (1 without a norm)
-    s_scl[4 + tid] = sx;       // [4, 8): part scale
-    s_scl[8 + tid] = 1.0f / sx;
+  for (int bb = 0; bb < 4; bb++) {
+    inv[bb] = 1.f; rsx[bb] = 1.f;
+    if (bb < B) {
+      float tot = 0.f, m = 0.f;
+#pragma unroll
+      for (int w = 0; w < NWARPS; w++) { tot += s_red2[w][bb]; m = fmaxf(m, s_red2[w][4 + bb]); }
+      // (hardware reciprocal square root: within 2 ulp of the reference's
+      // 1 / sqrtf, far inside the path's tolerance, and off the IEEE slow path)
+      inv[bb] = a.norm_w ? rsqrtf(tot * __frcp_rn((float)K) + a.eps) : 1.0f;
+      const float sx = fmaxf(m * inv[bb], 1e-30f) * (1.0f / 127.0f);
+      rsx[bb] = __frcp_rn(sx);
+      if (tid == 0) s_scl[4 + bb] = sx;   // part scale, read after the caller's barrier
+    }
   }
-  __syncthreads();
 #pragma unroll
   for (int i = 0; i < MAXQ; i++) {
     const int t = tid + i * NTHREADS;
     if (t < nq) {
       const int b = t / nk4, k = 4 * (t - b * nk4);
-      const float inv = s_scl[b], rsx = s_scl[8 + b];
+      float iv = inv[0], rs = rsx[0];
+#pragma unroll
+      for (int bb = 1; bb < 4; bb++)
+        if (b == bb) { iv = inv[bb]; rs = rsx[bb]; }
       uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        const float xn = a.norm_w ? (v[i][e] * inv) * g[i][e] : v[i][e];
-        float r = fminf(fmaxf(xn * rsx, -127.f), 127.f);
-#pragma unroll
-        for (int p = 0; p < 4; p++) {
-          const float q = rintf(r);
-          w[p] |= ((uint32_t)(int)q & 0xffu) << (8 * e);
-          r = (r - q) * 128.f;
-        }
+        const float xn = a.norm_w ? (v[i][e] * iv) * g[i][e] : v[i][e];
+        const float r = fminf(fmaxf(xn * rs, -127.f), 127.f);
+        // fixed point I = r * 2^21, then balanced base-128 digits:
+        // I = a0 2^21 + d1 2^14 + d2 2^7 + d3, |d| <= 64, |a0| <= 127
+        int I = __float2int_rn(r * 2097152.f);
+        const int d3 = ((I + 64) & 127) - 64;
+        I = (I - d3) >> 7;
+        const int d2 = ((I + 64) & 127) - 64;
+        I = (I - d2) >> 7;
+        const int d1 = ((I + 64) & 127) - 64;
+        const int a0 = (I - d1) >> 7;
+        w[0] |= ((uint32_t)a0 & 0xffu) << (8 * e);
+        w[1] |= ((uint32_t)d1 & 0xffu) << (8 * e);
+        w[2] |= ((uint32_t)d2 & 0xffu) << (8 * e);
+        w[3] |= ((uint32_t)d3 & 0xffu) << (8 * e);
       }
       const int c = k >> 5, half = (k >> 4) & 1, tq = (k >> 2) & 3;
 #pragma unroll
@@ -1220,7 +1271,7 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float
 
 template <int NCH>
 __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
-  const V2Sched s = v2_sched<FMT_INT8>(a, blockIdx.x, gridDim.x);
+  const V2Sched s = v2_sched<FMT_INT8>(a, kc.pring[kc.seq % NDESC]);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
   float *s_scl = reinterpret_cast<float *>(smem + SM_R_OFF);
   float *s_red = s_scl + 64;   // [nt][NWARPS][16][B]
@@ -1228,17 +1279,17 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
   const uint2 *s_xf = reinterpret_cast<const uint2 *>(s_xw);
 
   ckpt(kc, 11);
-  if (tid == 0) stream(kc, smem, kc.seq, kc.seq + 1);   // this stage's first fills, if not issued yet
+  if (warp == 0 && kc.pf_seq <= kc.seq) stream(kc, smem, kc.seq, kc.seq + 1);   // this stage's first fills, if not issued yet
   ckpt(kc, 0);
   if (s.nt == 0) return;
   {
     const int mq = (B * (a.K >> 2) + NTHREADS - 1) / NTHREADS;
-    if (mq <= 1) stage_x_s8<1>(a, B, NCH, s_scl, s_xw, kc, smem);
-    else if (mq <= 2) stage_x_s8<2>(a, B, NCH, s_scl, s_xw, kc, smem);
-    else if (mq <= 4) stage_x_s8<4>(a, B, NCH, s_scl, s_xw, kc, smem);
-    else stage_x_s8<8>(a, B, NCH, s_scl, s_xw, kc, smem);
+    const int nz = s.nt * NWARPS * 16 * B;
+    if (mq <= 1) stage_x_s8<1>(a, B, NCH, s_scl, s_xw, s_red, nz, kc);
+    else if (mq <= 2) stage_x_s8<2>(a, B, NCH, s_scl, s_xw, s_red, nz, kc);
+    else if (mq <= 4) stage_x_s8<4>(a, B, NCH, s_scl, s_xw, s_red, nz, kc);
+    else stage_x_s8<8>(a, B, NCH, s_scl, s_xw, s_red, nz, kc);
   }
-  for (int i = tid; i < s.nt * NWARPS * 16 * B; i += NTHREADS) s_red[i] = 0.f;
   __syncthreads();
   ckpt(kc, 2);
 
@@ -1321,8 +1372,9 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
     }
     ckpt(kc, 10);
     __syncthreads();
-    if (tid == 0 && w0 + per_wave < s.L) {   // this wave's slots are free again
-      kc.w_free = kc.wfill + (unsigned)((w0 + per_wave) / CPS);
+    if (w0 + per_wave < s.L && warp == 0) {   // this wave's slots are free again
+      if (lane == 0) kc.w_free = kc.wfill + (unsigned)((w0 + per_wave) / CPS);
+      __syncwarp();
       stream(kc, smem, kc.seq, kc.seq + 2);
     }
   }
@@ -1535,8 +1587,6 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
           rs[i] = __ldg(a.rope_sin + (size_t)pos * (HD / 2) + lane + 32 * i);
         }
       }
-      // while the rows are in flight: the next stage's weights
-      if (threadIdx.x == 0) stream(kc, smem - SM_X_OFF, kc.seq, kc.seq + 2);
       if (nw) {
         float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
         ss = warp_sum(ss);
@@ -1781,40 +1831,58 @@ __device__ __noinline__ void norm_stage(const NormArgs &n, int B) {
 // the stage counters.
 QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
   __shared__ int s_ok;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {   // warp 0: lane 0 polls, the warp runs the hook
+    const int lane = threadIdx.x;
+    __syncwarp();            // kc.last, written by lane 0 in grid_arrive
     int ok = kc.local_err ? 0 : 1;   // a CTA that raised an error leaves after arriving
     if (ok && !kc.last) {
       const unsigned target = (kc.epoch + 1u) * gridDim.x;
       const unsigned nxt = kc.seq + 1;
-      int phase = (nxt < kc.n_total) ? 0 : 2;
+      int phase = (nxt < kc.n_total) ? 0 : 3;
       const long long t0 = clock64();
       unsigned spins = 0;
       while (true) {
-        const uint2 w = ld_acquire_gpu_v2(&kc.ctl->bar_count);   // {count, err}
+        uint2 w = make_uint2(0u, 0u);
+        if (lane == 0) w = ld_acquire_gpu_v2(&kc.ctl->bar_count);   // {count, err}
+        w.x = __shfl_sync(0xffffffffu, w.x, 0);
+        w.y = __shfl_sync(0xffffffffu, w.y, 0);
         if (w.y != 0u) { ok = 0; break; }
         if ((int)(w.x - target) >= 0) break;
+        const int slot = (int)(nxt % NDESC);
         if (phase == 0) {
-          const int slot = (int)(nxt % NDESC);
-          if (mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u)) {
+          if (lane == 0 && mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u)) {
             const Stage *nx = kc.dring + slot;
             if (nx->kind == ST_ATTN) kc.att_pre = attn_prefetch(nx->a, nx->B, kc, smem + SM_X_OFF);
           }
+          __syncwarp();
           phase = 1;
         } else if (phase == 1) {
-          stream(kc, smem, nxt, nxt + 1);
+          // this stage's and the next one's weights: two stages of lead time
+          stream(kc, smem, nxt, nxt + 2);
           phase = 2;
+        } else if (phase == 2) {
+          // the coming GEMV stage's small operands into L2
+          if (lane == 0 && mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u)) {
+            const Stage *nx = kc.dring + slot;
+            if (nx->kind == ST_GEMV && nx->g.v2) prefetch_gemv_operands(nx->g, kc.pring[slot]);
+          }
+          __syncwarp();
+          phase = 3;
         }
-        if ((++spins & 31u) == 0 && clock64() - t0 > WAIT_LIMIT_CYCLES) {
-          raise_err(kc, ERR_BARRIER_TIMEOUT, (int)kc.epoch);
+        const int late = __shfl_sync(0xffffffffu, (++spins & 31u) == 0 && clock64() - t0 > WAIT_LIMIT_CYCLES, 0);
+        if (late) {
+          if (lane == 0) raise_err(kc, ERR_BARRIER_TIMEOUT, (int)kc.epoch);
           ok = 0;
           break;
         }
       }
     }
-    s_ok = ok;
-    kc.epoch++;
-    kc.seq++;
-    kc.stage = (kc.stage + 1 == kc.n_stages) ? 0 : kc.stage + 1;
+    if (lane == 0) {
+      s_ok = ok;
+      kc.epoch++;
+      kc.seq++;
+      kc.stage = (kc.stage + 1 == kc.n_stages) ? 0 : kc.stage + 1;
+    }
   }
   __syncthreads();
   return s_ok != 0;
@@ -1822,12 +1890,14 @@ QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
 
 // ====================================================== persistent kernel ==
 __global__ void __launch_bounds__(NTHREADS, 1)
-decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ctl, long long *trace) {
+decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, int n_stages, int n_iters, Ctl *ctl,
+              long long *trace) {
   extern __shared__ __align__(128) char smem[];
   __shared__ __align__(8) uint64_t bars[ATT_NBUF];
   __shared__ __align__(8) uint64_t wbars[NWSLOT];
   __shared__ __align__(8) uint64_t dbars[NDESC];
   __shared__ Stage dring[NDESC];   // stage descriptors, NDESC - 1 stages ahead
+  __shared__ V2Plan pring[NDESC];  // this CTA's plan entries for them ([stage][CTA] in `plan`)
   __shared__ KCtx kc;
   if (threadIdx.x == 0) {
     kc.epoch = 0;
@@ -1850,16 +1920,19 @@ decode_kernel(const Stage *__restrict__ prog, int n_stages, int n_iters, Ctl *ct
     kc.n_total = (unsigned)n_stages * (unsigned)n_iters;
     kc.n_stages = n_stages;
     kc.dring = dring;
+    kc.pring = pring;
     kc.dbars = dbars;
     kc.w_issued = 0;
     kc.w_free = 0;
     kc.pf_seq = 0;
     kc.pf_f = 0;
   }
-  auto issue_desc = [&](unsigned k) {   // thread 0: descriptor of stage k into its slot
+  auto issue_desc = [&](unsigned k) {   // thread 0: descriptor (+ plan entry) of stage k into its slot
     const int slot = (int)(k % NDESC);
-    mbar_arrive_expect_tx(dbars + slot, sizeof(Stage));
-    bulk_g2s(dring + slot, prog + k % (unsigned)n_stages, sizeof(Stage), dbars + slot);
+    const unsigned si = k % (unsigned)n_stages;
+    mbar_arrive_expect_tx(dbars + slot, sizeof(Stage) + (plan ? sizeof(V2Plan) : 0));
+    bulk_g2s(dring + slot, prog + si, sizeof(Stage), dbars + slot);
+    if (plan) bulk_g2s(pring + slot, plan + (size_t)si * gridDim.x + blockIdx.x, sizeof(V2Plan), dbars + slot);
   };
   if (threadIdx.x == 0) {
     for (int i = 0; i < ATT_NBUF; i++) mbar_init(bars + i, 1);
