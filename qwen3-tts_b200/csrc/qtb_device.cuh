@@ -195,6 +195,38 @@ QTB_DEV void prefetch_l2(const void *p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Distributed shared memory: the address of `p` (this CTA's shared memory) in
+// CTA `rank` of the cluster, a store there, and a remote mbarrier arrive whose
+// release orders this thread's earlier cluster stores.
+QTB_DEV uint32_t cluster_map(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+QTB_DEV void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+QTB_DEV void mbar_arrive_remote(uint32_t bar_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_addr) : "memory");
+}
+// Bounded wait on a local mbarrier phase completed by another CTA of the
+// cluster (acquire at cluster scope makes its stores visible).
+QTB_DEV bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, long long limit_cycles) {
+  uint32_t done = 0;
+  const long long t0 = clock64();
+  while (true) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > limit_cycles) return false;
+  }
+}
+
 QTB_DEV unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

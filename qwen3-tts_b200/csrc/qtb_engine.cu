@@ -27,6 +27,22 @@ using namespace qtb;
 
 // ------------------------------------------------------------ errors -------
 static thread_local std::string g_err;
+// Cooperative launch of the decode kernel in 2-CTA clusters (one CTA per SM).
+static void cluster_launch_config(cudaLaunchConfig_t &cfg, cudaLaunchAttribute (&at)[2], int n_sm, cudaStream_t st) {
+  cfg.gridDim = dim3(n_sm);
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeCooperative;
+  at[1].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+}
+
 static int set_err(int code, const char *fmt, ...) {
   char buf[512];
   va_list ap;
@@ -311,6 +327,7 @@ struct DStack {
 struct qtb_engine {
   int device = 0;
   int n_sm = 0;
+  int pairs = 0;   // launches run in 2-CTA clusters (K-split of small-tile int8 stages)
   Arena ar;
   DStack talker, cp;
   int has_talker = 0, has_cp = 0;
@@ -426,6 +443,18 @@ extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_eng
   qtb_engine *e = new qtb_engine();
   e->device = device;
   e->n_sm = prop.multiProcessorCount;
+  {
+    // 2-CTA clusters for the whole grid: only if all n_sm / 2 clusters can be
+    // resident at once (a cooperative launch needs every CTA resident)
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[2];
+    cluster_launch_config(cfg, at, e->n_sm, nullptr);
+    int ncl = 0;
+    if (e->n_sm % 2 == 0 && cudaOccupancyMaxActiveClusters(&ncl, (const void *)decode_kernel, &cfg) == cudaSuccess &&
+        ncl >= e->n_sm / 2)
+      e->pairs = 1;
+    cudaGetLastError();
+  }
   int rc = 0;
   e->has_talker = d->talker.n_layers > 0;
   if (e->has_talker) {
@@ -589,7 +618,7 @@ static bool v2_ok(int fmt, int rows, int K, int B, int G) {
                                           (xsum ? (size_t)((B * (K / 32) + 3) & ~3) * 4 : 0);
   if (xb > (size_t)SM_X2_BYTES) return false;
   const int T = rows / 16, nt_max = (T + G - 1) / G;
-  return 256 + (size_t)nt_max * (NWARPS + 1) * 16 * B * 4 <= (size_t)SM_R_BYTES;
+  return 256 + (size_t)nt_max * (NWARPS + 1) * 16 * B * 4 <= (size_t)(SM_PAIR_OFF - SM_R_OFF);
 }
 
 struct ProgBuilder {
@@ -727,12 +756,15 @@ static void build_cp_frame(ProgBuilder &pb, qtb_session *s, const float *talker_
   }
 }
 
-// Each CTA's share of every small-batch GEMV stage of a program ([stage][G]).
-static void make_plans(const std::vector<Stage> &st, int G, std::vector<V2Plan> &out) {
-  out.assign(st.size() * (size_t)G, V2Plan{0, 0, 0, 0});
+// Each CTA's share of every small-batch GEMV stage of a program ([stage][G]);
+// `pairs` when the program is launched in 2-CTA clusters.
+static void make_plans(const std::vector<Stage> &st, int G, bool pairs, std::vector<V2Plan> &out) {
+  out.assign(st.size() * (size_t)G, V2Plan{0, 0, 0, 0, 0, 0, 0, 0});
   for (size_t i = 0; i < st.size(); i++)
     if (st[i].kind == ST_GEMV && st[i].g.v2)
-      for (int c = 0; c < G; c++) out[i * G + c] = v2_plan(st[i].g.fmt, st[i].g.rows, st[i].g.K, c, G);
+      for (int c = 0; c < G; c++)
+        out[i * G + c] = v2_plan(st[i].g.fmt, st[i].g.rows, st[i].g.K, st[i].g.norm_w != nullptr, st[i].g.epi, c, G,
+                                 pairs);
 }
 
 static int upload_prog(qtb_session *s, int which, ProgBuilder &pb) {
@@ -742,7 +774,7 @@ static int upload_prog(qtb_session *s, int which, ProgBuilder &pb) {
   int rc = s->ar.upload(&d, pb.st.data(), pb.st.size() * sizeof(Stage));
   if (rc) return rc;
   std::vector<V2Plan> pl;
-  make_plans(pb.st, s->e->n_sm, pl);
+  make_plans(pb.st, s->e->n_sm, s->e->pairs != 0, pl);
   V2Plan *dp;
   if ((rc = s->ar.upload(&dp, pl.data(), pl.size() * sizeof(V2Plan)))) return rc;
   s->prog[which] = d;
@@ -995,8 +1027,15 @@ static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
   long long *trace = s->trace_on ? s->trace : nullptr;
   void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_iters, (void *)&ctl, (void *)&trace};
   if (timed) CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
-  CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(s->e->n_sm), dim3(NTHREADS), args,
-                                       SMEM_BYTES, s->stream));
+  if (s->e->pairs) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[2];
+    cluster_launch_config(cfg, at, s->e->n_sm, s->stream);
+    CUDA_TRY(cudaLaunchKernelExC(&cfg, (const void *)decode_kernel, args));
+  } else {
+    CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(s->e->n_sm), dim3(NTHREADS), args,
+                                         SMEM_BYTES, s->stream));
+  }
   if (timed) CUDA_TRY(cudaEventRecord(s->ev1, s->stream));
   s->last_launches = 1;
   return 0;
@@ -1194,7 +1233,7 @@ static int run_single_stage(MiniRun &mr, const Stage &S) {
   CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
   CUDA_TRY(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   std::vector<V2Plan> pl;
-  make_plans(std::vector<Stage>{S}, nsm, pl);
+  make_plans(std::vector<Stage>{S}, nsm, false, pl);
   V2Plan *dplan;
   if ((rc = mr.ar.upload(&dplan, pl.data(), pl.size() * sizeof(V2Plan)))) return rc;
   const Stage *prog = dp;
@@ -1542,7 +1581,7 @@ int op_matmat(OpCtx *c, float *Y, const uint16_t *W, const float *X, int rows, i
   g.x = c->dx; g.ldx = cp; g.y = c->dy; g.ldy = rp; g.epi = EPI_STORE; g.ws = c->ws; g.sem = c->sem;
   CUDA_TRY(cudaMemcpyAsync(c->dstage, &s, sizeof s, cudaMemcpyHostToDevice, c->st));
   std::vector<V2Plan> pl;
-  make_plans(std::vector<Stage>{s}, c->nsm, pl);
+  make_plans(std::vector<Stage>{s}, c->nsm, false, pl);
   CUDA_TRY(cudaMemcpyAsync(c->dplan, pl.data(), pl.size() * sizeof(V2Plan), cudaMemcpyHostToDevice, c->st));
   const Stage *prog = c->dstage;
   const V2Plan *plan = c->dplan;

@@ -55,6 +55,8 @@ constexpr int SM_X2_BYTES = 48 * 1024;
 constexpr int SM_R_OFF = SM_X_OFF + SM_X2_BYTES;
 constexpr int SM_R_BYTES = 12 * 1024;
 constexpr int SMEM_BYTES = SM_R_OFF + SM_R_BYTES;
+// the last 1 KB of the R region receives a cluster partner's partial sums
+constexpr int SM_PAIR_OFF = SM_R_OFF + SM_R_BYTES - 1024;
 // Stage descriptors travel through a ring of NDESC shared-memory slots,
 // bulk-copied NDESC - 1 stages ahead; the weight streamer looks at most
 // STREAM_AHEAD stages past the last completed one (STREAM_AHEAD < NDESC keeps
@@ -175,6 +177,8 @@ struct KCtx {
   unsigned pf_seq;      // next stage the streamer looks at
   int pf_f;             // next fill of that stage
   int last;             // this CTA's arrival completed the current barrier
+  uint64_t *pbar;       // receives the cluster partner's arrive (split stages)
+  unsigned pair_ctr;    // split stages combined so far (pbar phase source)
 };
 
 // Profiling checkpoint (CTA 0, thread 0) when stage tracing is on.
@@ -775,22 +779,43 @@ struct V2Sched {
 // there are fewer tiles than CTAs the rest idle -- the weights are streamed
 // ahead, so a CTA holding two tiles' worth costs less than a cross-CTA
 // reduction would), L chunks of 512 bytes in nfill ring fills.
+// pair: 0, or for an int8 stage without a norm and with fewer than half as
+// many tiles as CTAs, the tile's K is cut in two between the CTAs of one
+// 2-CTA cluster (CTAs 2u, 2u+1 for tile u): 1 = the first half, which also
+// adds the second half's sums (sent over distributed shared memory, in piece
+// order: deterministic) and runs the epilogue, 2 = the second half.
 struct __align__(16) V2Plan {
   int t0, nt, L, nfill;
+  int kb, kc, pair, pad;
 };
-static_assert(sizeof(V2Plan) == 16, "plans are bulk-copied");
+static_assert(sizeof(V2Plan) == 32, "plans are bulk-copied");
 
 template <int FMT>
 QTB_HOST_DEV constexpr int v2_cps() { return WSLOT_BYTES / (512 + 8 * FmtTraits<FMT>::GSZ); }
 
-QTB_HOST_DEV V2Plan v2_plan(int fmt, int rows, int K, int cta, int G) {
+// `pairs`: the launch runs in 2-CTA clusters, so K may be split across a pair.
+QTB_HOST_DEV V2Plan v2_plan(int fmt, int rows, int K, bool has_norm, int epi, int cta, int G, bool pairs) {
   const int gsz = fmt == FMT_Q4_0 ? 8 : (fmt == FMT_INT4G ? 16 : 0);
   const int ck = fmt == FMT_BF16 ? 1 : (fmt == FMT_INT8 ? 2 : 4);
   const int T = rows >> 4, nck = K / (16 * ck), cps = WSLOT_BYTES / (512 + 8 * gsz);
   V2Plan p;
-  p.t0 = (int)((long long)cta * T / G);
-  p.nt = (int)((long long)(cta + 1) * T / G) - p.t0;
-  p.L = p.nt * nck;
+  p.pad = 0;
+  if (pairs && fmt == FMT_INT8 && !has_norm && epi != EPI_ARGMAX && 2 * T <= G && nck >= 8) {
+    const int u = cta >> 1, h = cta & 1, n4 = nck >> 2;
+    p.t0 = u < T ? u : 0;
+    p.nt = u < T ? 1 : 0;
+    p.kb = h ? 4 * (n4 / 2) : 0;
+    p.kc = h ? nck - 4 * (n4 / 2) : 4 * (n4 / 2);
+    p.pair = p.nt ? 1 + h : 0;
+    p.L = p.nt * p.kc;
+  } else {
+    p.t0 = (int)((long long)cta * T / G);
+    p.nt = (int)((long long)(cta + 1) * T / G) - p.t0;
+    p.kb = 0;
+    p.kc = nck;
+    p.pair = 0;
+    p.L = p.nt * nck;
+  }
   p.nfill = (p.L + cps - 1) / cps;
   return p;
 }
@@ -802,8 +827,9 @@ QTB_DEV V2Sched v2_sched(const GemvArgs &a, const V2Plan &p) {
   s.cps = v2_cps<FMT>();
   s.t0 = p.t0;
   s.nt = p.nt;
-  s.kb = 0;
-  s.kc = a.K / (16 * Tr::CK);
+  s.kb = p.kb;
+  s.kc = p.kc;
+  (void)Tr::CK;
   s.L = p.L;
   s.nfill = p.nfill;
   return s;
@@ -1165,9 +1191,12 @@ __device__ __noinline__ void gemv2_stage_t(const GemvArgs &a, int B, char *smem,
 // row b are MMA columns 4b .. 4b+3; per k32 chunk c and column chunk j the
 // staged activation holds one (b0, b1) register pair per lane.
 template <int MAXQ>
-__device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float *s_scl, uint32_t *s_xw,
-                                        float *s_zero, int n_zero, KCtx &kc) {
-  const int K = a.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// Stages columns [k0, k0 + K) of the activation (a piece of it for a split
+// stage; then the part scale is the piece's own); chunk c of the staged
+// range is column chunk k0/32 + c.
+__device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, int k0, int K, float *s_scl,
+                                        uint32_t *s_xw, float *s_zero, int n_zero, KCtx &kc) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nk4 = K >> 2;
   const int nq = B * nk4;
   float v[MAXQ][4], g[MAXQ][4];
@@ -1177,10 +1206,10 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float
     const int t = tid + i * NTHREADS;
     if (t < nq) {
       const int b = t / nk4, k = 4 * (t - b * nk4);
-      const float4 x4 = __ldcg(reinterpret_cast<const float4 *>(a.x + (size_t)b * a.ldx + k));
+      const float4 x4 = __ldcg(reinterpret_cast<const float4 *>(a.x + (size_t)b * a.ldx + k0 + k));
       v[i][0] = x4.x; v[i][1] = x4.y; v[i][2] = x4.z; v[i][3] = x4.w;
       if (a.norm_w) {
-        const float4 g4 = __ldg(reinterpret_cast<const float4 *>(a.norm_w + k));
+        const float4 g4 = __ldg(reinterpret_cast<const float4 *>(a.norm_w + k0 + k));
         g[i][0] = g4.x; g[i][1] = g4.y; g[i][2] = g4.z; g[i][3] = g4.w;
       } else {
         g[i][0] = g[i][1] = g[i][2] = g[i][3] = 1.f;
@@ -1269,6 +1298,28 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, float
   }
 }
 
+// The two halves of a split stage (2-CTA cluster): the second half stores its
+// per-row sums into the first half's shared memory and arrives on its
+// mbarrier; the first half waits (bounded), adds them to its own (own first:
+// fixed order) and returns true to run the epilogue.
+QTB_CALL bool pair_combine(float *s_val, int n, int role, char *smem, KCtx &kc) {
+  float *recv = reinterpret_cast<float *>(smem + SM_PAIR_OFF);
+  const int tid = threadIdx.x;
+  if (role == 2) {
+    for (int i = tid; i < n; i += NTHREADS) st_cluster_f32(cluster_map(recv + i, 0), s_val[i]);
+    __syncthreads();
+    if (tid == 0) mbar_arrive_remote(cluster_map(kc.pbar, 0));
+    return false;
+  }
+  if (!mbar_wait_cluster(kc.pbar, kc.pair_ctr & 1u, WAIT_LIMIT_CYCLES)) {
+    if (tid == 0) raise_err(kc, ERR_MBAR_TIMEOUT, -4);
+  }
+  for (int i = tid; i < n; i += NTHREADS) s_val[i] = s_val[i] + recv[i];
+  __syncthreads();
+  if (tid == 0) kc.pair_ctr++;
+  return true;
+}
+
 template <int NCH>
 __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
   const V2Sched s = v2_sched<FMT_INT8>(a, kc.pring[kc.seq % NDESC]);
@@ -1283,12 +1334,13 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
   ckpt(kc, 0);
   if (s.nt == 0) return;
   {
-    const int mq = (B * (a.K >> 2) + NTHREADS - 1) / NTHREADS;
+    const int mq = (B * (32 * s.kc >> 2) + NTHREADS - 1) / NTHREADS;
     const int nz = s.nt * NWARPS * 16 * B;
-    if (mq <= 1) stage_x_s8<1>(a, B, NCH, s_scl, s_xw, s_red, nz, kc);
-    else if (mq <= 2) stage_x_s8<2>(a, B, NCH, s_scl, s_xw, s_red, nz, kc);
-    else if (mq <= 4) stage_x_s8<4>(a, B, NCH, s_scl, s_xw, s_red, nz, kc);
-    else stage_x_s8<8>(a, B, NCH, s_scl, s_xw, s_red, nz, kc);
+    const int k0 = 32 * s.kb, Kp = 32 * s.kc;   // the staged columns (a piece for split stages)
+    if (mq <= 1) stage_x_s8<1>(a, B, NCH, k0, Kp, s_scl, s_xw, s_red, nz, kc);
+    else if (mq <= 2) stage_x_s8<2>(a, B, NCH, k0, Kp, s_scl, s_xw, s_red, nz, kc);
+    else if (mq <= 4) stage_x_s8<4>(a, B, NCH, k0, Kp, s_scl, s_xw, s_red, nz, kc);
+    else stage_x_s8<8>(a, B, NCH, k0, Kp, s_scl, s_xw, s_red, nz, kc);
   }
   __syncthreads();
   ckpt(kc, 2);
@@ -1347,7 +1399,7 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
     while (ci < ce) {
       const int tl = ci / s.kc;
       const int te = min(ce, (tl + 1) * s.kc);
-      const int c0 = s.kb - tl * s.kc;
+      const int c0 = -tl * s.kc;   // staged chunk of chunk ci
       for (; ci + 4 <= te; ci += 4) {
         uint4 wv[4];
 #pragma unroll
@@ -1393,6 +1445,10 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
   }
   __syncthreads();
   ckpt(kc, 4);
+  {
+    const int role = kc.pring[kc.seq % NDESC].pair;
+    if (role && !pair_combine(s_val, 16 * B, role, smem, kc)) return;
+  }
   v2_epilogue(a, B, s.t0, s.nt, s_val, B, kc);
   ckpt(kc, 5);
 }
@@ -1898,6 +1954,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
   __shared__ __align__(8) uint64_t dbars[NDESC];
   __shared__ Stage dring[NDESC];   // stage descriptors, NDESC - 1 stages ahead
   __shared__ V2Plan pring[NDESC];  // this CTA's plan entries for them ([stage][CTA] in `plan`)
+  __shared__ __align__(8) uint64_t pbar;
   __shared__ KCtx kc;
   if (threadIdx.x == 0) {
     kc.epoch = 0;
@@ -1921,6 +1978,8 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     kc.n_stages = n_stages;
     kc.dring = dring;
     kc.pring = pring;
+    kc.pbar = &pbar;
+    kc.pair_ctr = 0;
     kc.dbars = dbars;
     kc.w_issued = 0;
     kc.w_free = 0;
@@ -1938,6 +1997,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     for (int i = 0; i < ATT_NBUF; i++) mbar_init(bars + i, 1);
     for (int i = 0; i < NWSLOT; i++) mbar_init(wbars + i, 1);
     for (int i = 0; i < NDESC; i++) mbar_init(dbars + i, 1);
+    mbar_init(&pbar, 1);
     fence_mbar_init();
     for (unsigned k = 0; k < NDESC - 1 && k < kc.n_total; k++) issue_desc(k);
     kc.t_start = clock64();
