@@ -145,9 +145,10 @@ def run_b200(args, rank, world, local_rank):
     else:
         lo, hi = (128, 2048) if cfg_name == "c4" else (256, 4096)
         lens = np.random.default_rng(0).integers(lo, hi + 1, B)
-        per = [(int(L) + W + K + 15) // 16 + 1 for L in lens]
+        grow = W + K + max(4, min(K, 64))   # positions appended: warm-up, timed and end-to-end frames
+        per = [(int(L) + grow + 15) // 16 + 1 for L in lens]
         n_pages = sum(per)
-        ses = Q.Session(eng, B, int(max(lens)) + W + K + 32, n_pages=n_pages)
+        ses = Q.Session(eng, B, int(max(lens)) + grow + 32, n_pages=n_pages)
         perm = np.random.default_rng(0).permutation(n_pages)
         off = 0
         for b in range(B):
@@ -305,7 +306,7 @@ def dist_init():
     import torch.distributed as dist
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device(f"cuda:{local}"))
     _dist = (torch, dist)
     return dist.get_rank(), world, local
 
@@ -352,6 +353,8 @@ def main():
             if "error" in cb:
                 line = {"impl": "reference", "unavailable": cb["error"].splitlines()[-1] if cb["error"] else "failed"}
             print(json.dumps(line), flush=True)
+        if _dist:
+            _dist[1].destroy_process_group()
         return
     out = run_b200(args, rank, world, local)
     if rank == 0:
