@@ -1333,6 +1333,18 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
   if (warp == 0 && kc.pf_seq <= kc.seq) stream(kc, smem, kc.seq, kc.seq + 1);   // this stage's first fills, if not issued yet
   ckpt(kc, 0);
   if (s.nt == 0) return;
+  // STORE / RESID with one output per thread: load the row scale and the
+  // residual now, so the epilogue does not wait on L2 after the MMA
+  const int role = kc.pring[kc.seq % NDESC].pair;
+  const bool fast_epi = (a.epi == EPI_STORE || a.epi == EPI_RESID) && !a.bias && s.nt * 16 * B <= NTHREADS &&
+                        role != 2;
+  float pre_rs = 1.f, pre_res = 0.f;
+  if (fast_epi && tid < s.nt * 16 * B) {
+    const int b = tid % B, r = (tid / B) % 16, tl = tid / (16 * B);
+    const int row = 16 * (s.t0 + tl) + r;
+    if (a.row_scale) pre_rs = __ldg(a.row_scale + row);
+    if (a.epi == EPI_RESID) pre_res = __ldcg(a.y + (size_t)b * a.ldy + row);
+  }
   {
     const int mq = (B * (32 * s.kc >> 2) + NTHREADS - 1) / NTHREADS;
     const int nz = s.nt * NWARPS * 16 * B;
@@ -1445,11 +1457,16 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
   }
   __syncthreads();
   ckpt(kc, 4);
-  {
-    const int role = kc.pring[kc.seq % NDESC].pair;
-    if (role && !pair_combine(s_val, 16 * B, role, smem, kc)) return;
+  if (role && !pair_combine(s_val, 16 * B, role, smem, kc)) return;
+  if (fast_epi) {
+    if (tid < s.nt * 16 * B) {
+      const int b = tid % B, r = (tid / B) % 16, tl = tid / (16 * B);
+      const int row = 16 * (s.t0 + tl) + r;
+      __stcg(a.y + (size_t)b * a.ldy + row, pre_res + pre_rs * s_val[tid]);
+    }
+  } else {
+    v2_epilogue(a, B, s.t0, s.nt, s_val, B, kc);
   }
-  v2_epilogue(a, B, s.t0, s.nt, s_val, B, kc);
   ckpt(kc, 5);
 }
 
