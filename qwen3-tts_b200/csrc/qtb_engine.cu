@@ -530,9 +530,18 @@ struct StackBufs {
   int n_pages = 0;
   int *page_table = nullptr;                    // [B][pt_stride]
   int pt_stride = 0;
-  int max_splits = 1;
+  int max_splits = 1, min_pps = 4;
   size_t layer_pool_elems() const { return 0; }
 };
+
+// Work distribution of an attention stage: with more (slot, kv head, split)
+// items than CTAs, CTAs take items from a grid-wide counter (dynamic order);
+// 16 page buffers unless the program also streams small-batch GEMV weights
+// (upload_prog then cuts it to 4).
+static void attn_schedule(AttnArgs &a, int B, int n_sm) {
+  a.dyn = (long long)B * a.n_kv * a.max_splits > n_sm ? 1 : 0;
+  a.nbuf = ATT_NBUF_MAX;
+}
 
 struct qtb_session {
   qtb_engine *e = nullptr;
@@ -677,8 +686,9 @@ struct ProgBuilder {
     a.n_pages = b.n_pages;
     a.n_heads = k.n_heads; a.n_kv = k.n_kv;
     a.eps = k.eps; a.scale = 1.0f / sqrtf((float)HD);
-    a.max_splits = b.max_splits; a.min_pps = 4;
+    a.max_splits = b.max_splits; a.min_pps = b.min_pps;
     a.ws = s->att_ws; a.sem = s->att_sem;
+    attn_schedule(a, B, s->e->n_sm);
     st.push_back(S);
   }
   void layers(const DStack &k, const StackBufs &b, int B, const int *pos_ptr, int pos_const, size_t layer_elems, int evict_last) {
@@ -770,6 +780,12 @@ static void make_plans(const std::vector<Stage> &st, int G, bool pairs, std::vec
 static int upload_prog(qtb_session *s, int which, ProgBuilder &pb) {
   if (pb.err) return pb.err;
   if (pb.st.empty()) return 0;
+  // the weight streamer of small-batch GEMV stages may fill the weight ring
+  // during an attention stage: its page ring then stays in the activation region
+  bool streams = false;
+  for (const Stage &st : pb.st) streams |= (st.kind == ST_GEMV && st.g.v2);
+  for (Stage &st : pb.st)
+    if (st.kind == ST_ATTN && streams) st.a.nbuf = ATT_NBUF;
   Stage *d;
   int rc = s->ar.upload(&d, pb.st.data(), pb.st.size() * sizeof(Stage));
   if (rc) return rc;
@@ -846,8 +862,16 @@ static int alloc_stack_bufs(qtb_session *s, const DStack &k, StackBufs &b, int B
   for (int i = 0; i < B; i++)
     for (int j = 0; j < b.pt_stride; j++) pt[(size_t)i * b.pt_stride + j] = (n_pages > 0) ? -1 : i * b.pt_stride + j;
   if ((rc = ar.upload(&b.page_table, pt.data(), pt.size() * 4))) return rc;
-  // at most one attention work item per CTA: a second item would double the stage
-  b.max_splits = std::max(1, std::min(32, s->e->n_sm / (B * k.n_kv)));
+  if (B * k.n_kv > s->e->n_sm / 2) {
+    // many sequences: items of 16-32 pages taken in dynamic order keep the
+    // CTAs evenly loaded whatever the length mix
+    b.max_splits = 16;
+    b.min_pps = 32;
+  } else {
+    // at most one attention work item per CTA: a second item would double the stage
+    b.max_splits = std::max(1, std::min(32, s->e->n_sm / (B * k.n_kv)));
+    b.min_pps = 4;
+  }
   return 0;
 }
 
@@ -1020,6 +1044,7 @@ static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
   if ((long long)n_iters * s->prog_n[which] * s->e->n_sm > 0x3fffffffLL)
     return set_err(QTB_E_INVALID, "too many iterations for one launch");
   CUDA_TRY(cudaMemsetAsync(&s->ctl->bar_count, 0, sizeof(unsigned), s->stream));
+  CUDA_TRY(cudaMemsetAsync(&s->ctl->att_work, 0, sizeof(unsigned), s->stream));
   const Stage *prog = s->prog[which];
   const V2Plan *plan = s->plan[which];
   int n_st = s->prog_n[which];
@@ -1334,6 +1359,12 @@ extern "C" int qtb_attention_host(const float *qkv, int batch, int n_heads, int 
   a.kpool = dk; a.vpool = dv; a.n_pages = n_pages; a.n_heads = n_heads; a.n_kv = n_kv;
   a.eps = eps; a.scale = 1.0f / sqrtf((float)HD); a.max_splits = max_splits; a.min_pps = 1;
   a.ws = ws; a.sem = sem;
+  {
+    int dev = 0, nsm = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    attn_schedule(a, batch, nsm);
+  }
   if ((rc = run_single_stage(mr, st))) return rc;
   CUDA_TRY(cudaMemcpy(out, dout, (size_t)batch * qd * 4, cudaMemcpyDeviceToHost));
   CUDA_TRY(cudaMemcpy(kpages, dk, pool * 2, cudaMemcpyDeviceToHost));
@@ -1475,6 +1506,7 @@ extern "C" int qtb_attention_noalloc(const float *qkv, int batch, int n_heads, i
   a.kpool = kpages; a.vpool = vpages; a.n_pages = n_pages; a.n_heads = n_heads; a.n_kv = n_kv;
   a.eps = eps; a.scale = 1.0f / sqrtf((float)HD); a.max_splits = max_splits; a.min_pps = 1;
   a.ws = ws; a.sem = sem;
+  attn_schedule(a, batch, nsm);
   // the control block and the split semaphores must start at zero; the
   // descriptor is copied from this stack frame (synchronously, so the frame
   // may go away when the call returns)

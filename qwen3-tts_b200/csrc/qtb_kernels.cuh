@@ -32,7 +32,9 @@ constexpr int NTHREADS = 256;
 constexpr int NWARPS = NTHREADS / 32;
 constexpr int HD = 128;       // head_dim (Qwen3-TTS talker and CP)
 constexpr int PAGE = 16;      // KV positions per page
-constexpr int ATT_NBUF = 4;   // K/V page buffers in flight per CTA
+constexpr int ATT_NBUF = 4;   // K/V page buffers in flight per CTA (small-batch programs)
+constexpr int ATT_NBUF_MAX = 16;   // ... when the weight ring is idle (no small-batch GEMV stage)
+constexpr int ATT_PAGE_BYTES = 2 * PAGE * HD * 2;   // one page of one KV head: K then V, bf16
 constexpr long long WAIT_LIMIT_CYCLES = 500000000LL;  // ~0.25 s at 1.9 GHz
 
 // Dynamic shared memory map (one CTA per SM):
@@ -108,6 +110,10 @@ struct AttnArgs {
   float eps, scale;
   int max_splits, min_pps;
   float *ws; unsigned *sem;
+  // nbuf: page buffers (ATT_NBUF, or ATT_NBUF_MAX in a program whose weight
+  // ring is idle).  dyn: CTAs take work items from a grid-wide counter in the
+  // dense order of attn_prefix instead of item = CTA + k * grid.
+  int nbuf, dyn;
 };
 
 struct EmbedArgs {
@@ -142,7 +148,8 @@ struct Ctl {
   int err;              // first error code (same 8 bytes: one load polls both)
   int err_stage;        // stage index that raised it
   int err_info;
-  int pad[60];
+  unsigned att_work;    // attention work items taken (dynamic order; zeroed before each launch)
+  int pad[59];
 };
 
 // Per-CTA kernel state, one copy in shared memory.  Fields are written by
@@ -155,10 +162,14 @@ struct KCtx {
   unsigned page_ctr;    // K/V page buffers consumed so far (mbarrier phase source)
   unsigned wfill;       // weight-ring slot fills consumed so far (mbarrier phase source)
   int att_pre;          // K/V pages already issued for the coming attention stage
-  unsigned att_issued;  // thread 0: K/V page copies issued so far
+  unsigned att_issued;  // K/V page copies issued so far (one past the last)
+  int att_nbuf;         // page buffers of the attention stages of this program
+  unsigned att_base;    // ctl->att_work at the start of the current dynamic attention stage
+  int att_first;        // first work item taken before the barrier, or -1
+  int att_tot;          // its stage's item count (valid with att_first >= 0)
   int local_err;        // this thread has raised an error
   uint64_t pol_first, pol_last;
-  uint64_t *bars;       // ATT_NBUF page-buffer mbarriers
+  uint64_t *bars;       // ATT_NBUF_MAX page-buffer mbarriers
   uint64_t *wbars;      // NWSLOT weight-slot mbarriers
   Ctl *ctl;
   int stage;
@@ -256,9 +267,13 @@ QTB_DEV void stage_inv_rms(const GemvArgs &a, int B, float *s_inv) {
   for (int b = warp; b < B; b += NWARPS) {
     const float *xb = a.x + (size_t)b * a.ldx;
     float ss = 0.f;
-    for (int i = lane * 4; i < a.K; i += 128) {
-      float4 v = ld_cg4(xb + i);
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    // eight loads in flight per lane, summed in the same order as one at a time
+    for (int i0 = lane * 4; i0 < a.K; i0 += 8 * 128) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = (i0 + 128 * u < a.K) ? ld_cg4(xb + i0 + 128 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; u++) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
     }
     ss = warp_sum(ss);
     if (lane == 0) s_inv[b] = 1.0f / sqrtf(ss / (float)a.K + a.eps);
@@ -388,6 +403,47 @@ QTB_DEV void stage_x(const GemvArgs &a, int B, int ent, int k0, int kslice, cons
   const int nch = a.nch, P = a.parts;
   const int ksteps = kslice >> 4;
   const int total = ksteps * nch * ent;
+  if (ent == 32 && P == 2) {
+    // large batches: entry e = (q * nch + j) * 32 + lane, so a thread's lane is
+    // fixed and (q, j) steps by NWARPS entries; four entries' loads in flight
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int lg = 31 - __clz(nch);   // nch is a power of two
+    const int nqj = ksteps * nch;
+    for (int qj0 = warp; qj0 < nqj; qj0 += 4 * NWARPS) {
+      float2 p0[4], p1[4];
+      int bb[4], kk[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int qj = qj0 + u * NWARPS;
+        const int j = qj & (nch - 1), q = qj >> lg;
+        const int b = (8 * j + gid) >> 1;
+        const int k = k0 + 16 * q + (perm4 ? 4 : 2) * tig, k2 = k + (perm4 ? 2 : 8);
+        bb[u] = (qj < nqj && b < B) ? b : -1;
+        kk[u] = k;
+        p0[u] = p1[u] = make_float2(0.f, 0.f);
+        if (bb[u] >= 0) {
+          const float *xb = a.x + (size_t)b * a.ldx;
+          p0[u] = __ldcg(reinterpret_cast<const float2 *>(xb + k));
+          p1[u] = __ldcg(reinterpret_cast<const float2 *>(xb + k2));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int qj = qj0 + u * NWARPS;
+        if (qj >= nqj) break;
+        uint32_t r0 = 0, r1 = 0;
+        if (bb[u] >= 0) {
+          const int b = bb[u], k = kk[u], k2 = k + (perm4 ? 2 : 8), lo = gid & 1;
+          const float v0 = norm_in(a, s_inv, b, k, p0[u].x), v1 = norm_in(a, s_inv, b, k + 1, p0[u].y);
+          const float v2 = norm_in(a, s_inv, b, k2, p1[u].x), v3 = norm_in(a, s_inv, b, k2 + 1, p1[u].y);
+          r0 = split_pack<F16>(v0, v1, lo);
+          r1 = split_pack<F16>(v2, v3, lo);
+        }
+        s_xf[qj * 32 + lane] = make_uint2(r0, r1);
+      }
+    }
+  } else
   for (int e = threadIdx.x; e < total; e += NTHREADS) {
     const int l = e % ent;
     const int qj = e / ent;
@@ -532,9 +588,10 @@ QTB_DEV void gemv_unit(const GemvArgs &a, int B, int t, int s, int kslice, const
                        int ent, const float *s_xsum, float (&res)[NCH][2], const KCtx &kc) {
   using Tr = FmtTraits<FMT>;
   constexpr int CK = Tr::CK;
-  // loads in flight per lane: deep for small batches (bandwidth-bound), shallow
-  // for large ones (tensor-bound, and the accumulators need the registers)
-  constexpr int PD = NCH >= 8 ? 2 : (NCH >= 4 ? 4 : 8);
+  // loads in flight per lane: the warp's chunk stream is latency-bound, so as
+  // deep as the registers allow -- less deep
+  // for large ones (the accumulators need the registers; int8 keeps two sets)
+  constexpr int PD = NCH >= 8 ? (FMT == FMT_BF16 ? 8 : 2) : (NCH >= 4 ? 4 : 8);
   const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
   const int nck_total = a.K / (16 * CK);
   const int nck = kslice / (16 * CK);
@@ -578,10 +635,12 @@ QTB_DEV void gemv_unit(const GemvArgs &a, int B, int t, int s, int kslice, const
       }
     }
   }
+  if (FMT == FMT_INT8) {   // (only int8 uses the second set)
 #pragma unroll
-  for (int j = 0; j < NCH; j++)
+    for (int j = 0; j < NCH; j++)
 #pragma unroll
-    for (int e2 = 0; e2 < 4; e2++) acc[j][e2] += acc2[j][e2];
+      for (int e2 = 0; e2 < 4; e2++) acc[j][e2] += acc2[j][e2];
+  }
   acc_finish<FMT, NCH, P>(acc, res);
 }
 
@@ -705,14 +764,17 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
   bool inv_done = false;
   for (int base = blockIdx.x * NWARPS; base < U; base += W) {
     if (a.norm_w && !inv_done) { stage_inv_rms(a, B, s_inv); __syncthreads(); inv_done = true; }
+    ckpt(kc, 12);
     const int s = base / T;
     stage_x<F16>(a, B, ent, s * kslice, kslice, s_inv, s_xsum, s_xf, XSUM, FMT == FMT_INT8);
     __syncthreads();
+    ckpt(kc, 13);
     const int u = base + warp;
     if (u < U) {
       const int t = u - s * T;
       float res[NCH][2];
       gemv_unit<FMT, NCH, P>(a, B, t, s, kslice, s_xf, ent, s_xsum, res, kc);
+      ckpt(kc, 14);
       bool finish = true;
       if (S > 1) {
 #pragma unroll
@@ -728,26 +790,40 @@ __device__ __noinline__ void gemv_stage_t(const GemvArgs &a, int B, char *smem, 
         if (lane == 0) { __threadfence(); old = atomicAdd(a.sem + t, 1u); }
         old = __shfl_sync(0xffffffffu, old, 0);
         finish = (old == (unsigned)(S - 1));
+        ckpt(kc, 15);
         if (finish) {
           __threadfence();
+          // the S partials in slice order; two slices' loads in flight at a
+          // time (S is a power of two)
 #pragma unroll
-          for (int j = 0; j < NCH; j++) {
-            const int b = col_batch<P>(j, tig);
-            float v0 = 0.f, v1 = 0.f;
-            if (b < B) {
-              for (int ss = 0; ss < S; ss++) {
-                const size_t uu = (size_t)ss * T + t;
-                v0 += __ldcg(a.ws + (uu * 16 + gid) * B + b);
-                v1 += __ldcg(a.ws + (uu * 16 + gid + 8) * B + b);
+          for (int j = 0; j < NCH; j++) res[j][0] = res[j][1] = 0.f;
+          for (int ss = 0; ss < S; ss += 2) {
+            float l[2][NCH][2];
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+              const size_t uu = (size_t)(ss + q) * T + t;
+#pragma unroll
+              for (int j = 0; j < NCH; j++) {
+                const int b = col_batch<P>(j, tig);
+                const bool ok = b < B && ss + q < S;
+                l[q][j][0] = ok ? __ldcg(a.ws + (uu * 16 + gid) * B + b) : 0.f;
+                l[q][j][1] = ok ? __ldcg(a.ws + (uu * 16 + gid + 8) * B + b) : 0.f;
               }
             }
-            res[j][0] = v0;
-            res[j][1] = v1;
+#pragma unroll
+            for (int q = 0; q < 2; q++)
+#pragma unroll
+              for (int j = 0; j < NCH; j++) {
+                res[j][0] += l[q][j][0];
+                res[j][1] += l[q][j][1];
+              }
           }
           if (lane == 0) a.sem[t] = 0u;
         }
       }
+      ckpt(kc, 16);
       if (finish) gemv_epilogue<NCH, P>(a, B, t, T, res, kc);
+      ckpt(kc, 17);
     }
     __syncthreads();
   }
@@ -950,7 +1026,10 @@ QTB_CALL void stream(KCtx &kc, char *smem, unsigned done, unsigned limit) {
 QTB_CALL void drain(KCtx &kc, unsigned cur) {
   constexpr long long LIM = 200000000LL;   // ~0.1 s per copy group
   for (unsigned c = kc.wfill; c != kc.w_issued; c++) mbar_wait(kc.wbars + c % NWSLOT, (c / NWSLOT) & 1u, LIM);
-  for (unsigned c = kc.page_ctr; c != kc.att_issued; c++) mbar_wait(kc.bars + c % ATT_NBUF, (c / ATT_NBUF) & 1u, LIM);
+  // page copies: at most the last att_nbuf issued can still be in flight
+  const unsigned nb = (unsigned)kc.att_nbuf;
+  const unsigned p0 = (kc.att_issued - kc.page_ctr > nb) ? kc.att_issued - nb : kc.page_ctr;
+  for (unsigned c = p0; c != kc.att_issued; c++) mbar_wait(kc.bars + c % nb, (c / nb) & 1u, LIM);
   for (unsigned k = cur + 1; k < cur + NDESC && k < kc.n_total; k++)
     mbar_wait(kc.dbars + k % NDESC, (k / NDESC) & 1u, LIM);
 }
@@ -1530,11 +1609,19 @@ QTB_DEV void gemv_stage(const GemvArgs &a, int B, char *smem, KCtx &kc) {
 // 203-251) and the new K/V of head g; the CTA whose split holds the newest
 // page also appends K/V (bf16 by truncation, qwen_tts_talker.c:612-615) into
 // the slot's page with 16-byte stores.  Pages are staged into shared memory
-// by 1D bulk copies (cp.async.bulk, mbarrier completion) through a 4-deep
-// ring.  Scores use the reference's order (dot, then * scale); the softmax is
-// the same online recurrence as qwen_causal_attention_bf16kv
+// by 1D bulk copies (cp.async.bulk, mbarrier completion) through a ring of 4
+// buffers, or 16 in programs whose weight ring is idle (large batches).  The
+// CTA's 8 warps work as 4 pairs (the two query heads of the GQA group), pair
+// p on pages p, p + 4, ..., each warp with its own online softmax, merged in
+// warp order at the end.  Scores use the reference's order (dot, then *
+// scale); the softmax is the online recurrence of qwen_causal_attention_bf16kv
 // (qwen_tts_kernels.c:3704-3846) applied per page.  When an item has several
 // splits the last finishing CTA combines them (deterministic order).
+// Items go to CTAs either statically (item = CTA + k * grid: at most one per
+// CTA in small batches) or, for large batches, from a grid-wide counter in the
+// dense order of attn_prefix, so CTAs that drew short sequences take more.
+// Either way an item's arithmetic does not depend on the CTA: results are
+// identical run to run.
 
 // The bf16 rows of the new token come first: they are read as 16-byte
 // vectors for the page store, so they must sit on 16-byte boundaries.
@@ -1542,20 +1629,37 @@ struct __align__(16) AttnSmem {
   uint16_t knew[HD];
   uint16_t vnew[HD];
   float q[2][HD];
-  float sc[2][PAGE];
-  float p[2][PAGE];
-  float corr[2];
-  float l[2];
-  float m[2];
+  unsigned cons[ATT_NBUF_MAX];   // per page buffer: warps done with its current page
+  int pre[65];                   // dynamic order: first item of each batch slot, items in all at [B]
+  int next;                      // dynamic order: the CTA's next item
   int flag;
 };
 static_assert(sizeof(AttnSmem) <= 2048, "attention scratch overlaps the page buffers");
-static_assert(2048 + ATT_NBUF * 2 * PAGE * HD * 2 <= SM_X2_BYTES, "page ring exceeds the attention region");
+// per-warp softmax states for the end-of-split combine: [NWARPS][HD] + [NWARPS][2]
+constexpr int ATT_COMB_OFF = 2048 + ATT_NBUF * ATT_PAGE_BYTES;
+static_assert(ATT_COMB_OFF + NWARPS * (HD + 2) * 4 <= SM_X2_BYTES, "page ring exceeds the attention region");
+static_assert(NWARPS == 2 * ATT_NBUF, "one warp pair (the two heads of a GQA group) per page buffer group");
+static_assert((ATT_NBUF_MAX - ATT_NBUF) * ATT_PAGE_BYTES <= NWSLOT * WSLOT_BYTES, "extra page buffers exceed the weight ring");
+
+// Page buffer i (of a.nbuf): the first ATT_NBUF follow the attention scratch
+// in the activation region; the others take the weight-ring region, which is
+// idle in a program without small-batch GEMV stages.
+QTB_DEV uint16_t *att_buf(char *smem, int i) {
+  return reinterpret_cast<uint16_t *>(i < ATT_NBUF ? smem + SM_X_OFF + 2048 + i * ATT_PAGE_BYTES
+                                                   : smem + SM_W_OFF + (i - ATT_NBUF) * ATT_PAGE_BYTES);
+}
 
 struct AttnItem {
   int b, g, sp, pos, L, npages, nsp, p_begin, p_end;
   bool bad_pos;
 };
+
+// Pages per split for a sequence of np pages: at least min_pps, at most
+// max_splits splits.
+QTB_DEV int attn_pps(const AttnArgs &a, int np) {
+  const int nsp = max(1, min(a.max_splits, (np + a.min_pps - 1) / a.min_pps));
+  return (np + nsp - 1) / nsp;
+}
 
 // Decode work item -> (slot, kv head, split) and the split's page range.
 // Returns false for items beyond the slot's split count (or a bad position).
@@ -1569,8 +1673,7 @@ QTB_DEV bool attn_item(const AttnArgs &a, int item, AttnItem &it) {
   if (it.pos < 0 || it.pos >= a.rope_len || it.pos >= a.pt_stride * PAGE) { it.bad_pos = true; return false; }
   it.L = it.pos + 1;
   it.npages = (it.L + PAGE - 1) / PAGE;
-  int nsp = min(a.max_splits, (it.npages + a.min_pps - 1) / a.min_pps);
-  const int pps = (it.npages + nsp - 1) / nsp;
+  const int pps = attn_pps(a, it.npages);
   it.nsp = (it.npages + pps - 1) / pps;
   if (it.sp >= it.nsp) return false;
   it.p_begin = it.sp * pps;
@@ -1578,53 +1681,172 @@ QTB_DEV bool attn_item(const AttnArgs &a, int item, AttnItem &it) {
   return true;
 }
 
-// Thread 0: bulk-copy pages [i0, i1) of the item's range into the page ring.
-QTB_DEV void attn_issue(const AttnArgs &a, const AttnItem &it, int i0, int i1, KCtx &kc, uint16_t *kvbuf) {
-  const int *pt = a.page_table + (size_t)it.b * a.pt_stride;
-  for (int i = i0; i < i1; i++) {
-    const unsigned ctr = kc.page_ctr + i;
-    const int buf = ctr % ATT_NBUF;
-    int page = __ldg(pt + it.p_begin + i);
-    if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
-    uint16_t *dstk = kvbuf + (size_t)buf * 2 * PAGE * HD;
-    const size_t off = (((size_t)page * a.n_kv + it.g) * PAGE) * HD;
-    mbar_arrive_expect_tx(kc.bars + buf, 2 * PAGE * HD * 2);
-    bulk_g2s(dstk, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
-    bulk_g2s(dstk + PAGE * HD, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
-    kc.att_issued = ctr + 1u;
+// Warp-wide, dynamic order: items of batch slot b are pre[b] .. pre[b+1]-1
+// (KV head major, then split); pre[B] = items in all.  Returns that count, or
+// -1 for a position outside the cache (nothing written then).
+QTB_DEV int attn_prefix(const AttnArgs &a, int B, AttnSmem *sm) {
+  const int lane = threadIdx.x & 31;
+  int run = 0;
+  bool bad = false;
+  for (int b0 = 0; b0 < B; b0 += 32) {
+    const int b = b0 + lane;
+    int cnt = 0;
+    if (b < B) {
+      const int pos = a.pos_ptr ? __ldcg(a.pos_ptr + b) : a.pos_const;
+      if (pos < 0 || pos >= a.rope_len || pos >= a.pt_stride * PAGE) {
+        bad = true;
+      } else {
+        const int np = (pos + PAGE) / PAGE;
+        const int pps = attn_pps(a, np);
+        cnt = a.n_kv * ((np + pps - 1) / pps);
+      }
+    }
+    int v = cnt;   // inclusive scan over the lanes
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    if (b < B) sm->pre[b] = run + v - cnt;
+    run += __shfl_sync(0xffffffffu, v, 31);
   }
+  if (__any_sync(0xffffffffu, bad)) return -1;
+  if (lane == 0) sm->pre[B] = run;
+  __syncwarp();
+  return run;
 }
 
-// Thread 0, before the grid barrier: issue the first pages of this CTA's first
-// attention item (older positions only; the newest token is patched in from
-// registers by the stage itself).  Returns the number of pages issued.
-QTB_CALL int attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem_attn) {
-  const int n_items = B * a.n_kv * a.max_splits;
-  if ((int)blockIdx.x >= n_items) return 0;
+// Dynamic-order item -> (slot, kv head, split); item < pre[B].
+QTB_DEV void attn_item_dyn(const AttnArgs &a, int B, int item, const AttnSmem *sm, AttnItem &it) {
+  int lo = 0, hi = B;   // pre[lo] <= item < pre[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (sm->pre[mid] <= item) lo = mid; else hi = mid;
+  }
+  it.bad_pos = false;
+  it.b = lo;
+  const int r = item - sm->pre[lo];
+  const int nsp = (sm->pre[lo + 1] - sm->pre[lo]) / a.n_kv;
+  it.g = r / nsp;
+  it.sp = r - it.g * nsp;
+  it.pos = a.pos_ptr ? __ldcg(a.pos_ptr + it.b) : a.pos_const;
+  it.L = it.pos + 1;
+  it.npages = (it.L + PAGE - 1) / PAGE;
+  const int pps = attn_pps(a, it.npages);
+  it.nsp = nsp;
+  it.p_begin = it.sp * pps;
+  it.p_end = min(it.npages, it.p_begin + pps);
+}
+
+// Take the next work item of a dynamic attention stage (one thread).
+QTB_DEV int attn_take(KCtx &kc) { return (int)(atomicAdd(&kc.ctl->att_work, 1u) - kc.att_base); }
+
+// Bulk-copy page i of the item's range into its ring buffer (one thread; the
+// caller records kc.att_issued).
+QTB_DEV void attn_issue1(const AttnArgs &a, const AttnItem &it, int i, KCtx &kc, char *smem) {
+  const int nb = a.nbuf;
+  const unsigned ctr = kc.page_ctr + i;
+  const int buf = ctr % nb;
+  int page = __ldg(a.page_table + (size_t)it.b * a.pt_stride + it.p_begin + i);
+  if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
+  uint16_t *dstk = att_buf(smem, buf);
+  const size_t off = (((size_t)page * a.n_kv + it.g) * PAGE) * HD;
+  mbar_arrive_expect_tx(kc.bars + buf, ATT_PAGE_BYTES);
+  bulk_g2s(dstk, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
+  bulk_g2s(dstk + PAGE * HD, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
+}
+
+// Warp-wide: bulk-copy pages [i0, i1) (i1 - i0 <= 32) of the item, one per lane.
+QTB_DEV void attn_issue(const AttnArgs &a, const AttnItem &it, int i0, int i1, KCtx &kc, char *smem) {
+  const int lane = threadIdx.x & 31;
+  if (i0 >= i1) return;
+  if (lane < i1 - i0) {
+    // the buffers were last touched through the generic proxy
+    asm volatile("fence.proxy.async;" ::: "memory");
+    attn_issue1(a, it, i0 + lane, kc, smem);
+  }
+  __syncwarp();
+  if (lane == 0) kc.att_issued = kc.page_ctr + i1;
+  __syncwarp();
+}
+
+// Warp 0, before the grid barrier: take this CTA's first item of the coming
+// attention stage and bulk-copy its first pages (older positions only; the
+// newest token is patched in from registers by the stage itself).  Sets
+// kc.att_pre to the pages issued.
+QTB_CALL void attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem) {
+  const int lane = threadIdx.x & 31;
+  AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem + SM_X_OFF);
   AttnItem it;
-  if (!attn_item(a, blockIdx.x, it)) return 0;
-  const int n = min(it.p_end - it.p_begin, ATT_NBUF);
-  fence_proxy_async();
-  attn_issue(a, it, 0, n, kc, reinterpret_cast<uint16_t *>(smem_attn + 2048));
-  return n;
+  if (a.dyn) {
+    const int tot = attn_prefix(a, B, sm);
+    if (tot < 0) return;   // the stage reports it
+    int item = 0;
+    if (lane == 0) item = attn_take(kc);
+    item = __shfl_sync(0xffffffffu, item, 0);
+    if (lane == 0) { kc.att_first = item; kc.att_tot = tot; }
+    __syncwarp();
+    if (item >= tot) return;
+    attn_item_dyn(a, B, item, sm, it);
+  } else {
+    const int n_items = B * a.n_kv * a.max_splits;
+    if ((int)blockIdx.x >= n_items || !attn_item(a, blockIdx.x, it)) return;
+  }
+  const int n = min(it.p_end - it.p_begin, a.nbuf);
+  if (lane == 0) kc.att_nbuf = a.nbuf;
+  attn_issue(a, it, 0, n, kc, smem);
+  if (lane == 0) kc.att_pre = n;
+  __syncwarp();
 }
 
-__device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KCtx &kc) {
+__device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_base, KCtx &kc) {
+  char *smem = smem_base + SM_X_OFF;
   AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem);
-  uint16_t *kvbuf = reinterpret_cast<uint16_t *>(smem + 2048);   // ATT_NBUF x [K 16x128 | V 16x128]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q_dim = a.n_heads * HD, kv_dim = a.n_kv * HD;
-  const int n_items = B * a.n_kv * a.max_splits;
+  const int NB = a.nbuf;
+
+  // ---- this CTA's first item ----
+  int n_items, item;
+  if (a.dyn) {
+    if (kc.att_first < 0) {   // not taken before the barrier
+      if (warp == 0) {
+        const int tot = attn_prefix(a, B, sm);
+        if (lane == 0) {
+          sm->flag = tot;
+          if (tot >= 0) sm->next = attn_take(kc);
+        }
+      }
+      __syncthreads();
+      n_items = sm->flag;
+      item = sm->next;
+      if (n_items < 0) {
+        if (threadIdx.x == 0) raise_err(kc, ERR_BAD_POS, -1);
+        return;
+      }
+    } else {
+      n_items = kc.att_tot;
+      item = kc.att_first;
+    }
+  } else {
+    n_items = B * a.n_kv * a.max_splits;
+    item = blockIdx.x;
+  }
+  __syncthreads();   // every thread has read the first item before it changes
+  if (threadIdx.x == 0) { kc.att_first = -1; kc.att_nbuf = NB; }
 
   bool first = true;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+  while (item < n_items) {
     AttnItem it;
-    if (!attn_item(a, item, it)) {
+    if (a.dyn) {
+      attn_item_dyn(a, B, item, sm, it);
+    } else if (!attn_item(a, item, it)) {
       if (it.bad_pos) {
         if (threadIdx.x == 0) raise_err(kc, ERR_BAD_POS, it.pos);
         return;
       }
       first = false;
+      item += gridDim.x;
       continue;
     }
     const int b = it.b, g = it.g, sp = it.sp, pos = it.pos, L = it.L, npages = it.npages, nsp = it.nsp;
@@ -1632,12 +1854,14 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
     const bool owns_new = (p_end == npages);
     const int *pt = a.page_table + (size_t)b * a.pt_stride;
     // pages first (the ones prefetched before the barrier are already in flight)
-    if (threadIdx.x == 0) {
+    if (warp == 7) {
       const int pre = first ? kc.att_pre : 0;
-      fence_proxy_async();
-      attn_issue(a, it, pre, min(p_end - p_begin, ATT_NBUF), kc, kvbuf);
-      kc.att_pre = 0;
+      attn_issue(a, it, pre, min(p_end - p_begin, NB), kc, smem_base);
+      if (lane == 0) kc.att_pre = 0;
     }
+    // dynamic order: take the next item now (the atomic's latency hides behind
+    // this one), from a warp that is idle in the prologue
+    if (a.dyn && threadIdx.x == 4 * 32) sm->next = attn_take(kc);
     first = false;
     ckpt(kc, 0);
 
@@ -1683,10 +1907,7 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
         for (int i = 0; i < 4; i++) dst[lane + 32 * i] = (uint16_t)f32_to_bf16_trunc(v[i]);
       }
     }
-    if (threadIdx.x == 0) {
-      sm->m[0] = sm->m[1] = -INFINITY;
-      sm->l[0] = sm->l[1] = 0.f;
-    }
+    if (threadIdx.x < ATT_NBUF_MAX) sm->cons[threadIdx.x] = 0u;
     __syncthreads();
     if (owns_new && threadIdx.x < 32) {
       const int page = __ldg(pt + pos / PAGE);
@@ -1703,114 +1924,137 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
     }
     if (__syncthreads_or(kc.local_err)) return;
     ckpt(kc, 1);
+    const int next = a.dyn ? sm->next : item + (int)gridDim.x;
+    if (a.dyn && warp == 4 && next < n_items) {
+      // the next item's first pages into L2 while this one runs
+      AttnItem nx;
+      attn_item_dyn(a, B, next, sm, nx);
+      const int nn = min(nx.p_end - nx.p_begin, NB);
+      if (lane < nn) {
+        int page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + lane);
+        if (page >= 0 && page < a.n_pages) {
+          const size_t off = (((size_t)page * a.n_kv + nx.g) * PAGE) * HD;
+          prefetch_l2(a.kpool + off, PAGE * HD * 2);
+          prefetch_l2(a.vpool + off, PAGE * HD * 2);
+        }
+      }
+    }
 
     // ---- main loop over this split's pages ----
+    // Warp w handles head h = w & 1 of the pages i = w / 2 (mod 4), so four
+    // pages are in work at once, each by the two warps of its GQA group; every
+    // warp keeps its own online softmax (running max m, sum l, output dims
+    // 4 lane .. 4 lane + 3), combined across warps in warp order at the end
+    // (deterministic).  A page buffer is refilled (page i + NB, which the same
+    // pair handles) by the second of its two warps to finish with it.
     const int n = p_end - p_begin;
     const int tid = threadIdx.x;
-    const int hh = tid >> 7, d = tid & 127;
-    float acc = 0.f;
-    for (int i = 0; i < n; i++) {
+    const int h = warp & 1, pw = warp >> 1;
+    const int t = lane & 15, half = lane >> 4;
+    float m_w = -INFINITY, l_w = 0.f, acc4[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = pw; i < n; i += NWARPS / 2) {
       const unsigned ctr = kc.page_ctr + i;
-      const int buf = ctr % ATT_NBUF;
-      const uint32_t parity = (ctr / ATT_NBUF) & 1u;
-      // every thread observes the phase flip, which makes the bulk-copied
-      // bytes visible to it
-      const bool landed = mbar_wait(kc.bars + buf, parity, WAIT_LIMIT_CYCLES);
-      if (__syncthreads_or(!landed)) {   // copies still in flight are drained on the way out
-        if (tid == 0) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-        return;
+      const int buf = ctr % NB;
+      // every lane observes the phase flip, which makes the bulk-copied bytes
+      // visible to it
+      if (!mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES)) {
+        if (lane == 0) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+        break;
       }
-      uint16_t *kb = kvbuf + (size_t)buf * 2 * PAGE * HD;
+      uint16_t *kb = att_buf(smem_base, buf);
       uint16_t *vb = kb + PAGE * HD;
       const int pg = p_begin + i;
       const int ntok = min(PAGE, L - pg * PAGE);
       if (pg == npages - 1 && owns_new) {
-        // The newest token is taken from registers/smem, not from the copy.
+        // the newest token comes from shared memory, not from the copy (both
+        // warps of the page write the same bytes)
         const int slot = pos % PAGE;
-        if (tid < HD) { kb[slot * HD + tid] = sm->knew[tid]; vb[slot * HD + tid] = sm->vnew[tid]; }
-        __syncthreads();
-      }
-      // scores: warp w -> tokens 2w, 2w+1; lane -> dims 4*lane .. 4*lane+3
-      {
-        float part[2][2];
-#pragma unroll
-        for (int tt = 0; tt < 2; tt++) {
-          const int tok = 2 * warp + tt;
-          const uint2 kv = *reinterpret_cast<const uint2 *>(kb + tok * HD + lane * 4);
-          const float k0 = bf16lo(kv.x), k1 = bf16hi(kv.x), k2 = bf16lo(kv.y), k3 = bf16hi(kv.y);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; h2++) {
-            const float *qq = sm->q[h2] + lane * 4;
-            part[tt][h2] = qq[0] * k0 + qq[1] * k1 + qq[2] * k2 + qq[3] * k3;
-          }
-        }
-#pragma unroll
-        for (int tt = 0; tt < 2; tt++)
-#pragma unroll
-          for (int h2 = 0; h2 < 2; h2++) part[tt][h2] = warp_sum(part[tt][h2]);
-        if (lane == 0) {
-#pragma unroll
-          for (int tt = 0; tt < 2; tt++) {
-            const int tok = 2 * warp + tt;
-#pragma unroll
-            for (int h2 = 0; h2 < 2; h2++) sm->sc[h2][tok] = (tok < ntok) ? part[tt][h2] * a.scale : -INFINITY;
-          }
-        }
-      }
-      __syncthreads();
-      if (tid < 32) {
-        const int h2 = tid >> 4, tok = tid & 15;
-        const float s = sm->sc[h2][tok];
-        float mx = s;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        const float m_old = sm->m[h2];
-        const float m_new = fmaxf(m_old, mx);
-        const float p = (tok < ntok) ? expf(s - m_new) : 0.f;
-        float ps = p;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-        sm->p[h2][tok] = p;
+        *reinterpret_cast<uint2 *>(kb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
+        *reinterpret_cast<uint2 *>(vb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
         __syncwarp();
-        if (tok == 0) {
-          const float corr = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-          sm->corr[h2] = corr;
-          sm->l[h2] = sm->l[h2] * corr + ps;
-          sm->m[h2] = m_new;
-        }
       }
-      __syncthreads();
-      {
-        float s = 0.f;
+      // score of token t: lanes t and t + 16 each take half of the 128 dims,
+      // walking them from a lane-dependent start so the 32 lanes hit 32 banks
+      float sdot = 0.f;
+      const float *qh = sm->q[h] + half * 64;
+      const uint16_t *kr = kb + t * HD + half * 64;
+#pragma unroll 8
+      for (int jj = 0; jj < 32; jj++) {
+        const int j = (jj + t + 16 * half) & 31;
+        const uint32_t kk = *reinterpret_cast<const uint32_t *>(kr + 2 * j);
+        const float2 qq = *reinterpret_cast<const float2 *>(qh + 2 * j);
+        sdot = fmaf(qq.x, bf16lo(kk), sdot);
+        sdot = fmaf(qq.y, bf16hi(kk), sdot);
+      }
+      sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+      const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
+      float mx = sc;
 #pragma unroll
-        for (int tok = 0; tok < PAGE; tok++) {
-          const float vv = __uint_as_float(((uint32_t)vb[tok * HD + d]) << 16);
-          s = fmaf(sm->p[hh][tok], vv, s);
-        }
-        acc = acc * sm->corr[hh] + s;
+      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float m_new = fmaxf(m_w, mx);
+      const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
+      float ps = pr;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
+      l_w = l_w * corr + ps;
+      m_w = m_new;
+#pragma unroll
+      for (int e = 0; e < 4; e++) acc4[e] *= corr;
+      // slots past the sequence end hold whatever the pool has there: skip them
+#pragma unroll
+      for (int tt = 0; tt < PAGE; tt++) {
+        if (tt >= ntok) break;
+        const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+        const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+        acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+        acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+        acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+        acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
       }
-      __syncthreads();
-      if (tid == 0 && i + ATT_NBUF < n) {
-        int page = __ldg(pt + p_begin + i + ATT_NBUF);
-        if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
-        const size_t off = (((size_t)page * a.n_kv + g) * PAGE) * HD;
-        mbar_arrive_expect_tx(kc.bars + buf, 2 * PAGE * HD * 2);
-        bulk_g2s(kb, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
-        bulk_g2s(vb, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
-        kc.att_issued = ctr + ATT_NBUF + 1u;
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();   // this warp's reads of the buffer before its count
+        const bool second = atomicAdd(sm->cons + buf, 1u) & 1u;
+        if (second && i + NB < n) {
+          // both warps are done with this buffer: bring page i + NB
+          __threadfence_block();
+          fence_proxy_async_smem();
+          attn_issue1(a, it, i + NB, kc, smem_base);
+          atomicMax(&kc.att_issued, ctr + NB + 1u);
+        }
       }
     }
-    if (tid == 0) kc.page_ctr += n;   // the loop's last barrier has passed
+    // per-warp states -> per-head totals, in warp order
+    float *s_acc = reinterpret_cast<float *>(smem + ATT_COMB_OFF);   // [NWARPS][HD]
+    float *s_ml = s_acc + NWARPS * HD;                                // [NWARPS][2]
+    *reinterpret_cast<float4 *>(s_acc + warp * HD + 4 * lane) = make_float4(acc4[0], acc4[1], acc4[2], acc4[3]);
+    if (lane == 0) { s_ml[2 * warp] = m_w; s_ml[2 * warp + 1] = l_w; }
+    if (__syncthreads_or(kc.local_err)) return;   // copies still in flight are drained on the way out
+    if (tid == 0) kc.page_ctr += n;
+    const int hh = tid >> 7, d = tid & 127;
+    float Mh = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < NWARPS / 2; q++) Mh = fmaxf(Mh, s_ml[2 * (2 * q + hh)]);
+    float Lh = 0.f, acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < NWARPS / 2; q++) {
+      const int w = 2 * q + hh;
+      const float mw = s_ml[2 * w];
+      const float e = (mw == -INFINITY) ? 0.f : expf(mw - Mh);
+      Lh += s_ml[2 * w + 1] * e;
+      acc += s_acc[w * HD + d] * e;
+    }
     ckpt(kc, 2);
 
     // ---- output / split combine ----
     const int head = 2 * g + hh;
     if (nsp == 1) {
-      __stcg(a.out + (size_t)b * a.ld_out + head * HD + d, acc * (1.0f / sm->l[hh]));
+      __stcg(a.out + (size_t)b * a.ld_out + head * HD + d, acc * (1.0f / Lh));
     } else {
       float *wsi = a.ws + ((((size_t)b * a.n_kv + g) * a.max_splits + sp) * 2 + hh) * (HD + 2);
       __stcg(wsi + d, acc);
-      if (d == 0) { __stcg(wsi + HD, sm->m[hh]); __stcg(wsi + HD + 1, sm->l[hh]); }
+      if (d == 0) { __stcg(wsi + HD, Mh); __stcg(wsi + HD + 1, Lh); }
       __threadfence();
       __syncthreads();
       if (tid == 0) sm->flag = (atomicAdd(a.sem + (size_t)b * a.n_kv + g, 1u) == (unsigned)(nsp - 1));
@@ -1832,7 +2076,11 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem, KC
       }
     }
     __syncthreads();
+    item = next;
   }
+  // every CTA took exactly one item past the end: the counter now stands at
+  // the next dynamic stage's base
+  if (a.dyn && threadIdx.x == 0) kc.att_base += (unsigned)n_items + gridDim.x;
 }
 
 // ============================================================ misc stages ==
@@ -1923,10 +2171,10 @@ QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
         if ((int)(w.x - target) >= 0) break;
         const int slot = (int)(nxt % NDESC);
         if (phase == 0) {
-          if (lane == 0 && mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u)) {
-            const Stage *nx = kc.dring + slot;
-            if (nx->kind == ST_ATTN) kc.att_pre = attn_prefetch(nx->a, nx->B, kc, smem + SM_X_OFF);
-          }
+          // every lane tests the descriptor's barrier itself (that makes the
+          // bulk-copied descriptor visible to it)
+          const bool landed = __all_sync(0xffffffffu, mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u));
+          if (landed && kc.dring[slot].kind == ST_ATTN) attn_prefetch(kc.dring[slot].a, kc.dring[slot].B, kc, smem);
           __syncwarp();
           phase = 1;
         } else if (phase == 1) {
@@ -1966,7 +2214,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, int n_stages, int n_iters, Ctl *ctl,
               long long *trace) {
   extern __shared__ __align__(128) char smem[];
-  __shared__ __align__(8) uint64_t bars[ATT_NBUF];
+  __shared__ __align__(8) uint64_t bars[ATT_NBUF_MAX];
   __shared__ __align__(8) uint64_t wbars[NWSLOT];
   __shared__ __align__(8) uint64_t dbars[NDESC];
   __shared__ Stage dring[NDESC];   // stage descriptors, NDESC - 1 stages ahead
@@ -1979,6 +2227,10 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     kc.wfill = 0;
     kc.att_pre = 0;
     kc.att_issued = 0;
+    kc.att_nbuf = ATT_NBUF;
+    kc.att_base = 0;   // ctl->att_work is zeroed before the launch
+    kc.att_first = -1;
+    kc.att_tot = 0;
     kc.local_err = 0;
     kc.wbars = wbars;
     kc.pol_first = policy_evict_first();
@@ -2011,7 +2263,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     if (plan) bulk_g2s(pring + slot, plan + (size_t)si * gridDim.x + blockIdx.x, sizeof(V2Plan), dbars + slot);
   };
   if (threadIdx.x == 0) {
-    for (int i = 0; i < ATT_NBUF; i++) mbar_init(bars + i, 1);
+    for (int i = 0; i < ATT_NBUF_MAX; i++) mbar_init(bars + i, 1);
     for (int i = 0; i < NWSLOT; i++) mbar_init(wbars + i, 1);
     for (int i = 0; i < NDESC; i++) mbar_init(dbars + i, 1);
     mbar_init(&pbar, 1);
@@ -2035,7 +2287,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
       const int B = st->B;
       switch (st->kind) {
         case ST_GEMV: gemv_stage(st->g, B, smem, kc); break;
-        case ST_ATTN: attn_stage(st->a, B, smem + SM_X_OFF, kc); break;
+        case ST_ATTN: attn_stage(st->a, B, smem, kc); break;
         case ST_EMBED: embed_stage(st->e, B, kc); break;
         case ST_NORM: norm_stage(st->n, B); break;
         case ST_POS_INC:

@@ -77,8 +77,12 @@ def make_attention_case(rng, B, pos, n_pages, nh=16, nkv=8, permute=True):
     return qkv, kp, vp, pt, qn, kn, cs, sn
 
 
+_MANY = [int(v) for v in np.random.default_rng(77).integers(0, 1500, 24)]
+
+
+# the last two cases have more items than CTAs: CTAs take them in dynamic order
 @pytest.mark.parametrize("pos,max_splits", [([0, 15, 16, 37], 4), ([200, 1, 513, 2047], 8), ([4095], 32),
-                                            ([63, 64], 1)])
+                                            ([63, 64], 1), (_MANY, 1), (_MANY, 8)])
 def test_attention_append_matches_oracle(have_gpu, pos, max_splits):
     rng = np.random.default_rng(sum(pos) + max_splits)
     B, nh, nkv, hd, eps = len(pos), 16, 8, 128, 1e-6
@@ -113,6 +117,29 @@ def test_attention_append_matches_oracle(have_gpu, pos, max_splits):
                 assert np.array_equal(vp[page, :, slot], vp0[page, :, slot])
 
 
+def test_attention_ignores_pool_slots_past_the_end(have_gpu):
+    # slots after the newest token hold NaN in the pool: they must not reach
+    # the output (neither through the scores nor through P.V)
+    rng = np.random.default_rng(11)
+    pos = [5, 37, 70]
+    B, nh, nkv, hd, eps = len(pos), 16, 8, 128, 1e-6
+    n_pages = sum(p // 16 + 1 for p in pos) + 2
+    qkv, kp, vp, pt, qn, kn, cs, sn = make_attention_case(rng, B, pos, n_pages)
+    nan = np.uint16(0x7FC0)
+    for b in range(B):
+        page = pt[b, pos[b] // 16]
+        kp[page, :, pos[b] % 16 + 1:, :] = nan
+        vp[page, :, pos[b] % 16 + 1:, :] = nan
+    out = Q.attention(qkv, nh, nkv, qn, kn, eps, cs, sn, kp, vp, pt, np.array(pos, np.int32), 2)
+    assert np.all(np.isfinite(out))
+    for b in range(B):
+        p = pos[b]
+        q = O.rope_neox(O.rms_norm_per_head(qkv[b, :nh * hd], qn, nh, hd, eps), nh, hd, cs, sn, p)
+        K, V = O.gather_pages(kp, vp, pt[b], p + 1)
+        ref = O.attention_bf16kv(q, K, V, nh, nkv, hd, p + 1)
+        assert rel_l2(out[b], ref) < 1e-5, (b, rel_l2(out[b], ref))
+
+
 def test_attention_rejects_bad_page_table(have_gpu):
     rng = np.random.default_rng(4)
     qkv, kp, vp, pt, qn, kn, cs, sn = make_attention_case(rng, 1, [40], 8)
@@ -136,9 +163,14 @@ def test_backend_vtable_matmat_bf16(have_gpu):
     ctx = L.qwen_cuda_init()
     assert ctx
     rng = np.random.default_rng(31)
+    # the resident-weight cache is keyed by the host pointer, as in the
+    # reference, whose weights live as long as the process: every matrix stays
+    # alive here so no later one can reuse a freed address
+    keep = []
     try:
         for rows, cols, B in [(100, 200, 1), (256, 1024, 3), (72, 640, 64)]:
             W = Q.bf16_from_f32(rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
+            keep.append(W)
             Wf = O.f32_from_bf16(W).astype(np.float64)
             for call in range(2):
                 X = rng.standard_normal((cols, B), dtype=np.float32)
@@ -148,6 +180,7 @@ def test_backend_vtable_matmat_bf16(have_gpu):
                 assert rel_l2(Y, Wf @ X.astype(np.float64)) < GEMV_TOL, (rows, cols, B, call)
         x = rng.standard_normal(200, dtype=np.float32)
         W = Q.bf16_from_f32(rng.standard_normal((100, 200), dtype=np.float32) * np.float32(0.02))
+        keep.append(W)
         y = np.empty(100, np.float32)
         L.qwen_cuda_matvec_bf16(ctx, y.ctypes.data, W.ctypes.data, x.ctypes.data, 100, 200)
         assert rel_l2(y, O.f32_from_bf16(W).astype(np.float64) @ x) < GEMV_TOL
