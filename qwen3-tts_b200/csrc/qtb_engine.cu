@@ -906,7 +906,10 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
     if (max_ctx > e->talker.rope_len) max_ctx = e->talker.rope_len;
   }
   s->max_ctx = max_ctx;
-  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess ||
+  // A blocking stream: set-up work (memsets, cudaMemcpy from pageable host
+  // memory, which may return before its DMA has landed) goes through the
+  // legacy default stream, and the session's kernels must run behind it.
+  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamDefault) != cudaSuccess ||
       cudaEventCreate(&s->ev0) != cudaSuccess || cudaEventCreate(&s->ev1) != cudaSuccess) {
     rc = set_err(QTB_E_CUDA, "stream/event creation failed");
     goto fail;
@@ -1277,7 +1280,7 @@ static int run_single_stage(MiniRun &mr, const Stage &S) {
 extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols, const float *x, int batch, float *y) {
   if (!w || !x || !y || batch < 1 || batch > 64) return set_err(QTB_E_INVALID, "bad argument");
   MiniRun mr;
-  CUDA_TRY(cudaStreamCreateWithFlags(&mr.st, cudaStreamNonBlocking));
+  CUDA_TRY(cudaStreamCreateWithFlags(&mr.st, cudaStreamDefault));   // behind the legacy-stream uploads
   int dev = 0, nsm = 0;
   CUDA_TRY(cudaGetDevice(&dev));
   CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
@@ -1327,7 +1330,7 @@ extern "C" int qtb_attention_host(const float *qkv, int batch, int n_heads, int 
     }
   }
   MiniRun mr;
-  CUDA_TRY(cudaStreamCreateWithFlags(&mr.st, cudaStreamNonBlocking));
+  CUDA_TRY(cudaStreamCreateWithFlags(&mr.st, cudaStreamDefault));   // behind the legacy-stream uploads
   const int qd = n_heads * HD, kvd = n_kv * HD, qkvd = qd + 2 * kvd;
   const size_t pool = (size_t)n_pages * n_kv * PAGE * HD;
   int rc;
@@ -1653,7 +1656,7 @@ extern "C" void *qwen_cuda_init(void) {
     rc = 1;
   } else {
     c->nsm = p.multiProcessorCount;
-    if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess ||
+    if (cudaStreamCreateWithFlags(&c->st, cudaStreamDefault) != cudaSuccess ||   // behind legacy-stream uploads
         cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
         c->weights.alloc((void **)&c->ctl, sizeof(Ctl)) || c->weights.alloc((void **)&c->dstage, sizeof(Stage)) ||
         c->weights.alloc((void **)&c->dplan, (size_t)c->nsm * sizeof(V2Plan)))

@@ -161,7 +161,6 @@ struct KCtx {
   unsigned epoch;
   unsigned page_ctr;    // K/V page buffers consumed so far (mbarrier phase source)
   unsigned wfill;       // weight-ring slot fills consumed so far (mbarrier phase source)
-  int att_pre;          // K/V pages already issued for the coming attention stage
   unsigned att_issued;  // K/V page copies issued so far (one past the last)
   int att_nbuf;         // page buffers of the attention stages of this program
   unsigned att_base;    // ctl->att_work at the start of the current dynamic attention stage
@@ -1741,11 +1740,10 @@ QTB_DEV void attn_item_dyn(const AttnArgs &a, int B, int item, const AttnSmem *s
 // Take the next work item of a dynamic attention stage (one thread).
 QTB_DEV int attn_take(KCtx &kc) { return (int)(atomicAdd(&kc.ctl->att_work, 1u) - kc.att_base); }
 
-// Bulk-copy page i of the item's range into its ring buffer (one thread; the
-// caller records kc.att_issued).
-QTB_DEV void attn_issue1(const AttnArgs &a, const AttnItem &it, int i, KCtx &kc, char *smem) {
+// Bulk-copy page i of the item's range into the ring buffer of stream
+// position ctr (one thread; the caller records kc.att_issued).
+QTB_DEV void attn_issue1(const AttnArgs &a, const AttnItem &it, int i, unsigned ctr, KCtx &kc, char *smem) {
   const int nb = a.nbuf;
-  const unsigned ctr = kc.page_ctr + i;
   const int buf = ctr % nb;
   int page = __ldg(a.page_table + (size_t)it.b * a.pt_stride + it.p_begin + i);
   if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
@@ -1763,7 +1761,7 @@ QTB_DEV void attn_issue(const AttnArgs &a, const AttnItem &it, int i0, int i1, K
   if (lane < i1 - i0) {
     // the buffers were last touched through the generic proxy
     asm volatile("fence.proxy.async;" ::: "memory");
-    attn_issue1(a, it, i0 + lane, kc, smem);
+    attn_issue1(a, it, i0 + lane, kc.page_ctr + i0 + lane, kc, smem);
   }
   __syncwarp();
   if (lane == 0) kc.att_issued = kc.page_ctr + i1;
@@ -1772,8 +1770,7 @@ QTB_DEV void attn_issue(const AttnArgs &a, const AttnItem &it, int i0, int i1, K
 
 // Warp 0, before the grid barrier: take this CTA's first item of the coming
 // attention stage and bulk-copy its first pages (older positions only; the
-// newest token is patched in from registers by the stage itself).  Sets
-// kc.att_pre to the pages issued.
+// newest token is patched in from registers by the stage itself).
 QTB_CALL void attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem) {
   const int lane = threadIdx.x & 31;
   AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem + SM_X_OFF);
@@ -1795,8 +1792,6 @@ QTB_CALL void attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem) {
   const int n = min(it.p_end - it.p_begin, a.nbuf);
   if (lane == 0) kc.att_nbuf = a.nbuf;
   attn_issue(a, it, 0, n, kc, smem);
-  if (lane == 0) kc.att_pre = n;
-  __syncwarp();
 }
 
 __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_base, KCtx &kc) {
@@ -1835,7 +1830,6 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
   __syncthreads();   // every thread has read the first item before it changes
   if (threadIdx.x == 0) { kc.att_first = -1; kc.att_nbuf = NB; }
 
-  bool first = true;
   while (item < n_items) {
     AttnItem it;
     if (a.dyn) {
@@ -1845,7 +1839,6 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
         if (threadIdx.x == 0) raise_err(kc, ERR_BAD_POS, it.pos);
         return;
       }
-      first = false;
       item += gridDim.x;
       continue;
     }
@@ -1853,16 +1846,16 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
     const int p_begin = it.p_begin, p_end = it.p_end;
     const bool owns_new = (p_end == npages);
     const int *pt = a.page_table + (size_t)b * a.pt_stride;
-    // pages first (the ones prefetched before the barrier are already in flight)
+    // pages first: the stream positions issued so far are a prefix (the hook
+    // before the barrier, or the previous item's refills, may have covered
+    // the first ones)
     if (warp == 7) {
-      const int pre = first ? kc.att_pre : 0;
-      attn_issue(a, it, pre, min(p_end - p_begin, NB), kc, smem_base);
-      if (lane == 0) kc.att_pre = 0;
+      const int done = (int)min(kc.att_issued - kc.page_ctr, (unsigned)NB);
+      attn_issue(a, it, done, min(p_end - p_begin, NB), kc, smem_base);
     }
     // dynamic order: take the next item now (the atomic's latency hides behind
     // this one), from a warp that is idle in the prologue
     if (a.dyn && threadIdx.x == 4 * 32) sm->next = attn_take(kc);
-    first = false;
     ckpt(kc, 0);
 
     // ---- prologue: QK RMSNorm + RoPE (+ KV append) ----
@@ -1925,28 +1918,28 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
     if (__syncthreads_or(kc.local_err)) return;
     ckpt(kc, 1);
     const int next = a.dyn ? sm->next : item + (int)gridDim.x;
-    if (a.dyn && warp == 4 && next < n_items) {
-      // the next item's first pages into L2 while this one runs
-      AttnItem nx;
+    // dynamic order: the next item's pages follow this one's in the stream, so
+    // buffers freed near the end of this item already take the next one's
+    // pages.  Only from an item of at least NB pages: then the refills cover
+    // the next item's first positions without a gap (the issued positions stay
+    // a prefix of the stream, which the next item's first issue relies on).
+    AttnItem nx;
+    int nx_n = 0;
+    if (a.dyn && next < n_items && p_end - p_begin >= NB) {
       attn_item_dyn(a, B, next, sm, nx);
-      const int nn = min(nx.p_end - nx.p_begin, NB);
-      if (lane < nn) {
-        int page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + lane);
-        if (page >= 0 && page < a.n_pages) {
-          const size_t off = (((size_t)page * a.n_kv + nx.g) * PAGE) * HD;
-          prefetch_l2(a.kpool + off, PAGE * HD * 2);
-          prefetch_l2(a.vpool + off, PAGE * HD * 2);
-        }
-      }
+      nx_n = nx.p_end - nx.p_begin;
     }
 
     // ---- main loop over this split's pages ----
-    // Warp w handles head h = w & 1 of the pages i = w / 2 (mod 4), so four
-    // pages are in work at once, each by the two warps of its GQA group; every
-    // warp keeps its own online softmax (running max m, sum l, output dims
-    // 4 lane .. 4 lane + 3), combined across warps in warp order at the end
-    // (deterministic).  A page buffer is refilled (page i + NB, which the same
-    // pair handles) by the second of its two warps to finish with it.
+    // Warp w handles head h = w & 1 of the item's pages i = w / 2 (mod 4), so
+    // four pages are in work at once, each by the two warps of its GQA group;
+    // every warp keeps its own online softmax (running max m, sum l, output
+    // dims 4 lane .. 4 lane + 3), combined across warps in warp order at the
+    // end.  The split of pages among warps depends on the item alone, so the
+    // result does not depend on which CTA ran it.  Page i sits in ring buffer
+    // (stream position) % NB; the second warp to finish with a buffer refills
+    // it with stream position + NB (this item's page i + NB, or a page of the
+    // next item).
     const int n = p_end - p_begin;
     const int tid = threadIdx.x;
     const int h = warp & 1, pw = warp >> 1;
@@ -2016,11 +2009,13 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
       if (lane == 0) {
         __threadfence_block();   // this warp's reads of the buffer before its count
         const bool second = atomicAdd(sm->cons + buf, 1u) & 1u;
-        if (second && i + NB < n) {
-          // both warps are done with this buffer: bring page i + NB
+        const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
+        if (second && (tgt < n || tgt - n < nx_n)) {
+          // both warps are done with this buffer: bring stream position ctr + NB
           __threadfence_block();
           fence_proxy_async_smem();
-          attn_issue1(a, it, i + NB, kc, smem_base);
+          if (tgt < n) attn_issue1(a, it, tgt, ctr + NB, kc, smem_base);
+          else attn_issue1(a, nx, tgt - n, ctr + NB, kc, smem_base);
           atomicMax(&kc.att_issued, ctr + NB + 1u);
         }
       }
@@ -2225,7 +2220,6 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     kc.epoch = 0;
     kc.page_ctr = 0;
     kc.wfill = 0;
-    kc.att_pre = 0;
     kc.att_issued = 0;
     kc.att_nbuf = ATT_NBUF;
     kc.att_base = 0;   // ctl->att_work is zeroed before the launch

@@ -134,28 +134,40 @@ def test_paged_equals_identity_pages_and_batch_equals_single(have_gpu, tiny):
 
 def test_large_batch_matches_single_sessions(have_gpu, tiny):
     # 24 slots with mixed cache lengths: the large-batch GEMV path and the
-    # dynamically scheduled attention against one B=1 session per slot
+    # dynamically scheduled attention against one B=1 session per slot.  Twice,
+    # on fresh sessions: the results must repeat bit for bit (work items go to
+    # CTAs in a run-dependent order, and the KV uploads must land before the
+    # first step reads them)
     cfg, m, path = tiny
     eng = Q.Engine(Q.HostModel(cfg, m.talker, m.codec_head, m.codec_embedding), Q.FMT_BF16)
     B, steps = 24, 3
-    rng = np.random.default_rng(9)
-    lens = rng.integers(1, 700, B)
-    big = Q.Session(eng, B, 1024)
-    singles = []
-    for b in range(B):
-        L = int(lens[b])
-        kv = Q.bf16_from_f32(rng.standard_normal((cfg.layers, L, 1024), dtype=np.float32))
-        big.upload_kv(b, kv, kv, L, L)
-        one = Q.Session(eng, 1, 1024)
-        one.upload_kv(0, kv, kv, L, L)
-        singles.append(one)
-    for t in range(steps):
-        E = (0.1 * rng.standard_normal((B, cfg.hidden))).astype(np.float32)
-        pos = (lens + t).astype(np.int32)
-        y = big.talker_step(E, pos)
+    runs = []
+    for rep in range(2):
+        rng = np.random.default_rng(9)
+        lens = rng.integers(1, 700, B)
+        big = Q.Session(eng, B, 1024)
+        singles = []
         for b in range(B):
-            s = singles[b].talker_step(E[b], int(pos[b]))
-            assert rel_l2(s[0], y[b]) < 1e-3, (t, b, rel_l2(s[0], y[b]))
+            L = int(lens[b])
+            kv = Q.bf16_from_f32(rng.standard_normal((cfg.layers, L, 1024), dtype=np.float32))
+            big.upload_kv(b, kv, kv, L, L)
+            one = Q.Session(eng, 1, 1024)
+            one.upload_kv(0, kv, kv, L, L)
+            singles.append(one)
+        outs = []
+        for t in range(steps):
+            E = (0.1 * rng.standard_normal((B, cfg.hidden))).astype(np.float32)
+            pos = (lens + t).astype(np.int32)
+            y = big.talker_step(E, pos)
+            s1 = np.stack([singles[b].talker_step(E[b], int(pos[b]))[0] for b in range(B)])
+            for b in range(B):
+                assert rel_l2(s1[b], y[b]) < 1e-3, (rep, t, b, rel_l2(s1[b], y[b]))
+            outs.append((y, s1))
+        runs.append(outs)
+        del big, singles
+    for t in range(steps):
+        assert np.array_equal(runs[0][t][0], runs[1][t][0]), t
+        assert np.array_equal(runs[0][t][1], runs[1][t][1]), t
 
 
 def test_kv_upload_download_roundtrip(have_gpu, tiny):
