@@ -403,44 +403,51 @@ QTB_DEV void stage_x(const GemvArgs &a, int B, int ent, int k0, int kslice, cons
   const int ksteps = kslice >> 4;
   const int total = ksteps * nch * ent;
   if (ent == 32 && P == 2) {
-    // large batches: entry e = (q * nch + j) * 32 + lane, so a thread's lane is
-    // fixed and (q, j) steps by NWARPS entries; four entries' loads in flight
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gid = lane >> 2, tig = lane & 3;
-    const int lg = 31 - __clz(nch);   // nch is a power of two
-    const int nqj = ksteps * nch;
-    for (int qj0 = warp; qj0 < nqj; qj0 += 4 * NWARPS) {
-      float2 p0[4], p1[4];
-      int bb[4], kk[4];
+    // large batches: coalesced float4 reads of each row's slice (eight in
+    // flight per thread); a float4 holds two k pairs, each written as its two
+    // parts into the fragment word that carries it (entry e = (q * nch + j) *
+    // 32 + lane with column 8 j + gid = 2 b + part)
+    const int nq4 = kslice >> 2, total4 = B * nq4;
+    uint32_t *w = reinterpret_cast<uint32_t *>(s_xf);
+    for (int base = threadIdx.x; base < total4; base += 8 * NTHREADS) {
+      float4 v[8], nw[8];
 #pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const int qj = qj0 + u * NWARPS;
-        const int j = qj & (nch - 1), q = qj >> lg;
-        const int b = (8 * j + gid) >> 1;
-        const int k = k0 + 16 * q + (perm4 ? 4 : 2) * tig, k2 = k + (perm4 ? 2 : 8);
-        bb[u] = (qj < nqj && b < B) ? b : -1;
-        kk[u] = k;
-        p0[u] = p1[u] = make_float2(0.f, 0.f);
-        if (bb[u] >= 0) {
-          const float *xb = a.x + (size_t)b * a.ldx;
-          p0[u] = __ldcg(reinterpret_cast<const float2 *>(xb + k));
-          p1[u] = __ldcg(reinterpret_cast<const float2 *>(xb + k2));
+      for (int u = 0; u < 8; u++) {
+        const int idx = base + u * NTHREADS;
+        if (idx < total4) {
+          const int b = idx / nq4, c = idx - b * nq4;
+          v[u] = ld_cg4(a.x + (size_t)b * a.ldx + k0 + 4 * c);
+          if (a.norm_w) nw[u] = __ldg(reinterpret_cast<const float4 *>(a.norm_w + k0 + 4 * c));
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const int qj = qj0 + u * NWARPS;
-        if (qj >= nqj) break;
-        uint32_t r0 = 0, r1 = 0;
-        if (bb[u] >= 0) {
-          const int b = bb[u], k = kk[u], k2 = k + (perm4 ? 2 : 8), lo = gid & 1;
-          const float v0 = norm_in(a, s_inv, b, k, p0[u].x), v1 = norm_in(a, s_inv, b, k + 1, p0[u].y);
-          const float v2 = norm_in(a, s_inv, b, k2, p1[u].x), v3 = norm_in(a, s_inv, b, k2 + 1, p1[u].y);
-          r0 = split_pack<F16>(v0, v1, lo);
-          r1 = split_pack<F16>(v2, v3, lo);
+      for (int u = 0; u < 8; u++) {
+        const int idx = base + u * NTHREADS;
+        if (idx >= total4) break;
+        const int b = idx / nq4, c = idx - b * nq4;
+        float x4[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        if (a.norm_w) {
+          const float r = s_inv[b];
+          x4[0] = (x4[0] * r) * nw[u].x; x4[1] = (x4[1] * r) * nw[u].y;
+          x4[2] = (x4[2] * r) * nw[u].z; x4[3] = (x4[3] * r) * nw[u].w;
         }
-        s_xf[qj * 32 + lane] = make_uint2(r0, r1);
+#pragma unroll
+        for (int pr = 0; pr < 2; pr++) {
+          const int kp = 2 * c + pr, q = kp >> 3, pi = kp & 7;
+          const int tg = perm4 ? (pi >> 1) : (pi & 3), which = perm4 ? (pi & 1) : (pi >> 2);
+#pragma unroll
+          for (int lo = 0; lo < 2; lo++) {
+            const int col = 2 * b + lo, jj = col >> 3, gg = col & 7;
+            w[(((q * nch + jj) * 32) + gg * 4 + tg) * 2 + which] = split_pack<F16>(x4[2 * pr], x4[2 * pr + 1], lo);
+          }
+        }
       }
+    }
+    // MMA columns past the last batch row are zero
+    const int pad = 8 * nch - 2 * B;
+    for (int idx = threadIdx.x; idx < ksteps * pad * 4; idx += NTHREADS) {
+      const int tg = idx & 3, r = idx >> 2, q = r / pad, col = 2 * B + (r - q * pad);
+      s_xf[(q * nch + (col >> 3)) * 32 + (col & 7) * 4 + tg] = make_uint2(0u, 0u);
     }
   } else
   for (int e = threadIdx.x; e < total; e += NTHREADS) {
