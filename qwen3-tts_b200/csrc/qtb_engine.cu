@@ -445,13 +445,18 @@ extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_eng
   e->n_sm = prop.multiProcessorCount;
   {
     // 2-CTA clusters for the whole grid: only if all n_sm / 2 clusters can be
-    // resident at once (a cooperative launch needs every CTA resident)
+    // resident at once (a cooperative launch needs every CTA resident).
+    // QTB_NO_CLUSTERS=1 selects the unclustered schedule (every int8 tile whole
+    // in one CTA): under a kernel profiler the clustered cooperative launch did
+    // not keep every CTA running at once, so its grid barrier timed out.
+    const char *nc = getenv("QTB_NO_CLUSTERS");
+    const bool allow = !(nc && nc[0] == '1');
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[2];
     cluster_launch_config(cfg, at, e->n_sm, nullptr);
     int ncl = 0;
-    if (e->n_sm % 2 == 0 && cudaOccupancyMaxActiveClusters(&ncl, (const void *)decode_kernel, &cfg) == cudaSuccess &&
-        ncl >= e->n_sm / 2)
+    if (allow && e->n_sm % 2 == 0 &&
+        cudaOccupancyMaxActiveClusters(&ncl, (const void *)decode_kernel, &cfg) == cudaSuccess && ncl >= e->n_sm / 2)
       e->pairs = 1;
     cudaGetLastError();
   }

@@ -2,12 +2,19 @@
 capturing one `decode_kernel` launch under a profiler.
 
     python qwen3-tts_b200/profile_frame.py [--config c2] [--frames 3] [--pos 64]
+    python qwen3-tts_b200/profile_frame.py --stage gemv [--rows 1024 --cols 2048 --batch 64]
+    python qwen3-tts_b200/profile_frame.py --stage attn [--batch 64]
 
 Builds the same synthetic engine as bench.py (seeded random weights of the
 config's shapes), places the session at context position --pos (KV contents
 are whatever the fresh pool holds: timing and traffic do not depend on them)
 and runs --frames launches of one frame each.  Launch 0 is the cold first
 launch; capture launch 1 (`ncu -k regex:decode_kernel -s 1 -c 1 ...`).
+
+--stage runs one stage kind alone, three launches of one stage each (capture
+launch 2): a BF16 GEMV stage of the given shape and batch, or a paged decode
+attention stage (16 query / 8 KV heads) of --batch slots at context lengths
+drawn from U[128, 2048), the config-4 mix.
 """
 import argparse
 import os
@@ -21,12 +28,53 @@ import qtts_b200 as Q  # noqa: E402
 CFG = {"c1": ("0.6B", "bf16", False), "c2": ("0.6B", "int8", True), "c3": ("1.7B", "int4g32", False)}
 
 
+def one_stage(args):
+    rng = np.random.default_rng(0)
+    if args.stage == "gemv":
+        rows, K, B = args.rows, args.cols, args.batch
+        W = Q.bf16_from_f32(rng.standard_normal((rows, K), dtype=np.float32) * np.float32(0.02))
+        q = Q.quantize(W, Q.FMT_BF16)
+        x = rng.standard_normal((B, K), dtype=np.float32)
+        for _ in range(3):
+            y = Q.gemv(Q.FMT_BF16, q, rows, K, x)
+        ref = Q.f32_from_bf16(W).astype(np.float64) @ x.T.astype(np.float64)
+        print("gemv", y.shape, "rel err %.2e" % (np.linalg.norm(y - ref.T) / np.linalg.norm(ref)))
+        return
+    B = args.batch
+    pos = rng.integers(128, 2048, B)
+    nkv, nh, hd = 8, 16, 128
+    pt_stride = int(max(pos)) // 16 + 2
+    n_pages = int(sum(p // 16 + 1 for p in pos)) + 4
+    pt = np.full((B, pt_stride), -1, np.int32)
+    perm = rng.permutation(n_pages)
+    nxt = 0
+    for b in range(B):
+        for i in range(int(pos[b]) // 16 + 1):
+            pt[b, i] = perm[nxt]
+            nxt += 1
+    kp = np.full((n_pages, nkv, 16, hd), 0x3F80, np.uint16)
+    vp = np.full((n_pages, nkv, 16, hd), 0x3F00, np.uint16)
+    qkv = rng.standard_normal((B, (nh + 2 * nkv) * hd), dtype=np.float32)
+    ones = np.ones(hd, np.float32)
+    cs, sn = Q.rope_tables(1e6, hd, 8192)
+    for _ in range(3):
+        out = Q.attention(qkv, nh, nkv, ones, ones, 1e-6, cs, sn, kp, vp, pt, pos.astype(np.int32), 16)
+    print("attention", out.shape, "finite", bool(np.isfinite(out).all()))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", default="c2", choices=sorted(CFG))
     ap.add_argument("--frames", type=int, default=3)
     ap.add_argument("--pos", type=int, default=64)
+    ap.add_argument("--stage", choices=["gemv", "attn"])
+    ap.add_argument("--rows", type=int, default=1024)
+    ap.add_argument("--cols", type=int, default=2048)
+    ap.add_argument("--batch", type=int, default=64)
     args = ap.parse_args()
+    if args.stage:
+        one_stage(args)
+        return
     model, fmt, with_cp = CFG[args.config]
     mcfg = Q.CFG_06B if model == "0.6B" else Q.CFG_17B
     m = Q.synth_model(mcfg, seed=0, with_cp=with_cp, norm_gain="ones")
