@@ -176,6 +176,24 @@ QTB_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, long long limit_cycles) {
   }
 }
 
+// Named barrier `id` over `nthreads` threads (whole warps, warp-uniform call).
+QTB_DEV void bar_sync_n(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// ... that also returns the AND of `v` over the participating threads.
+QTB_DEV bool bar_and_n(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // Non-blocking probe of an mbarrier phase (true once the phase of the given
 // parity has completed).
 QTB_DEV bool mbar_test(uint64_t *bar, uint32_t parity) {

@@ -1635,7 +1635,6 @@ struct __align__(16) AttnSmem {
   uint16_t knew[HD];
   uint16_t vnew[HD];
   float q[2][HD];
-  unsigned cons[ATT_NBUF_MAX];   // per page buffer: warps done with its current page
   int pre[65];                   // dynamic order: first item of each batch slot, items in all at [B]
   int next;                      // dynamic order: the CTA's next item
   int flag;
@@ -1747,18 +1746,21 @@ QTB_DEV void attn_item_dyn(const AttnArgs &a, int B, int item, const AttnSmem *s
 // Take the next work item of a dynamic attention stage (one thread).
 QTB_DEV int attn_take(KCtx &kc) { return (int)(atomicAdd(&kc.ctl->att_work, 1u) - kc.att_base); }
 
-// Bulk-copy page i of the item's range into the ring buffer of stream
+// Bulk-copy pool page `page` of KV head g into the ring buffer of stream
 // position ctr (one thread; the caller records kc.att_issued).
-QTB_DEV void attn_issue1(const AttnArgs &a, const AttnItem &it, int i, unsigned ctr, KCtx &kc, char *smem) {
+QTB_DEV void attn_issue_pg(const AttnArgs &a, int page, int g, unsigned ctr, KCtx &kc, char *smem) {
   const int nb = a.nbuf;
   const int buf = ctr % nb;
-  int page = __ldg(a.page_table + (size_t)it.b * a.pt_stride + it.p_begin + i);
   if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
   uint16_t *dstk = att_buf(smem, buf);
-  const size_t off = (((size_t)page * a.n_kv + it.g) * PAGE) * HD;
+  const size_t off = (((size_t)page * a.n_kv + g) * PAGE) * HD;
   mbar_arrive_expect_tx(kc.bars + buf, ATT_PAGE_BYTES);
   bulk_g2s(dstk, a.kpool + off, PAGE * HD * 2, kc.bars + buf);
   bulk_g2s(dstk + PAGE * HD, a.vpool + off, PAGE * HD * 2, kc.bars + buf);
+}
+// ... page i of the item's range.
+QTB_DEV void attn_issue1(const AttnArgs &a, const AttnItem &it, int i, unsigned ctr, KCtx &kc, char *smem) {
+  attn_issue_pg(a, __ldg(a.page_table + (size_t)it.b * a.pt_stride + it.p_begin + i), it.g, ctr, kc, smem);
 }
 
 // Warp-wide: bulk-copy pages [i0, i1) (i1 - i0 <= 32) of the item, one per lane.
@@ -1907,7 +1909,6 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
         for (int i = 0; i < 4; i++) dst[lane + 32 * i] = (uint16_t)f32_to_bf16_trunc(v[i]);
       }
     }
-    if (threadIdx.x < ATT_NBUF_MAX) sm->cons[threadIdx.x] = 0u;
     __syncthreads();
     if (owns_new && threadIdx.x < 32) {
       const int page = __ldg(pt + pos / PAGE);
@@ -1944,9 +1945,9 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
     // dims 4 lane .. 4 lane + 3), combined across warps in warp order at the
     // end.  The split of pages among warps depends on the item alone, so the
     // result does not depend on which CTA ran it.  Page i sits in ring buffer
-    // (stream position) % NB; the second warp to finish with a buffer refills
-    // it with stream position + NB (this item's page i + NB, or a page of the
-    // next item).
+    // (stream position) % NB; once both warps of the pair are done with a
+    // buffer (named barrier per pair) the head-0 warp refills it with stream
+    // position + NB (this item's page i + NB, or a page of the next item).
     const int n = p_end - p_begin;
     const int tid = threadIdx.x;
     const int h = warp & 1, pw = warp >> 1;
@@ -1956,9 +1957,11 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
       const unsigned ctr = kc.page_ctr + i;
       const int buf = ctr % NB;
       // every lane observes the phase flip, which makes the bulk-copied bytes
-      // visible to it
-      if (!mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES)) {
-        if (lane == 0) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+      // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
+      // so a timeout ends both warps' loops at the same page
+      const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+      if (!bar_and_n(1 + pw, 64, landed)) {
+        if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
         break;
       }
       uint16_t *kb = att_buf(smem_base, buf);
@@ -1973,19 +1976,37 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
         *reinterpret_cast<uint2 *>(vb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
         __syncwarp();
       }
-      // score of token t: lanes t and t + 16 each take half of the 128 dims,
-      // walking them from a lane-dependent start so the 32 lanes hit 32 banks
-      float sdot = 0.f;
+      // the page that will reuse this buffer: its index is loaded now, so
+      // the refill at the end of the page does not wait for it
+      int refill_page = -1;
+      if (h == 0 && lane == 0) {
+        const int tgt = i + NB;
+        if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
+        else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+      }
+      // score of token t: lanes t and t + 16 each take half of the 128 dims
+      // in 16-byte groups, walking them from a token-dependent start so each
+      // 8-lane phase of a 16-byte read hits 8 distinct bank groups; four
+      // partial sums
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
       const float *qh = sm->q[h] + half * 64;
       const uint16_t *kr = kb + t * HD + half * 64;
-#pragma unroll 8
-      for (int jj = 0; jj < 32; jj++) {
-        const int j = (jj + t + 16 * half) & 31;
-        const uint32_t kk = *reinterpret_cast<const uint32_t *>(kr + 2 * j);
-        const float2 qq = *reinterpret_cast<const float2 *>(qh + 2 * j);
-        sdot = fmaf(qq.x, bf16lo(kk), sdot);
-        sdot = fmaf(qq.y, bf16hi(kk), sdot);
+#pragma unroll
+      for (int jj = 0; jj < 8; jj++) {
+        const int jq = (jj + t) & 7;
+        const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+        const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+        const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+        s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+        s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+        s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+        s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+        s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+        s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+        s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+        s3 = fmaf(qb.w, bf16hi(kk.w), s3);
       }
+      float sdot = (s0 + s1) + (s2 + s3);
       sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
       const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
       float mx = sc;
@@ -1993,40 +2014,44 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
       for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float m_new = fmaxf(m_w, mx);
       const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
-      float ps = pr;
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
       const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
-      l_w = l_w * corr + ps;
+      l_w = l_w * corr + pr;   // this lane's token share; summed over the lanes after the loop
       m_w = m_new;
 #pragma unroll
       for (int e = 0; e < 4; e++) acc4[e] *= corr;
       // slots past the sequence end hold whatever the pool has there: skip them
+      if (ntok == PAGE) {
 #pragma unroll
-      for (int tt = 0; tt < PAGE; tt++) {
-        if (tt >= ntok) break;
-        const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-        const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-        acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-        acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-        acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-        acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
-      }
-      __syncwarp();
-      if (lane == 0) {
-        __threadfence_block();   // this warp's reads of the buffer before its count
-        const bool second = atomicAdd(sm->cons + buf, 1u) & 1u;
-        const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
-        if (second && (tgt < n || tgt - n < nx_n)) {
-          // both warps are done with this buffer: bring stream position ctr + NB
-          __threadfence_block();
-          fence_proxy_async_smem();
-          if (tgt < n) attn_issue1(a, it, tgt, ctr + NB, kc, smem_base);
-          else attn_issue1(a, nx, tgt - n, ctr + NB, kc, smem_base);
-          atomicMax(&kc.att_issued, ctr + NB + 1u);
+        for (int tt = 0; tt < PAGE; tt++) {
+          const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+          const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+          acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+          acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+          acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+          acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+        }
+      } else {
+        for (int tt = 0; tt < ntok; tt++) {
+          const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+          const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+          acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+          acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+          acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+          acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
         }
       }
+      // both warps of the pair are done with the buffer: the head-0 warp
+      // refills it with stream position ctr + NB
+      bar_sync_n(1 + pw, 64);
+      const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
+      if (h == 0 && lane == 0 && (tgt < n || tgt - n < nx_n)) {
+        fence_proxy_async_smem();
+        attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
+        atomicMax(&kc.att_issued, ctr + NB + 1u);
+      }
     }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) l_w += __shfl_xor_sync(0xffffffffu, l_w, o);
     // per-warp states -> per-head totals, in warp order
     float *s_acc = reinterpret_cast<float *>(smem + ATT_COMB_OFF);   // [NWARPS][HD]
     float *s_ml = s_acc + NWARPS * HD;                                // [NWARPS][2]
