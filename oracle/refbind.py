@@ -51,15 +51,17 @@ class Cfg(C.Structure):
 _libs = {}
 
 
-def ref_lib(flavour: str | None = None, dropin: bool = False):
+def ref_lib(flavour: str | None = None, dropin: bool = False, refcuda: bool = False):
+    """refcuda: the drop-in flavour linked with the reference's own CUDA
+    talker / code predictor (qwen_tts_cuda_talker.cu built for sm_100a)."""
     flavour = flavour or isa()
-    name = f"libqwen_ref_{'dropin_' if dropin else ''}{flavour}.so"
+    name = f"libqwen_ref_{'refcuda_' if refcuda else ('dropin_' if dropin else '')}{flavour}.so"
     if name in _libs:
         return _libs[name]
     path = os.path.join(REF_DIR, name)
     if not os.path.exists(path):
         raise RuntimeError(f"oracle library missing: {path} (build with make -C oracle)")
-    L = C.CDLL(path, mode=C.RTLD_GLOBAL if dropin else C.RTLD_LOCAL)
+    L = C.CDLL(path, mode=C.RTLD_GLOBAL if (dropin and not refcuda) else C.RTLD_LOCAL)
     vp = C.c_void_p
     L.qref_load.restype = vp
     L.qref_load.argtypes = [C.c_char_p, C.POINTER(Cfg), C.c_int, C.c_int]
@@ -95,7 +97,7 @@ def ref_lib(flavour: str | None = None, dropin: bool = False):
     L.qwen_rms_norm_per_head.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, C.c_float]
     L.qwen_swiglu_inplace.argtypes = [vp, vp, C.c_int]
     L.qwen_argmax_matvec_bf16.argtypes = [vp, vp, C.c_int, C.c_int]
-    if dropin:
+    if dropin or refcuda:
         L.qref_dropin_attach.argtypes = [vp, C.c_int, C.c_int]
     _libs[name] = L
     return L
@@ -170,8 +172,8 @@ class RefModel:
     """The reference's talker + CP loaded from a synthetic safetensors file."""
 
     def __init__(self, st_path: str, cfg, use_int8=False, use_int4=False, threads=None, flavour=None,
-                 dropin=False, cp=True):
-        self.L = ref_lib(flavour, dropin=dropin)
+                 dropin=False, cp=True, refcuda=False):
+        self.L = ref_lib(flavour, dropin=dropin, refcuda=refcuda)
         self.cfg = cfg
         c = Cfg(cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.inter, cfg.codec_vocab,
                 cfg.codebook, cfg.cp_hidden, cfg.cp_layers if cp else 0, cfg.cp_heads, cfg.cp_kv_heads,
