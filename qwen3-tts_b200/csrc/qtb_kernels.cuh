@@ -1953,103 +1953,285 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
     const int h = warp & 1, pw = warp >> 1;
     const int t = lane & 15, half = lane >> 4;
     float m_w = -INFINITY, l_w = 0.f, acc4[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int i = pw; i < n; i += NWARPS / 2) {
-      const unsigned ctr = kc.page_ctr + i;
-      const int buf = ctr % NB;
-      // every lane observes the phase flip, which makes the bulk-copied bytes
-      // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
-      // so a timeout ends both warps' loops at the same page
-      const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
-      if (!bar_and_n(1 + pw, 64, landed)) {
-        if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-        break;
-      }
-      uint16_t *kb = att_buf(smem_base, buf);
-      uint16_t *vb = kb + PAGE * HD;
-      const int pg = p_begin + i;
-      const int ntok = min(PAGE, L - pg * PAGE);
-      if (pg == npages - 1 && owns_new) {
-        // the newest token comes from shared memory, not from the copy (both
-        // warps of the page write the same bytes)
-        const int slot = pos % PAGE;
-        *reinterpret_cast<uint2 *>(kb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
-        *reinterpret_cast<uint2 *>(vb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
-        __syncwarp();
-      }
-      // the page that will reuse this buffer: its index is loaded now, so
-      // the refill at the end of the page does not wait for it
-      int refill_page = -1;
-      if (h == 0 && lane == 0) {
-        const int tgt = i + NB;
-        if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
-        else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
-      }
-      // score of token t: lanes t and t + 16 each take half of the 128 dims
-      // in 16-byte groups, walking them from a token-dependent start so each
-      // 8-lane phase of a 16-byte read hits 8 distinct bank groups; four
-      // partial sums
-      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-      const float *qh = sm->q[h] + half * 64;
-      const uint16_t *kr = kb + t * HD + half * 64;
-#pragma unroll
-      for (int jj = 0; jj < 8; jj++) {
-        const int jq = (jj + t) & 7;
-        const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
-        const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
-        const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
-        s0 = fmaf(qa.x, bf16lo(kk.x), s0);
-        s1 = fmaf(qa.y, bf16hi(kk.x), s1);
-        s2 = fmaf(qa.z, bf16lo(kk.y), s2);
-        s3 = fmaf(qa.w, bf16hi(kk.y), s3);
-        s0 = fmaf(qb.x, bf16lo(kk.z), s0);
-        s1 = fmaf(qb.y, bf16hi(kk.z), s1);
-        s2 = fmaf(qb.z, bf16lo(kk.w), s2);
-        s3 = fmaf(qb.w, bf16hi(kk.w), s3);
-      }
-      float sdot = (s0 + s1) + (s2 + s3);
-      sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
-      const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
-      float mx = sc;
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_new = fmaxf(m_w, mx);
-      const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
-      const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
-      l_w = l_w * corr + pr;   // this lane's token share; summed over the lanes after the loop
-      m_w = m_new;
-#pragma unroll
-      for (int e = 0; e < 4; e++) acc4[e] *= corr;
-      // slots past the sequence end hold whatever the pool has there: skip them
-      if (ntok == PAGE) {
-#pragma unroll
-        for (int tt = 0; tt < PAGE; tt++) {
-          const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-          const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-          acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-          acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-          acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-          acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+    // With 16 buffers a pair takes two of its pages per step (i and i + 4):
+    // the two pages' dot products and P.V run as independent chains and share
+    // one softmax update; with 4 buffers (small batches) one page per step.
+    float acc4b[4] = {0.f, 0.f, 0.f, 0.f};
+    if (NB >= 2 * (NWARPS / 2)) {
+      for (int i = pw; i < n; i += 2 * (NWARPS / 2)) {
+        const int i2 = i + NWARPS / 2;
+        const bool two = i2 < n;
+        const unsigned ctr = kc.page_ctr + i, ctr2 = ctr + NWARPS / 2;
+        const int buf = ctr % NB, buf2 = ctr2 % NB;
+        // every lane observes the phase flips, which makes the bulk-copied bytes
+        // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
+        // so a timeout ends both warps' loops at the same page
+        bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+        if (two) landed = mbar_wait(kc.bars + buf2, (ctr2 / NB) & 1u, WAIT_LIMIT_CYCLES) && landed;
+        if (!bar_and_n(1 + pw, 64, landed)) {
+          if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+          break;
         }
-      } else {
-        for (int tt = 0; tt < ntok; tt++) {
-          const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-          const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-          acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-          acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-          acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-          acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+        uint16_t *kb = att_buf(smem_base, buf);
+        uint16_t *vb = kb + PAGE * HD;
+        uint16_t *kb2 = att_buf(smem_base, buf2);
+        uint16_t *vb2 = kb2 + PAGE * HD;
+        const int ntok = min(PAGE, L - (p_begin + i) * PAGE);
+        const int ntok2 = two ? min(PAGE, L - (p_begin + i2) * PAGE) : 0;
+        if (owns_new && (p_begin + i == npages - 1 || (two && p_begin + i2 == npages - 1))) {
+          // the newest token comes from shared memory, not from the copy (both
+          // warps of the page write the same bytes)
+          const int slot = pos % PAGE;
+          uint16_t *kp = (p_begin + i == npages - 1) ? kb : kb2;
+          uint16_t *vp = kp + PAGE * HD;
+          *reinterpret_cast<uint2 *>(kp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
+          *reinterpret_cast<uint2 *>(vp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
+          __syncwarp();
+        }
+        // the pages that will reuse these buffers: their indices are loaded
+        // now, so the refills at the end of the step do not wait for them
+        int refill_page = -1, refill_page2 = -1;
+        if (h == 0 && lane == 0) {
+          const int tgt = i + NB, tgt2 = i2 + NB;
+          if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
+          else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+          if (two) {
+            if (tgt2 < n) refill_page2 = __ldg(pt + p_begin + tgt2);
+            else if (tgt2 - n < nx_n) refill_page2 = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt2 - n));
+          }
+        }
+        // scores of both pages, as in the one-page loop; the q reads are shared
+        const float *qh = sm->q[h] + half * 64;
+        float sdot, sdot2 = 0.f;
+        {
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+          const uint16_t *kr = kb + t * HD + half * 64;
+          if (two) {
+            float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
+            const uint16_t *kr2 = kb2 + t * HD + half * 64;
+  #pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+              const int jq = (jj + t) & 7;
+              const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+              const uint4 k2 = *reinterpret_cast<const uint4 *>(kr2 + 8 * jq);
+              const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+              const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+              s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+              s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+              s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+              s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+              u0 = fmaf(qa.x, bf16lo(k2.x), u0);
+              u1 = fmaf(qa.y, bf16hi(k2.x), u1);
+              u2 = fmaf(qa.z, bf16lo(k2.y), u2);
+              u3 = fmaf(qa.w, bf16hi(k2.y), u3);
+              s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+              s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+              s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+              s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+              u0 = fmaf(qb.x, bf16lo(k2.z), u0);
+              u1 = fmaf(qb.y, bf16hi(k2.z), u1);
+              u2 = fmaf(qb.z, bf16lo(k2.w), u2);
+              u3 = fmaf(qb.w, bf16hi(k2.w), u3);
+            }
+            sdot2 = (u0 + u1) + (u2 + u3);
+          } else {
+  #pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+              const int jq = (jj + t) & 7;
+              const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+              const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+              const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+              s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+              s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+              s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+              s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+              s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+              s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+              s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+              s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+            }
+          }
+          sdot = (s0 + s1) + (s2 + s3);
+        }
+        sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+        sdot2 += __shfl_xor_sync(0xffffffffu, sdot2, 16);
+        const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
+        const float sc2 = (t < ntok2) ? sdot2 * a.scale : -INFINITY;
+        float mx = fmaxf(sc, sc2);
+  #pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float m_new = fmaxf(m_w, mx);
+        const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
+        const float pr2 = (t < ntok2) ? expf(sc2 - m_new) : 0.f;
+        const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
+        l_w = l_w * corr + (pr + pr2);   // this lane's token shares; summed over the lanes after the loop
+        m_w = m_new;
+  #pragma unroll
+        for (int e = 0; e < 4; e++) {
+          acc4[e] *= corr;
+          acc4b[e] *= corr;
+        }
+        // slots past the sequence end hold whatever the pool has there: skip them
+        if (ntok == PAGE && ntok2 == PAGE) {
+  #pragma unroll
+          for (int tt = 0; tt < PAGE; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+            const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
+            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+            acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
+            acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
+            acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
+            acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
+          }
+        } else if (ntok == PAGE && ntok2 == 0) {
+  #pragma unroll
+          for (int tt = 0; tt < PAGE; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+          }
+        } else {
+          for (int tt = 0; tt < PAGE; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
+            if (tt < ntok) {
+              const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+              acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+              acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+              acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+              acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+            }
+            if (tt < ntok2) {
+              const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
+              acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
+              acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
+              acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
+              acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
+            }
+          }
+        }
+        // both warps of the pair are done with the buffers: the head-0 warp
+        // refills each with its stream position + NB
+        bar_sync_n(1 + pw, 64);
+        if (h == 0 && lane == 0) {
+          const int tgt = i + NB, tgt2 = i2 + NB;   // item-relative; >= n: the next item's page tgt - n
+          const bool r1 = tgt < n || tgt - n < nx_n;
+          const bool r2 = two && (tgt2 < n || tgt2 - n < nx_n);
+          if (r1 || r2) fence_proxy_async_smem();
+          if (r1) attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
+          if (r2) attn_issue_pg(a, refill_page2, tgt2 < n ? g : nx.g, ctr2 + NB, kc, smem_base);
+          if (r1 || r2) atomicMax(&kc.att_issued, (r2 ? ctr2 : ctr) + NB + 1u);
         }
       }
-      // both warps of the pair are done with the buffer: the head-0 warp
-      // refills it with stream position ctr + NB
-      bar_sync_n(1 + pw, 64);
-      const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
-      if (h == 0 && lane == 0 && (tgt < n || tgt - n < nx_n)) {
-        fence_proxy_async_smem();
-        attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
-        atomicMax(&kc.att_issued, ctr + NB + 1u);
+    } else {
+      for (int i = pw; i < n; i += NWARPS / 2) {
+        const unsigned ctr = kc.page_ctr + i;
+        const int buf = ctr % NB;
+        // every lane observes the phase flip, which makes the bulk-copied bytes
+        // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
+        // so a timeout ends both warps' loops at the same page
+        const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+        if (!bar_and_n(1 + pw, 64, landed)) {
+          if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+          break;
+        }
+        uint16_t *kb = att_buf(smem_base, buf);
+        uint16_t *vb = kb + PAGE * HD;
+        const int pg = p_begin + i;
+        const int ntok = min(PAGE, L - pg * PAGE);
+        if (pg == npages - 1 && owns_new) {
+          // the newest token comes from shared memory, not from the copy (both
+          // warps of the page write the same bytes)
+          const int slot = pos % PAGE;
+          *reinterpret_cast<uint2 *>(kb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
+          *reinterpret_cast<uint2 *>(vb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
+          __syncwarp();
+        }
+        // the page that will reuse this buffer: its index is loaded now, so
+        // the refill at the end of the page does not wait for it
+        int refill_page = -1;
+        if (h == 0 && lane == 0) {
+          const int tgt = i + NB;
+          if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
+          else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+        }
+        // score of token t: lanes t and t + 16 each take half of the 128 dims
+        // in 16-byte groups, walking them from a token-dependent start so each
+        // 8-lane phase of a 16-byte read hits 8 distinct bank groups; four
+        // partial sums
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        const float *qh = sm->q[h] + half * 64;
+        const uint16_t *kr = kb + t * HD + half * 64;
+  #pragma unroll
+        for (int jj = 0; jj < 8; jj++) {
+          const int jq = (jj + t) & 7;
+          const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+          const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+          const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+          s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+          s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+          s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+          s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+          s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+          s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+          s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+          s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+        }
+        float sdot = (s0 + s1) + (s2 + s3);
+        sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+        const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
+        float mx = sc;
+  #pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float m_new = fmaxf(m_w, mx);
+        const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
+        const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
+        l_w = l_w * corr + pr;   // this lane's token share; summed over the lanes after the loop
+        m_w = m_new;
+  #pragma unroll
+        for (int e = 0; e < 4; e++) acc4[e] *= corr;
+        // slots past the sequence end hold whatever the pool has there: skip them
+        if (ntok == PAGE) {
+  #pragma unroll
+          for (int tt = 0; tt < PAGE; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+          }
+        } else {
+          for (int tt = 0; tt < ntok; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+          }
+        }
+        // both warps of the pair are done with the buffer: the head-0 warp
+        // refills it with stream position ctr + NB
+        bar_sync_n(1 + pw, 64);
+        const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
+        if (h == 0 && lane == 0 && (tgt < n || tgt - n < nx_n)) {
+          fence_proxy_async_smem();
+          attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
+          atomicMax(&kc.att_issued, ctr + NB + 1u);
+        }
       }
     }
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc4[e] += acc4b[e];
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) l_w += __shfl_xor_sync(0xffffffffu, l_w, o);
     // per-warp states -> per-head totals, in warp order
