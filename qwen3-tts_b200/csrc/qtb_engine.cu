@@ -868,10 +868,11 @@ static int alloc_stack_bufs(qtb_session *s, const DStack &k, StackBufs &b, int B
     for (int j = 0; j < b.pt_stride; j++) pt[(size_t)i * b.pt_stride + j] = (n_pages > 0) ? -1 : i * b.pt_stride + j;
   if ((rc = ar.upload(&b.page_table, pt.data(), pt.size() * 4))) return rc;
   if (B * k.n_kv > s->e->n_sm / 2) {
-    // many sequences: items of 16-32 pages taken in dynamic order keep the
-    // CTAs evenly loaded whatever the length mix
+    // many sequences: items of 32-64 pages taken in dynamic order keep the
+    // CTAs evenly loaded whatever the length mix (pages stream across items,
+    // so longer items only cut the per-item prologue and combine)
     b.max_splits = 16;
-    b.min_pps = 32;
+    b.min_pps = 64;
   } else {
     // at most one attention work item per CTA: a second item would double the stage
     b.max_splits = std::max(1, std::min(32, s->e->n_sm / (B * k.n_kv)));
