@@ -269,7 +269,7 @@ threads = {threads!r} or os.cpu_count()
 ref = refbind.RefModel(path, cfg, use_int8=(fmt == 'int8'), use_int4=(fmt in ('q4_0', 'int4g32')), threads=threads,
                        cp=with_cp)
 rng = np.random.default_rng(0)
-for p in range(8):
+for p in range({CONFIGS[cfg_name][4] or 64}):   # the same prefill length as the GPU arm
     h = ref.talker_step((0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32))
 n = {frames!r}
 e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
@@ -337,6 +337,9 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = dist_init()
+    if args.gpus != world:
+        sys.exit(f"bench.py: --gpus {args.gpus} but WORLD_SIZE is {world}; launch N>1 GPUs with "
+                 f"torchrun --nproc-per-node {args.gpus} (one process per GPU)")
     if args.impl == "reference":
         if rank == 0:
             cb = cpu_baseline_sample(args.config)   # a ~12 s sample of the same workload
@@ -346,8 +349,8 @@ def main():
                     "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                     "config": config_dict(args.config, world),
                     "cpu_baseline": {"value": cb.get("value"), "unit": unit, "cores": cb.get("cores"),
-                                     "kind": "reference", "sample": f"{cb.get('frames')} steps (~12 s) after an 8-step "
-                                     f"prefill, default dispatch ({cb.get('isa')}), all host threads"},
+                                     "kind": "reference", "sample": f"{cb.get('frames')} steps (~12 s) after a "
+                                     f"{CONFIGS[args.config][4] or 64}-step prefill, default dispatch ({cb.get('isa')}), all host threads"},
                     "e2e": {"value": round(cb.get("value", 0.0), 3), "unit": unit, "h2d_bytes_per_step": 0,
                             "d2h_bytes_per_step": 0}}
             if "error" in cb:

@@ -103,6 +103,13 @@ typedef struct qtb_session qtb_session_t;
 
 const char *qtb_last_error(void);
 int qtb_device_count(void);
+/* How the per-head QK RMSNorm before the K/V append computes 1/sqrt:
+ * 1 = as the reference's x86 build does (qwen_rms_norm_per_head,
+ * qwen_tts_kernels.c:486-577, compiled with -ffast-math: this host CPU's
+ * rsqrtss seed and one Newton step), so appended K bytes equal the
+ * reference's on this host; 0 = IEEE 1/sqrtf (non-x86 hosts, a host whose
+ * rsqrtss the engine cannot tabulate, or QTB_QK_NORM=ieee). */
+int qtb_qk_norm_mode(void);
 
 int  qtb_engine_create(const qtb_engine_desc_t *desc, int device, qtb_engine_t **out);
 void qtb_engine_destroy(qtb_engine_t *e);
@@ -220,7 +227,7 @@ int qtb_attention_host(const float *qkv, int batch, int n_heads, int n_kv, int h
  * qtb_attention_host, but every pointer is DEVICE memory owned by the caller
  * (same layouts), `stream` is a cudaStream_t (NULL = legacy default stream),
  * and the call allocates nothing: the launch's scratch lives in one fixed
- * file-scope device array (about 263 KB) that bounds batch <= 4, n_kv <= 16
+ * file-scope device array (1,068,032 bytes, ~1.04 MB) that bounds batch <= 4, n_kv <= 16
  * and max_splits <= 16; larger requests return QTB_E_INVALID untouched.  For
  * callers that must not allocate device memory while they run -- code between
  * a pool's reservation and its release, or code whose memory budget is fixed

@@ -198,6 +198,45 @@ int qref_rope_len(void *h, int cp) {
     return cp ? ctx->cp_rope_cache_len : ctx->rope_cache_len;
 }
 
+/* The talker's K/V append for one token from its pre-norm q/k/v rows
+ * (qwen_tts_talker.c:603-615): the reference's own qwen_rms_norm_per_head
+ * (exported by qwen_tts_kernels.c) on q and k, then NeoX RoPE as
+ * apply_rope_neox_inplace's AVX2 branch computes it (qwen_tts_talker.c:
+ * 203-251, static there, so restated here: x1 c - (x2 s) and x2 c + (x1 s),
+ * each one fused multiply-add over a rounded product), then bf16 truncation of
+ * k and v (f32_to_bf16_vec, qwen_tts_talker.c:125-159).  q (in place), k (in
+ * place) and the bf16 rows k_out / v_out. */
+void qref_qk_norm_rope_append(float *q, float *k, const float *v, int n_heads, int n_kv, int head_dim,
+                              const float *q_norm, const float *k_norm, float eps,
+                              const float *cos_cache, const float *sin_cache, int pos,
+                              uint16_t *k_out, uint16_t *v_out) {
+    qwen_rms_norm_per_head(q, q_norm, 1, n_heads, head_dim, eps);
+    qwen_rms_norm_per_head(k, k_norm, 1, n_kv, head_dim, eps);
+    const int half = head_dim / 2;
+    const float *c = cos_cache + (size_t)pos * half, *sn = sin_cache + (size_t)pos * half;
+    for (int t = 0; t < 2; t++) {
+        float *x = t ? k : q;
+        const int nh = t ? n_kv : n_heads;
+        for (int h = 0; h < nh; h++) {
+            float *xh = x + (size_t)h * head_dim;
+            for (int i = 0; i < half; i++) {
+                const float x1 = xh[i], x2 = xh[i + half];
+                volatile float p2s = x2 * sn[i], p1s = x1 * sn[i];   /* rounded products */
+                xh[i] = fmaf(x1, c[i], -p2s);
+                xh[i + half] = fmaf(x2, c[i], p1s);
+            }
+        }
+    }
+    const int kvd = n_kv * head_dim;
+    for (int i = 0; i < kvd; i++) {
+        uint32_t a, b;
+        memcpy(&a, &k[i], 4);
+        memcpy(&b, &v[i], 4);
+        k_out[i] = (uint16_t)(a >> 16);
+        v_out[i] = (uint16_t)(b >> 16);
+    }
+}
+
 void qref_free(void *h) {
     qwen_tts_ctx_t *ctx = (qwen_tts_ctx_t *)h;
     if (!ctx) return;

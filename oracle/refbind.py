@@ -83,6 +83,8 @@ def ref_lib(flavour: str | None = None, dropin: bool = False, refcuda: bool = Fa
     L.qref_rope.argtypes = [vp, C.c_int, C.c_int]
     L.qref_rope_len.argtypes = [vp, C.c_int]
     L.qref_set_threads.argtypes = [C.c_int]
+    L.qref_qk_norm_rope_append.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, C.c_float, vp, vp, C.c_int,
+                                           vp, vp]
     L.qref_ctx.restype = vp
     L.qref_ctx.argtypes = [vp]
     # the reference's own kernels, exported by the same library

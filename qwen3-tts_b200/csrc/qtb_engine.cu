@@ -22,6 +22,9 @@
 #include <vector>
 #include <algorithm>
 #include <functional>
+#if defined(__x86_64__) || defined(__i386__)
+#include <xmmintrin.h>
+#endif
 
 using namespace qtb;
 
@@ -65,6 +68,82 @@ extern "C" int qtb_device_count(void) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
   return n;
+}
+
+// ------------------------------------------ QK-norm rsqrt seeds -----------
+// The reference's x86 build computes the per-head QK RMSNorm's 1 / sqrt with
+// an rsqrtss seed and one Newton step (qwen_rms_norm_per_head,
+// qwen_tts_kernels.c:486-577, built with -O3 -ffast-math as its Makefile
+// does).  rsqrtss is implementation-defined to ~12 bits, so the device
+// reproduces it from a table of this host CPU's results (qk_inv_rms in
+// qtb_kernels.cuh): [exponent parity][12 leading mantissa bits] for inputs in
+// [1, 4).  The table is built once per process and kept only if it
+// reproduces rsqrtss on every normal input of [1, 4) (all 2^24 of them);
+// otherwise, off x86, or with QTB_QK_NORM=ieee in the environment, the norm
+// uses IEEE 1 / sqrtf.
+constexpr int RSQ_TAB_N = 2 << 12;
+static __device__ unsigned g_rsq_tab[RSQ_TAB_N];
+
+namespace {
+std::once_flag g_rsq_once;
+std::vector<unsigned> g_rsq_host;   // empty: IEEE mode
+std::mutex g_rsq_mu;
+const unsigned *g_rsq_dev[64];      // per device, set up once
+bool g_rsq_dev_done[64];
+}  // namespace
+
+static unsigned rsqrt_seed_bits(unsigned x_bits) {
+#if defined(__x86_64__) || defined(__i386__)
+  float x, r;
+  memcpy(&x, &x_bits, 4);
+  r = _mm_cvtss_f32(_mm_rsqrt_ss(_mm_set_ss(x)));
+  unsigned u;
+  memcpy(&u, &r, 4);
+  return u;
+#else
+  (void)x_bits;
+  return 0u;
+#endif
+}
+
+static void build_rsq_table() {
+  const char *env = getenv("QTB_QK_NORM");
+  if (env && strcmp(env, "ieee") == 0) return;
+#if defined(__x86_64__) || defined(__i386__)
+  std::vector<unsigned> t(RSQ_TAB_N);
+  for (unsigned par = 0; par < 2; par++)
+    for (unsigned hi = 0; hi < 4096; hi++) t[(par << 12) | hi] = rsqrt_seed_bits(((127u + par) << 23) | (hi << 11));
+  for (unsigned par = 0; par < 2; par++)
+    for (unsigned m = 0; m < (1u << 23); m++)
+      if (rsqrt_seed_bits(((127u + par) << 23) | m) != t[(par << 12) | (m >> 11)]) return;
+  g_rsq_host.swap(t);
+#endif
+}
+
+// Device address of the seed table on the current device (filled at the
+// first call per device), or null in IEEE mode.
+static int qk_rsq_table(const unsigned **out) {
+  std::call_once(g_rsq_once, build_rsq_table);
+  *out = nullptr;
+  if (g_rsq_host.empty()) return 0;
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_err(QTB_E_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_rsq_mu);
+  if (!g_rsq_dev_done[dev]) {
+    void *p = nullptr;
+    CUDA_TRY(cudaGetSymbolAddress(&p, g_rsq_tab));
+    CUDA_TRY(cudaMemcpyToSymbol(g_rsq_tab, g_rsq_host.data(), RSQ_TAB_N * sizeof(unsigned)));
+    g_rsq_dev[dev] = static_cast<const unsigned *>(p);
+    g_rsq_dev_done[dev] = true;
+  }
+  *out = g_rsq_dev[dev];
+  return 0;
+}
+
+extern "C" int qtb_qk_norm_mode(void) {
+  std::call_once(g_rsq_once, build_rsq_table);
+  return g_rsq_host.empty() ? 0 : 1;
 }
 
 // ------------------------------------------------------ device arena -------
@@ -341,6 +420,7 @@ struct qtb_engine {
   DMat mtp;
   const float *mtp_bias = nullptr;
   int has_mtp = 0;
+  const unsigned *rsq_tab = nullptr;   // QK-norm rsqrt seeds (qk_rsq_table) or null
 };
 
 static int upload_stack(qtb_engine *e, const qtb_stack_desc_t &d, DStack &s) {
@@ -461,6 +541,7 @@ extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_eng
     cudaGetLastError();
   }
   int rc = 0;
+  if ((rc = qk_rsq_table(&e->rsq_tab))) goto fail;
   e->has_talker = d->talker.n_layers > 0;
   if (e->has_talker) {
     if ((rc = upload_stack(e, d->talker, e->talker))) goto fail;
@@ -693,6 +774,7 @@ struct ProgBuilder {
     a.eps = k.eps; a.scale = 1.0f / sqrtf((float)HD);
     a.max_splits = b.max_splits; a.min_pps = b.min_pps;
     a.ws = s->att_ws; a.sem = s->att_sem;
+    a.rsq_tab = s->e->rsq_tab;
     attn_schedule(a, B, s->e->n_sm);
     st.push_back(S);
   }
@@ -1368,6 +1450,7 @@ extern "C" int qtb_attention_host(const float *qkv, int batch, int n_heads, int 
   a.kpool = dk; a.vpool = dv; a.n_pages = n_pages; a.n_heads = n_heads; a.n_kv = n_kv;
   a.eps = eps; a.scale = 1.0f / sqrtf((float)HD); a.max_splits = max_splits; a.min_pps = 1;
   a.ws = ws; a.sem = sem;
+  if ((rc = qk_rsq_table(&a.rsq_tab))) return rc;
   {
     int dev = 0, nsm = 0;
     CUDA_TRY(cudaGetDevice(&dev));
@@ -1459,7 +1542,8 @@ constexpr size_t NOALLOC_SEM_OFF = NOALLOC_CTL_OFF + 1024;                 // un
 constexpr size_t NOALLOC_WS_OFF = NOALLOC_SEM_OFF + 1024;                  // float workspace
 constexpr size_t NOALLOC_WS_BYTES =
     (size_t)NOALLOC_MAX_B * NOALLOC_MAX_KV * NOALLOC_MAX_SPLITS * 2 * (HD + 2) * sizeof(float);
-constexpr size_t NOALLOC_BYTES = NOALLOC_WS_OFF + NOALLOC_WS_BYTES;        // 269,312 bytes
+constexpr size_t NOALLOC_BYTES = NOALLOC_WS_OFF + NOALLOC_WS_BYTES;        // 1,068,032 bytes (~1.04 MB)
+static_assert(NOALLOC_BYTES == 1068032, "the documented size of the fixed scratch array");
 static_assert(sizeof(Stage) <= 1024 && sizeof(Ctl) <= 1024, "scratch layout");
 static_assert((size_t)NOALLOC_MAX_B * NOALLOC_MAX_KV * sizeof(unsigned) <= 1024, "scratch layout");
 constexpr int NOALLOC_MAX_DEV = 64;
@@ -1515,6 +1599,10 @@ extern "C" int qtb_attention_noalloc(const float *qkv, int batch, int n_heads, i
   a.kpool = kpages; a.vpool = vpages; a.n_pages = n_pages; a.n_heads = n_heads; a.n_kv = n_kv;
   a.eps = eps; a.scale = 1.0f / sqrtf((float)HD); a.max_splits = max_splits; a.min_pps = 1;
   a.ws = ws; a.sem = sem;
+  {
+    const int rc = qk_rsq_table(&a.rsq_tab);   // set up on this device's first call
+    if (rc) return rc;
+  }
   attn_schedule(a, batch, nsm);
   // the control block and the split semaphores must start at zero; the
   // descriptor is copied from this stack frame (synchronously, so the frame

@@ -114,6 +114,9 @@ struct AttnArgs {
   // ring is idle).  dyn: CTAs take work items from a grid-wide counter in the
   // dense order of attn_prefix instead of item = CTA + k * grid.
   int nbuf, dyn;
+  // the host CPU's reciprocal-square-root seeds for the per-head QK RMSNorm
+  // (qk_inv_rms), or null for IEEE 1 / sqrtf
+  const unsigned *rsq_tab;
 };
 
 struct EmbedArgs {
@@ -1666,6 +1669,26 @@ QTB_DEV int attn_pps(const AttnArgs &a, int np) {
   return (np + nsp - 1) / nsp;
 }
 
+// 1 / sqrt(a) of the per-head QK RMSNorm (a = mean of squares + eps > 0).
+// With `tab` it follows the reference's x86 build of qwen_rms_norm_per_head
+// (qwen_tts_kernels.c:486-577 compiled with -O3 -ffast-math, which lowers
+// 1.0f / sqrtf(x) to an rsqrtss seed x0 and one Newton step
+// (x0 a x0 - 3) (-x0 / 2), with that FMA): tab holds the host CPU's rsqrtss
+// result for every input in [1, 4) at 12 leading mantissa bits (the seed
+// depends only on those and the exponent's parity, and scales exactly by
+// powers of 4; checked on the host when the table is built), so the K/V bytes
+// this engine appends equal the reference's on that host.  Without a table (or
+// for a subnormal a) it is IEEE 1 / sqrtf.
+QTB_DEV float qk_inv_rms(float a, const unsigned *tab) {
+  const unsigned u = __float_as_uint(a);
+  if (!tab || u < 0x00800000u || u >= 0x7f800000u) return 1.0f / sqrtf(a);
+  const int e = (int)(u >> 23) - 127, par = e & 1;
+  const unsigned seed = __ldg(tab + (((unsigned)par << 12) | ((u >> 11) & 0xfffu)));
+  const float x0 = __uint_as_float(seed - ((unsigned)((e - par) / 2) << 23));
+  const float t = __fmul_rn(x0, a);
+  return __fmul_rn(__fmaf_rn(t, x0, -3.0f), __fmul_rn(x0, -0.5f));
+}
+
 // Decode work item -> (slot, kv head, split) and the split's page range.
 // Returns false for items beyond the slot's split count (or a bad position).
 QTB_DEV bool attn_item(const AttnArgs &a, int item, AttnItem &it) {
@@ -1887,11 +1910,19 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
         }
       }
       if (nw) {
-        float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+        // the reference's per-head RMSNorm in its x86 build's operation order
+        // (qwen_rms_norm_per_head, qwen_tts_kernels.c:486-577): sixteen-lane
+        // FMA accumulators over dims j, j+32, j+64, j+96 (lane j) and j+16, ...
+        // (lane j+16) -- this lane's own four values -- then the pairwise tree
+        // (+16, +8, +4, +2, +1); mean + eps as one FMA; x * w * inv
+        float ss = __fmul_rn(v[0], v[0]);
+        ss = __fmaf_rn(v[1], v[1], ss);
+        ss = __fmaf_rn(v[2], v[2], ss);
+        ss = __fmaf_rn(v[3], v[3], ss);
         ss = warp_sum(ss);
-        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+        const float inv = qk_inv_rms(__fmaf_rn(ss, 1.0f / (float)HD, a.eps), a.rsq_tab);
 #pragma unroll
-        for (int i = 0; i < 4; i++) v[i] = (v[i] * inv) * gw[i];
+        for (int i = 0; i < 4; i++) v[i] = __fmul_rn(__fmul_rn(v[i], gw[i]), inv);
 #pragma unroll
         for (int i = 0; i < 2; i++) {
           const float c = rc[i], s = rs[i];

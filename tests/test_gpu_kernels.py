@@ -117,6 +117,46 @@ def test_attention_append_matches_oracle(have_gpu, pos, max_splits):
                 assert np.array_equal(vp[page, :, slot], vp0[page, :, slot])
 
 
+@pytest.mark.parametrize("scale", [1.0, 300.0, 1e-3])
+def test_kv_append_bit_exact_vs_reference(have_gpu, scale):
+    """Identical f32 q/k/v rows into the reference's own K/V append (its
+    qwen_rms_norm_per_head from oracle/_ref, NeoX RoPE in its FMA order, bf16
+    truncation: qwen_tts_talker.c:603-615) and into the engine's attention
+    prologue: the appended K and V bytes must be identical, every element."""
+    import platform
+    import ctypes as C
+    import refbind
+    if platform.machine() in ("x86_64", "AMD64"):
+        # the engine reproduces this host's rsqrtss (the reference's -ffast-math
+        # 1/sqrtf) from a table it checks when it builds it
+        assert Q.lib().qtb_qk_norm_mode() == 1
+    L = refbind.ref_lib()
+    rng = np.random.default_rng(int(scale * 1000) + 5)
+    nh, nkv, hd, eps = 16, 8, 128, 1e-6
+    pos = [int(p) for p in rng.integers(0, 4000, 64)]
+    B = len(pos)
+    n_pages = sum(p // 16 + 1 for p in pos) + 3
+    qkv, kp, vp, pt, qn, kn, cs, sn = make_attention_case(rng, B, pos, n_pages)
+    qkv = (qkv * np.float32(scale) * (1 + rng.random(qkv.shape[1], dtype=np.float32))).astype(np.float32)
+    Q.attention(qkv, nh, nkv, qn, kn, eps, cs, sn, kp, vp, pt, np.array(pos, np.int32), 4)
+    bad = 0
+    for b in range(B):
+        q = qkv[b, :nh * hd].copy()
+        k = qkv[b, nh * hd:(nh + nkv) * hd].copy()
+        v = qkv[b, (nh + nkv) * hd:].copy()
+        k_ref = np.empty(nkv * hd, np.uint16)
+        v_ref = np.empty(nkv * hd, np.uint16)
+        L.qref_qk_norm_rope_append(refbind.p(q), refbind.p(k), refbind.p(v), nh, nkv, hd, refbind.p(qn),
+                                   refbind.p(kn), C.c_float(eps), refbind.p(cs), refbind.p(sn), pos[b],
+                                   refbind.p(k_ref), refbind.p(v_ref))
+        page, slot = pt[b, pos[b] // 16], pos[b] % 16
+        got_k = kp[page, :, slot, :].reshape(-1)
+        got_v = vp[page, :, slot, :].reshape(-1)
+        assert np.array_equal(got_v, v_ref), b
+        bad += int(np.count_nonzero(got_k != k_ref))
+    assert bad == 0, f"{bad} of {B * nkv * hd} K elements differ from the reference's bytes"
+
+
 def test_attention_ignores_pool_slots_past_the_end(have_gpu):
     # slots after the newest token hold NaN in the pool: they must not reach
     # the output (neither through the scores nor through P.V)

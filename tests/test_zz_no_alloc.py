@@ -23,12 +23,16 @@ def _noalloc():
     return f
 
 
-def test_noalloc_attention_equals_allocating_entry_point(have_gpu):
+# the second case sits at the limits (batch 4, n_kv 16, max_splits 16) with
+# 1024 work items, more than the CTAs: the dynamic item order, whose counter
+# lives in the shared scratch, runs through this entry point too
+@pytest.mark.parametrize("pos,nh,nkv,n_pages,max_splits",
+                         [([37, 200, 5], 16, 8, 40, 4), ([300, 511, 257, 400], 32, 16, 110, 16)])
+def test_noalloc_attention_equals_allocating_entry_point(have_gpu, pos, nh, nkv, n_pages, max_splits):
     import torch
-    rng = np.random.default_rng(21)
-    pos = [37, 200, 5]
-    nh, nkv, n_pages, max_splits, eps = 16, 8, 40, 4, 1e-6
-    qkv, kp, vp, pt, qn, kn, cs, sn = make_attention_case(rng, len(pos), pos, n_pages)
+    rng = np.random.default_rng(21 + len(pos))
+    eps = 1e-6
+    qkv, kp, vp, pt, qn, kn, cs, sn = make_attention_case(rng, len(pos), pos, n_pages, nh=nh, nkv=nkv)
     kp_ref, vp_ref = kp.copy(), vp.copy()
     out_ref = Q.attention(qkv, nh, nkv, qn, kn, eps, cs, sn, kp_ref, vp_ref, pt, np.array(pos, np.int32), max_splits)
 
