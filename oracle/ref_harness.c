@@ -186,6 +186,17 @@ const void *qref_cp_lm_head(void *h, int g, int kind) {
     return ctx->cp_lm_head_q4[g];
 }
 
+/* The code predictor's small_to_mtp_projection (qwen_tts_code_predictor.c:
+ * 458-479): kind 0 bf16 weight, 1 its int8 twin, 2 the int8 row scales,
+ * 3 the f32 bias (NULL when the talker and CP widths match). */
+const void *qref_cp_mtp(void *h, int kind) {
+    qwen_tts_ctx_t *ctx = (qwen_tts_ctx_t *)h;
+    if (kind == 0) return ctx->cp_mtp_proj_bf16;
+    if (kind == 1) return ctx->cp_mtp_proj_int8;
+    if (kind == 2) return ctx->cp_mtp_proj_scale;
+    return ctx->cp_mtp_proj_bias;
+}
+
 /* RoPE tables the reference built at load (qwen_tts_talker.c:478-495,
  * qwen_tts_code_predictor.c:498-507): which 0 = cos, 1 = sin. */
 const float *qref_rope(void *h, int cp, int which) {

@@ -76,6 +76,8 @@ def ref_lib(flavour: str | None = None, dropin: bool = False, refcuda: bool = Fa
     L.qref_codec_embed.argtypes = [vp, C.c_int, vp]
     L.qref_weight.restype = vp
     L.qref_weight.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int]
+    L.qref_cp_mtp.restype = vp
+    L.qref_cp_mtp.argtypes = [vp, C.c_int]
     L.qref_cp_lm_head.restype = vp
     L.qref_cp_lm_head.argtypes = [vp, C.c_int, C.c_int]
     L.qref_free.argtypes = [vp]
@@ -248,6 +250,13 @@ class RefModel:
         if not addr:
             return None
         return np.ctypeslib.as_array((C.c_uint8 * nbytes).from_address(addr)).view(dtype).copy()
+
+    def cp_mtp(self, kind, nbytes, dtype):
+        """The reference's MTP projection pieces (qref_cp_mtp kinds), or None."""
+        addr = self.L.qref_cp_mtp(self.h, int(kind))
+        if not addr:
+            return None
+        return np.frombuffer((C.c_char * nbytes).from_address(addr), dtype=dtype).copy()
 
     def rope(self, cp=False):
         n = self.L.qref_rope_len(self.h, int(cp))

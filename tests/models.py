@@ -53,6 +53,10 @@ def ref_quantized(ref, cfg, fmt, cp=False, n_layers=None):
             elif fmt == "q4_0":
                 b = ref.weight(cp, l, which[nm], 3, r * (c // 32) * 18, np.uint8).reshape(r, c // 32 * 18)
                 out[f"{pre}{l}.{nm}"] = {"data": b}
+    if cp and cfg.hidden != cfg.cp_hidden and fmt in ("int8", "q4_0"):
+        # the MTP projection's int8 twin (int8 under --int4 too)
+        r, c = cfg.cp_hidden, cfg.hidden
+        out["mtp"] = {"data": ref.cp_mtp(1, r * c, np.int8).reshape(r, c), "row_scale": ref.cp_mtp(2, r * 4, np.float32)}
     if cp:
         for g in range(15):
             r, c = cfg.codebook, cfg.cp_hidden

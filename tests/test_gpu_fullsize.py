@@ -1,0 +1,127 @@
+"""Full-size parity on the B200 (the BASELINE.json model shapes, seeded
+synthetic weights), against the reference's own CPU decode path
+(oracle/_ref) or, for the format the reference does not have, the numpy
+restatement:
+
+- config 2: the 0.6B talker + code predictor in INT8 (the reference's own
+  quantized bytes), a 64-token prefill, then 64 whole greedy frames on the
+  device: all 16 codes of every frame identical to the reference frame loop;
+- config 3: the 1.7B talker in q4_0 against the reference (rel L2 < 1e-2 over
+  32 steps after a 128-token prefill), and in asymmetric INT4 g32 against the
+  restatement (32 steps);
+- config 5's code predictor: the 1.7B-width CP with the MTP projection
+  (qwen_tts_code_predictor.c:907-924, INT8 twin) at batch 1 and batch 8: codes
+  identical to the reference's qwen_cp_predict.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import qtts_b200 as Q
+import qtts_oracle as O
+import refbind
+from models import build, rel_l2
+from test_gpu_model import check_greedy, engine_from_ref, frame_loop_reference
+
+pytestmark = [pytest.mark.gpu, pytest.mark.slow]
+
+THREADS = os.cpu_count()
+
+
+def test_c2_06b_int8_64_frames_identical(have_gpu):
+    cfg = Q.CFG_06B
+    m, path = build(cfg, seed=0, norm_gain="ones", with_cp=True)
+    ref = refbind.RefModel(path, cfg, use_int8=True, threads=THREADS)
+    eng = engine_from_ref(ref, m, cfg, "int8", with_cp=True)
+    ses = Q.Session(eng, 1, 512)
+    rng = np.random.default_rng(0)
+    for pos in range(64):
+        e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+        h = ref.talker_step(e)
+        hg = ses.talker_step(e, pos)
+    assert rel_l2(hg[0], h) < 1e-3
+    ses.set_pos([64])
+    e0 = ref.codec_embed(ref.codec_argmax(h, cfg.codebook))
+    want, hs = frame_loop_reference(ref, m, cfg, e0, 64, True)
+    got, h_gpu = ses.decode_frames(e0, 64)
+    matched = check_greedy(got[:, 0, :], want, hs, ref, m, cfg, "int8", True, near_tie_ok=False)
+    assert matched == 64
+    assert rel_l2(h_gpu[0], hs[-1]) < 1e-3
+    ref.close()
+
+
+@pytest.fixture(scope="module")
+def m17():
+    cfg = Q.CFG_17B
+    m, path = build(cfg, seed=3, norm_gain="ones", with_cp=False)
+    return cfg, m, path
+
+
+def test_c3_17b_q4_0_talker_matches_reference(have_gpu, m17):
+    cfg, m, path = m17
+    ref = refbind.RefModel(path, cfg, use_int4=True, threads=THREADS, cp=False)
+    eng = engine_from_ref(ref, m, cfg, "q4_0", with_cp=False)
+    ses = Q.Session(eng, 1, 512)
+    rng = np.random.default_rng(1)
+    worst = 0.0
+    for pos in range(128 + 32):
+        e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+        h_ref = ref.talker_step(e)
+        h_gpu = ses.talker_step(e, pos)
+        if pos >= 128:
+            worst = max(worst, rel_l2(h_gpu[0], h_ref))
+    assert worst < 1e-2, worst
+    ref.close()
+
+
+def test_c3_17b_int4g32_talker_matches_restatement(have_gpu, m17):
+    cfg, m, _ = m17
+    qd = {}
+    for i, ly in enumerate(m.talker.layers):
+        for nm in ("wq", "wk", "wv", "wo", "gate_up", "down"):
+            qd[f"{i}.{nm}"] = Q.quantize(getattr(ly, nm), Q.FMT_INT4G32)
+    cs, sn = Q.rope_tables(cfg.theta, 128, 8192)
+    eng = Q.Engine(Q.HostModel(cfg, m.talker, m.codec_head, m.codec_embedding), Q.FMT_INT4G32, rope=(cs, sn),
+                   quantized={"t" + k: v for k, v in qd.items()})
+    O.MV_F64 = False
+    try:
+        st = O.Stack(m.talker.layers, cfg.hidden, cfg.heads, cfg.kv_heads, 128, cfg.inter, cfg.eps, cs, sn,
+                     m.talker.final_norm, "int4g32", qd)
+        del qd
+        caches = O.new_caches(st, 64)
+        ses = Q.Session(eng, 1, 512)
+        rng = np.random.default_rng(2)
+        worst = 0.0
+        for pos in range(8 + 32):
+            e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+            h_ref, _ = O.talker_step(st, e, caches, pos)
+            h_gpu = ses.talker_step(e, pos)
+            if pos >= 8:
+                worst = max(worst, rel_l2(h_gpu[0], h_ref))
+        assert worst < 1e-2, worst
+    finally:
+        O.MV_F64 = True
+
+
+@pytest.mark.parametrize("batch", [1, 8])
+def test_c5_17b_cp_with_mtp_codes_identical(have_gpu, batch):
+    # the 1.7B widths (talker hidden 2048 -> MTP projection -> CP hidden 1024);
+    # two talker layers are enough, only the CP runs here
+    cfg = Q.ModelCfg(hidden=2048, inter=6144, layers=2)
+    m, path = build(cfg, seed=5, norm_gain="ones", with_cp=True)
+    assert m.mtp_w is not None
+    ref = refbind.RefModel(path, cfg, use_int8=True, threads=THREADS)
+    assert ref.cp_mtp(1, 16, np.int8) is not None   # the reference built its int8 twin
+    eng = engine_from_ref(ref, m, cfg, "int8", with_cp=True, talker=False)
+    ses = Q.Session(eng, batch)
+    rng = np.random.default_rng(6 + batch)
+    frames = 6 if batch == 1 else 2
+    for _ in range(frames):
+        hidden = rng.standard_normal((batch, cfg.hidden)).astype(np.float32)
+        code0 = rng.integers(0, cfg.codebook, batch).astype(np.int32)
+        got = ses.cp_frame(hidden, code0)
+        for b in range(batch):
+            want = ref.cp_predict(hidden[b], int(code0[b]))
+            assert np.array_equal(got[b], want), (b, got[b], want)
+    ref.close()
