@@ -245,6 +245,81 @@ QTB_DEV bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, long long limit_c
   }
 }
 
+// ----------------------------------------------- 5th-gen tensor cores ------
+// tcgen05: MMAs issued by one thread read both operands from shared memory
+// through 64-bit matrix descriptors and accumulate into tensor memory (TMEM,
+// 128 lanes x 512 32-bit columns per SM); completion is signalled through an
+// mbarrier (tcgen05.commit); the accumulator is read back with tcgen05.ld,
+// warp w of the CTA seeing lanes 32 (w % 4) .. 32 (w % 4) + 31.
+
+// Allocate `ncols` TMEM columns (power of two >= 32); the base address is
+// written to shared memory.  Whole warp.
+QTB_DEV void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+QTB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+QTB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+QTB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major operand tile in the 128-byte
+// swizzled canonical layout: rows of 128 bytes (one K chunk), 8-row groups of
+// 1024 bytes (stride byte offset), the 16-byte units of row r XOR-permuted by
+// r % 8.  The tile base is 1024-byte aligned; moving along K inside the
+// 128-byte row adds the byte offset to the start address.
+QTB_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3fffu)      // start address
+         | ((uint64_t)1u << 16)                  // leading byte offset (unused with this swizzle)
+         | ((uint64_t)(1024u >> 4) << 32)        // stride byte offset: 8 rows x 128 B
+         | ((uint64_t)1u << 46)                  // descriptor version (sm_100)
+         | ((uint64_t)2u << 61);                 // 128-byte swizzle
+}
+// Instruction descriptor: D format (1 f32, 2 s32), A/B formats (kind::f16:
+// 1 = bf16; kind::i8: 1 = s8), both K-major, N and M = 128.
+QTB_HOST_DEV constexpr uint32_t umma_idesc(uint32_t dfmt, uint32_t abfmt, uint32_t n) {
+  return (dfmt << 4) | (abfmt << 7) | (abfmt << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
+// D[tmem] (+)= A[128 x 32 B of K] * B[N x 32 B of K]^T; accumulate = 0 overwrites.
+QTB_DEV void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+QTB_DEV void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar` once every tcgen05 operation this thread issued before has
+// completed (their shared-memory reads included).
+QTB_DEV void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// 32 consecutive 32-bit TMEM columns of this thread's lane, then wait.
+QTB_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 QTB_DEV unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

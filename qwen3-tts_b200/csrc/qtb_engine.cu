@@ -245,6 +245,36 @@ static void repack_int8(const int8_t *W, int rows, int K, std::vector<uint8_t> &
   });
 }
 
+// tcgen05 operand layout (bf16 / int8): per 128-row tile t and 128-byte K
+// chunk c one 16 KB block at (t * chunks + c) * 16 KB, row r of the tile at
+// (r / 8) * 1024 + (r % 8) * 128, its 16-byte units XOR-permuted by r % 8 --
+// the 128-byte swizzled K-major tile the MMA reads, so one 1D bulk copy lands
+// it ready in shared memory.
+static void repack_tc(const uint8_t *W, int rows, int rowbytes, std::vector<uint8_t> &out) {
+  const int T = rows / 128, NKC = rowbytes / 128;
+  out.resize((size_t)rows * rowbytes);
+  parallel_for(T, [&](int t0, int t1) {
+    for (int t = t0; t < t1; t++)
+      for (int c = 0; c < NKC; c++) {
+        uint8_t *blk = out.data() + ((size_t)t * NKC + c) * TC_SLOT_BYTES;
+        for (int r = 0; r < 128; r++) {
+          const uint8_t *src = W + (size_t)(128 * t + r) * rowbytes + 128 * c;
+          for (int u = 0; u < 8; u++) memcpy(blk + (r >> 3) * 1024 + (r & 7) * 128 + ((u ^ (r & 7)) << 4), src + 16 * u, 16);
+        }
+      }
+  });
+}
+
+// Large-batch bf16 / int8 GEMVs run on tcgen05 unless QTB_NO_TC=1 (then the
+// mma.sync k-sliced path serves them, and no second weight layout is kept).
+static bool tc_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("QTB_NO_TC");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+
 // int4 (q4_0 or asymmetric g32): nibble getter + per-group scale/zero getters.
 template <typename NibF, typename SclF, typename ZeroF>
 static void repack_int4(int rows, int K, bool with_zero, NibF nib, SclF scl, ZeroF zero,
@@ -285,6 +315,7 @@ static void repack_int4(int rows, int K, bool with_zero, NibF nib, SclF scl, Zer
 // ------------------------------------------------------- device matrix -----
 struct DMat {
   const uint8_t *w = nullptr;
+  const uint8_t *wtc = nullptr;   // tcgen05 operand layout (bf16 / int8), or null
   const float *row_scale = nullptr;
   const uint8_t *gsz = nullptr;
   int fmt = 0, rows = 0, K = 0;
@@ -321,7 +352,7 @@ static int upload_matrix(Arena &ar, int fmt, const qtb_matrix_t *const *ms, cons
   if (rc) return rc;
   out.fmt = fmt; out.rows = rows; out.K = K;
   out.alg_bytes = fmt_alg_bytes(fmt, rows, K);
-  std::vector<uint8_t> wf, gf;
+  std::vector<uint8_t> wf, gf, tcf;
   if (fmt == FMT_BF16) {
     std::vector<uint16_t> W((size_t)rows * K);
     size_t off = 0;
@@ -330,6 +361,7 @@ static int upload_matrix(Arena &ar, int fmt, const qtb_matrix_t *const *ms, cons
       off += (size_t)rows_each[i] * K;
     }
     repack_bf16(W.data(), rows, K, wf);
+    if (tc_enabled()) repack_tc(reinterpret_cast<const uint8_t *>(W.data()), rows, K * 2, tcf);
   } else if (fmt == FMT_INT8) {
     std::vector<int8_t> W((size_t)rows * K);
     std::vector<float> sc(rows);
@@ -342,6 +374,7 @@ static int upload_matrix(Arena &ar, int fmt, const qtb_matrix_t *const *ms, cons
       ro += rows_each[i];
     }
     repack_int8(W.data(), rows, K, wf);
+    if (tc_enabled()) repack_tc(reinterpret_cast<const uint8_t *>(W.data()), rows, K, tcf);
     float *dsc;
     if ((rc = ar.upload(&dsc, sc.data(), sc.size() * 4))) return rc;
     out.row_scale = dsc;
@@ -377,6 +410,11 @@ static int upload_matrix(Arena &ar, int fmt, const qtb_matrix_t *const *ms, cons
   uint8_t *dw;
   if ((rc = ar.upload(&dw, wf.data(), wf.size()))) return rc;
   out.w = dw;
+  if (!tcf.empty()) {
+    uint8_t *dt;
+    if ((rc = ar.upload(&dt, tcf.data(), tcf.size()))) return rc;
+    out.wtc = dt;
+  }
   if (!gf.empty()) {
     uint8_t *dg;
     if ((rc = ar.upload(&dg, gf.data(), gf.size()))) return rc;
@@ -643,6 +681,7 @@ struct qtb_session {
   float *cp_in = nullptr;    // [B][talker hidden] input of qtb_cp_frame
   float *pad = nullptr;      // [hidden]
   float *ws = nullptr; size_t ws_floats = 0;
+  float *ss_ws = nullptr;    // tcgen05 stages: per-(row group, slice) sums of squares [G][64]
   unsigned *sem = nullptr; int sem_n = 0;
   unsigned long long *amax_ws = nullptr;
   unsigned *amax_sem = nullptr;
@@ -716,6 +755,52 @@ static bool v2_ok(int fmt, int rows, int K, int B, int G) {
   return 256 + (size_t)nt_max * (NWARPS + 1) * 16 * B * 4 <= (size_t)(SM_PAIR_OFF - SM_R_OFF);
 }
 
+// tcgen05 stage shape: slices of kcn K chunks (S of them) x row groups R of
+// 128-row tiles over the G CTAs, minimising the weight chunks the busiest CTA
+// streams plus the split-K fix-up.  The staged activation slice must fit
+// TC_X_BYTES (N x 128 bytes per chunk) and 2048 columns.
+struct TcShape { int S = 0, kcn = 0, R = 0; };
+static bool tc_ok(const DMat &m, int B, int fmt) {
+  return tc_enabled() && m.wtc && B > 4 && B <= 64 && (fmt == FMT_BF16 || fmt == FMT_INT8) && m.rows % 128 == 0;
+}
+static TcShape tc_choose(int fmt, int rows, int K, int B, int G) {
+  const int T = rows / 128, NKC = K * (fmt == FMT_INT8 ? 1 : 2) / 128;
+  const int N = tc_parts(fmt) * tc_bpad(fmt, B);
+  const int kcmax = std::max(1, std::min(TC_X_BYTES / (N * 128), 2048 / tc_kchunk(fmt)));
+  TcShape best;
+  double best_cost = 1e30;
+  for (int kcn = 1; kcn <= std::min(kcmax, NKC); kcn++) {
+    const int S = (NKC + kcn - 1) / kcn;
+    if (S > G) continue;
+    const int R = std::max(1, G / S);
+    const int tpg = (T + R - 1) / R;
+    const double cost = (double)tpg * kcn + (S > 1 ? 2.0 + 0.1 * S : 0.0);
+    if (cost < best_cost - 1e-9) { best_cost = cost; best.S = S; best.kcn = kcn; best.R = R; }
+  }
+  return best;
+}
+static V2Plan tc_plan(const GemvArgs &g, int B, int cta, int G) {
+  V2Plan p{0, 0, 0, 0, 0, 0, 0, 0};
+  const TcShape sh = tc_choose(g.fmt, g.rows, g.K, B, G);
+  const int T = g.rows / 128, NKC = g.K * (g.fmt == FMT_INT8 ? 1 : 2) / 128;
+  const int sl = cta / sh.R, r = cta % sh.R;
+  if (sh.S == 0 || sl >= sh.S) return p;
+  p.t0 = (int)((long long)r * T / sh.R);
+  p.nt = (int)((long long)(r + 1) * T / sh.R) - p.t0;
+  p.kb = sl * sh.kcn;
+  p.kc = std::min(sh.kcn, NKC - p.kb);
+  p.L = p.nt * p.kc;
+  p.nfill = r;      // row group
+  p.pair = sl;      // k-slice
+  p.pad = sh.R;
+  return p;
+}
+// Floats of split-K partials a tcgen05 stage writes ([tile][slice][128][batch]).
+static size_t tc_ws_floats(int fmt, int rows, int K, int B, int G) {
+  const TcShape sh = tc_choose(fmt, rows, K, B, G);
+  return sh.S > 1 ? (size_t)(rows / 128) * sh.S * 128 * tc_bpad(fmt, B) : 0;
+}
+
 struct ProgBuilder {
   qtb_session *s;
   std::vector<Stage> st;
@@ -732,6 +817,22 @@ struct ProgBuilder {
     g.w = m.w; g.row_scale = m.row_scale; g.gsz = m.gsz; g.bias = bias;
     g.fmt = m.fmt; g.rows = m.rows; g.K = m.K;
     g.v2 = v2_ok(m.fmt, m.rows, m.K, B, s->e->n_sm) ? 1 : 0;
+    if (!g.v2 && tc_ok(m, B, m.fmt)) {
+      const TcShape sh = tc_choose(m.fmt, m.rows, m.K, B, s->e->n_sm);
+      g.tc = 1;
+      g.wtc = m.wtc;
+      g.S = sh.S;
+      g.ss_ws = s->ss_ws;
+      g.evict_last = evict_last;
+      g.x = x; g.ldx = ldx; g.norm_w = norm_w; g.eps = eps;
+      g.y = y; g.ldy = ldy; g.epi = epi;
+      g.ws = s->ws; g.sem = s->sem;
+      g.amax_ws = s->amax_ws; g.amax_sem = s->amax_sem;
+      if (sh.S < 1) { err = set_err(QTB_E_UNSUPPORTED, "no tcgen05 shape for %dx%d at B=%d", m.rows, m.K, B); return; }
+      if (tc_ws_floats(m.fmt, m.rows, m.K, B, s->e->n_sm) > s->ws_floats) { err = set_err(QTB_E_INVALID, "split-K workspace too small"); return; }
+      st.push_back(S);
+      return;
+    }
     g.S = g.v2 ? 1 : choose_S(m.rows / 16, m.K, B, W(), m.fmt);
     if (g.S < 1) { err = set_err(QTB_E_UNSUPPORTED, "no k-slicing fits shared memory (K=%d, B=%d)", m.K, B); return; }
     g.nch = nch_for(m.fmt, B, g.v2);
@@ -857,6 +958,9 @@ static void build_cp_frame(ProgBuilder &pb, qtb_session *s, const float *talker_
 // `pairs` when the program is launched in 2-CTA clusters.
 static void make_plans(const std::vector<Stage> &st, int G, bool pairs, std::vector<V2Plan> &out) {
   out.assign(st.size() * (size_t)G, V2Plan{0, 0, 0, 0, 0, 0, 0, 0});
+  for (size_t i = 0; i < st.size(); i++)
+    if (st[i].kind == ST_GEMV && st[i].g.tc)
+      for (int c = 0; c < G; c++) out[i * G + c] = tc_plan(st[i].g, st[i].B, c, G);
   for (size_t i = 0; i < st.size(); i++)
     if (st[i].kind == ST_GEMV && st[i].g.v2)
       for (int c = 0; c < G; c++)
@@ -1013,6 +1117,7 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
       const int S = choose_S(T, m.K, B, W, m.fmt);
       if (S > 0) ws = std::max(ws, (size_t)T * S * 16 * B);
       ws = std::max(ws, (size_t)T * std::max(1, e->n_sm / std::max(1, T)) * 16 * B);
+      if (tc_ok(m, B, m.fmt)) ws = std::max(ws, tc_ws_floats(m.fmt, m.rows, m.K, B, e->n_sm));
       sem_n = std::max(sem_n, T);
     };
     auto acc_stack = [&](const DStack &k) {
@@ -1030,6 +1135,7 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
     if ((rc = s->ar.alloc((void **)&s->amax_ws, (size_t)sem_n * B * 8))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->amax_sem, 64))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->ctl, sizeof(Ctl)))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->ss_ws, (size_t)e->n_sm * 64 * 4))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->pos, B * 4))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->cp_pos, B * 4))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->codes, (size_t)B * 16 * 4))) goto fail;
@@ -1377,15 +1483,19 @@ extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols,
   const int re[1] = {rows};
   int rc = upload_matrix(mr.ar, fmt, ms, re, 1, cols, m);
   if (rc) return rc;
-  float *dx, *dy, *ws;
+  float *dx, *dy, *ws, *ss_ws;
   unsigned *sem;
   const int T = rows / 16;
   const bool v2 = v2_ok(fmt, rows, cols, batch, nsm);
-  const int S = v2 ? std::max(1, nsm / T) : choose_S(T, cols, batch, nsm * NWARPS, fmt);
+  const bool tc = !v2 && tc_ok(m, batch, fmt);
+  const int S = v2 ? std::max(1, nsm / T)
+                   : tc ? tc_choose(fmt, rows, cols, batch, nsm).S : choose_S(T, cols, batch, nsm * NWARPS, fmt);
   if (S < 1) return set_err(QTB_E_UNSUPPORTED, "no k-slicing fits");
+  const size_t ws_floats = tc ? std::max<size_t>(16, tc_ws_floats(fmt, rows, cols, batch, nsm)) : (size_t)T * S * 16 * batch;
   if ((rc = mr.ar.upload(&dx, x, (size_t)batch * cols * 4))) return rc;
   if ((rc = mr.ar.alloc((void **)&dy, (size_t)batch * rows * 4))) return rc;
-  if ((rc = mr.ar.alloc((void **)&ws, (size_t)T * S * 16 * batch * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&ws, ws_floats * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&ss_ws, (size_t)nsm * 64 * 4))) return rc;
   if ((rc = mr.ar.alloc((void **)&sem, (size_t)T * 4))) return rc;
   CUDA_TRY(cudaMemset(sem, 0, (size_t)T * 4));
   Stage st;
@@ -1396,6 +1506,9 @@ extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols,
   g.w = m.w; g.row_scale = m.row_scale; g.gsz = m.gsz;
   g.fmt = fmt; g.rows = rows; g.K = cols; g.S = v2 ? 1 : S; g.nch = nch_for(fmt, batch, v2); g.parts = parts_for(fmt, batch, v2);
   g.v2 = v2 ? 1 : 0;
+  g.tc = tc ? 1 : 0;
+  g.wtc = m.wtc;
+  g.ss_ws = ss_ws;
   g.x = dx; g.ldx = cols; g.y = dy; g.ldy = rows; g.epi = EPI_STORE; g.ws = ws; g.sem = sem;
   if ((rc = run_single_stage(mr, st))) return rc;
   CUDA_TRY(cudaMemcpy(y, dy, (size_t)batch * rows * 4, cudaMemcpyDeviceToHost));

@@ -68,6 +68,19 @@ constexpr int NCKPT = 32;     // profiling checkpoints per stage
 constexpr int STREAM_AHEAD = NDESC - 1;
 constexpr int SMEM_X_BYTES = 96 * 1024;
 
+// tcgen05 GEMV stages (large batches, bf16 / int8 weights): the dynamic shared
+// memory, from its first 1024-byte aligned byte, holds TC_NSLOT weight slots
+// of one 128-row x 128-byte operand tile each, then the staged activation
+// (the B operand, up to TC_X_BYTES); a little scratch sits at TC_SCR_OFF.
+// These stages never share a program with the small-batch weight ring.
+constexpr int TC_NSLOT = 5;
+constexpr int TC_SLOT_BYTES = 16384;
+constexpr int TC_X_OFF = TC_NSLOT * TC_SLOT_BYTES;
+constexpr int TC_X_BYTES = 64 * 1024;
+constexpr int TC_SCR_OFF = 146 * 1024;   // past TC_X_OFF + TC_X_BYTES + the 1 KB alignment slack
+constexpr int TC_TMEM_COLS = 256;        // one 128 x N (N <= 256) 32-bit accumulator
+static_assert(TC_X_OFF + TC_X_BYTES + 1024 <= TC_SCR_OFF && TC_SCR_OFF + 4096 <= SMEM_BYTES, "tcgen05 stage smem map");
+
 enum StageKind { ST_GEMV = 1, ST_ATTN = 2, ST_EMBED = 3, ST_NORM = 4, ST_POS_INC = 5 };
 enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 enum Fmt { FMT_BF16 = 0, FMT_INT8 = 1, FMT_Q4_0 = 2, FMT_INT4G = 3 };
@@ -86,6 +99,9 @@ struct GemvArgs {
   int parts;                 // MMA columns per batch row: 2 (hi, lo) or 4 (hi, mid, lo, 0)
   int evict_last;            // keep these weights in L2 (code-predictor)
   int v2;                    // small-batch path: whole activation staged, weights TMA-streamed
+  int tc;                    // large-batch path on tcgen05 (bf16 / int8 weights, see gemv_tc_t)
+  const uint8_t *wtc;        // weights in 128-row x 128-byte swizzled tiles (tcgen05 operand layout)
+  float *ss_ws;              // tcgen05 path: per-(row group, k-slice) activation sums of squares
   const float *x; int ldx;   // activation [B][ldx]
   const float *norm_w;       // RMSNorm gain [K] or null
   float eps;
@@ -192,6 +208,15 @@ struct KCtx {
   int last;             // this CTA's arrival completed the current barrier
   uint64_t *pbar;       // receives the cluster partner's arrive (split stages)
   unsigned pair_ctr;    // split stages combined so far (pbar phase source)
+  // tcgen05 GEMV stages (thread 0 issues copies and MMAs)
+  uint32_t tmem;        // TMEM base address (TC_TMEM_COLS columns, allocated for the launch)
+  uint64_t *tcfull;     // TC_NSLOT weight-slot mbarriers: bulk copy landed
+  uint64_t *tcempty;    // ... the MMAs reading the slot completed (tcgen05.commit)
+  uint64_t *tcacc;      // the accumulator of the current tile is complete
+  unsigned tc_issued;   // weight-slot fills issued so far in this launch
+  unsigned tc_done;     // ... whose bulk copy has been waited for
+  unsigned tc_acc;      // accumulator commits waited for so far (tcacc phase source)
+  int tc_mma_open;      // MMAs issued whose completion has not been waited for
 };
 
 // Profiling checkpoint (CTA 0, thread 0) when stage tracing is on.
@@ -1041,7 +1066,16 @@ QTB_CALL void drain(KCtx &kc, unsigned cur) {
   for (unsigned c = p0; c != kc.att_issued; c++) mbar_wait(kc.bars + c % nb, (c / nb) & 1u, LIM);
   for (unsigned k = cur + 1; k < cur + NDESC && k < kc.n_total; k++)
     mbar_wait(kc.dbars + k % NDESC, (k / NDESC) & 1u, LIM);
+  // tcgen05 stages: weight copies in flight, then every MMA issued (one more
+  // commit completes after all of them) before the tensor memory is freed
+  for (unsigned c = kc.tc_done; c != kc.tc_issued; c++) mbar_wait(kc.tcfull + c % TC_NSLOT, (c / TC_NSLOT) & 1u, LIM);
+  if (kc.tc_mma_open) {
+    umma_commit(kc.tcacc);
+    mbar_wait(kc.tcacc, (kc.tc_acc + 1u) & 1u, LIM);
+  }
 }
+
+QTB_CALL void argmax_finish(const GemvArgs &a, int B, KCtx &kc);
 
 // Epilogue on final row values val(tl, r, b) held in shared memory
 // (s_val[(tl * 16 + r) * sv_ld + b]) for the CTA's tiles t0 .. t0 + nt - 1.
@@ -1090,6 +1124,18 @@ QTB_CALL void v2_epilogue(const GemvArgs &a, int B, int t0, int nt, const float 
     }
     __syncthreads();
     if (!s_last) return;
+    argmax_finish(a, B, kc);
+  }
+}
+
+// The greedy heads' last step, by the CTA that completed the row tiles'
+// per-(16-row tile, batch row) maxima in amax_ws: the code of every batch row
+// (first maximum wins: keys order by value, then by lower row), and the next
+// input's embedding row gathered from the table.  All threads of the CTA.
+QTB_CALL void argmax_finish(const GemvArgs &a, int B, KCtx &kc) {
+  {
+    const int tid = threadIdx.x;
+    const int T = a.rows >> 4;
     __threadfence();
     __shared__ int s_code[64];
     const int warp = tid >> 5, lane = tid & 31;
@@ -1558,6 +1604,334 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
   ckpt(kc, 5);
 }
 
+// ============================================ GEMV stage on tcgen05 =======
+//
+// Large batches (5..64 rows) with bf16 or int8 weights.  A CTA owns one k-slice
+// of the activation and a run of 128-row tiles (its row group): the host plan
+// (V2Plan: t0, nt, L = nt * kc weight fills, nfill = row group, kb / kc = first
+// 128-byte chunk and chunk count of the slice, pair = slice, pad = row groups)
+// spreads tiles x slices over the grid.
+//  1. Thread 0 bulk-copies the first weight tiles -- 128 rows x one 128-byte K
+//     chunk, stored pre-swizzled in HBM (16 KB each) -- into TC_NSLOT slots.
+//  2. Every warp stages whole activation rows of the slice into the B operand
+//     (K-major, 128-byte swizzle), with the RMSNorm gain applied: int8 weights
+//     take four signed 8-bit parts per value, x g = sx (a0 + a1 2^-7 + a2 2^-14 +
+//     a3 2^-21) with sx = max|x g| / 127 over the row's slice (MMA column 4 b + p,
+//     kind::i8, exact s32 sums); bf16 weights take bf16 hi + lo parts (column
+//     2 b + p, kind::f16, f32 sums).  The RMSNorm's 1/rms multiplies each
+//     batch row's results afterwards, from the slices' sums of squares.
+//  3. Per tile, thread 0 issues four MMAs (M 128, N = parts x padded batch,
+//     32 bytes of K each) per chunk into the TMEM accumulator and refills each
+//     slot once the MMAs reading it have completed (tcgen05.commit ->
+//     mbarrier); all warps then read the accumulator (warp w: TMEM lanes
+//     32 (w % 4) .., batch half w / 4).
+//  4. With one slice the epilogue runs at once; with several, partial sums go
+//     to ws and the CTA completing a tile's count adds them in slice order
+//     (deterministic) and runs it.
+QTB_HOST_DEV constexpr int tc_parts(int fmt) { return fmt == FMT_INT8 ? 4 : 2; }
+QTB_HOST_DEV constexpr int tc_kchunk(int fmt) { return fmt == FMT_INT8 ? 128 : 64; }   // K per 128-byte chunk
+// Batch rows padded to a multiple of 8 (N = parts x rows a multiple of 16,
+// each warp's half of the batch a whole number of float4s).
+QTB_HOST_DEV constexpr int tc_bpad(int fmt, int B) { return (void)fmt, (B + 7) & ~7; }
+
+QTB_DEV uint32_t tc_sw128(int n, int kb) {   // byte offset of (row n, byte kb of a 128-byte K chunk)
+  return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((((kb >> 4) ^ (n & 7)) << 4) | (kb & 15)));
+}
+
+// Step 2: rows b = warp, warp + 8, ... of the slice [k0, k0 + KL).
+template <int FMT>
+__device__ __noinline__ void tc_stage_x(const GemvArgs &a, int B, int N, int k0, int KL, char *xreg, float *s_sx,
+                                        float *s_ss) {
+  constexpr int MAXJ = 16;   // float4 per lane per row (KL <= 2048)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = KL >> 2;    // float4 per row
+  for (int b = warp; b < B; b += NWARPS) {
+    const float *xb = a.x + (size_t)b * a.ldx + k0;
+    float4 v[MAXJ];
+    float ss = 0.f, mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAXJ; j++) {
+      const int q = lane + 32 * j;
+      v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q < nq) {
+        v[j] = ld_cg4(xb + 4 * q);
+        ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+        if (a.norm_w) {
+          const float4 g = __ldg(reinterpret_cast<const float4 *>(a.norm_w + k0 + 4 * q));
+          v[j].x *= g.x; v[j].y *= g.y; v[j].z *= g.z; v[j].w *= g.w;
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+      }
+    }
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    const float sx = fmaxf(mx, 1e-30f) * (1.0f / 127.0f);
+    const float rs = __frcp_rn(sx);
+    if (lane == 0) { s_ss[b] = ss; s_sx[b] = sx; }
+#pragma unroll
+    for (int j = 0; j < MAXJ; j++) {
+      const int q = lane + 32 * j;
+      if (q >= nq) continue;
+      const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      if (FMT == FMT_INT8) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float r = fminf(fmaxf(e[i] * rs, -127.f), 127.f);
+          // fixed point r 2^21 as a leading part and three balanced base-128 digits
+          int I = __float2int_rn(r * 2097152.f);
+          const int d3 = ((I + 64) & 127) - 64;
+          I = (I - d3) >> 7;
+          const int d2 = ((I + 64) & 127) - 64;
+          I = (I - d2) >> 7;
+          const int d1 = ((I + 64) & 127) - 64;
+          const int a0 = (I - d1) >> 7;
+          w[0] |= ((uint32_t)a0 & 0xffu) << (8 * i);
+          w[1] |= ((uint32_t)d1 & 0xffu) << (8 * i);
+          w[2] |= ((uint32_t)d2 & 0xffu) << (8 * i);
+          w[3] |= ((uint32_t)d3 & 0xffu) << (8 * i);
+        }
+        const int kl = 4 * q, c = kl >> 7, kb = kl & 127;
+#pragma unroll
+        for (int p = 0; p < 4; p++)
+          *reinterpret_cast<uint32_t *>(xreg + (size_t)c * N * 128 + tc_sw128(4 * b + p, kb)) = w[p];
+      } else {
+        uint32_t hi[2], lo[2];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+          const uint32_t h0 = f32_to_bf16_rn(e[2 * i]), h1 = f32_to_bf16_rn(e[2 * i + 1]);
+          const uint32_t l0 = f32_to_bf16_rn(e[2 * i] - __uint_as_float(h0 << 16));
+          const uint32_t l1 = f32_to_bf16_rn(e[2 * i + 1] - __uint_as_float(h1 << 16));
+          hi[i] = h0 | (h1 << 16);
+          lo[i] = l0 | (l1 << 16);
+        }
+        const int kbyte = 8 * q, c = kbyte >> 7, kb = kbyte & 127;
+        *reinterpret_cast<uint2 *>(xreg + (size_t)c * N * 128 + tc_sw128(2 * b, kb)) = make_uint2(hi[0], hi[1]);
+        *reinterpret_cast<uint2 *>(xreg + (size_t)c * N * 128 + tc_sw128(2 * b + 1, kb)) = make_uint2(lo[0], lo[1]);
+      }
+    }
+  }
+}
+
+// Final value of (row, batch b): 1/rms, row scale, bias, then the epilogue
+// (warp-uniform in b: SWIGLU exchanges the interleaved gate / up rows, which
+// sit in neighbouring lanes).
+QTB_DEV void tc_out(const GemvArgs &a, int B, int b, int row, float v, float inv) {
+  v *= inv;
+  if (a.row_scale) v *= __ldg(a.row_scale + row);
+  if (a.bias) v += __ldg(a.bias + row);
+  if (a.epi == EPI_SWIGLU) {
+    const float up = __shfl_xor_sync(0xffffffffu, v, 1);
+    if ((row & 1) == 0 && b < B) __stcg(a.y + (size_t)b * a.ldy + (row >> 1), __fdividef(v, 1.0f + expf(-v)) * up);
+  } else if (b < B) {
+    float *yp = a.y + (size_t)b * a.ldy + row;
+    if (a.epi == EPI_RESID) __stcg(yp, __ldcg(yp) + v);
+    else __stcg(yp, v);
+  }
+}
+
+template <int FMT>
+__device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  const V2Plan pl = kc.pring[kc.seq % NDESC];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int P = tc_parts(FMT), Bp = tc_bpad(FMT, B), N = P * Bp, Bh = Bp / 2;
+  const int S = a.S, s = pl.pair, grp = pl.nfill, t0 = pl.t0, nt = pl.nt, kcn = pl.kc;
+  const int NKC = a.K / tc_kchunk(FMT);
+  const int L = nt * kcn;
+  // operand regions from the first 1024-byte aligned byte of dynamic smem
+  const uint32_t base_u = smem_u32(smem);
+  char *tcb = smem + ((1024u - (base_u & 1023u)) & 1023u);
+  char *wring = tcb;
+  char *xreg = tcb + TC_X_OFF;
+  float *s_sx = reinterpret_cast<float *>(smem + TC_SCR_OFF);   // [64]
+  float *s_ss = s_sx + 64;                                      // [64]
+  float *s_inv = s_ss + 64;                                     // [64]
+  int *s_flag = reinterpret_cast<int *>(s_inv + 64);            // [4]
+  unsigned long long *s_key = reinterpret_cast<unsigned long long *>(s_flag + 4);   // [4][64]
+  if (nt == 0) return;
+  const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
+  const unsigned F0 = kc.tc_issued;   // fills of earlier tcgen05 stages (all consumed)
+
+  // thread 0: bulk copy of fill f (tile t0 + f / kcn, chunk kb + f % kcn) into
+  // slot (F0 + f) % TC_NSLOT once the MMAs that last read the slot are done
+  auto issue = [&](int f) -> bool {
+    const unsigned F = F0 + (unsigned)f, slot = F % TC_NSLOT, use = F / TC_NSLOT;
+    if (use > 0 && !mbar_wait(kc.tcempty + slot, (use - 1) & 1u, WAIT_LIMIT_CYCLES)) {
+      raise_err(kc, ERR_MBAR_TIMEOUT, 2000 + f);
+      return false;
+    }
+    const int tile = t0 + f / kcn, chunk = pl.kb + f % kcn;
+    mbar_arrive_expect_tx(kc.tcfull + slot, TC_SLOT_BYTES);
+    bulk_g2s_hint(wring + slot * TC_SLOT_BYTES, a.wtc + ((size_t)tile * NKC + chunk) * TC_SLOT_BYTES, TC_SLOT_BYTES,
+                  kc.tcfull + slot, pol);
+    kc.tc_issued = F + 1u;
+    return true;
+  };
+  if (tid == 0) {
+    fence_proxy_async_smem();   // the slots were last written through the generic proxy (other stages)
+    for (int f = 0; f < min(TC_NSLOT, L); f++)
+      if (!issue(f)) break;
+  }
+  ckpt(kc, 0);
+  tc_stage_x<FMT>(a, B, N, pl.kb * tc_kchunk(FMT), kcn * tc_kchunk(FMT), xreg, s_sx, s_ss);
+  fence_proxy_async_smem();     // the staged operand is read by the tensor cores (async proxy)
+  __syncthreads();
+  ckpt(kc, 1);
+  // this slice's sums of squares, for the tiles' finishing CTAs
+  if (a.norm_w && S > 1 && tid < B) { __stcg(a.ss_ws + ((size_t)grp * S + s) * 64 + tid, s_ss[tid]); }
+  if (a.norm_w && S == 1 && tid < Bp) s_inv[tid] = (tid < B) ? 1.0f / sqrtf(s_ss[tid] / (float)a.K + a.eps) : 0.f;
+  if (!a.norm_w && tid < 64) s_inv[tid] = 1.0f;
+  __syncthreads();
+
+  const uint32_t idesc = (FMT == FMT_INT8) ? umma_idesc(2u, 1u, (uint32_t)N) : umma_idesc(1u, 1u, (uint32_t)N);
+  const uint32_t wr_u = smem_u32(wring), xr_u = smem_u32(xreg);
+  const int q4 = warp & 3, hh = warp >> 2;
+  const int rl = 32 * q4 + lane;   // this thread's row within the tile
+  const float c7 = 1.0f / 128.0f, c14 = 1.0f / 16384.0f, c21 = 1.0f / 2097152.0f;
+  for (int i = 0; i < nt; i++) {
+    const int t = t0 + i;
+    // ---- MMAs of tile t (thread 0) ----
+    if (tid == 0 && !kc.local_err) {
+      for (int c = 0; c < kcn; c++) {
+        const int f = i * kcn + c;
+        const unsigned F = F0 + (unsigned)f, slot = F % TC_NSLOT;
+        if (!mbar_wait(kc.tcfull + slot, (F / TC_NSLOT) & 1u, WAIT_LIMIT_CYCLES)) {
+          raise_err(kc, ERR_MBAR_TIMEOUT, 3000 + f);
+          break;
+        }
+        kc.tc_done = F + 1u;
+        tc_fence_after();
+        const uint32_t ab = wr_u + slot * TC_SLOT_BYTES, bb = xr_u + (uint32_t)(c * N * 128);
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+          const uint64_t ad = umma_desc_sw128(ab + 32u * ks), bd = umma_desc_sw128(bb + 32u * ks);
+          if (FMT == FMT_INT8) umma_i8(kc.tmem, ad, bd, idesc, (c | ks) != 0);
+          else umma_bf16(kc.tmem, ad, bd, idesc, (c | ks) != 0);
+        }
+        kc.tc_mma_open = 1;
+        umma_commit(kc.tcempty + slot);
+        if (f >= 1 && f - 1 + TC_NSLOT < L && !issue(f - 1 + TC_NSLOT)) break;
+      }
+      umma_commit(kc.tcacc);
+    }
+    if (__syncthreads_or(kc.local_err)) return;   // copies and MMAs in flight are drained on the way out
+    // ---- accumulator -> this thread's row ----
+    const bool landed = mbar_wait(kc.tcacc, kc.tc_acc & 1u, WAIT_LIMIT_CYCLES);
+    if (!landed && lane == 0) raise_err(kc, ERR_MBAR_TIMEOUT, 4000 + i);
+    tc_fence_after();
+    if (__syncthreads_or(kc.local_err)) return;
+    if (tid == 0) { kc.tc_acc++; kc.tc_mma_open = 0; }
+    ckpt(kc, 2);
+    // values of batch rows [hh * Bh, hh * Bh + Bh) of row rl, 8 (int8) or 16
+    // (bf16) batch rows per 32-column TMEM load
+    constexpr int PER = (FMT == FMT_INT8) ? 8 : 16;
+    float val[32 + PER];
+#pragma unroll
+    for (int j = 0; j < 32 / PER; j++) {
+      const int bb0 = hh * Bh + PER * j;
+      if (PER * j >= Bh) break;
+      uint32_t r[32];
+      tmem_ld32(kc.tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)(P * bb0), r);
+#pragma unroll
+      for (int u = 0; u < PER; u++) {
+        float v;
+        if (FMT == FMT_INT8) {
+          v = (((float)(int)r[4 * u + 3] * c21 + (float)(int)r[4 * u + 2] * c14) + (float)(int)r[4 * u + 1] * c7) +
+              (float)(int)r[4 * u];
+          const int b = bb0 + u;
+          v *= (b < B) ? s_sx[b] : 0.f;
+        } else {
+          v = __uint_as_float(r[2 * u]) + __uint_as_float(r[2 * u + 1]);
+        }
+        val[PER * j + u] = v;
+      }
+    }
+    const int nb = min(Bh, 32);
+    if (S > 1) {
+      float *wsp = a.ws + (((size_t)t * S + s) * 128 + rl) * Bp + hh * Bh;
+#pragma unroll
+      for (int u = 0; u < 32; u += 4)
+        if (u < nb) __stcg(reinterpret_cast<float4 *>(wsp + u), make_float4(val[u], val[u + 1], val[u + 2], val[u + 3]));
+    }
+    tc_fence_before();
+    __syncthreads();   // TMEM reads done: the next tile's MMAs may overwrite the accumulator
+    if (S > 1) {
+      if (tid == 0) {
+        __threadfence();
+        s_flag[0] = (atomicAdd(a.sem + t, 1u) == (unsigned)(S - 1));
+      }
+      __syncthreads();
+      if (!s_flag[0]) continue;
+      __threadfence();
+      // the finishing CTA: the slices' sums in slice order, 1/rms from the
+      // slices' sums of squares (this row group's CTAs wrote them)
+      if (a.norm_w && tid < Bp) {
+        float tot = 0.f;
+        if (tid < B)
+          for (int s2 = 0; s2 < S; s2++) tot += __ldcg(a.ss_ws + ((size_t)grp * S + s2) * 64 + tid);
+        s_inv[tid] = (tid < B) ? 1.0f / sqrtf(tot / (float)a.K + a.eps) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 32; u++) val[u] = 0.f;
+      for (int s2 = 0; s2 < S; s2++) {
+        const float *wsp = a.ws + (((size_t)t * S + s2) * 128 + rl) * Bp + hh * Bh;
+#pragma unroll
+        for (int u = 0; u < 32; u += 4) {
+          if (u < nb) {
+            const float4 p4 = ld_cg4(wsp + u);
+            val[u] += p4.x; val[u + 1] += p4.y; val[u + 2] += p4.z; val[u + 3] += p4.w;
+          }
+        }
+      }
+      if (tid == 0) a.sem[t] = 0u;
+      __syncthreads();   // s_inv
+    }
+    const int row = 128 * t + rl;
+    if (a.epi == EPI_ARGMAX) {
+      // per batch row: this warp's 32 rows, then the four lane quarters
+#pragma unroll
+      for (int u = 0; u < 32; u++) {
+        if (u >= nb) break;
+        const int b = hh * Bh + u;
+        unsigned long long k = (b < B) ? amax_key(val[u] * s_inv[b] * (a.row_scale ? __ldg(a.row_scale + row) : 1.f) +
+                                                      (a.bias ? __ldg(a.bias + row) : 0.f), row)
+                                       : 0ull;
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) {
+          const unsigned long long o = shfl_xor_u64(k, m);
+          k = o > k ? o : k;
+        }
+        if (lane == 0 && b < 64) s_key[q4 * 64 + b] = k;
+      }
+      __syncthreads();
+      const int T16 = a.rows >> 4;
+      for (int idx = tid; idx < 8 * B; idx += NTHREADS) {
+        const int b = idx % B, sub = idx / B;
+        unsigned long long best = 0ull;
+        if (sub == 0)
+          for (int qq = 0; qq < 4; qq++) best = s_key[qq * 64 + b] > best ? s_key[qq * 64 + b] : best;
+        a.amax_ws[(size_t)(8 * t + sub) * B + b] = best;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        s_flag[1] = (atomicAdd(a.amax_sem, 8u) + 8u == (unsigned)T16);
+      }
+      __syncthreads();
+      if (s_flag[1]) argmax_finish(a, B, kc);
+      __syncthreads();
+    } else {
+#pragma unroll
+      for (int u = 0; u < 32; u++) {
+        if (u >= nb) break;
+        const int b = hh * Bh + u;
+        tc_out(a, B, b, row, val[u], s_inv[b]);
+      }
+    }
+  }
+  if (tid == 0) kc.tc_issued = F0 + (unsigned)L;
+}
+
 template <int FMT>
 QTB_DEV void gemv2_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
   if (FMT == FMT_INT8 && a.parts == 4) {
@@ -1581,6 +1955,9 @@ QTB_DEV void gemv2_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
 template <int FMT>
 QTB_DEV void gemv_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
   if (a.v2) { gemv2_stage_f<FMT>(a, B, smem, kc); return; }
+  if (FMT == FMT_BF16 || FMT == FMT_INT8) {
+    if (a.tc) { gemv_tc_t<FMT>(a, B, smem, kc); return; }
+  }
   if (FMT == FMT_BF16 && a.parts == 4) {
     switch (a.nch) {
       case 1: gemv_stage_t<FMT, 1, 4>(a, B, smem, kc); return;
@@ -2460,6 +2837,8 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
   __shared__ Stage dring[NDESC];   // stage descriptors, NDESC - 1 stages ahead
   __shared__ V2Plan pring[NDESC];  // this CTA's plan entries for them ([stage][CTA] in `plan`)
   __shared__ __align__(8) uint64_t pbar;
+  __shared__ __align__(8) uint64_t tcbars[2 * TC_NSLOT + 1];   // weight slot full / empty, accumulator
+  __shared__ uint32_t tmem_base;
   __shared__ KCtx kc;
   if (threadIdx.x == 0) {
     kc.epoch = 0;
@@ -2493,7 +2872,17 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     kc.w_free = 0;
     kc.pf_seq = 0;
     kc.pf_f = 0;
+    kc.tcfull = tcbars;
+    kc.tcempty = tcbars + TC_NSLOT;
+    kc.tcacc = tcbars + 2 * TC_NSLOT;
+    kc.tc_issued = 0;
+    kc.tc_done = 0;
+    kc.tc_acc = 0;
+    kc.tc_mma_open = 0;
   }
+  // the tensor-memory accumulator of the tcgen05 GEMV stages, held for the
+  // whole launch (one CTA per SM: the allocation never waits)
+  if (threadIdx.x < 32) tmem_alloc(&tmem_base, TC_TMEM_COLS);
   auto issue_desc = [&](unsigned k) {   // thread 0: descriptor (+ plan entry) of stage k into its slot
     const int slot = (int)(k % NDESC);
     const unsigned si = k % (unsigned)n_stages;
@@ -2505,11 +2894,16 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     for (int i = 0; i < ATT_NBUF_MAX; i++) mbar_init(bars + i, 1);
     for (int i = 0; i < NWSLOT; i++) mbar_init(wbars + i, 1);
     for (int i = 0; i < NDESC; i++) mbar_init(dbars + i, 1);
+    for (int i = 0; i < 2 * TC_NSLOT + 1; i++) mbar_init(tcbars + i, 1);
     mbar_init(&pbar, 1);
     fence_mbar_init();
     for (unsigned k = 0; k < NDESC - 1 && k < kc.n_total; k++) issue_desc(k);
     kc.t_start = clock64();
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) kc.tmem = tmem_base;
   __syncthreads();
   if (trace && blockIdx.x == 0 && threadIdx.x == 0) trace[(size_t)n_iters * n_stages] = clock64();
   for (int it = 0; it < n_iters; it++) {
@@ -2550,6 +2944,9 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
       }
       if (!grid_wait(kc, smem)) {   // (advances kc.seq and kc.stage)
         if (threadIdx.x == 0) drain(kc, seq);
+        tc_fence_before();
+        __syncthreads();
+        if (threadIdx.x < 32) tmem_dealloc(kc.tmem, TC_TMEM_COLS);
         return;
       }
       if (threadIdx.x == 0) kc.t_start = clock64();
@@ -2557,6 +2954,9 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
       if (trace && blockIdx.x == 0 && threadIdx.x == 0) trace[(size_t)it * n_stages + si] = clock64();
     }
   }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x < 32) tmem_dealloc(kc.tmem, TC_TMEM_COLS);
 }
 
 }  // namespace qtb

@@ -29,26 +29,47 @@ pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 THREADS = os.cpu_count()
 
 
-def test_c2_06b_int8_64_frames_identical(have_gpu):
+def first_fork(a, b):
+    d = np.argwhere(np.asarray(a) != np.asarray(b))
+    return (int(d[0][0]), int(d[0][1])) if len(d) else (len(a), -1)
+
+
+def test_c2_06b_int8_64_frames_match_reference(have_gpu):
+    """64 whole greedy frames (1 024 codes) against the reference's frame loop.
+    Greedy codes are defined only up to the reference's own f32 arithmetic:
+    its AVX2 build and its AVX-512 build, on the same weights and inputs,
+    disagree at the first near-tie of the logits.  So the engine must agree
+    with the AVX-512 build on every code up to the first frame at which the
+    reference's two builds disagree (here frame 45, head 6: the engine forks at
+    that same code), and fork only at a near-tie of the reference's logits."""
     cfg = Q.CFG_06B
     m, path = build(cfg, seed=0, norm_gain="ones", with_cp=True)
-    ref = refbind.RefModel(path, cfg, use_int8=True, threads=THREADS)
+    ref = refbind.RefModel(path, cfg, use_int8=True, threads=THREADS, flavour="avx512")
+    ref2 = refbind.RefModel(path, cfg, use_int8=True, threads=THREADS, flavour="avx2")
     eng = engine_from_ref(ref, m, cfg, "int8", with_cp=True)
     ses = Q.Session(eng, 1, 512)
     rng = np.random.default_rng(0)
     for pos in range(64):
         e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
         h = ref.talker_step(e)
+        ref2.talker_step(e)
         hg = ses.talker_step(e, pos)
     assert rel_l2(hg[0], h) < 1e-3
     ses.set_pos([64])
     e0 = ref.codec_embed(ref.codec_argmax(h, cfg.codebook))
     want, hs = frame_loop_reference(ref, m, cfg, e0, 64, True)
+    want2, _ = frame_loop_reference(ref2, m, cfg, e0, 64, True)
     got, h_gpu = ses.decode_frames(e0, 64)
-    matched = check_greedy(got[:, 0, :], want, hs, ref, m, cfg, "int8", True, near_tie_ok=False)
-    assert matched == 64
-    assert rel_l2(h_gpu[0], hs[-1]) < 1e-3
+    f_gpu, f_ref = first_fork(got[:, 0, :], want), first_fork(want2, want)
+    print(f"first fork from the AVX-512 reference: engine {f_gpu}, the reference's AVX2 build {f_ref}")
+    assert f_gpu[0] >= min(f_ref[0], 64), (f_gpu, f_ref)
+    if f_gpu[0] < 64:
+        # and that fork sits at a near-tie of the reference's own logits
+        check_greedy(got[:, 0, :], want, hs, ref, m, cfg, "int8", True, near_tie_ok=True)
+    else:
+        assert rel_l2(h_gpu[0], hs[-1]) < 1e-3
     ref.close()
+    ref2.close()
 
 
 @pytest.fixture(scope="module")
@@ -115,6 +136,7 @@ def test_c5_17b_cp_with_mtp_codes_identical(have_gpu, batch):
     assert ref.cp_mtp(1, 16, np.int8) is not None   # the reference built its int8 twin
     eng = engine_from_ref(ref, m, cfg, "int8", with_cp=True, talker=False)
     ses = Q.Session(eng, batch)
+    one = Q.Session(eng, 1) if batch > 1 else ses
     rng = np.random.default_rng(6 + batch)
     frames = 6 if batch == 1 else 2
     for _ in range(frames):
@@ -122,6 +144,9 @@ def test_c5_17b_cp_with_mtp_codes_identical(have_gpu, batch):
         code0 = rng.integers(0, cfg.codebook, batch).astype(np.int32)
         got = ses.cp_frame(hidden, code0)
         for b in range(batch):
+            single = one.cp_frame(hidden[b], int(code0[b]))[0]
             want = ref.cp_predict(hidden[b], int(code0[b]))
-            assert np.array_equal(got[b], want), (b, got[b], want)
+            # the batched slots equal the single-slot path, and both the reference
+            assert np.array_equal(got[b], single), ("batched vs single", b, got[b], single)
+            assert np.array_equal(got[b], want), ("vs reference", b, got[b], want)
     ref.close()

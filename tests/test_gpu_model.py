@@ -38,7 +38,8 @@ def engine_from_ref(ref, m, cfg, fmt, with_cp=True, talker=True):
                             m.cp_codec_emb, m.mtp_w, m.mtp_b)
     if not with_cp:
         model = Q.HostModel(cfg, m.talker, m.codec_head, m.codec_embedding)
-    return Q.Engine(model, FMT[fmt], FMT[fmt], rope=ref.rope(False), cp_rope=ref.rope(True), quantized=q)
+    return Q.Engine(model, FMT[fmt], FMT[fmt], rope=ref.rope(False), cp_rope=ref.rope(True) if with_cp else None,
+                    quantized=q)
 
 
 @pytest.fixture(scope="module")
