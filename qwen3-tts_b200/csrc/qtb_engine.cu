@@ -690,6 +690,8 @@ struct qtb_session {
   Ctl *ctl = nullptr;
   Stage *prog[PROG_N] = {};
   V2Plan *plan[PROG_N] = {};   // [stage][CTA] shares of the small-batch GEMV stages
+  unsigned *tc_sem[PROG_N] = {};   // per-tile counters of the split tcgen05 stages
+  int tc_sem_n[PROG_N] = {};
   int prog_n[PROG_N] = {};
   int has_pad = 0;
   long long *trace = nullptr;   // per-stage clock64 trace (CTA 0), profiling only
@@ -769,7 +771,7 @@ static TcShape tc_choose(int fmt, int rows, int K, int B, int G) {
   const int kcmax = std::max(1, std::min(TC_X_BYTES / (N * 128), 2048 / tc_kchunk(fmt)));
   TcShape best;
   double best_cost = 1e30;
-  for (int kcn = 1; kcn <= std::min(kcmax, NKC); kcn++) {
+  for (int kcn = 1; kcn <= std::min(kcmax, NKC); kcn *= 2) {   // powers of two (activation staging)
     const int S = (NKC + kcn - 1) / kcn;
     if (S > G) continue;
     const int R = std::max(1, G / S);
@@ -977,6 +979,20 @@ static int upload_prog(qtb_session *s, int which, ProgBuilder &pb) {
   for (const Stage &st : pb.st) streams |= (st.kind == ST_GEMV && st.g.v2);
   for (Stage &st : pb.st)
     if (st.kind == ST_ATTN && streams) st.a.nbuf = ATT_NBUF;
+  // per-tile counters of the split tcgen05 stages: a disjoint range per stage,
+  // zeroed at every launch of the program
+  int tc_sem_n = 0;
+  for (Stage &st : pb.st)
+    if (st.kind == ST_GEMV && st.g.tc && st.g.S > 1) { st.g.sem_off = tc_sem_n; tc_sem_n += st.g.rows / 128; }
+  if (tc_sem_n > 0) {
+    unsigned *ts;
+    int rc0 = s->ar.alloc((void **)&ts, (size_t)tc_sem_n * 4);
+    if (rc0) return rc0;
+    for (Stage &st : pb.st)
+      if (st.kind == ST_GEMV && st.g.tc && st.g.S > 1) st.g.sem = ts;
+    s->tc_sem[which] = ts;
+  }
+  s->tc_sem_n[which] = tc_sem_n;
   Stage *d;
   int rc = s->ar.upload(&d, pb.st.data(), pb.st.size() * sizeof(Stage));
   if (rc) return rc;
@@ -1242,6 +1258,8 @@ static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
     return set_err(QTB_E_INVALID, "too many iterations for one launch");
   CUDA_TRY(cudaMemsetAsync(&s->ctl->bar_count, 0, sizeof(unsigned), s->stream));
   CUDA_TRY(cudaMemsetAsync(&s->ctl->att_work, 0, sizeof(unsigned), s->stream));
+  if (s->tc_sem_n[which] > 0)
+    CUDA_TRY(cudaMemsetAsync(s->tc_sem[which], 0, (size_t)s->tc_sem_n[which] * sizeof(unsigned), s->stream));
   const Stage *prog = s->prog[which];
   const V2Plan *plan = s->plan[which];
   int n_st = s->prog_n[which];

@@ -78,7 +78,8 @@ constexpr int TC_SLOT_BYTES = 16384;
 constexpr int TC_X_OFF = TC_NSLOT * TC_SLOT_BYTES;
 constexpr int TC_X_BYTES = 64 * 1024;
 constexpr int TC_SCR_OFF = 146 * 1024;   // past TC_X_OFF + TC_X_BYTES + the 1 KB alignment slack
-constexpr int TC_TMEM_COLS = 256;        // one 128 x N (N <= 256) 32-bit accumulator
+constexpr int TC_ACC_COLS = 256;         // one 128 x N (N <= 256) 32-bit accumulator
+constexpr int TC_TMEM_COLS = 2 * TC_ACC_COLS;   // two: a tile is read back while the next accumulates
 static_assert(TC_X_OFF + TC_X_BYTES + 1024 <= TC_SCR_OFF && TC_SCR_OFF + 4096 <= SMEM_BYTES, "tcgen05 stage smem map");
 
 enum StageKind { ST_GEMV = 1, ST_ATTN = 2, ST_EMBED = 3, ST_NORM = 4, ST_POS_INC = 5 };
@@ -102,6 +103,7 @@ struct GemvArgs {
   int tc;                    // large-batch path on tcgen05 (bf16 / int8 weights, see gemv_tc_t)
   const uint8_t *wtc;        // weights in 128-row x 128-byte swizzled tiles (tcgen05 operand layout)
   float *ss_ws;              // tcgen05 path: per-(row group, k-slice) activation sums of squares
+  int sem_off;               // tcgen05 path: this stage's per-tile counters are sem[sem_off + tile]
   const float *x; int ldx;   // activation [B][ldx]
   const float *norm_w;       // RMSNorm gain [K] or null
   float eps;
@@ -212,11 +214,11 @@ struct KCtx {
   uint32_t tmem;        // TMEM base address (TC_TMEM_COLS columns, allocated for the launch)
   uint64_t *tcfull;     // TC_NSLOT weight-slot mbarriers: bulk copy landed
   uint64_t *tcempty;    // ... the MMAs reading the slot completed (tcgen05.commit)
-  uint64_t *tcacc;      // the accumulator of the current tile is complete
+  uint64_t *tcacc;      // [2] the accumulator in TMEM buffer 0 / 1 is complete
   unsigned tc_issued;   // weight-slot fills issued so far in this launch
   unsigned tc_done;     // ... whose bulk copy has been waited for
-  unsigned tc_acc;      // accumulator commits waited for so far (tcacc phase source)
-  int tc_mma_open;      // MMAs issued whose completion has not been waited for
+  unsigned tc_committed;// tile accumulators committed so far (the g-th uses buffer g & 1)
+  unsigned tc_waited;   // ... and waited for
 };
 
 // Profiling checkpoint (CTA 0, thread 0) when stage tracing is on.
@@ -1069,10 +1071,7 @@ QTB_CALL void drain(KCtx &kc, unsigned cur) {
   // tcgen05 stages: weight copies in flight, then every MMA issued (one more
   // commit completes after all of them) before the tensor memory is freed
   for (unsigned c = kc.tc_done; c != kc.tc_issued; c++) mbar_wait(kc.tcfull + c % TC_NSLOT, (c / TC_NSLOT) & 1u, LIM);
-  if (kc.tc_mma_open) {
-    umma_commit(kc.tcacc);
-    mbar_wait(kc.tcacc, (kc.tc_acc + 1u) & 1u, LIM);
-  }
+  for (unsigned g = kc.tc_waited; g != kc.tc_committed; g++) mbar_wait(kc.tcacc + (g & 1u), (g >> 1) & 1u, LIM);
 }
 
 QTB_CALL void argmax_finish(const GemvArgs &a, int B, KCtx &kc);
@@ -1638,46 +1637,58 @@ QTB_DEV uint32_t tc_sw128(int n, int kb) {   // byte offset of (row n, byte kb o
   return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((((kb >> 4) ^ (n & 7)) << 4) | (kb & 15)));
 }
 
-// Step 2: rows b = warp, warp + 8, ... of the slice [k0, k0 + KL).
-template <int FMT>
+// Step 2: rows b = warp, warp + 8, ... of the slice [k0, k0 + KL).  A warp
+// takes 16 / N4 rows per pass (N4 = float4 per lane per row), all their loads
+// in flight together, then reduces and converts each row.
+template <int FMT, int N4>
 __device__ __noinline__ void tc_stage_x(const GemvArgs &a, int B, int N, int k0, int KL, char *xreg, float *s_sx,
                                         float *s_ss) {
-  constexpr int MAXJ = 16;   // float4 per lane per row (KL <= 2048)
+  constexpr int RPP = 16 / N4;                  // rows per pass
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nq = KL >> 2;    // float4 per row
-  for (int b = warp; b < B; b += NWARPS) {
-    const float *xb = a.x + (size_t)b * a.ldx + k0;
-    float4 v[MAXJ];
-    float ss = 0.f, mx = 0.f;
+  const int nq = KL >> 2;                       // float4 per row
+  // the RMSNorm gains of this lane's columns (the same for every row)
+  float4 gn[N4];
 #pragma unroll
-    for (int j = 0; j < MAXJ; j++) {
-      const int q = lane + 32 * j;
-      v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (q < nq) {
-        v[j] = ld_cg4(xb + 4 * q);
-        ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
-        if (a.norm_w) {
-          const float4 g = __ldg(reinterpret_cast<const float4 *>(a.norm_w + k0 + 4 * q));
-          v[j].x *= g.x; v[j].y *= g.y; v[j].z *= g.z; v[j].w *= g.w;
-        }
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
-      }
+  for (int j = 0; j < N4; j++) {
+    const int q = lane + 32 * j;
+    gn[j] = (a.norm_w && q < nq) ? __ldg(reinterpret_cast<const float4 *>(a.norm_w + k0 + 4 * q))
+                                 : make_float4(1.f, 1.f, 1.f, 1.f);
+  }
+  for (int b0 = warp; b0 < B; b0 += NWARPS * RPP) {
+    float4 v[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const int b = b0 + NWARPS * (i / N4), q = lane + 32 * (i % N4);
+      v[i] = (b < B && q < nq) ? ld_cg4(a.x + (size_t)b * a.ldx + k0 + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    ss = warp_sum(ss);
-    mx = warp_max(mx);
-    const float sx = fmaxf(mx, 1e-30f) * (1.0f / 127.0f);
-    const float rs = __frcp_rn(sx);
-    if (lane == 0) { s_ss[b] = ss; s_sx[b] = sx; }
+    float ss[RPP], rs[RPP];
 #pragma unroll
-    for (int j = 0; j < MAXJ; j++) {
-      const int q = lane + 32 * j;
-      if (q >= nq) continue;
-      const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    for (int rr = 0; rr < RPP; rr++) {
+      float s2 = 0.f, m = 0.f;
+#pragma unroll
+      for (int j = 0; j < N4; j++) {
+        float4 &x = v[rr * N4 + j];
+        s2 += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+        const float4 g = gn[j];
+        x.x *= g.x; x.y *= g.y; x.z *= g.z; x.w *= g.w;
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+      }
+      ss[rr] = warp_sum(s2);
+      const float sx = fmaxf(warp_max(m), 1e-30f) * (1.0f / 127.0f);
+      rs[rr] = __frcp_rn(sx);
+      const int b = b0 + NWARPS * rr;
+      if (lane == 0 && b < B) { s_ss[b] = ss[rr]; s_sx[b] = sx; }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const int rr = i / N4, b = b0 + NWARPS * rr, q = lane + 32 * (i % N4);
+      if (b >= B || q >= nq) continue;
+      const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
       if (FMT == FMT_INT8) {
         uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const float r = fminf(fmaxf(e[i] * rs, -127.f), 127.f);
+        for (int k = 0; k < 4; k++) {
+          const float r = fminf(fmaxf(e[k] * rs[rr], -127.f), 127.f);
           // fixed point r 2^21 as a leading part and three balanced base-128 digits
           int I = __float2int_rn(r * 2097152.f);
           const int d3 = ((I + 64) & 127) - 64;
@@ -1686,10 +1697,10 @@ __device__ __noinline__ void tc_stage_x(const GemvArgs &a, int B, int N, int k0,
           I = (I - d2) >> 7;
           const int d1 = ((I + 64) & 127) - 64;
           const int a0 = (I - d1) >> 7;
-          w[0] |= ((uint32_t)a0 & 0xffu) << (8 * i);
-          w[1] |= ((uint32_t)d1 & 0xffu) << (8 * i);
-          w[2] |= ((uint32_t)d2 & 0xffu) << (8 * i);
-          w[3] |= ((uint32_t)d3 & 0xffu) << (8 * i);
+          w[0] |= ((uint32_t)a0 & 0xffu) << (8 * k);
+          w[1] |= ((uint32_t)d1 & 0xffu) << (8 * k);
+          w[2] |= ((uint32_t)d2 & 0xffu) << (8 * k);
+          w[3] |= ((uint32_t)d3 & 0xffu) << (8 * k);
         }
         const int kl = 4 * q, c = kl >> 7, kb = kl & 127;
 #pragma unroll
@@ -1698,12 +1709,12 @@ __device__ __noinline__ void tc_stage_x(const GemvArgs &a, int B, int N, int k0,
       } else {
         uint32_t hi[2], lo[2];
 #pragma unroll
-        for (int i = 0; i < 2; i++) {
-          const uint32_t h0 = f32_to_bf16_rn(e[2 * i]), h1 = f32_to_bf16_rn(e[2 * i + 1]);
-          const uint32_t l0 = f32_to_bf16_rn(e[2 * i] - __uint_as_float(h0 << 16));
-          const uint32_t l1 = f32_to_bf16_rn(e[2 * i + 1] - __uint_as_float(h1 << 16));
-          hi[i] = h0 | (h1 << 16);
-          lo[i] = l0 | (l1 << 16);
+        for (int k = 0; k < 2; k++) {
+          const uint32_t h0 = f32_to_bf16_rn(e[2 * k]), h1 = f32_to_bf16_rn(e[2 * k + 1]);
+          const uint32_t l0 = f32_to_bf16_rn(e[2 * k] - __uint_as_float(h0 << 16));
+          const uint32_t l1 = f32_to_bf16_rn(e[2 * k + 1] - __uint_as_float(h1 << 16));
+          hi[k] = h0 | (h1 << 16);
+          lo[k] = l0 | (l1 << 16);
         }
         const int kbyte = 8 * q, c = kbyte >> 7, kb = kbyte & 127;
         *reinterpret_cast<uint2 *>(xreg + (size_t)c * N * 128 + tc_sw128(2 * b, kb)) = make_uint2(hi[0], hi[1]);
@@ -1711,6 +1722,16 @@ __device__ __noinline__ void tc_stage_x(const GemvArgs &a, int B, int N, int k0,
       }
     }
   }
+}
+
+template <int FMT>
+QTB_DEV void tc_stage_x_f(const GemvArgs &a, int B, int N, int k0, int KL, char *xreg, float *s_sx, float *s_ss) {
+  const int n4 = ((KL >> 2) + 31) >> 5;
+  if (n4 <= 1) tc_stage_x<FMT, 1>(a, B, N, k0, KL, xreg, s_sx, s_ss);
+  else if (n4 <= 2) tc_stage_x<FMT, 2>(a, B, N, k0, KL, xreg, s_sx, s_ss);
+  else if (n4 <= 4) tc_stage_x<FMT, 4>(a, B, N, k0, KL, xreg, s_sx, s_ss);
+  else if (n4 <= 8) tc_stage_x<FMT, 8>(a, B, N, k0, KL, xreg, s_sx, s_ss);
+  else tc_stage_x<FMT, 16>(a, B, N, k0, KL, xreg, s_sx, s_ss);
 }
 
 // Final value of (row, batch b): 1/rms, row scale, bias, then the epilogue
@@ -1750,7 +1771,8 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
   unsigned long long *s_key = reinterpret_cast<unsigned long long *>(s_flag + 4);   // [4][64]
   if (nt == 0) return;
   const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
-  const unsigned F0 = kc.tc_issued;   // fills of earlier tcgen05 stages (all consumed)
+  const unsigned F0 = kc.tc_issued;   // weight fills of earlier tcgen05 stages (all consumed)
+  const unsigned g0 = kc.tc_waited;   // accumulator uses so far (buffer g & 1 for the g-th)
 
   // thread 0: bulk copy of fill f (tile t0 + f / kcn, chunk kb + f % kcn) into
   // slot (F0 + f) % TC_NSLOT once the MMAs that last read the slot are done
@@ -1773,57 +1795,64 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
       if (!issue(f)) break;
   }
   ckpt(kc, 0);
-  tc_stage_x<FMT>(a, B, N, pl.kb * tc_kchunk(FMT), kcn * tc_kchunk(FMT), xreg, s_sx, s_ss);
+  tc_stage_x_f<FMT>(a, B, N, pl.kb * tc_kchunk(FMT), kcn * tc_kchunk(FMT), xreg, s_sx, s_ss);
   fence_proxy_async_smem();     // the staged operand is read by the tensor cores (async proxy)
   __syncthreads();
   ckpt(kc, 1);
-  // this slice's sums of squares, for the tiles' finishing CTAs
+  // this slice's sums of squares, for the CTAs that finish the tiles
   if (a.norm_w && S > 1 && tid < B) { __stcg(a.ss_ws + ((size_t)grp * S + s) * 64 + tid, s_ss[tid]); }
   if (a.norm_w && S == 1 && tid < Bp) s_inv[tid] = (tid < B) ? 1.0f / sqrtf(s_ss[tid] / (float)a.K + a.eps) : 0.f;
   if (!a.norm_w && tid < 64) s_inv[tid] = 1.0f;
-  __syncthreads();
 
   const uint32_t idesc = (FMT == FMT_INT8) ? umma_idesc(2u, 1u, (uint32_t)N) : umma_idesc(1u, 1u, (uint32_t)N);
   const uint32_t wr_u = smem_u32(wring), xr_u = smem_u32(xreg);
+  // thread 0: the MMAs of tile i into accumulator buffer (g0 + i) & 1
+  auto mma_tile = [&](int i) {
+    const unsigned g = g0 + (unsigned)i;
+    const uint32_t d = kc.tmem + (g & 1u) * (uint32_t)TC_ACC_COLS;
+    for (int c = 0; c < kcn; c++) {
+      const int f = i * kcn + c;
+      const unsigned F = F0 + (unsigned)f, slot = F % TC_NSLOT;
+      if (!mbar_wait(kc.tcfull + slot, (F / TC_NSLOT) & 1u, WAIT_LIMIT_CYCLES)) {
+        raise_err(kc, ERR_MBAR_TIMEOUT, 3000 + f);
+        break;
+      }
+      kc.tc_done = F + 1u;
+      tc_fence_after();
+      const uint32_t ab = wr_u + slot * TC_SLOT_BYTES, bb = xr_u + (uint32_t)(c * N * 128);
+#pragma unroll
+      for (int ks = 0; ks < 4; ks++) {
+        const uint64_t ad = umma_desc_sw128(ab + 32u * ks), bd = umma_desc_sw128(bb + 32u * ks);
+        if (FMT == FMT_INT8) umma_i8(d, ad, bd, idesc, (c | ks) != 0);
+        else umma_bf16(d, ad, bd, idesc, (c | ks) != 0);
+      }
+      umma_commit(kc.tcempty + slot);
+      if (f >= 1 && f - 1 + TC_NSLOT < L && !issue(f - 1 + TC_NSLOT)) break;
+    }
+    umma_commit(kc.tcacc + (g & 1u));
+    kc.tc_committed = g + 1u;
+  };
+  __syncthreads();   // s_inv; every warp is past the staging
+  if (tid == 0 && !kc.local_err) mma_tile(0);
+
   const int q4 = warp & 3, hh = warp >> 2;
   const int rl = 32 * q4 + lane;   // this thread's row within the tile
   const float c7 = 1.0f / 128.0f, c14 = 1.0f / 16384.0f, c21 = 1.0f / 2097152.0f;
+  const int nb = min(Bh, 32);
   for (int i = 0; i < nt; i++) {
     const int t = t0 + i;
-    // ---- MMAs of tile t (thread 0) ----
-    if (tid == 0 && !kc.local_err) {
-      for (int c = 0; c < kcn; c++) {
-        const int f = i * kcn + c;
-        const unsigned F = F0 + (unsigned)f, slot = F % TC_NSLOT;
-        if (!mbar_wait(kc.tcfull + slot, (F / TC_NSLOT) & 1u, WAIT_LIMIT_CYCLES)) {
-          raise_err(kc, ERR_MBAR_TIMEOUT, 3000 + f);
-          break;
-        }
-        kc.tc_done = F + 1u;
-        tc_fence_after();
-        const uint32_t ab = wr_u + slot * TC_SLOT_BYTES, bb = xr_u + (uint32_t)(c * N * 128);
-#pragma unroll
-        for (int ks = 0; ks < 4; ks++) {
-          const uint64_t ad = umma_desc_sw128(ab + 32u * ks), bd = umma_desc_sw128(bb + 32u * ks);
-          if (FMT == FMT_INT8) umma_i8(kc.tmem, ad, bd, idesc, (c | ks) != 0);
-          else umma_bf16(kc.tmem, ad, bd, idesc, (c | ks) != 0);
-        }
-        kc.tc_mma_open = 1;
-        umma_commit(kc.tcempty + slot);
-        if (f >= 1 && f - 1 + TC_NSLOT < L && !issue(f - 1 + TC_NSLOT)) break;
-      }
-      umma_commit(kc.tcacc);
-    }
-    if (__syncthreads_or(kc.local_err)) return;   // copies and MMAs in flight are drained on the way out
-    // ---- accumulator -> this thread's row ----
-    const bool landed = mbar_wait(kc.tcacc, kc.tc_acc & 1u, WAIT_LIMIT_CYCLES);
+    const unsigned g = g0 + (unsigned)i;
+    // the next tile's MMAs go into the other buffer while this one is read
+    if (tid == 0 && i + 1 < nt && !kc.local_err) mma_tile(i + 1);
+    ckpt(kc, 12);
+    if (i < 3) ckpt(kc, 17 + 4 * i);
+    const bool landed = mbar_wait(kc.tcacc + (g & 1u), (g >> 1) & 1u, WAIT_LIMIT_CYCLES);
     if (!landed && lane == 0) raise_err(kc, ERR_MBAR_TIMEOUT, 4000 + i);
     tc_fence_after();
-    if (__syncthreads_or(kc.local_err)) return;
-    if (tid == 0) { kc.tc_acc++; kc.tc_mma_open = 0; }
-    ckpt(kc, 2);
-    // values of batch rows [hh * Bh, hh * Bh + Bh) of row rl, 8 (int8) or 16
-    // (bf16) batch rows per 32-column TMEM load
+    ckpt(kc, 13);
+    if (i < 3) ckpt(kc, 18 + 4 * i);
+    // batch rows [hh * Bh, hh * Bh + Bh) of row rl, 8 (int8) or 16 (bf16) per
+    // 32-column TMEM load
     constexpr int PER = (FMT == FMT_INT8) ? 8 : 16;
     float val[32 + PER];
 #pragma unroll
@@ -1831,7 +1860,7 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
       const int bb0 = hh * Bh + PER * j;
       if (PER * j >= Bh) break;
       uint32_t r[32];
-      tmem_ld32(kc.tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)(P * bb0), r);
+      tmem_ld32(kc.tmem + (g & 1u) * (uint32_t)TC_ACC_COLS + ((uint32_t)(32 * q4) << 16) + (uint32_t)(P * bb0), r);
 #pragma unroll
       for (int u = 0; u < PER; u++) {
         float v;
@@ -1846,48 +1875,16 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
         val[PER * j + u] = v;
       }
     }
-    const int nb = min(Bh, 32);
+    tc_fence_before();
+    if (i < 3) ckpt(kc, 19 + 4 * i);
+    const int row = 128 * t + rl;
     if (S > 1) {
+      // this slice's partial sums of the tile; added up after the last tile
       float *wsp = a.ws + (((size_t)t * S + s) * 128 + rl) * Bp + hh * Bh;
 #pragma unroll
       for (int u = 0; u < 32; u += 4)
         if (u < nb) __stcg(reinterpret_cast<float4 *>(wsp + u), make_float4(val[u], val[u + 1], val[u + 2], val[u + 3]));
-    }
-    tc_fence_before();
-    __syncthreads();   // TMEM reads done: the next tile's MMAs may overwrite the accumulator
-    if (S > 1) {
-      if (tid == 0) {
-        __threadfence();
-        s_flag[0] = (atomicAdd(a.sem + t, 1u) == (unsigned)(S - 1));
-      }
-      __syncthreads();
-      if (!s_flag[0]) continue;
-      __threadfence();
-      // the finishing CTA: the slices' sums in slice order, 1/rms from the
-      // slices' sums of squares (this row group's CTAs wrote them)
-      if (a.norm_w && tid < Bp) {
-        float tot = 0.f;
-        if (tid < B)
-          for (int s2 = 0; s2 < S; s2++) tot += __ldcg(a.ss_ws + ((size_t)grp * S + s2) * 64 + tid);
-        s_inv[tid] = (tid < B) ? 1.0f / sqrtf(tot / (float)a.K + a.eps) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 32; u++) val[u] = 0.f;
-      for (int s2 = 0; s2 < S; s2++) {
-        const float *wsp = a.ws + (((size_t)t * S + s2) * 128 + rl) * Bp + hh * Bh;
-#pragma unroll
-        for (int u = 0; u < 32; u += 4) {
-          if (u < nb) {
-            const float4 p4 = ld_cg4(wsp + u);
-            val[u] += p4.x; val[u + 1] += p4.y; val[u + 2] += p4.z; val[u + 3] += p4.w;
-          }
-        }
-      }
-      if (tid == 0) a.sem[t] = 0u;
-      __syncthreads();   // s_inv
-    }
-    const int row = 128 * t + rl;
-    if (a.epi == EPI_ARGMAX) {
+    } else if (a.epi == EPI_ARGMAX) {
       // per batch row: this warp's 32 rows, then the four lane quarters
 #pragma unroll
       for (int u = 0; u < 32; u++) {
@@ -1904,7 +1901,6 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
         if (lane == 0 && b < 64) s_key[q4 * 64 + b] = k;
       }
       __syncthreads();
-      const int T16 = a.rows >> 4;
       for (int idx = tid; idx < 8 * B; idx += NTHREADS) {
         const int b = idx % B, sub = idx / B;
         unsigned long long best = 0ull;
@@ -1915,11 +1911,10 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
       __syncthreads();
       if (tid == 0) {
         __threadfence();
-        s_flag[1] = (atomicAdd(a.amax_sem, 8u) + 8u == (unsigned)T16);
+        s_flag[1] = (atomicAdd(a.amax_sem, 8u) + 8u == (unsigned)(a.rows >> 4));
       }
       __syncthreads();
       if (s_flag[1]) argmax_finish(a, B, kc);
-      __syncthreads();
     } else {
 #pragma unroll
       for (int u = 0; u < 32; u++) {
@@ -1928,8 +1923,110 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
         tc_out(a, B, b, row, val[u], s_inv[b]);
       }
     }
+    // this buffer may take tile i + 2
+    if (__syncthreads_or(kc.local_err)) return;   // copies and MMAs in flight are drained on the way out
+    if (tid == 0) kc.tc_waited = g + 1u;
+    ckpt(kc, 14);
+    if (i < 3) ckpt(kc, 20 + 4 * i);
   }
   if (tid == 0) kc.tc_issued = F0 + (unsigned)L;
+  if (S == 1) return;
+
+  // ---- split K: every slice CTA of a tile adds up its share of 16-row
+  // sub-tiles (st = s, s + S, ...) over the slices, in slice order ----
+  __threadfence();
+  __syncthreads();   // partial sums and sums of squares stored
+  if (tid == 0)
+    for (int i = 0; i < nt; i++) atom_add_release_gpu(a.sem + a.sem_off + t0 + i, 1u);
+  if (s >= 8) return;   // no sub-tile left for this slice
+  // each program iteration adds S to the counters (zeroed at launch): wait
+  // for every slice of this CTA's tiles
+  const unsigned target = (unsigned)S * (kc.seq / (unsigned)kc.n_stages + 1u);
+  if (tid == 0) {
+    const long long w0 = clock64();
+    for (int i = 0; i < nt && !kc.local_err; i++) {
+      const unsigned *tsem = a.sem + a.sem_off + t0 + i;
+      while ((int)(ld_acquire_gpu(tsem) - target) < 0) {
+        if (clock64() - w0 > WAIT_LIMIT_CYCLES || ld_acquire_gpu((const unsigned *)&kc.ctl->err)) {
+          raise_err(kc, ERR_BARRIER_TIMEOUT, 5000 + t0 + i);
+          break;
+        }
+      }
+    }
+  }
+  ckpt(kc, 16);
+  if (__syncthreads_or(kc.local_err)) return;
+  __threadfence();
+  if (a.norm_w && tid < Bp) {   // 1/rms from every slice of the row group
+    float tot = 0.f;
+    if (tid < B)
+      for (int s2 = 0; s2 < S; s2++) tot += __ldcg(a.ss_ws + ((size_t)grp * S + s2) * 64 + tid);
+    s_inv[tid] = (tid < B) ? 1.0f / sqrtf(tot / (float)a.K + a.eps) : 0.f;
+  }
+  __syncthreads();
+  // work items (tile i, sub-tile st of this slice): thread = row r of the
+  // sub-tile x batch rows 4 bq .. 4 bq + 3
+  const int per_tile = (8 - s + S - 1) / S;   // sub-tiles s, s + S, ... < 8
+  const int nitems = nt * per_tile;
+  const int r = tid & 15, bq = tid >> 4;
+  const bool act = 4 * bq < Bp;
+  const size_t sstride = (size_t)128 * Bp;
+  for (int w = 0; w < nitems; w++) {
+    const int i = w / per_tile, st = s + S * (w - i * per_tile);
+    const int t = t0 + i;
+    const int rrow = 128 * t + 16 * st + r;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (act) {
+      const float *src = a.ws + (((size_t)t * S) * 128 + 16 * st + r) * Bp + 4 * bq;
+      int s2 = 0;
+      for (; s2 + 8 <= S; s2 += 8) {   // eight slices' loads in flight, added in slice order
+        float4 p[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) p[k] = ld_cg4(src + (s2 + k) * sstride);
+#pragma unroll
+        for (int k = 0; k < 8; k++) { acc.x += p[k].x; acc.y += p[k].y; acc.z += p[k].z; acc.w += p[k].w; }
+      }
+      for (; s2 < S; s2++) {
+        const float4 p0 = ld_cg4(src + s2 * sstride);
+        acc.x += p0.x; acc.y += p0.y; acc.z += p0.z; acc.w += p0.w;
+      }
+    }
+    const float vv[4] = {acc.x, acc.y, acc.z, acc.w};
+    if (a.epi == EPI_ARGMAX) {
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int b = 4 * bq + k;
+        unsigned long long key =
+            (act && b < B) ? amax_key(vv[k] * s_inv[b] * (a.row_scale ? __ldg(a.row_scale + rrow) : 1.f) +
+                                          (a.bias ? __ldg(a.bias + rrow) : 0.f), rrow)
+                           : 0ull;
+#pragma unroll
+        for (int m = 8; m > 0; m >>= 1) {
+          const unsigned long long o = shfl_xor_u64(key, m);
+          key = o > key ? o : key;
+        }
+        if (r == 0 && act && b < B) a.amax_ws[(size_t)(8 * t + st) * B + b] = key;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int b = 4 * bq + k;
+        // (SWIGLU pairs rows r, r ^ 1: neighbouring lanes of one 16-lane group)
+        tc_out(a, act ? B : 0, b, rrow, vv[k], (act && b < Bp) ? s_inv[b] : 0.f);
+      }
+    }
+  }
+  const int nsub = nitems;
+  if (a.epi == EPI_ARGMAX) {
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      s_flag[1] = (atomicAdd(a.amax_sem, (unsigned)nsub) + (unsigned)nsub == (unsigned)(a.rows >> 4));
+    }
+    __syncthreads();
+    if (s_flag[1]) argmax_finish(a, B, kc);
+  }
+  ckpt(kc, 15);
 }
 
 template <int FMT>
@@ -2837,7 +2934,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
   __shared__ Stage dring[NDESC];   // stage descriptors, NDESC - 1 stages ahead
   __shared__ V2Plan pring[NDESC];  // this CTA's plan entries for them ([stage][CTA] in `plan`)
   __shared__ __align__(8) uint64_t pbar;
-  __shared__ __align__(8) uint64_t tcbars[2 * TC_NSLOT + 1];   // weight slot full / empty, accumulator
+  __shared__ __align__(8) uint64_t tcbars[2 * TC_NSLOT + 2];   // weight slot full / empty, accumulators
   __shared__ uint32_t tmem_base;
   __shared__ KCtx kc;
   if (threadIdx.x == 0) {
@@ -2877,8 +2974,8 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     kc.tcacc = tcbars + 2 * TC_NSLOT;
     kc.tc_issued = 0;
     kc.tc_done = 0;
-    kc.tc_acc = 0;
-    kc.tc_mma_open = 0;
+    kc.tc_committed = 0;
+    kc.tc_waited = 0;
   }
   // the tensor-memory accumulator of the tcgen05 GEMV stages, held for the
   // whole launch (one CTA per SM: the allocation never waits)
@@ -2894,7 +2991,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     for (int i = 0; i < ATT_NBUF_MAX; i++) mbar_init(bars + i, 1);
     for (int i = 0; i < NWSLOT; i++) mbar_init(wbars + i, 1);
     for (int i = 0; i < NDESC; i++) mbar_init(dbars + i, 1);
-    for (int i = 0; i < 2 * TC_NSLOT + 1; i++) mbar_init(tcbars + i, 1);
+    for (int i = 0; i < 2 * TC_NSLOT + 2; i++) mbar_init(tcbars + i, 1);
     mbar_init(&pbar, 1);
     fence_mbar_init();
     for (unsigned k = 0; k < NDESC - 1 && k < kc.n_total; k++) issue_desc(k);
