@@ -165,6 +165,25 @@ int qtb_cp_frame(qtb_session_t *s, const float *talker_hidden, const int32_t *co
 int qtb_decode_frames(qtb_session_t *s, const float *embeds, const float *pad, int n_frames,
                       int32_t *codes_out, float *last_hidden_out);
 
+/* The codec vocabulary's end-of-speech token (QWEN_TTS_CODEC_EOS, qwen_tts.h:49). */
+#define QTB_CODEC_EOS 2150
+
+/* Switch qtb_decode_frames' codec head to the reference's generation-loop
+ * rules with greedy sampling (qwen_tts.c:1648-1720, qwen_tts_sampling.c:160-181):
+ * logits clipped to +-100, special tokens >= codebook masked except EOS, EOS
+ * masked for a slot's first 2 frames and boosted by min(0.5 (frame - 2 E), 10)
+ * once frame > 2 E (E = expected_frames[b], 3 x the slot's text tokens in the
+ * reference; <= 0 or expected_frames == NULL: no boost), the repetition penalty
+ * rep_penalty over the slot's earlier code0 tokens (1 = off; the reference's
+ * default is 1.05), then the first maximum.  Frame counters, repetition counts
+ * and stop flags restart at zero.  A slot that samples EOS stops: its position
+ * no longer advances; qtb_decode_frames reports code0 = QTB_CODEC_EOS with
+ * codes 1..15 = -1 in that frame and -1 everywhere afterwards.  Without this
+ * call the head is a plain greedy argmax over the first `codebook` rows. */
+int qtb_session_begin_generation(qtb_session_t *s, const int32_t *expected_frames, float rep_penalty);
+/* Per-slot stop flags of the generation (1 = sampled EOS), host [batch]. */
+int qtb_session_get_done(qtb_session_t *s, int32_t *done);
+
 /* KV pages <-> contiguous bf16 ([layer][len][kv_dim] with per-layer stride
  * layer_stride positions, the reference's host layout qwen_tts_talker.c:454-460). */
 int qtb_session_upload_kv(qtb_session_t *s, int b, const uint16_t *k, const uint16_t *v,

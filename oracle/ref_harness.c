@@ -149,6 +149,41 @@ int qref_codec_argmax(void *h, const float *hidden, int limit) {
     return qwen_argmax_matvec_bf16(hidden, ctx->codec_head_bf16, ctx->config.hidden_size, limit);
 }
 
+int qwen_tts_sample(float *logits, int vocab_size, float temp, int top_k, float top_p,
+                    float rep_penalty, int *prev_tokens, int n_prev);
+
+/* code0 of one frame of the reference's generation loop with greedy sampling:
+ * the codec-head logits over the whole vocabulary (qwen_tts.c:1650), the
+ * clip / special-token mask / EOS rules of qwen_tts.c:1652-1676 (restated here:
+ * qwen_tts_generate is not part of this harness), then the reference's own
+ * qwen_tts_sample at temperature 0 with the repetition penalty over the
+ * earlier code0 tokens (qwen_tts_sampling.c:160-181).  2150 = EOS. */
+int qref_codec_sample(void *h, const float *hidden, int frame, int expected_frames, float rep_penalty,
+                      int *prev_tokens, int n_prev) {
+    qwen_tts_ctx_t *ctx = (qwen_tts_ctx_t *)h;
+    const int V = ctx->config.codec_vocab_size, H = ctx->config.hidden_size;
+    float *logits = (float *)malloc((size_t)V * sizeof(float));
+    qwen_matvec_bf16(logits, ctx->codec_head_bf16, hidden, V, H);
+    for (int t = 0; t < V; t++) {
+        if (logits[t] > 100.0f) logits[t] = 100.0f;
+        if (logits[t] < -100.0f) logits[t] = -100.0f;
+    }
+    for (int t = 2048; t < V; t++)
+        if (t != 2150) logits[t] = -1e30f;
+    if (frame < 2) logits[2150] = -1e30f;
+    {
+        int boost_start = expected_frames * 2;
+        if (expected_frames > 0 && frame > boost_start) {
+            float boost = 0.5f * (frame - boost_start);
+            if (boost > 10.0f) boost = 10.0f;
+            logits[2150] += boost;
+        }
+    }
+    int c = qwen_tts_sample(logits, V, 0.0f, 50, 1.0f, rep_penalty, prev_tokens, n_prev);
+    free(logits);
+    return c;
+}
+
 /* Talker codec embedding row -> f32 (qwen_tts.c:1768-1778, first term). */
 void qref_codec_embed(void *h, int code, float *out) {
     qwen_tts_ctx_t *ctx = (qwen_tts_ctx_t *)h;

@@ -74,6 +74,7 @@ def ref_lib(flavour: str | None = None, dropin: bool = False, refcuda: bool = Fa
     L.qref_copy_cp_kv.argtypes = [vp, C.c_int, C.c_int, vp, vp]
     L.qref_codec_argmax.argtypes = [vp, vp, C.c_int]
     L.qref_codec_embed.argtypes = [vp, C.c_int, vp]
+    L.qref_codec_sample.argtypes = [vp, vp, C.c_int, C.c_int, C.c_float, vp, C.c_int]
     L.qref_weight.restype = vp
     L.qref_weight.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int]
     L.qref_cp_mtp.restype = vp
@@ -233,6 +234,13 @@ class RefModel:
     def codec_argmax(self, hidden, limit=None):
         hh = np.ascontiguousarray(hidden, np.float32)
         return self.L.qref_codec_argmax(self.h, p(hh), int(limit or self.cfg.codebook))
+
+    def codec_sample(self, hidden, frame, expected_frames, rep_penalty, prev_tokens):
+        """code0 under the reference's generation-loop rules (qref_codec_sample)."""
+        hh = np.ascontiguousarray(hidden, np.float32)
+        prev = np.ascontiguousarray(prev_tokens if len(prev_tokens) else [0], np.int32)
+        return self.L.qref_codec_sample(self.h, p(hh), int(frame), int(expected_frames), C.c_float(rep_penalty),
+                                        p(prev), len(prev_tokens))
 
     def codec_embed(self, code):
         out = np.empty(self.cfg.hidden, np.float32)

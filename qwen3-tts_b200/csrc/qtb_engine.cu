@@ -265,15 +265,9 @@ static void repack_tc(const uint8_t *W, int rows, int rowbytes, std::vector<uint
   });
 }
 
-// Large-batch bf16 / int8 GEMVs run on tcgen05 unless QTB_NO_TC=1 (then the
-// mma.sync k-sliced path serves them, and no second weight layout is kept).
-static bool tc_enabled() {
-  static const bool on = [] {
-    const char *e = getenv("QTB_NO_TC");
-    return !(e && e[0] == '1');
-  }();
-  return on;
-}
+// Large-batch (B > 4) bf16 / int8 GEMVs run on tcgen05: every bf16 / int8
+// matrix also keeps the tcgen05 operand layout.
+static bool tc_enabled() { return true; }
 
 // int4 (q4_0 or asymmetric g32): nibble getter + per-group scale/zero getters.
 template <typename NibF, typename SclF, typename ZeroF>
@@ -336,6 +330,7 @@ static int check_dims(int fmt, int rows, int K) {
   if (rows <= 0 || K <= 0 || rows % 128 != 0 || K % 64 != 0)
     return set_err(QTB_E_INVALID, "matrix %dx%d: rows must be a multiple of 128 and cols of 64", rows, K);
   if (fmt < 0 || fmt > 3) return set_err(QTB_E_INVALID, "bad weight format %d", fmt);
+  if (fmt == FMT_INT8 && K % 128 != 0) return set_err(QTB_E_INVALID, "int8 matrix cols %d: a multiple of 128", K);
   return 0;
 }
 
@@ -459,6 +454,8 @@ struct qtb_engine {
   const float *mtp_bias = nullptr;
   int has_mtp = 0;
   const unsigned *rsq_tab = nullptr;   // QK-norm rsqrt seeds (qk_rsq_table) or null
+  int codec_eos_row = 0;               // device codec-head row of the EOS token
+  int has_eos = 0;
 };
 
 static int upload_stack(qtb_engine *e, const qtb_stack_desc_t &d, DStack &s) {
@@ -584,10 +581,21 @@ extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_eng
   if (e->has_talker) {
     if ((rc = upload_stack(e, d->talker, e->talker))) goto fail;
     if (d->codec_head && d->codebook > 0) {
-      qtb_matrix_t ch = {d->codec_head, nullptr, nullptr, nullptr};
+      // the codebook rows, then the EOS token's row (when the vocabulary has
+      // one), then zero rows up to a whole 128-row tile: the special tokens the
+      // reference masks never need their logits
+      const int H = d->talker.hidden;
+      const int rows = (d->codebook + 1 + 127) / 128 * 128;
+      std::vector<uint16_t> head((size_t)rows * H, 0);
+      memcpy(head.data(), d->codec_head, (size_t)d->codebook * H * 2);
+      if (d->codec_vocab > QTB_CODEC_EOS)
+        memcpy(head.data() + (size_t)d->codebook * H, d->codec_head + (size_t)QTB_CODEC_EOS * H, (size_t)H * 2);
+      e->codec_eos_row = d->codebook;
+      e->has_eos = d->codec_vocab > QTB_CODEC_EOS;
+      qtb_matrix_t ch = {head.data(), nullptr, nullptr, nullptr};
       const qtb_matrix_t *m[1] = {&ch};
-      const int r[1] = {d->codebook};
-      if ((rc = upload_matrix(e->ar, FMT_BF16, m, r, 1, d->talker.hidden, e->codec_head))) goto fail;
+      const int r[1] = {rows};
+      if ((rc = upload_matrix(e->ar, FMT_BF16, m, r, 1, H, e->codec_head))) goto fail;
     }
   }
   if (d->codec_embedding && d->codec_vocab > 0) {
@@ -682,6 +690,9 @@ struct qtb_session {
   float *pad = nullptr;      // [hidden]
   float *ws = nullptr; size_t ws_floats = 0;
   float *ss_ws = nullptr;    // tcgen05 stages: per-(row group, slice) sums of squares [G][64]
+  GenState *gen = nullptr;   // codec-head generation state (device); gen_h mirrors its pointers
+  GenState gen_h = {};
+  int gen_on = 0;
   unsigned *sem = nullptr; int sem_n = 0;
   unsigned long long *amax_ws = nullptr;
   unsigned *amax_sem = nullptr;
@@ -1033,6 +1044,7 @@ static int build_programs(qtb_session *s) {
     pb.norm(s->tk.x, k.hidden, k.final_norm, s->tk.hidden, k.hidden, k.hidden, k.eps, B);
     // greedy code0 over the first `codebook` rows of the codec head
     pb.argmax(e->codec_head, B, s->tk.x, k.hidden, k.final_norm, k.eps, s->codes, 16, nullptr, 0, 0, nullptr, 0, 0);
+    pb.st.back().g.gen = s->gen;
     if (e->has_cp) build_cp_frame(pb, s, s->tk.hidden);
     Stage &S = pb.embed(s->tk.x, k.hidden, k.hidden, B, nullptr, 0);
     ProgBuilder::add_tab(S, e->codec_emb, k.hidden, e->codec_vocab, s->codes, 16);
@@ -1040,6 +1052,7 @@ static int build_programs(qtb_session *s) {
       for (int g = 0; g < 15; g++) ProgBuilder::add_tab(S, e->cp_emb[g], e->cp_emb_dim, e->codebook, s->codes + 1 + g, 16);
     S.e.add = s->pad;
     pb.pos_inc(s->pos, B);
+    pb.st.back().p.gen = s->gen;
     if ((rc = upload_prog(s, PROG_FRAME, pb))) return rc;
   }
   return 0;
@@ -1155,6 +1168,24 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
     if ((rc = s->ar.alloc((void **)&s->pos, B * 4))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->cp_pos, B * 4))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->codes, (size_t)B * 16 * 4))) goto fail;
+    {
+      GenState &g = s->gen_h;
+      g.enabled = 0;
+      g.eos_row = e->codec_eos_row;
+      g.eos_token = QTB_CODEC_EOS;
+      g.vocab = std::max(1, e->codebook);
+      g.rep_pen = 1.0f;
+      g.rep_inv = 1.0f;
+      if ((rc = s->ar.alloc((void **)&g.frame, (size_t)B * 4))) goto fail;
+      if ((rc = s->ar.alloc((void **)&g.boost_start, (size_t)B * 4))) goto fail;
+      if ((rc = s->ar.alloc((void **)&g.done, (size_t)B * 4))) goto fail;
+      if ((rc = s->ar.alloc((void **)&g.rep_count, (size_t)B * g.vocab * 2))) goto fail;
+      cudaMemset(g.frame, 0, (size_t)B * 4);
+      cudaMemset(g.boost_start, 0xff, (size_t)B * 4);
+      cudaMemset(g.done, 0, (size_t)B * 4);
+      cudaMemset(g.rep_count, 0, (size_t)B * g.vocab * 2);
+      if ((rc = s->ar.upload(&s->gen, &g, sizeof g))) goto fail;
+    }
     cudaMemset(s->sem, 0, (size_t)sem_n * 4);
     cudaMemset(s->amax_sem, 0, 64);
     cudaMemset(s->ctl, 0, sizeof(Ctl));
@@ -1359,6 +1390,34 @@ extern "C" int qtb_cp_frame(qtb_session_t *s, const float *talker_hidden, const 
   return 0;
 }
 
+extern "C" int qtb_session_begin_generation(qtb_session_t *s, const int32_t *expected_frames, float rep_penalty) {
+  if (!s) return set_err(QTB_E_INVALID, "null session");
+  if (!s->e->has_eos) return set_err(QTB_E_UNSUPPORTED, "the codec vocabulary has no EOS token (%d)", QTB_CODEC_EOS);
+  if (!(rep_penalty > 0.0f)) return set_err(QTB_E_INVALID, "repetition penalty %g", (double)rep_penalty);
+  const int B = s->B;
+  std::vector<int32_t> bs(B, -1);
+  for (int b = 0; b < B && expected_frames; b++) bs[b] = expected_frames[b] > 0 ? 2 * expected_frames[b] : -1;
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemcpy(s->gen_h.boost_start, bs.data(), (size_t)B * 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemset(s->gen_h.frame, 0, (size_t)B * 4));
+  CUDA_TRY(cudaMemset(s->gen_h.done, 0, (size_t)B * 4));
+  CUDA_TRY(cudaMemset(s->gen_h.rep_count, 0, (size_t)B * s->gen_h.vocab * 2));
+  GenState g = s->gen_h;
+  g.enabled = 1;
+  g.rep_pen = rep_penalty;
+  g.rep_inv = 1.0f / rep_penalty;   // the reference's build multiplies by this reciprocal
+  CUDA_TRY(cudaMemcpy(s->gen, &g, sizeof g, cudaMemcpyHostToDevice));
+  s->gen_on = 1;
+  return 0;
+}
+
+extern "C" int qtb_session_get_done(qtb_session_t *s, int32_t *done) {
+  if (!s || !done) return set_err(QTB_E_INVALID, "null argument");
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemcpy(done, s->gen_h.done, (size_t)s->B * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
 extern "C" int qtb_decode_frames(qtb_session_t *s, const float *embeds, const float *pad, int n_frames,
                                  int32_t *codes_out, float *last_hidden_out) {
   if (!s || n_frames < 1) return set_err(QTB_E_INVALID, "bad argument");
@@ -1378,13 +1437,33 @@ extern "C" int qtb_decode_frames(qtb_session_t *s, const float *embeds, const fl
   int rc = 0;
   if (codes_out) {
     // one launch per frame so every frame's codes can be read back
+    std::vector<int32_t> done((size_t)(n_frames + 1) * B, 0);
+    if (s->gen_on) CUDA_TRY(cudaMemcpyAsync(done.data(), s->gen_h.done, (size_t)B * 4, cudaMemcpyDeviceToHost, s->stream));
     CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
     for (int f = 0; f < n_frames; f++) {
       if ((rc = launch_prog(s, PROG_FRAME, 1, false))) return rc;
       CUDA_TRY(cudaMemcpyAsync(codes_out + (size_t)f * B * 16, s->codes, (size_t)B * 16 * 4, cudaMemcpyDeviceToHost, s->stream));
+      if (s->gen_on)
+        CUDA_TRY(cudaMemcpyAsync(done.data() + (size_t)(f + 1) * B, s->gen_h.done, (size_t)B * 4, cudaMemcpyDeviceToHost,
+                                 s->stream));
     }
     CUDA_TRY(cudaEventRecord(s->ev1, s->stream));
     s->last_launches = n_frames;
+    if (s->gen_on) {
+      // a slot that sampled EOS reports it as its code0 of that frame, with no
+      // code-predictor codes (the reference stops before them), and -1 after
+      CUDA_TRY(cudaStreamSynchronize(s->stream));
+      for (int f = 0; f < n_frames; f++)
+        for (int b = 0; b < B; b++) {
+          int32_t *c = codes_out + ((size_t)f * B + b) * 16;
+          if (done[(size_t)f * B + b]) {
+            for (int g = 0; g < 16; g++) c[g] = -1;
+          } else if (done[(size_t)(f + 1) * B + b]) {
+            c[0] = QTB_CODEC_EOS;
+            for (int g = 1; g < 16; g++) c[g] = -1;
+          }
+        }
+    }
   } else {
     if ((rc = launch_prog(s, PROG_FRAME, n_frames, true))) return rc;
   }
@@ -1774,12 +1853,12 @@ struct OpCtx {
   Arena weights;
   std::vector<OpWeight> cache;
   cudaStream_t st = nullptr;
-  float *dx = nullptr, *dy = nullptr, *ws = nullptr;
+  float *dx = nullptr, *dy = nullptr, *ws = nullptr, *ss_ws = nullptr;
   unsigned *sem = nullptr;
   Ctl *ctl = nullptr;
   Stage *dstage = nullptr;
   V2Plan *dplan = nullptr;
-  size_t x_cap = 0, y_cap = 0, ws_cap = 0, sem_cap = 0;
+  size_t x_cap = 0, y_cap = 0, ws_cap = 0, sem_cap = 0, ss_cap = 0;
 };
 
 int op_grow(void **p, size_t *cap, size_t need) {
@@ -1817,12 +1896,16 @@ int op_matmat(OpCtx *c, float *Y, const uint16_t *W, const float *X, int rows, i
   }
   const int T = rp / 16;
   const bool v2 = v2_ok(FMT_BF16, rp, cp, B, c->nsm);
-  const int S = v2 ? std::max(1, c->nsm / T) : choose_S(T, cp, B, c->nsm * NWARPS, FMT_BF16);
+  const bool tc = !v2 && tc_ok(ow->m, B, FMT_BF16);
+  const int S = v2 ? std::max(1, c->nsm / T)
+                   : tc ? tc_choose(FMT_BF16, rp, cp, B, c->nsm).S : choose_S(T, cp, B, c->nsm * NWARPS, FMT_BF16);
   if (S < 1) return set_err(QTB_E_UNSUPPORTED, "no k-slicing fits (cols %d, B %d)", cols, B);
+  const size_t ws_floats = tc ? std::max<size_t>(16, tc_ws_floats(FMT_BF16, rp, cp, B, c->nsm)) : (size_t)T * S * 16 * B;
   int rc;
   if ((rc = op_grow((void **)&c->dx, &c->x_cap, (size_t)B * cp * 4))) return rc;
   if ((rc = op_grow((void **)&c->dy, &c->y_cap, (size_t)B * rp * 4))) return rc;
-  if ((rc = op_grow((void **)&c->ws, &c->ws_cap, (size_t)T * S * 16 * B * 4))) return rc;
+  if ((rc = op_grow((void **)&c->ws, &c->ws_cap, ws_floats * 4))) return rc;
+  if ((rc = op_grow((void **)&c->ss_ws, &c->ss_cap, (size_t)c->nsm * 64 * 4))) return rc;
   if ((rc = op_grow((void **)&c->sem, &c->sem_cap, (size_t)T * 4))) return rc;
   // X [cols][B] -> [B][cp] (zero-padded columns)
   std::vector<float> xt((size_t)B * cp, 0.f), yt((size_t)B * rp);
@@ -1838,6 +1921,7 @@ int op_matmat(OpCtx *c, float *Y, const uint16_t *W, const float *X, int rows, i
   GemvArgs &g = s.g;
   g.w = ow->m.w; g.fmt = FMT_BF16; g.rows = rp; g.K = cp; g.S = v2 ? 1 : S;
   g.nch = nch_for(FMT_BF16, B, v2); g.parts = parts_for(FMT_BF16, B, v2); g.v2 = v2 ? 1 : 0;
+  g.tc = tc ? 1 : 0; g.wtc = ow->m.wtc; g.ss_ws = c->ss_ws;
   g.x = c->dx; g.ldx = cp; g.y = c->dy; g.ldy = rp; g.epi = EPI_STORE; g.ws = c->ws; g.sem = c->sem;
   CUDA_TRY(cudaMemcpyAsync(c->dstage, &s, sizeof s, cudaMemcpyHostToDevice, c->st));
   std::vector<V2Plan> pl;
@@ -1902,7 +1986,7 @@ extern "C" void qwen_cuda_free(void *ctx) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->st) cudaStreamSynchronize(c->st);
-  for (void *p : {(void *)c->dx, (void *)c->dy, (void *)c->ws, (void *)c->sem})
+  for (void *p : {(void *)c->dx, (void *)c->dy, (void *)c->ws, (void *)c->sem, (void *)c->ss_ws})
     if (p) cudaFree(p);
   if (c->st) cudaStreamDestroy(c->st);
   c->weights.release();

@@ -90,6 +90,22 @@ enum ErrCode {
   ERR_BAD_POS = 4, ERR_BAD_CODE = 5, ERR_BAD_STAGE = 6
 };
 
+// Generation state of the codec head (the reference's frame loop, qwen_tts.c:
+// 1648-1720), in device memory; read by the codec head's argmax epilogue and
+// the position advance.  With enabled == 0 the head is a plain greedy argmax
+// over its first eos_row rows.
+struct GenState {
+  int enabled;
+  int eos_row;               // device row holding the EOS token's weights (rows past it are padding)
+  int eos_token;             // 2150 (QWEN_TTS_CODEC_EOS)
+  int vocab;                 // rep_count row length (the codebook)
+  float rep_pen, rep_inv;    // repetition penalty and its reciprocal (as the reference's -ffast-math build uses)
+  int *frame;                // [B] frames generated so far by the slot
+  int *boost_start;          // [B] 2 x expected frames, or -1: no EOS boost
+  int *done;                 // [B] the slot has sampled EOS
+  uint16_t *rep_count;       // [B][vocab] occurrences of each code0 so far
+};
+
 struct GemvArgs {
   const uint8_t *w;          // fragment-ordered weights
   const float *row_scale;    // int8: [rows]
@@ -114,6 +130,7 @@ struct GemvArgs {
   unsigned long long *amax_ws; unsigned *amax_sem;
   int *codes; int code_stride;
   const uint16_t *emb_table; int emb_ld; int emb_rows; float *emb_out; int emb_out_ld;
+  const GenState *gen;       // the codec head: its logit rules (codec_logit); null for the CP heads
 };
 
 struct AttnArgs {
@@ -147,7 +164,7 @@ struct EmbedArgs {
 };
 
 struct NormArgs { const float *x; int ldx; const float *w; float *y; int ldy; int dim; float eps; };
-struct PosArgs { int *pos; };
+struct PosArgs { int *pos; const GenState *gen; };
 
 // One stage of a program.  16-byte aligned and sized so the kernel can bulk-copy
 // the next stage's descriptor into shared memory while the current one runs.
@@ -683,6 +700,34 @@ QTB_DEV void gemv_unit(const GemvArgs &a, int B, int t, int s, int kslice, const
 QTB_DEV unsigned long long amax_key(float v, int row) {
   return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xffffffffu - (unsigned)row);
 }
+// The codec head's logit of device row `row` for slot b, as the reference's
+// frame loop forms it before greedy sampling (qwen_tts.c:1650-1676 and the
+// repetition penalty of qwen_tts_sample, qwen_tts_sampling.c:160-181): clipped
+// to +-100; special tokens masked (-1e30) except EOS, which is masked for the
+// slot's first two frames and boosted by min(0.5 (frame - boost_start), 10)
+// after its boost start; then every earlier occurrence of the token scales it
+// by 1 / penalty (positive) or penalty (otherwise), one rounding each.
+QTB_DEV float codec_logit(const GenState *gs, int b, int row, float v) {
+  if (row > gs->eos_row) return -1e30f;
+  if (!gs->enabled) return row == gs->eos_row ? -1e30f : v;
+  if (v > 100.0f) v = 100.0f;
+  if (v < -100.0f) v = -100.0f;
+  const int frame = __ldcg(gs->frame + b);
+  if (row == gs->eos_row) {
+    if (frame < 2) return -1e30f;
+    const int bs = __ldcg(gs->boost_start + b);
+    if (bs >= 0 && frame > bs) {
+      float boost = 0.5f * (float)(frame - bs);
+      if (boost > 10.0f) boost = 10.0f;
+      v += boost;
+    }
+    return v;
+  }
+  const int c = __ldcg(gs->rep_count + (size_t)b * gs->vocab + row);
+  for (int i = 0; i < c; i++) v = (v > 0.0f) ? __fmul_rn(v, gs->rep_inv) : __fmul_rn(v, gs->rep_pen);
+  return v;
+}
+
 QTB_DEV unsigned long long shfl_xor_u64(unsigned long long v, int m) {
   unsigned lo = (unsigned)v, hi = (unsigned)(v >> 32);
   lo = __shfl_xor_sync(0xffffffffu, lo, m);
@@ -708,7 +753,10 @@ QTB_DEV void gemv_epilogue(const GemvArgs &a, int B, int t, int T, float (&res)[
   if (a.epi == EPI_ARGMAX) {
 #pragma unroll
     for (int j = 0; j < NCH; j++) {
-      unsigned long long k0 = amax_key(res[j][0], 16 * t + gid), k1 = amax_key(res[j][1], 16 * t + gid + 8);
+      const int bj = col_batch<P>(j, tig);
+      const float v0 = (a.gen && bj < B) ? codec_logit(a.gen, bj, 16 * t + gid, res[j][0]) : res[j][0];
+      const float v1 = (a.gen && bj < B) ? codec_logit(a.gen, bj, 16 * t + gid + 8, res[j][1]) : res[j][1];
+      unsigned long long k0 = amax_key(v0, 16 * t + gid), k1 = amax_key(v1, 16 * t + gid + 8);
       unsigned long long k = k0 > k1 ? k0 : k1;
 #pragma unroll
       for (int m = 4; m < 32; m <<= 1) {
@@ -1109,7 +1157,10 @@ QTB_CALL void v2_epilogue(const GemvArgs &a, int B, int t0, int nt, const float 
       const int b = idx % B, tl = idx / B;
       unsigned long long best = 0ull;
       for (int r = 0; r < 16; r++) {
-        const unsigned long long k = amax_key(val(tl, r, b), 16 * (t0 + tl) + r);
+        const int row = 16 * (t0 + tl) + r;
+        float v = val(tl, r, b);
+        if (a.gen) v = codec_logit(a.gen, b, row, v);
+        const unsigned long long k = amax_key(v, row);
         best = k > best ? k : best;
       }
       a.amax_ws[(size_t)(t0 + tl) * B + b] = best;
@@ -1149,8 +1200,18 @@ QTB_CALL void argmax_finish(const GemvArgs &a, int B, KCtx &kc) {
         const unsigned long long o = shfl_xor_u64(best, m);
         best = o > best ? o : best;
       }
-      const int code = (int)(0xffffffffu - (unsigned)(best & 0xffffffffull));
+      int code = (int)(0xffffffffu - (unsigned)(best & 0xffffffffull));
       if (lane == 0) {
+        if (a.gen && a.gen->enabled && !__ldcg(a.gen->done + b)) {
+          // the codec head of a running slot: EOS stops it; other codes count
+          // towards its repetition penalty
+          if (code == a.gen->eos_row) {
+            code = a.gen->eos_token;
+            a.gen->done[b] = 1;
+          } else {
+            a.gen->rep_count[(size_t)b * a.gen->vocab + code] += 1;
+          }
+        }
         a.codes[(size_t)b * a.code_stride] = code;
         s_code[b] = code;
       }
@@ -1890,9 +1951,12 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
       for (int u = 0; u < 32; u++) {
         if (u >= nb) break;
         const int b = hh * Bh + u;
-        unsigned long long k = (b < B) ? amax_key(val[u] * s_inv[b] * (a.row_scale ? __ldg(a.row_scale + row) : 1.f) +
-                                                      (a.bias ? __ldg(a.bias + row) : 0.f), row)
-                                       : 0ull;
+        unsigned long long k = 0ull;
+        if (b < B) {
+          float v = val[u] * s_inv[b] * (a.row_scale ? __ldg(a.row_scale + row) : 1.f) + (a.bias ? __ldg(a.bias + row) : 0.f);
+          if (a.gen) v = codec_logit(a.gen, b, row, v);
+          k = amax_key(v, row);
+        }
 #pragma unroll
         for (int m = 16; m > 0; m >>= 1) {
           const unsigned long long o = shfl_xor_u64(k, m);
@@ -1996,10 +2060,12 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const int b = 4 * bq + k;
-        unsigned long long key =
-            (act && b < B) ? amax_key(vv[k] * s_inv[b] * (a.row_scale ? __ldg(a.row_scale + rrow) : 1.f) +
-                                          (a.bias ? __ldg(a.bias + rrow) : 0.f), rrow)
-                           : 0ull;
+        unsigned long long key = 0ull;
+        if (act && b < B) {
+          float v = vv[k] * s_inv[b] * (a.row_scale ? __ldg(a.row_scale + rrow) : 1.f) + (a.bias ? __ldg(a.bias + rrow) : 0.f);
+          if (a.gen) v = codec_logit(a.gen, b, rrow, v);
+          key = amax_key(v, rrow);
+        }
 #pragma unroll
         for (int m = 8; m > 0; m >>= 1) {
           const unsigned long long o = shfl_xor_u64(key, m);
@@ -2053,16 +2119,13 @@ template <int FMT>
 QTB_DEV void gemv_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
   if (a.v2) { gemv2_stage_f<FMT>(a, B, smem, kc); return; }
   if (FMT == FMT_BF16 || FMT == FMT_INT8) {
-    if (a.tc) { gemv_tc_t<FMT>(a, B, smem, kc); return; }
+    // large batches of bf16 / int8 weights always run on tcgen05
+    if (a.tc) gemv_tc_t<FMT>(a, B, smem, kc);
+    else if (threadIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, 2000 + FMT);
+    return;
   }
-  if (FMT == FMT_BF16 && a.parts == 4) {
-    switch (a.nch) {
-      case 1: gemv_stage_t<FMT, 1, 4>(a, B, smem, kc); return;
-      case 2: gemv_stage_t<FMT, 2, 4>(a, B, smem, kc); return;
-      case 4: gemv_stage_t<FMT, 4, 4>(a, B, smem, kc); return;
-      case 8: gemv_stage_t<FMT, 8, 4>(a, B, smem, kc); return;
-    }
-  } else if (a.parts == 2) {
+  // large batches of 4-bit weights: the k-sliced mma.sync path
+  if (a.parts == 2) {
     switch (a.nch) {
       case 1: if (FMT != FMT_BF16) { gemv_stage_t<FMT, 1, 2>(a, B, smem, kc); return; } break;
       case 2: if (FMT != FMT_BF16) { gemv_stage_t<FMT, 2, 2>(a, B, smem, kc); return; } break;
@@ -3021,7 +3084,14 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
         case ST_EMBED: embed_stage(st->e, B, kc); break;
         case ST_NORM: norm_stage(st->n, B); break;
         case ST_POS_INC:
-          if (blockIdx.x == 0) for (int b = threadIdx.x; b < B; b += NTHREADS) st->p.pos[b] += 1;
+          // slots stopped at EOS keep their position and frame count
+          if (blockIdx.x == 0)
+            for (int b = threadIdx.x; b < B; b += NTHREADS) {
+              const GenState *gs = st->p.gen;
+              if (gs && gs->enabled && __ldcg(gs->done + b)) continue;
+              st->p.pos[b] += 1;
+              if (gs && gs->enabled) gs->frame[b] += 1;
+            }
           break;
         default:
           if (threadIdx.x == 0 && blockIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, st->kind);

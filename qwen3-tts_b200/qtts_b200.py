@@ -53,6 +53,7 @@ class EngineDesc(C.Structure):
 _lib = None
 
 
+CODEC_EOS = 2150   # QWEN_TTS_CODEC_EOS (qwen_tts.h:49)
 NCKPT = 32   # intra-stage profiling checkpoints per stage (kernel constant)
 
 
@@ -85,6 +86,8 @@ def lib():
     L.qtb_cp_pass.argtypes = [_vp, _vp, _vp]
     L.qtb_cp_frame.argtypes = [_vp, _vp, _vp, _vp]
     L.qtb_decode_frames.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp]
+    L.qtb_session_begin_generation.argtypes = [_vp, _vp, C.c_float]
+    L.qtb_session_get_done.argtypes = [_vp, _vp]
     for n in ("qtb_session_upload_kv", "qtb_session_download_kv", "qtb_session_download_cp_kv"):
         getattr(L, n).argtypes = [_vp, C.c_int, _vp, _vp, C.c_int, C.c_int]
     L.qtb_session_profile.argtypes = [_vp, C.c_int, _vp, _vp, _vp, C.c_int]
@@ -412,6 +415,18 @@ class Session:
         hid = np.empty((self.B, cfg.hidden), np.float32)
         check(lib().qtb_decode_frames(self.h, ptr(e), ptr(pd), n_frames, ptr(codes), ptr(hid)))
         return codes, hid
+
+    def begin_generation(self, expected_frames=None, rep_penalty=1.0):
+        """The reference's generation-loop codec head for decode_frames
+        (qtb_session_begin_generation): EOS rules, repetition penalty, stops."""
+        ef = None if expected_frames is None else np.ascontiguousarray(np.broadcast_to(expected_frames, (self.B,)),
+                                                                       np.int32)
+        check(lib().qtb_session_begin_generation(self.h, ptr(ef), C.c_float(rep_penalty)))
+
+    def get_done(self):
+        d = np.zeros(self.B, np.int32)
+        check(lib().qtb_session_get_done(self.h, ptr(d)))
+        return d
 
     def profile(self, which=3, max_stages=4096):
         """Per-stage SM cycles of one iteration of a program (see

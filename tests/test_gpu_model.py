@@ -248,6 +248,78 @@ def test_decode_frames_match_reference_loop(have_gpu, tiny, fmt):
     ref.close()
 
 
+def gen_loop_reference(ref, m, cfg, e_last, n_frames, expected, rep):
+    """The reference's generation loop with greedy sampling (qwen_tts.c:
+    1648-1816): talker step on the last prompt token, then per frame the codec
+    head under the loop's rules (EOS, repetition penalty), the CP codes and the
+    next embedding.  Returns [frames][16] codes, EOS frame as (2150, -1, ...)."""
+    cpe = [O.f32_from_bf16(t) for t in m.cp_codec_emb]
+    h = ref.talker_step(e_last)
+    prev, out = [], []
+    for f in range(n_frames):
+        c0 = ref.codec_sample(h, f, expected, rep, prev)
+        if c0 == Q.CODEC_EOS:
+            out.append([Q.CODEC_EOS] + [-1] * 15)
+            break
+        prev.append(c0)
+        codes = ref.cp_predict(h, c0)
+        out.append([c0] + list(codes))
+        nxt = ref.codec_embed(c0)
+        for g in range(15):
+            nxt = (nxt + cpe[g][codes[g]]).astype(np.float32)
+        h = ref.talker_step(nxt)
+    return np.array(out, np.int32)
+
+
+def test_generation_rules_eos_and_repetition_match_reference(have_gpu, tmp_path):
+    """The device codec head under the reference's frame-loop rules: clip,
+    special-token mask, EOS suppressed for 2 frames and boosted after twice the
+    expected length, the repetition penalty (1.05) over earlier code0 tokens,
+    per-slot stop at EOS.  The codec head is biased so a few tokens dominate
+    (they repeat, so the penalty decides) and EOS (a zero row) wins once
+    boosted.  Two slots with different expected lengths stop at different
+    frames; every code up to each slot's EOS equals the reference's loop."""
+    cfg = tiny_cfg(layers=3, cp_layers=2)
+    m = Q.synth_model(cfg, seed=21, with_cp=True, norm_gain="random")
+    head = O.f32_from_bf16(m.codec_head).copy()
+    keep = [5, 9, 13, 300]
+    scale = np.full(cfg.codec_vocab, 0.1, np.float32)
+    scale[keep] = 3.0
+    head *= scale[:, None]
+    head[Q.CODEC_EOS] = 0.0
+    m.codec_head = Q.bf16_from_f32(head)
+    path = str(tmp_path / "gen.safetensors")
+    refbind.write_safetensors(path, refbind.model_tensors(m))
+    rep = 1.05
+    want = []
+    rng = np.random.default_rng(22)
+    prompt = (0.1 * rng.standard_normal((9, cfg.hidden))).astype(np.float32)
+    expected = [3, 6]
+    for b in range(2):
+        ref = refbind.RefModel(path, cfg, threads=8)
+        for pos in range(8):
+            ref.talker_step(prompt[pos])
+        want.append(gen_loop_reference(ref, m, cfg, prompt[8], 48, expected[b], rep))
+        if b == 0:
+            eng = engine_from_ref(ref, m, cfg, "bf16", with_cp=True)
+        ref.close()
+    assert all(w[-1, 0] == Q.CODEC_EOS for w in want), [len(w) for w in want]
+    assert len(want[0]) != len(want[1])
+    ses = Q.Session(eng, 2, 256)
+    for pos in range(8):
+        ses.talker_step(np.stack([prompt[pos]] * 2), pos)
+    ses.set_pos([8, 8])
+    ses.begin_generation(expected, rep)
+    got, _ = ses.decode_frames(np.stack([prompt[8]] * 2), 48)
+    for b in range(2):
+        n = len(want[b])
+        assert np.array_equal(got[:n, b, :], want[b]), (b, got[:n, b, :4], want[b][:, :4])
+        assert np.all(got[n:, b, :] == -1), b
+    assert list(ses.get_done()) == [1, 1]
+    # stopped slots keep their positions: prompt (9) + frames before EOS
+    assert list(ses.get_pos()) == [8 + len(want[0]) - 1 + 1, 8 + len(want[1]) - 1 + 1]
+
+
 @pytest.mark.slow
 def test_06b_bf16_greedy_256_steps_identical(have_gpu):
     """0.6B BF16 talker, 64-token prefill of N(0,1)*0.1
