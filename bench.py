@@ -48,6 +48,8 @@ CONFIGS = {
     # name: (model, talker fmt, cp?, batch, prefill, description)
     "c1": ("0.6B", "bf16", False, 1, 64, "0.6B talker BF16, B=1, 64-token prefill, greedy decode"),
     "c2": ("0.6B", "int8", True, 1, 64, "0.6B talker + code predictor, INT8 per-row, B=1, 64-token prefill"),
+    "c2t": ("0.6B", "int8", False, 1, 64, "0.6B talker alone, INT8 per-row, B=1, 64-token prefill (talker step + "
+                                          "codec-head argmax + next embedding per frame)"),
     "c3": ("1.7B", "int4g32", False, 1, 128, "1.7B talker INT4 g32 asymmetric, B=1, context from 128"),
     "c4": ("0.6B", "bf16", False, 64, None, "0.6B talker BF16, 64 requests, paged KV L~U[128,2048]"),
     "c5": ("1.7B", "int8", True, 64, None, "1.7B talker + CP INT8, 64 requests/GPU, paged KV L~U[256,4096]"),
@@ -143,8 +145,14 @@ def run_b200(args, rank, world, local_rank):
         ses.decode_frames(e0, W, want_codes=False)           # warm-up frames
         start_pos = int(ses.get_pos()[0])
     else:
+        # the global request set (B per GPU), partitioned over the ranks by KV
+        # bytes (qtb_shard.partition): this rank serves its share
+        import qtb_shard
         lo, hi = (128, 2048) if cfg_name == "c4" else (256, 4096)
-        lens = np.random.default_rng(0).integers(lo, hi + 1, B)
+        all_lens = np.random.default_rng(0).integers(lo, hi + 1, B * world)
+        reqs = [qtb_shard.Request(i, int(all_lens[i]), W + K) for i in range(B * world)]
+        mine = qtb_shard.partition(reqs, list(range(world)))[rank]
+        lens = np.array([q.kv_len for q in mine][:B] + [int(all_lens[0])] * max(0, B - len(mine)), np.int64)
         grow = W + K + max(4, min(K, 64))   # positions appended: warm-up, timed and end-to-end frames
         per = [(int(L) + grow + 15) // 16 + 1 for L in lens]
         n_pages = sum(per)

@@ -165,6 +165,18 @@ int qtb_cp_frame(qtb_session_t *s, const float *talker_hidden, const int32_t *co
 int qtb_decode_frames(qtb_session_t *s, const float *embeds, const float *pad, int n_frames,
                       int32_t *codes_out, float *last_hidden_out);
 
+/* Talker prefill of n prompt tokens of slot b on the device (the reference's
+ * qwen_talker_prefill, qwen_tts_talker.c:730-1038, which the reference runs
+ * on the CPU and uploads with qwen_cuda_talker_upload_kv): embeds host
+ * [n][hidden] at positions pos0 .. pos0 + n - 1, in chunks of up to 64 tokens
+ * run as a batch on the large-batch tensor-core GEMVs (every token's K/V is
+ * appended before any of them attends, causally).  Fills the slot's KV pages
+ * and sets its position to pos0 + n.  hidden_out: host [hidden] final-normed
+ * hidden of the last token, or NULL; dec_x_out: its pre-norm residual, or
+ * NULL.  The slot's pages must cover the positions. */
+int qtb_prefill(qtb_session_t *s, int b, const float *embeds, int n, int pos0, float *hidden_out,
+                float *dec_x_out);
+
 /* The codec vocabulary's end-of-speech token (QWEN_TTS_CODEC_EOS, qwen_tts.h:49). */
 #define QTB_CODEC_EOS 2150
 

@@ -108,6 +108,20 @@ int qref_talker_step(void *h, const float *embed, float *hidden_out) {
     return rc;
 }
 
+int qwen_talker_prefill(qwen_tts_ctx_t *ctx, float *input_embeds, int seq_len);
+
+/* The reference's batched CPU prefill (qwen_tts_talker.c:730-1038) of n prompt
+ * embeddings at positions 0..n-1: fills the host KV cache and dec_x. */
+int qref_talker_prefill(void *h, const float *embeds, int n, float *dec_x_out) {
+    qwen_tts_ctx_t *ctx = (qwen_tts_ctx_t *)h;
+    float *e = (float *)malloc((size_t)n * ctx->config.hidden_size * sizeof(float));
+    memcpy(e, embeds, (size_t)n * ctx->config.hidden_size * sizeof(float));
+    int rc = qwen_talker_prefill(ctx, e, n);
+    free(e);
+    if (dec_x_out) memcpy(dec_x_out, ctx->dec_x, (size_t)ctx->config.hidden_size * sizeof(float));
+    return rc;
+}
+
 int qref_cp_predict(void *h, const float *talker_hidden, int code0, int *out_codes) {
     qwen_tts_ctx_t *ctx = (qwen_tts_ctx_t *)h;
     int H = ctx->config.hidden_size;

@@ -75,6 +75,7 @@ def ref_lib(flavour: str | None = None, dropin: bool = False, refcuda: bool = Fa
     L.qref_codec_argmax.argtypes = [vp, vp, C.c_int]
     L.qref_codec_embed.argtypes = [vp, C.c_int, vp]
     L.qref_codec_sample.argtypes = [vp, vp, C.c_int, C.c_int, C.c_float, vp, C.c_int]
+    L.qref_talker_prefill.argtypes = [vp, vp, C.c_int, vp]
     L.qref_weight.restype = vp
     L.qref_weight.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int]
     L.qref_cp_mtp.restype = vp
@@ -234,6 +235,15 @@ class RefModel:
     def codec_argmax(self, hidden, limit=None):
         hh = np.ascontiguousarray(hidden, np.float32)
         return self.L.qref_codec_argmax(self.h, p(hh), int(limit or self.cfg.codebook))
+
+    def talker_prefill(self, embeds):
+        """The reference's CPU prefill of embeds [n][hidden] at positions 0..n-1;
+        returns dec_x (the last token's pre-norm residual)."""
+        e = np.ascontiguousarray(embeds, np.float32)
+        dx = np.empty(self.cfg.hidden, np.float32)
+        if self.L.qref_talker_prefill(self.h, p(e), e.shape[0], p(dx)) != 0:
+            raise RuntimeError("reference prefill failed")
+        return dx
 
     def codec_sample(self, hidden, frame, expected_frames, rep_penalty, prev_tokens):
         """code0 under the reference's generation-loop rules (qref_codec_sample)."""

@@ -654,7 +654,8 @@ extern "C" int64_t qtb_engine_cp_pass_weight_bytes(const qtb_engine_t *e) {
 extern "C" int64_t qtb_engine_cp_head_weight_bytes(const qtb_engine_t *e) { return e ? e->lm_head[0].alg_bytes : 0; }
 
 // --------------------------------------------------------- the session -----
-enum { PROG_TALKER = 0, PROG_CP_PASS = 1, PROG_CP_FRAME = 2, PROG_FRAME = 3, PROG_N = 4 };
+enum { PROG_TALKER = 0, PROG_CP_PASS = 1, PROG_CP_FRAME = 2, PROG_FRAME = 3, PROG_PREFILL = 4, PROG_N = 5 };
+constexpr int PREFILL_CHUNK = 64;   // prompt tokens per prefill launch (the large-batch GEMV's widest batch)
 
 struct StackBufs {
   float *x = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *hidden = nullptr, *tmp = nullptr;
@@ -690,6 +691,8 @@ struct qtb_session {
   float *pad = nullptr;      // [hidden]
   float *ws = nullptr; size_t ws_floats = 0;
   float *ss_ws = nullptr;    // tcgen05 stages: per-(row group, slice) sums of squares [G][64]
+  StackBufs pf;              // prefill chunk buffers (PREFILL_CHUNK rows) over the talker's KV pools
+  int *pf_pos = nullptr;     // [PREFILL_CHUNK] positions of the chunk's tokens
   GenState *gen = nullptr;   // codec-head generation state (device); gen_h mirrors its pointers
   GenState gen_h = {};
   int gen_on = 0;
@@ -869,12 +872,14 @@ struct ProgBuilder {
     g.codes = codes; g.code_stride = code_stride;
     g.emb_table = emb; g.emb_ld = emb_ld; g.emb_rows = emb_rows; g.emb_out = emb_out; g.emb_out_ld = emb_out_ld;
   }
-  void attn(const DStack &k, const StackBufs &b, int layer, int B, const int *pos_ptr, int pos_const, size_t layer_elems) {
+  void attn(const DStack &k, const StackBufs &b, int layer, int B, const int *pos_ptr, int pos_const, size_t layer_elems,
+            int mode = ATT_DECODE) {
     Stage S;
     memset(&S, 0, sizeof S);
     S.kind = ST_ATTN;
     S.B = B;
     AttnArgs &a = S.a;
+    a.mode = mode;
     a.qkv = b.qkv; a.ld_qkv = k.qkv_dim();
     a.out = b.attn; a.ld_out = k.q_dim();
     a.q_norm = k.layers[layer].q_norm; a.k_norm = k.layers[layer].k_norm;
@@ -889,8 +894,24 @@ struct ProgBuilder {
     a.max_splits = b.max_splits; a.min_pps = b.min_pps;
     a.ws = s->att_ws; a.sem = s->att_sem;
     a.rsq_tab = s->e->rsq_tab;
+    if (mode == ATT_APPEND) { a.max_splits = 1; a.min_pps = 1 << 20; }   // one item per slot and KV head
     attn_schedule(a, B, s->e->n_sm);
     st.push_back(S);
+  }
+  // A prompt chunk of one sequence as B slots (positions pos[i], the same page
+  // table row): per layer the QKV GEMV, every token's K/V appended, then every
+  // token's attention over positions <= its own, O, gate/up, down.
+  void prefill_layers(const DStack &k, const StackBufs &b, int B, const int *pos_ptr, size_t layer_elems) {
+    const int H = k.hidden;
+    for (int l = 0; l < k.n_layers && !err; l++) {
+      const DLayer &L = k.layers[l];
+      gemv(L.qkv, B, b.x, H, L.in_norm, k.eps, b.qkv, k.qkv_dim(), EPI_STORE, 0);
+      attn(k, b, l, B, pos_ptr, 0, layer_elems, ATT_APPEND);
+      attn(k, b, l, B, pos_ptr, 0, layer_elems, ATT_ATTEND);
+      gemv(L.o, B, b.attn, k.q_dim(), nullptr, k.eps, b.x, H, EPI_RESID, 0);
+      gemv(L.gu, B, b.x, H, L.post_norm, k.eps, b.h, k.inter, EPI_SWIGLU, 0);
+      gemv(L.down, B, b.h, k.inter, nullptr, k.eps, b.x, H, EPI_RESID, 0);
+    }
   }
   void layers(const DStack &k, const StackBufs &b, int B, const int *pos_ptr, int pos_const, size_t layer_elems, int evict_last) {
     const int H = k.hidden;
@@ -1027,6 +1048,12 @@ static int build_programs(qtb_session *s) {
     pb.layers(k, s->tk, B, s->pos, 0, s->tk_layer_elems, 0);
     pb.norm(s->tk.x, k.hidden, k.final_norm, s->tk.hidden, k.hidden, k.hidden, k.eps, B);
     if ((rc = upload_prog(s, PROG_TALKER, pb))) return rc;
+    if (s->pf.x) {
+      ProgBuilder pp{s};
+      pp.prefill_layers(k, s->pf, PREFILL_CHUNK, s->pf_pos, s->tk_layer_elems);
+      pp.norm(s->pf.x, k.hidden, k.final_norm, s->pf.hidden, k.hidden, k.hidden, k.eps, PREFILL_CHUNK);
+      if ((rc = upload_prog(s, PROG_PREFILL, pp))) return rc;
+    }
   }
   if (e->has_cp) {
     const DStack &k = e->cp;
@@ -1140,19 +1167,23 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
     const int W = e->n_sm * NWARPS;
     size_t ws = 16;
     int sem_n = 16;
-    auto acc = [&](const DMat &m) {
+    auto acc_b = [&](const DMat &m, int Bx) {
       if (!m.w) return;
       const int T = m.rows / 16;
-      const int S = choose_S(T, m.K, B, W, m.fmt);
-      if (S > 0) ws = std::max(ws, (size_t)T * S * 16 * B);
-      ws = std::max(ws, (size_t)T * std::max(1, e->n_sm / std::max(1, T)) * 16 * B);
-      if (tc_ok(m, B, m.fmt)) ws = std::max(ws, tc_ws_floats(m.fmt, m.rows, m.K, B, e->n_sm));
+      const int S = choose_S(T, m.K, Bx, W, m.fmt);
+      if (S > 0) ws = std::max(ws, (size_t)T * S * 16 * Bx);
+      ws = std::max(ws, (size_t)T * std::max(1, e->n_sm / std::max(1, T)) * 16 * Bx);
+      if (tc_ok(m, Bx, m.fmt)) ws = std::max(ws, tc_ws_floats(m.fmt, m.rows, m.K, Bx, e->n_sm));
       sem_n = std::max(sem_n, T);
     };
+    auto acc = [&](const DMat &m) { acc_b(m, B); };
     auto acc_stack = [&](const DStack &k) {
       for (const DLayer &L : k.layers) { acc(L.qkv); acc(L.o); acc(L.gu); acc(L.down); }
     };
     acc_stack(e->talker);
+    for (const DLayer &L : e->talker.layers) {   // the prefill program's chunks
+      acc_b(L.qkv, PREFILL_CHUNK); acc_b(L.o, PREFILL_CHUNK); acc_b(L.gu, PREFILL_CHUNK); acc_b(L.down, PREFILL_CHUNK);
+    }
     acc_stack(e->cp);
     acc(e->codec_head);
     for (int g = 0; g < 15; g++) acc(e->lm_head[g]);
@@ -1202,6 +1233,25 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
       nkv = e->talker.n_kv;
       if ((rc = s->ar.alloc((void **)&s->pad, (size_t)e->talker.hidden * 4))) goto fail;
       cudaMemset(s->pad, 0, (size_t)e->talker.hidden * 4);
+      // prefill chunks: PREFILL_CHUNK rows of activations over the same KV pools
+      {
+        StackBufs &p = s->pf;
+        const DStack &k = e->talker;
+        const size_t R = PREFILL_CHUNK;
+        if ((rc = s->ar.alloc((void **)&p.x, R * k.hidden * 4))) goto fail;
+        if ((rc = s->ar.alloc((void **)&p.hidden, R * k.hidden * 4))) goto fail;
+        if ((rc = s->ar.alloc((void **)&p.qkv, R * k.qkv_dim() * 4))) goto fail;
+        if ((rc = s->ar.alloc((void **)&p.attn, R * k.q_dim() * 4))) goto fail;
+        if ((rc = s->ar.alloc((void **)&p.h, R * k.inter * 4))) goto fail;
+        if ((rc = s->ar.alloc((void **)&p.page_table, R * s->tk.pt_stride * 4))) goto fail;
+        if ((rc = s->ar.alloc((void **)&s->pf_pos, R * 4))) goto fail;
+        cudaMemset(s->pf_pos, 0, R * 4);
+        cudaMemset(p.page_table, 0, R * s->tk.pt_stride * 4);
+        p.kpool = s->tk.kpool; p.vpool = s->tk.vpool;
+        p.n_pages = s->tk.n_pages; p.pt_stride = s->tk.pt_stride;
+        p.max_splits = 16; p.min_pps = 64;
+        att_splits = std::max(att_splits, p.max_splits);
+      }
     }
     if (e->has_cp) {
       const int th = e->has_talker ? e->talker.hidden : e->cp_emb_dim;
@@ -1211,9 +1261,10 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
       s->cp.max_splits = 1;
       nkv = std::max(nkv, e->cp.n_kv);
     }
-    if ((rc = s->ar.alloc((void **)&s->att_ws, (size_t)B * nkv * att_splits * 2 * (HD + 2) * 4))) goto fail;
-    if ((rc = s->ar.alloc((void **)&s->att_sem, (size_t)B * nkv * 4))) goto fail;
-    cudaMemset(s->att_sem, 0, (size_t)B * nkv * 4);
+    const int Ba = e->has_talker ? std::max(B, PREFILL_CHUNK) : B;
+    if ((rc = s->ar.alloc((void **)&s->att_ws, (size_t)Ba * nkv * att_splits * 2 * (HD + 2) * 4))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->att_sem, (size_t)Ba * nkv * 4))) goto fail;
+    cudaMemset(s->att_sem, 0, (size_t)Ba * nkv * 4);
   }
   {
     const int H = e->has_talker ? e->talker.hidden : e->cp.hidden;
@@ -1388,6 +1439,53 @@ extern "C" int qtb_cp_frame(qtb_session_t *s, const float *talker_hidden, const 
   if (rc) return rc;
   for (int b = 0; b < B; b++) memcpy(codes_out + (size_t)b * 15, s->h_codes + (size_t)b * 16 + 1, 15 * 4);
   return 0;
+}
+
+extern "C" int qtb_prefill(qtb_session_t *s, int b, const float *embeds, int n, int pos0, float *hidden_out,
+                           float *dec_x_out) {
+  if (!s || !embeds || n < 1) return set_err(QTB_E_INVALID, "bad argument");
+  if (!s->prog[PROG_PREFILL]) return set_err(QTB_E_UNSUPPORTED, "engine has no talker");
+  if (b < 0 || b >= s->B) return set_err(QTB_E_INVALID, "bad slot %d", b);
+  if (pos0 < 0 || pos0 + n > s->max_ctx) return set_err(QTB_E_INVALID, "positions [%d,%d) outside [0,%d)", pos0, pos0 + n, s->max_ctx);
+  const int H = s->e->talker.hidden, R = PREFILL_CHUNK, pts = s->tk.pt_stride;
+  { int rc0 = begin_call(s); if (rc0) return rc0; }
+  // every chunk row reads and appends through slot b's page table
+  std::vector<int32_t> row(pts);
+  CUDA_TRY(cudaMemcpy(row.data(), s->tk.page_table + (size_t)b * pts, (size_t)pts * 4, cudaMemcpyDeviceToHost));
+  for (int i = 0; i <= (pos0 + n - 1) / PAGE; i++)
+    if (row[i] < 0 || row[i] >= s->tk.n_pages) return set_err(QTB_E_INVALID, "slot %d has no page for position %d", b, 16 * i);
+  std::vector<int32_t> pt((size_t)R * pts);
+  for (int r = 0; r < R; r++) memcpy(pt.data() + (size_t)r * pts, row.data(), (size_t)pts * 4);
+  CUDA_TRY(cudaMemcpyAsync(s->pf.page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice, s->stream));
+  std::vector<float> x((size_t)R * H);
+  std::vector<int32_t> pos(R);
+  int rc = 0;
+  CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
+  for (int c0 = 0; c0 < n; c0 += R) {
+    const int m = std::min(R, n - c0);
+    // rows past the chunk's last token repeat it (same position, same K/V bytes)
+    for (int r = 0; r < R; r++) {
+      const int t = c0 + std::min(r, m - 1);
+      memcpy(x.data() + (size_t)r * H, embeds + (size_t)t * H, (size_t)H * 4);
+      pos[r] = pos0 + t;
+    }
+    CUDA_TRY(cudaMemcpyAsync(s->pf.x, x.data(), x.size() * 4, cudaMemcpyHostToDevice, s->stream));
+    CUDA_TRY(cudaMemcpyAsync(s->pf_pos, pos.data(), (size_t)R * 4, cudaMemcpyHostToDevice, s->stream));
+    if ((rc = launch_prog(s, PROG_PREFILL, 1, false))) return rc;
+    // the copies above reuse host buffers: wait before the next chunk refills them
+    CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (c0 + m == n) {
+      if (hidden_out)
+        CUDA_TRY(cudaMemcpy(hidden_out, s->pf.hidden + (size_t)(m - 1) * H, (size_t)H * 4, cudaMemcpyDeviceToHost));
+      if (dec_x_out)
+        CUDA_TRY(cudaMemcpy(dec_x_out, s->pf.x + (size_t)(m - 1) * H, (size_t)H * 4, cudaMemcpyDeviceToHost));
+    }
+  }
+  CUDA_TRY(cudaEventRecord(s->ev1, s->stream));
+  s->last_launches = (n + R - 1) / R;
+  const int32_t np = pos0 + n;
+  CUDA_TRY(cudaMemcpy(s->pos + b, &np, 4, cudaMemcpyHostToDevice));
+  return finish(s, true);
 }
 
 extern "C" int qtb_session_begin_generation(qtb_session_t *s, const int32_t *expected_frames, float rep_penalty) {

@@ -152,7 +152,13 @@ struct AttnArgs {
   // the host CPU's reciprocal-square-root seeds for the per-head QK RMSNorm
   // (qk_inv_rms), or null for IEEE 1 / sqrtf
   const unsigned *rsq_tab;
+  // ATT_DECODE: append the token's K/V, then attend; ATT_APPEND: append only
+  // (one item per slot and KV head); ATT_ATTEND: attend to K/V already in the
+  // pages.  A prefill runs its prompt tokens as slots of one sequence: all of
+  // them append first, then all attend, causally by position.
+  int mode;
 };
+enum AttnMode { ATT_DECODE = 0, ATT_APPEND = 1, ATT_ATTEND = 2 };
 
 struct EmbedArgs {
   float *dst; int ld_dst; int dim;
@@ -2413,12 +2419,14 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
     }
     const int b = it.b, g = it.g, sp = it.sp, pos = it.pos, L = it.L, npages = it.npages, nsp = it.nsp;
     const int p_begin = it.p_begin, p_end = it.p_end;
-    const bool owns_new = (p_end == npages);
+    // the item that holds the newest page appends the token (decode, append)
+    // and patches it into its page buffer from registers (decode only)
+    const bool owns_new = (p_end == npages) && a.mode != ATT_ATTEND;
     const int *pt = a.page_table + (size_t)b * a.pt_stride;
     // pages first: the stream positions issued so far are a prefix (the hook
     // before the barrier, or the previous item's refills, may have covered
     // the first ones)
-    if (warp == 7) {
+    if (warp == 7 && a.mode != ATT_APPEND) {
       const int done = (int)min(kc.att_issued - kc.page_ctr, (unsigned)NB);
       attn_issue(a, it, done, min(p_end - p_begin, NB), kc, smem_base);
     }
@@ -2494,6 +2502,11 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
     if (__syncthreads_or(kc.local_err)) return;
     ckpt(kc, 1);
     const int next = a.dyn ? sm->next : item + (int)gridDim.x;
+    if (a.mode == ATT_APPEND) {   // no attention in this stage
+      __syncthreads();   // every thread has read sm->next and the new K/V rows
+      item = next;
+      continue;
+    }
     // dynamic order: the next item's pages follow this one's in the stream, so
     // buffers freed near the end of this item already take the next one's
     // pages.  Only from an item of at least NB pages: then the refills cover
@@ -2951,7 +2964,8 @@ QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
           // every lane tests the descriptor's barrier itself (that makes the
           // bulk-copied descriptor visible to it)
           const bool landed = __all_sync(0xffffffffu, mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u));
-          if (landed && kc.dring[slot].kind == ST_ATTN) attn_prefetch(kc.dring[slot].a, kc.dring[slot].B, kc, smem);
+          if (landed && kc.dring[slot].kind == ST_ATTN && kc.dring[slot].a.mode != ATT_APPEND)
+            attn_prefetch(kc.dring[slot].a, kc.dring[slot].B, kc, smem);
           __syncwarp();
           phase = 1;
         } else if (phase == 1) {

@@ -87,6 +87,7 @@ def lib():
     L.qtb_cp_frame.argtypes = [_vp, _vp, _vp, _vp]
     L.qtb_decode_frames.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp]
     L.qtb_session_begin_generation.argtypes = [_vp, _vp, C.c_float]
+    L.qtb_prefill.argtypes = [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]
     L.qtb_session_get_done.argtypes = [_vp, _vp]
     for n in ("qtb_session_upload_kv", "qtb_session_download_kv", "qtb_session_download_cp_kv"):
         getattr(L, n).argtypes = [_vp, C.c_int, _vp, _vp, C.c_int, C.c_int]
@@ -415,6 +416,16 @@ class Session:
         hid = np.empty((self.B, cfg.hidden), np.float32)
         check(lib().qtb_decode_frames(self.h, ptr(e), ptr(pd), n_frames, ptr(codes), ptr(hid)))
         return codes, hid
+
+    def prefill(self, b, embeds, pos0=0):
+        """Device prefill of slot b (qtb_prefill): embeds [n][hidden] at
+        positions pos0.. ; returns (last hidden, last pre-norm residual)."""
+        cfg = self.eng.cfg
+        e = np.ascontiguousarray(embeds, np.float32).reshape(-1, cfg.hidden)
+        h = np.empty(cfg.hidden, np.float32)
+        dx = np.empty(cfg.hidden, np.float32)
+        check(lib().qtb_prefill(self.h, int(b), ptr(e), e.shape[0], int(pos0), ptr(h), ptr(dx)))
+        return h, dx
 
     def begin_generation(self, expected_frames=None, rep_penalty=1.0):
         """The reference's generation-loop codec head for decode_frames

@@ -171,6 +171,46 @@ def test_large_batch_matches_single_sessions(have_gpu, tiny):
         assert np.array_equal(runs[0][t][1], runs[1][t][1]), t
 
 
+@pytest.mark.parametrize("fmt", ["bf16", "int8"])
+def test_prefill_matches_reference_prefill(have_gpu, tiny, fmt):
+    """Device prefill (qtb_prefill, 40 tokens in one 64-row chunk) against
+    the reference's own CPU prefill (qwen_talker_prefill): last-token residual
+    and the KV cache; then a 100-token prefill (two chunks) continuing from a
+    10-token prefix against single decode steps on the device."""
+    cfg, m, path = tiny
+    ref = refbind.RefModel(path, cfg, use_int8=(fmt == "int8"), threads=8, cp=False)
+    eng = engine_from_ref(ref, m, cfg, fmt, with_cp=False)
+    rng = np.random.default_rng(31)
+    E = (0.1 * rng.standard_normal((40, cfg.hidden))).astype(np.float32)
+    dx_ref = ref.talker_prefill(E)
+    ses = Q.Session(eng, 2, 256)
+    h, dx = ses.prefill(1, E, 0)
+    assert rel_l2(dx, dx_ref) < 1e-3, rel_l2(dx, dx_ref)
+    assert list(ses.get_pos()) == [0, 40]
+    kg, vg = ses.download_kv(1, cfg.layers, cfg.kv_heads * 128, 40)
+    for l in range(cfg.layers):
+        k, v = ref.kv(l, 40)
+        assert kv_close(kg[l], k, 0.85) and kv_close(vg[l], v, 0.85), l
+    ref.close()
+    # prefix of 10 single steps, then 100 tokens by prefill, against 110 steps
+    E2 = (0.1 * rng.standard_normal((110, cfg.hidden))).astype(np.float32)
+    a = Q.Session(eng, 1, 256)
+    bb = Q.Session(eng, 1, 256)
+    for p in range(110):
+        hs = a.talker_step(E2[p], p)
+    for p in range(10):
+        bb.talker_step(E2[p], p)
+    hp, _ = bb.prefill(0, E2[10:], 10)
+    assert rel_l2(hp, hs[0]) < 1e-3, rel_l2(hp, hs[0])
+    ka, va = a.download_kv(0, cfg.layers, cfg.kv_heads * 128, 110)
+    kb, vb = bb.download_kv(0, cfg.layers, cfg.kv_heads * 128, 110)
+    for l in range(cfg.layers):
+        assert kv_close(kb[l], ka[l], 0.85) and kv_close(vb[l], va[l], 0.85), l
+    # and decoding continues from the prefilled cache
+    e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+    assert rel_l2(bb.talker_step(e, 110)[0], a.talker_step(e, 110)[0]) < 1e-3
+
+
 def test_kv_upload_download_roundtrip(have_gpu, tiny):
     cfg, m, path = tiny
     eng = Q.Engine(Q.HostModel(cfg, m.talker, m.codec_head, m.codec_embedding), Q.FMT_BF16)
