@@ -195,6 +195,18 @@ int qtb_prefill(qtb_session_t *s, int b, const float *embeds, int n, int pos0, f
 int qtb_session_begin_generation(qtb_session_t *s, const int32_t *expected_frames, float rep_penalty);
 /* Per-slot stop flags of the generation (1 = sampled EOS), host [batch]. */
 int qtb_session_get_done(qtb_session_t *s, int32_t *done);
+/* Continuous batching (the reference's admit / evict loop, qwen_tts.c:
+ * 2389-2740): restart slot b's generation state -- frame counter, repetition
+ * counts, EOS boost start (2 x expected_frames, <= 0: none) -- as a running
+ * slot (active = 1) or a parked one that neither advances nor reports codes
+ * (active = 0).  Needs qtb_session_begin_generation first. */
+int qtb_session_reset_slot(qtb_session_t *s, int b, int32_t expected_frames, int active);
+/* Slot b's decode position alone (qtb_session_set_pos sets every slot). */
+int qtb_session_set_slot_pos(qtb_session_t *s, int b, int32_t pos);
+/* Slot b's next talker input (host [hidden]), as qtb_decode_frames with
+ * embeds == NULL then consumes it: the embedding of an admitted request's last
+ * prompt token, while the other slots keep the inputs their last frame made. */
+int qtb_session_set_embed(qtb_session_t *s, int b, const float *embed);
 
 /* KV pages <-> contiguous bf16 ([layer][len][kv_dim] with per-layer stride
  * layer_stride positions, the reference's host layout qwen_tts_talker.c:454-460). */

@@ -777,7 +777,7 @@ static bool v2_ok(int fmt, int rows, int K, int B, int G) {
 // TC_X_BYTES (N x 128 bytes per chunk) and 2048 columns.
 struct TcShape { int S = 0, kcn = 0, R = 0; };
 static bool tc_ok(const DMat &m, int B, int fmt) {
-  return tc_enabled() && m.wtc && B > 4 && B <= 64 && (fmt == FMT_BF16 || fmt == FMT_INT8) && m.rows % 128 == 0;
+  return tc_enabled() && m.wtc && B >= 1 && B <= 64 && (fmt == FMT_BF16 || fmt == FMT_INT8) && m.rows % 128 == 0;
 }
 static TcShape tc_choose(int fmt, int rows, int K, int B, int G) {
   const int T = rows / 128, NKC = K * (fmt == FMT_INT8 ? 1 : 2) / 128;
@@ -1506,6 +1506,34 @@ extern "C" int qtb_session_begin_generation(qtb_session_t *s, const int32_t *exp
   g.rep_inv = 1.0f / rep_penalty;   // the reference's build multiplies by this reciprocal
   CUDA_TRY(cudaMemcpy(s->gen, &g, sizeof g, cudaMemcpyHostToDevice));
   s->gen_on = 1;
+  return 0;
+}
+
+extern "C" int qtb_session_reset_slot(qtb_session_t *s, int b, int32_t expected_frames, int active) {
+  if (!s || b < 0 || b >= s->B) return set_err(QTB_E_INVALID, "bad slot");
+  if (!s->gen_on) return set_err(QTB_E_INVALID, "qtb_session_begin_generation first");
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  const int32_t z = 0, d = active ? 0 : 1, bs = expected_frames > 0 ? 2 * expected_frames : -1;
+  CUDA_TRY(cudaMemcpy(s->gen_h.frame + b, &z, 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(s->gen_h.done + b, &d, 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(s->gen_h.boost_start + b, &bs, 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemset(s->gen_h.rep_count + (size_t)b * s->gen_h.vocab, 0, (size_t)s->gen_h.vocab * 2));
+  return 0;
+}
+
+extern "C" int qtb_session_set_slot_pos(qtb_session_t *s, int b, int32_t pos) {
+  if (!s || b < 0 || b >= s->B) return set_err(QTB_E_INVALID, "bad slot");
+  if (pos < 0 || pos >= s->max_ctx) return set_err(QTB_E_INVALID, "position %d outside [0,%d)", pos, s->max_ctx);
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemcpy(s->pos + b, &pos, 4, cudaMemcpyHostToDevice));
+  return 0;
+}
+
+extern "C" int qtb_session_set_embed(qtb_session_t *s, int b, const float *embed) {
+  if (!s || !embed || b < 0 || b >= s->B || !s->e->has_talker) return set_err(QTB_E_INVALID, "bad argument");
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  const int H = s->e->talker.hidden;
+  CUDA_TRY(cudaMemcpy(s->tk.x + (size_t)b * H, embed, (size_t)H * 4, cudaMemcpyHostToDevice));
   return 0;
 }
 

@@ -88,6 +88,9 @@ def lib():
     L.qtb_decode_frames.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp]
     L.qtb_session_begin_generation.argtypes = [_vp, _vp, C.c_float]
     L.qtb_prefill.argtypes = [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]
+    L.qtb_session_reset_slot.argtypes = [_vp, C.c_int, C.c_int, C.c_int]
+    L.qtb_session_set_slot_pos.argtypes = [_vp, C.c_int, C.c_int]
+    L.qtb_session_set_embed.argtypes = [_vp, C.c_int, _vp]
     L.qtb_session_get_done.argtypes = [_vp, _vp]
     for n in ("qtb_session_upload_kv", "qtb_session_download_kv", "qtb_session_download_cp_kv"):
         getattr(L, n).argtypes = [_vp, C.c_int, _vp, _vp, C.c_int, C.c_int]
@@ -433,6 +436,16 @@ class Session:
         ef = None if expected_frames is None else np.ascontiguousarray(np.broadcast_to(expected_frames, (self.B,)),
                                                                        np.int32)
         check(lib().qtb_session_begin_generation(self.h, ptr(ef), C.c_float(rep_penalty)))
+
+    def reset_slot(self, b, expected_frames=0, active=True):
+        check(lib().qtb_session_reset_slot(self.h, int(b), int(expected_frames), int(bool(active))))
+
+    def set_slot_pos(self, b, pos):
+        check(lib().qtb_session_set_slot_pos(self.h, int(b), int(pos)))
+
+    def set_embed(self, b, embed):
+        e = np.ascontiguousarray(embed, np.float32)
+        check(lib().qtb_session_set_embed(self.h, int(b), ptr(e)))
 
     def get_done(self):
         d = np.zeros(self.B, np.int32)

@@ -311,6 +311,21 @@ def gen_loop_reference(ref, m, cfg, e_last, n_frames, expected, rep):
     return np.array(out, np.int32)
 
 
+def biased_head_model():
+    """Tiny model whose codec head favours four tokens (they repeat, so the
+    repetition penalty decides between them) and whose EOS row is zero (EOS
+    wins once the boost passes the leading logits)."""
+    cfg = tiny_cfg(layers=3, cp_layers=2)
+    m = Q.synth_model(cfg, seed=21, with_cp=True, norm_gain="random")
+    head = O.f32_from_bf16(m.codec_head).copy()
+    scale = np.full(cfg.codec_vocab, 0.1, np.float32)
+    scale[[5, 9, 13, 300]] = 3.0
+    head *= scale[:, None]
+    head[Q.CODEC_EOS] = 0.0
+    m.codec_head = Q.bf16_from_f32(head)
+    return cfg, m
+
+
 def test_generation_rules_eos_and_repetition_match_reference(have_gpu, tmp_path):
     """The device codec head under the reference's frame-loop rules: clip,
     special-token mask, EOS suppressed for 2 frames and boosted after twice the
@@ -319,15 +334,7 @@ def test_generation_rules_eos_and_repetition_match_reference(have_gpu, tmp_path)
     (they repeat, so the penalty decides) and EOS (a zero row) wins once
     boosted.  Two slots with different expected lengths stop at different
     frames; every code up to each slot's EOS equals the reference's loop."""
-    cfg = tiny_cfg(layers=3, cp_layers=2)
-    m = Q.synth_model(cfg, seed=21, with_cp=True, norm_gain="random")
-    head = O.f32_from_bf16(m.codec_head).copy()
-    keep = [5, 9, 13, 300]
-    scale = np.full(cfg.codec_vocab, 0.1, np.float32)
-    scale[keep] = 3.0
-    head *= scale[:, None]
-    head[Q.CODEC_EOS] = 0.0
-    m.codec_head = Q.bf16_from_f32(head)
+    cfg, m = biased_head_model()
     path = str(tmp_path / "gen.safetensors")
     refbind.write_safetensors(path, refbind.model_tensors(m))
     rep = 1.05
@@ -358,6 +365,33 @@ def test_generation_rules_eos_and_repetition_match_reference(have_gpu, tmp_path)
     assert list(ses.get_done()) == [1, 1]
     # stopped slots keep their positions: prompt (9) + frames before EOS
     assert list(ses.get_pos()) == [8 + len(want[0]) - 1 + 1, 8 + len(want[1]) - 1 + 1]
+
+
+def test_continuous_batching_admit_evict(have_gpu):
+    """Continuous batching (qtb_batcher): 6 requests of different prompt
+    lengths and expected lengths through 2 slots of a paged session; slots are
+    refilled as requests stop at EOS or at their frame limit, their pages
+    recycled.  Every request's codes equal the same request served alone."""
+    import qtb_batcher as QB
+    cfg, m = biased_head_model()
+    eng = Q.Engine(m, Q.FMT_BF16, Q.FMT_BF16)
+    rng = np.random.default_rng(41)
+    reqs = [QB.GenRequest(i, (0.1 * rng.standard_normal((int(n), cfg.hidden))).astype(np.float32), int(mf), int(ef))
+            for i, (n, mf, ef) in enumerate([(1, 30, 2), (7, 30, 4), (12, 5, 3), (3, 30, 5), (20, 30, 2), (2, 9, 0)])]
+
+    def serve(rs):
+        ses = Q.Session(eng, 2, 256, n_pages=2 + 12)
+        return QB.ContinuousBatcher(ses, rep_penalty=1.05).run(rs)
+
+    got = serve(reqs)
+    assert sorted(got) == list(range(6))
+    stopped = 0
+    for r in reqs:
+        alone = serve([r])[r.rid]
+        assert np.array_equal(got[r.rid], alone), r.rid
+        assert len(alone) <= r.max_frames
+        stopped += int(alone[-1, 0] == Q.CODEC_EOS)
+    assert stopped >= 2   # some requests end at EOS, others at their frame limit
 
 
 @pytest.mark.slow
