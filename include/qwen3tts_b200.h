@@ -96,6 +96,11 @@ typedef struct {
     qtb_matrix_t cp_mtp_proj;        /* [cp_hidden][cp_emb_dim] or data == NULL   */
     int cp_mtp_fmt;                  /* QTB_FMT_BF16 or QTB_FMT_INT8              */
     const float *cp_mtp_bias;        /* [cp_hidden] or NULL                       */
+    /* The talker's layers in QTB_FMT_BF16 for qtb_prefill, or NULL (prefill
+     * then uses the decode weights).  The reference prefills from its bf16
+     * weights in every mode (qwen_talker_prefill, qwen_tts_talker.c:840-851,
+     * 911-918, 940-981) and decodes from the quantized ones. */
+    const qtb_layer_t *talker_prefill_layers;
 } qtb_engine_desc_t;
 
 typedef struct qtb_engine qtb_engine_t;
@@ -170,8 +175,12 @@ int qtb_decode_frames(qtb_session_t *s, const float *embeds, const float *pad, i
  * on the CPU and uploads with qwen_cuda_talker_upload_kv): embeds host
  * [n][hidden] at positions pos0 .. pos0 + n - 1, in chunks of up to 64 tokens
  * run as a batch on the large-batch tensor-core GEMVs (every token's K/V is
- * appended before any of them attends, causally).  Fills the slot's KV pages
- * and sets its position to pos0 + n.  hidden_out: host [hidden] final-normed
+ * appended before any of them attends, causally).  As in the reference, the
+ * prompt's tokens attend to the prompt's K/V in f32 (positions before pos0
+ * come from the bf16 cache); the cache receives the bf16 K/V.  Fills the
+ * slot's KV pages and sets its position to pos0 + n.  The f32 prompt K/V
+ * buffer (layers x kv heads x 128 x 8 bytes per prompt token) is allocated on
+ * the first call and grown to the longest prompt.  hidden_out: host [hidden] final-normed
  * hidden of the last token, or NULL; dec_x_out: its pre-norm residual, or
  * NULL.  The slot's pages must cover the positions. */
 int qtb_prefill(qtb_session_t *s, int b, const float *embeds, int n, int pos0, float *hidden_out,

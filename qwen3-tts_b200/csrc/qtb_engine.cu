@@ -456,6 +456,8 @@ struct qtb_engine {
   const unsigned *rsq_tab = nullptr;   // QK-norm rsqrt seeds (qk_rsq_table) or null
   int codec_eos_row = 0;               // device codec-head row of the EOS token
   int has_eos = 0;
+  DStack talker_pf;                    // bf16 talker weights of the prefill (when given)
+  int has_talker_pf = 0;
 };
 
 static int upload_stack(qtb_engine *e, const qtb_stack_desc_t &d, DStack &s) {
@@ -559,6 +561,12 @@ extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_eng
   e->device = device;
   e->n_sm = prop.multiProcessorCount;
   {
+    // QTB_GRID=n: run the persistent kernel on n CTAs instead of one per SM
+    // (a latency-bound small batch trades bandwidth for cheaper grid barriers)
+    const char *gs = getenv("QTB_GRID");
+    if (gs && atoi(gs) >= 2) e->n_sm = std::min(e->n_sm, atoi(gs) & ~1);
+  }
+  {
     // 2-CTA clusters for the whole grid: only if all n_sm / 2 clusters can be
     // resident at once (a cooperative launch needs every CTA resident).
     // QTB_NO_CLUSTERS=1 selects the unclustered schedule (every int8 tile whole
@@ -580,6 +588,13 @@ extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_eng
   e->has_talker = d->talker.n_layers > 0;
   if (e->has_talker) {
     if ((rc = upload_stack(e, d->talker, e->talker))) goto fail;
+    if (d->talker_prefill_layers && d->talker.fmt != FMT_BF16) {
+      qtb_stack_desc_t pd = d->talker;
+      pd.fmt = FMT_BF16;
+      pd.layers = d->talker_prefill_layers;
+      if ((rc = upload_stack(e, pd, e->talker_pf))) goto fail;
+      e->has_talker_pf = 1;
+    }
     if (d->codec_head && d->codebook > 0) {
       // the codebook rows, then the EOS token's row (when the vocabulary has
       // one), then zero rows up to a whole 128-row tile: the special tokens the
@@ -693,6 +708,8 @@ struct qtb_session {
   float *ss_ws = nullptr;    // tcgen05 stages: per-(row group, slice) sums of squares [G][64]
   StackBufs pf;              // prefill chunk buffers (PREFILL_CHUNK rows) over the talker's KV pools
   int *pf_pos = nullptr;     // [PREFILL_CHUNK] positions of the chunk's tokens
+  PromptKV *pkv = nullptr;   // device descriptor of the prompt's f32 K/V (pkv_h: its host copy)
+  PromptKV pkv_h = {};       // k, v: cudaMalloc'd on the first prefill, grown to the longest prompt
   GenState *gen = nullptr;   // codec-head generation state (device); gen_h mirrors its pointers
   GenState gen_h = {};
   int gen_on = 0;
@@ -894,8 +911,12 @@ struct ProgBuilder {
     a.max_splits = b.max_splits; a.min_pps = b.min_pps;
     a.ws = s->att_ws; a.sem = s->att_sem;
     a.rsq_tab = s->e->rsq_tab;
-    if (mode == ATT_APPEND) { a.max_splits = 1; a.min_pps = 1 << 20; }   // one item per slot and KV head
+    if (mode != ATT_DECODE) {   // prefill: one item per slot and KV head, the prompt's f32 K/V
+      a.max_splits = 1; a.min_pps = 1 << 20;
+      a.pkv = s->pkv; a.layer = layer;
+    }
     attn_schedule(a, B, s->e->n_sm);
+    if (mode == ATT_ATTEND) a.dyn = 0;   // static item order (attn_prefill_stage)
     st.push_back(S);
   }
   // A prompt chunk of one sequence as B slots (positions pos[i], the same page
@@ -1050,8 +1071,9 @@ static int build_programs(qtb_session *s) {
     if ((rc = upload_prog(s, PROG_TALKER, pb))) return rc;
     if (s->pf.x) {
       ProgBuilder pp{s};
-      pp.prefill_layers(k, s->pf, PREFILL_CHUNK, s->pf_pos, s->tk_layer_elems);
-      pp.norm(s->pf.x, k.hidden, k.final_norm, s->pf.hidden, k.hidden, k.hidden, k.eps, PREFILL_CHUNK);
+      const DStack &kp = e->has_talker_pf ? e->talker_pf : k;
+      pp.prefill_layers(kp, s->pf, PREFILL_CHUNK, s->pf_pos, s->tk_layer_elems);
+      pp.norm(s->pf.x, kp.hidden, kp.final_norm, s->pf.hidden, kp.hidden, kp.hidden, kp.eps, PREFILL_CHUNK);
       if ((rc = upload_prog(s, PROG_PREFILL, pp))) return rc;
     }
   }
@@ -1129,6 +1151,8 @@ extern "C" void qtb_session_destroy(qtb_session_t *s) {
   if (s->stream) cudaStreamSynchronize(s->stream);
   s->ar.release();
   if (s->trace) cudaFree(s->trace);
+  if (s->pkv_h.k) cudaFree(s->pkv_h.k);
+  if (s->pkv_h.v) cudaFree(s->pkv_h.v);
   if (s->ev0) cudaEventDestroy(s->ev0);
   if (s->ev1) cudaEventDestroy(s->ev1);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -1245,7 +1269,9 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
         if ((rc = s->ar.alloc((void **)&p.h, R * k.inter * 4))) goto fail;
         if ((rc = s->ar.alloc((void **)&p.page_table, R * s->tk.pt_stride * 4))) goto fail;
         if ((rc = s->ar.alloc((void **)&s->pf_pos, R * 4))) goto fail;
+        if ((rc = s->ar.alloc((void **)&s->pkv, sizeof(PromptKV)))) goto fail;
         cudaMemset(s->pf_pos, 0, R * 4);
+        cudaMemset(s->pkv, 0, sizeof(PromptKV));
         cudaMemset(p.page_table, 0, R * s->tk.pt_stride * 4);
         p.kpool = s->tk.kpool; p.vpool = s->tk.vpool;
         p.n_pages = s->tk.n_pages; p.pt_stride = s->tk.pt_stride;
@@ -1457,6 +1483,21 @@ extern "C" int qtb_prefill(qtb_session_t *s, int b, const float *embeds, int n, 
   std::vector<int32_t> pt((size_t)R * pts);
   for (int r = 0; r < R; r++) memcpy(pt.data() + (size_t)r * pts, row.data(), (size_t)pts * 4);
   CUDA_TRY(cudaMemcpyAsync(s->pf.page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice, s->stream));
+  // the prompt's f32 K/V, positions pos0 .. pos0 + n - 1 of every layer
+  const DStack &tk = s->e->talker;
+  if (s->pkv_h.cap < n) {
+    CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (s->pkv_h.k) cudaFree(s->pkv_h.k);
+    if (s->pkv_h.v) cudaFree(s->pkv_h.v);
+    s->pkv_h = PromptKV{nullptr, nullptr, 0, 0};
+    const int cap = (n + R - 1) / R * R;
+    const size_t bytes = (size_t)tk.n_layers * tk.n_kv * cap * HD * sizeof(float);
+    CUDA_TRY(cudaMalloc((void **)&s->pkv_h.k, bytes));
+    CUDA_TRY(cudaMalloc((void **)&s->pkv_h.v, bytes));
+    s->pkv_h.cap = cap;
+  }
+  s->pkv_h.p0 = pos0;
+  CUDA_TRY(cudaMemcpyAsync(s->pkv, &s->pkv_h, sizeof(PromptKV), cudaMemcpyHostToDevice, s->stream));
   std::vector<float> x((size_t)R * H);
   std::vector<int32_t> pos(R);
   int rc = 0;

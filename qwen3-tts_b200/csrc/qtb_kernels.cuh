@@ -153,12 +153,22 @@ struct AttnArgs {
   // (qk_inv_rms), or null for IEEE 1 / sqrtf
   const unsigned *rsq_tab;
   // ATT_DECODE: append the token's K/V, then attend; ATT_APPEND: append only
-  // (one item per slot and KV head); ATT_ATTEND: attend to K/V already in the
-  // pages.  A prefill runs its prompt tokens as slots of one sequence: all of
-  // them append first, then all attend, causally by position.
+  // (one item per slot and KV head); ATT_ATTEND: attend, causally by position,
+  // to K/V appended before.  A prefill runs its prompt tokens as slots of one
+  // sequence: all of them append first, then all attend.
   int mode;
+  // prefill only: the prompt's K/V in f32 (pkv, layer `layer`).  APPEND
+  // writes them there as well as into the pages; ATTEND reads positions from
+  // the prompt's first one on from there, older ones from the pages.
+  const struct PromptKV *pkv; int layer;
 };
 enum AttnMode { ATT_DECODE = 0, ATT_APPEND = 1, ATT_ATTEND = 2 };
+
+// The prompt of one prefill call in f32, [layer][n_kv][cap][HD] for K and V:
+// positions p0 .. p0 + cap - 1.  The reference's prefill attends to its
+// prompt's own K/V before the bf16 rounding of the cache
+// (qwen_talker_prefill, qwen_tts_talker.c:904-914).
+struct PromptKV { float *k, *v; int cap, p0; };
 
 struct EmbedArgs {
   float *dst; int ld_dst; int dim;
@@ -2232,6 +2242,53 @@ QTB_DEV float qk_inv_rms(float a, const unsigned *tab) {
   return __fmul_rn(__fmaf_rn(t, x0, -3.0f), __fmul_rn(x0, -0.5f));
 }
 
+// Warp-wide: the prologue values of one 128-dim row of slot b's QKV output at
+// position pos -- which = 0, 1: query head 2g + which; 2: key head g; 3: value
+// head g -- with the per-head QK RMSNorm and RoPE applied to q and k.  Lane j
+// holds dims j, j + 32, j + 64, j + 96.
+QTB_DEV void attn_row(const AttnArgs &a, int b, int g, int which, int pos, int lane, float v[4]) {
+  const int q_dim = a.n_heads * HD, kv_dim = a.n_kv * HD;
+  const float *src;
+  const float *nw = nullptr;
+  if (which < 2) { src = a.qkv + (size_t)b * a.ld_qkv + (2 * g + which) * HD; nw = a.q_norm; }
+  else if (which == 2) { src = a.qkv + (size_t)b * a.ld_qkv + q_dim + g * HD; nw = a.k_norm; }
+  else src = a.qkv + (size_t)b * a.ld_qkv + q_dim + kv_dim + g * HD;
+  float gw[4], rc[2], rs[2];
+#pragma unroll
+  for (int i = 0; i < 4; i++) v[i] = __ldcg(src + lane + 32 * i);
+  if (nw) {   // independent of the row values: issue with them
+#pragma unroll
+    for (int i = 0; i < 4; i++) gw[i] = __ldg(nw + lane + 32 * i);
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      rc[i] = __ldg(a.rope_cos + (size_t)pos * (HD / 2) + lane + 32 * i);
+      rs[i] = __ldg(a.rope_sin + (size_t)pos * (HD / 2) + lane + 32 * i);
+    }
+  }
+  if (nw) {
+    // the reference's per-head RMSNorm in its x86 build's operation order
+    // (qwen_rms_norm_per_head, qwen_tts_kernels.c:486-577): sixteen-lane
+    // FMA accumulators over dims j, j+32, j+64, j+96 (lane j) and j+16, ...
+    // (lane j+16) -- this lane's own four values -- then the pairwise tree
+    // (+16, +8, +4, +2, +1); mean + eps as one FMA; x * w * inv
+    float ss = __fmul_rn(v[0], v[0]);
+    ss = __fmaf_rn(v[1], v[1], ss);
+    ss = __fmaf_rn(v[2], v[2], ss);
+    ss = __fmaf_rn(v[3], v[3], ss);
+    ss = warp_sum(ss);
+    const float inv = qk_inv_rms(__fmaf_rn(ss, 1.0f / (float)HD, a.eps), a.rsq_tab);
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = __fmul_rn(__fmul_rn(v[i], gw[i]), inv);
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const float c = rc[i], s = rs[i];
+      const float x1 = v[i], x2 = v[i + 2];
+      v[i] = fmaf(x1, c, -(x2 * s));
+      v[i + 2] = fmaf(x2, c, x1 * s);
+    }
+  }
+}
+
 // Decode work item -> (slot, kv head, split) and the split's page range.
 // Returns false for items beyond the slot's split count (or a bad position).
 QTB_DEV bool attn_item(const AttnArgs &a, int item, AttnItem &it) {
@@ -2373,7 +2430,6 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
   char *smem = smem_base + SM_X_OFF;
   AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q_dim = a.n_heads * HD, kv_dim = a.n_kv * HD;
   const int NB = a.nbuf;
 
   // ---- this CTA's first item ----
@@ -2437,45 +2493,8 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
 
     // ---- prologue: QK RMSNorm + RoPE (+ KV append) ----
     if (warp < 4) {
-      const float *src;
-      const float *nw = nullptr;
-      if (warp < 2) { src = a.qkv + (size_t)b * a.ld_qkv + (2 * g + warp) * HD; nw = a.q_norm; }
-      else if (warp == 2) { src = a.qkv + (size_t)b * a.ld_qkv + q_dim + g * HD; nw = a.k_norm; }
-      else src = a.qkv + (size_t)b * a.ld_qkv + q_dim + kv_dim + g * HD;
-      float v[4], gw[4], rc[2], rs[2];
-#pragma unroll
-      for (int i = 0; i < 4; i++) v[i] = __ldcg(src + lane + 32 * i);
-      if (nw) {   // independent of the row values: issue with them
-#pragma unroll
-        for (int i = 0; i < 4; i++) gw[i] = __ldg(nw + lane + 32 * i);
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-          rc[i] = __ldg(a.rope_cos + (size_t)pos * (HD / 2) + lane + 32 * i);
-          rs[i] = __ldg(a.rope_sin + (size_t)pos * (HD / 2) + lane + 32 * i);
-        }
-      }
-      if (nw) {
-        // the reference's per-head RMSNorm in its x86 build's operation order
-        // (qwen_rms_norm_per_head, qwen_tts_kernels.c:486-577): sixteen-lane
-        // FMA accumulators over dims j, j+32, j+64, j+96 (lane j) and j+16, ...
-        // (lane j+16) -- this lane's own four values -- then the pairwise tree
-        // (+16, +8, +4, +2, +1); mean + eps as one FMA; x * w * inv
-        float ss = __fmul_rn(v[0], v[0]);
-        ss = __fmaf_rn(v[1], v[1], ss);
-        ss = __fmaf_rn(v[2], v[2], ss);
-        ss = __fmaf_rn(v[3], v[3], ss);
-        ss = warp_sum(ss);
-        const float inv = qk_inv_rms(__fmaf_rn(ss, 1.0f / (float)HD, a.eps), a.rsq_tab);
-#pragma unroll
-        for (int i = 0; i < 4; i++) v[i] = __fmul_rn(__fmul_rn(v[i], gw[i]), inv);
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-          const float c = rc[i], s = rs[i];
-          const float x1 = v[i], x2 = v[i + 2];
-          v[i] = fmaf(x1, c, -(x2 * s));
-          v[i + 2] = fmaf(x2, c, x1 * s);
-        }
-      }
+      float v[4];
+      attn_row(a, b, g, warp, pos, lane, v);
       if (warp < 2) {
 #pragma unroll
         for (int i = 0; i < 4; i++) sm->q[warp][lane + 32 * i] = v[i];
@@ -2483,6 +2502,17 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
         uint16_t *dst = (warp == 2) ? sm->knew : sm->vnew;
 #pragma unroll
         for (int i = 0; i < 4; i++) dst[lane + 32 * i] = (uint16_t)f32_to_bf16_trunc(v[i]);
+        if (a.mode == ATT_APPEND && a.pkv) {   // a prefill's prompt K/V, unrounded
+          const PromptKV P = *a.pkv;
+          const int r = pos - P.p0;
+          if (r < 0 || r >= P.cap) {
+            if (lane == 0) raise_err(kc, ERR_BAD_POS, pos);
+          } else {
+            float *dstf = (warp == 2 ? P.k : P.v) + (((size_t)a.layer * a.n_kv + g) * P.cap + r) * HD;
+#pragma unroll
+            for (int i = 0; i < 4; i++) __stcg(dstf + lane + 32 * i, v[i]);
+          }
+        }
       }
     }
     __syncthreads();
@@ -2873,6 +2903,156 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
   if (a.dyn && threadIdx.x == 0) kc.att_base += (unsigned)n_items + gridDim.x;
 }
 
+// ATT_ATTEND (a prefill's attention): program slot b is one prompt token at
+// position pos_ptr[b] of one sequence (slot b's page-table row holds that
+// sequence's pages); it attends to positions 0 .. pos.  Positions before the
+// prompt come from the bf16 pages, prompt positions from the f32 prompt
+// buffer (a.pkv), as in the reference's prefill, which attends to its
+// prompt's unrounded K/V (qwen_tts_talker.c:904-914, qwen_causal_attention at
+// qwen_tts_kernels.c:3454).  One item per (slot, KV head), CTA + k * grid.
+// Tiles of 16 positions go to the warp pairs in turn (pair pw: tiles pw,
+// pw + 4, ...); the pair stages a tile's K and V in f32 in shared memory
+// (two page buffers of its own), then each warp of the pair runs the online
+// softmax of one query head over it, as the decode loop does per page; the
+// per-warp states combine in warp order.  The result does not depend on the
+// CTA that ran the item.
+__device__ __noinline__ void attn_prefill_stage(const AttnArgs &a, int B, char *smem_base, KCtx &kc) {
+  char *smem = smem_base + SM_X_OFF;
+  AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  if (!a.pkv || !a.pos_ptr || a.nbuf < NWARPS) {
+    if (tid == 0) raise_err(kc, ERR_BAD_STAGE, 3000 + a.nbuf);
+    return;
+  }
+  const PromptKV P = *a.pkv;
+  const int h = warp & 1, pw = warp >> 1;
+  const int t = lane & 15, half = lane >> 4;
+  float *kt = reinterpret_cast<float *>(att_buf(smem_base, 2 * pw));       // [PAGE][HD]
+  float *vt = reinterpret_cast<float *>(att_buf(smem_base, 2 * pw + 1));   // [PAGE][HD]
+  float *s_acc = reinterpret_cast<float *>(smem + ATT_COMB_OFF);            // [NWARPS][HD]
+  float *s_ml = s_acc + NWARPS * HD;                                         // [NWARPS][2]
+  const int n_items = B * a.n_kv;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const int b = item / a.n_kv, g = item - b * a.n_kv;
+    const int pos = __ldcg(a.pos_ptr + b);
+    if (pos < 0 || pos >= a.rope_len || pos >= a.pt_stride * PAGE || pos < P.p0 || pos - P.p0 >= P.cap) {
+      if (tid == 0) raise_err(kc, ERR_BAD_POS, pos);
+      return;
+    }
+    const int *pt = a.page_table + (size_t)b * a.pt_stride;
+    if (warp < 2) {
+      float v[4];
+      attn_row(a, b, g, warp, pos, lane, v);
+#pragma unroll
+      for (int i = 0; i < 4; i++) sm->q[warp][lane + 32 * i] = v[i];
+    }
+    __syncthreads();
+    const int n = pos / PAGE + 1;
+    const float *kf = P.k + ((size_t)a.layer * a.n_kv + g) * P.cap * HD;
+    const float *vf = P.v + ((size_t)a.layer * a.n_kv + g) * P.cap * HD;
+    float m_w = -INFINITY, l_w = 0.f, acc4[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = pw; i < n; i += NWARPS / 2) {
+      // stage tile i: warp h of the pair takes rows h, h + 2, ..., lane the
+      // 4 dims 4 lane .. 4 lane + 3; rows past pos are zeros
+      float4 rk[PAGE / 2], rv[PAGE / 2];
+      int page = 0;
+      if (i * PAGE < P.p0) {
+        page = __ldg(pt + i);
+        if (page < 0 || page >= a.n_pages) {
+          if (lane == 0) raise_err(kc, ERR_BAD_PAGE, page);
+          page = 0;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < PAGE / 2; k++) {
+        const int r = 2 * k + h, j = i * PAGE + r;
+        rk[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        rv[k] = rk[k];
+        if (j <= pos) {
+          if (j >= P.p0) {
+            const size_t off = (size_t)(j - P.p0) * HD + 4 * lane;
+            rk[k] = __ldcg(reinterpret_cast<const float4 *>(kf + off));
+            rv[k] = __ldcg(reinterpret_cast<const float4 *>(vf + off));
+          } else {
+            const size_t off = (((size_t)page * a.n_kv + g) * PAGE + r) * HD + 4 * lane;
+            const uint2 kb = __ldcg(reinterpret_cast<const uint2 *>(a.kpool + off));
+            const uint2 vb = __ldcg(reinterpret_cast<const uint2 *>(a.vpool + off));
+            rk[k] = make_float4(bf16lo(kb.x), bf16hi(kb.x), bf16lo(kb.y), bf16hi(kb.y));
+            rv[k] = make_float4(bf16lo(vb.x), bf16hi(vb.x), bf16lo(vb.y), bf16hi(vb.y));
+          }
+        }
+      }
+      bar_sync_n(1 + pw, 64);   // the pair is done with the previous tile
+#pragma unroll
+      for (int k = 0; k < PAGE / 2; k++) {
+        const int r = 2 * k + h;
+        *reinterpret_cast<float4 *>(kt + r * HD + 4 * lane) = rk[k];
+        *reinterpret_cast<float4 *>(vt + r * HD + 4 * lane) = rv[k];
+      }
+      bar_sync_n(1 + pw, 64);
+      // score of token t: lanes t and t + 16 each take half of the dims, in
+      // 16-byte groups from a token-dependent start (distinct banks per
+      // 8-lane phase)
+      const float *qh = sm->q[h] + half * 64;
+      const float *kr = kt + t * HD + half * 64;
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 16; jj++) {
+        const int jq = (jj + t) & 15;
+        const float4 kk = *reinterpret_cast<const float4 *>(kr + 4 * jq);
+        const float4 qq = *reinterpret_cast<const float4 *>(qh + 4 * jq);
+        s0 = fmaf(qq.x, kk.x, s0);
+        s1 = fmaf(qq.y, kk.y, s1);
+        s2 = fmaf(qq.z, kk.z, s2);
+        s3 = fmaf(qq.w, kk.w, s3);
+      }
+      float sdot = (s0 + s1) + (s2 + s3);
+      sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+      const bool live = i * PAGE + t <= pos;
+      const float sc = live ? sdot * a.scale : -INFINITY;
+      float mx = sc;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float m_new = fmaxf(m_w, mx);   // finite: position i * PAGE <= pos
+      const float pr = live ? expf(sc - m_new) : 0.f;
+      const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
+      l_w = l_w * corr + pr;
+      m_w = m_new;
+#pragma unroll
+      for (int e = 0; e < 4; e++) acc4[e] *= corr;
+#pragma unroll
+      for (int tt = 0; tt < PAGE; tt++) {
+        const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+        const float4 vv = *reinterpret_cast<const float4 *>(vt + tt * HD + 4 * lane);
+        acc4[0] = fmaf(p_t, vv.x, acc4[0]);
+        acc4[1] = fmaf(p_t, vv.y, acc4[1]);
+        acc4[2] = fmaf(p_t, vv.z, acc4[2]);
+        acc4[3] = fmaf(p_t, vv.w, acc4[3]);
+      }
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) l_w += __shfl_xor_sync(0xffffffffu, l_w, o);
+    *reinterpret_cast<float4 *>(s_acc + warp * HD + 4 * lane) = make_float4(acc4[0], acc4[1], acc4[2], acc4[3]);
+    if (lane == 0) { s_ml[2 * warp] = m_w; s_ml[2 * warp + 1] = l_w; }
+    if (__syncthreads_or(kc.local_err)) return;
+    const int hh = tid >> 7, d = tid & 127;
+    float Mh = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < NWARPS / 2; q++) Mh = fmaxf(Mh, s_ml[2 * (2 * q + hh)]);
+    float Lh = 0.f, acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < NWARPS / 2; q++) {
+      const int w = 2 * q + hh;
+      const float mw = s_ml[2 * w];
+      const float e = (mw == -INFINITY) ? 0.f : expf(mw - Mh);
+      Lh += s_ml[2 * w + 1] * e;
+      acc += s_acc[w * HD + d] * e;
+    }
+    __stcg(a.out + (size_t)b * a.ld_out + (2 * g + hh) * HD + d, acc * (1.0f / Lh));
+    __syncthreads();   // q, the tiles and the states are rewritten by the next item
+  }
+}
+
 // ============================================================ misc stages ==
 __device__ __noinline__ void embed_stage(const EmbedArgs &e, int B, KCtx &kc) {
   const int total = B * e.dim;
@@ -2964,7 +3144,7 @@ QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
           // every lane tests the descriptor's barrier itself (that makes the
           // bulk-copied descriptor visible to it)
           const bool landed = __all_sync(0xffffffffu, mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u));
-          if (landed && kc.dring[slot].kind == ST_ATTN && kc.dring[slot].a.mode != ATT_APPEND)
+          if (landed && kc.dring[slot].kind == ST_ATTN && kc.dring[slot].a.mode == ATT_DECODE)
             attn_prefetch(kc.dring[slot].a, kc.dring[slot].B, kc, smem);
           __syncwarp();
           phase = 1;
@@ -3094,7 +3274,10 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
       const int B = st->B;
       switch (st->kind) {
         case ST_GEMV: gemv_stage(st->g, B, smem, kc); break;
-        case ST_ATTN: attn_stage(st->a, B, smem, kc); break;
+        case ST_ATTN:
+          if (st->a.mode == ATT_ATTEND) attn_prefill_stage(st->a, B, smem, kc);
+          else attn_stage(st->a, B, smem, kc);
+          break;
         case ST_EMBED: embed_stage(st->e, B, kc); break;
         case ST_NORM: norm_stage(st->n, B); break;
         case ST_POS_INC:

@@ -2,8 +2,8 @@
 capturing one `decode_kernel` launch under a profiler.
 
     python qwen3-tts_b200/profile_frame.py [--config c2] [--frames 3] [--pos 64]
-    python qwen3-tts_b200/profile_frame.py --stage gemv [--rows 1024 --cols 2048 --batch 64]
-    python qwen3-tts_b200/profile_frame.py --stage attn [--batch 64]
+    python qwen3-tts_b200/profile_frame.py --stage gemv [--rows 1024 --cols 2048 --batch 64 --fmt bf16]
+    python qwen3-tts_b200/profile_frame.py --stage attn [--batch 64] [--pos P]
 
 Builds the same synthetic engine as bench.py (seeded random weights of the
 config's shapes), places the session at context position --pos (KV contents
@@ -12,9 +12,10 @@ and runs --frames launches of one frame each.  Launch 0 is the cold first
 launch; capture launch 1 (`ncu -k regex:decode_kernel -s 1 -c 1 ...`).
 
 --stage runs one stage kind alone, three launches of one stage each (capture
-launch 2): a BF16 GEMV stage of the given shape and batch, or a paged decode
-attention stage (16 query / 8 KV heads) of --batch slots at context lengths
-drawn from U[128, 2048), the config-4 mix.
+launch 2): a GEMV stage (bf16 or int8) of the given shape and batch, or a
+paged decode attention stage with its K/V append (16 query / 8 KV heads) of
+--batch slots at context lengths drawn from U[128, 2048), the config-4 mix, or
+all at position --pos.
 """
 import argparse
 import os
@@ -33,15 +34,16 @@ def one_stage(args):
     if args.stage == "gemv":
         rows, K, B = args.rows, args.cols, args.batch
         W = Q.bf16_from_f32(rng.standard_normal((rows, K), dtype=np.float32) * np.float32(0.02))
-        q = Q.quantize(W, Q.FMT_BF16)
+        fmt = Q.FMT_NAMES[args.fmt]
+        q = Q.quantize(W, fmt)
         x = rng.standard_normal((B, K), dtype=np.float32)
         for _ in range(3):
-            y = Q.gemv(Q.FMT_BF16, q, rows, K, x)
+            y = Q.gemv(fmt, q, rows, K, x)
         ref = Q.f32_from_bf16(W).astype(np.float64) @ x.T.astype(np.float64)
         print("gemv", y.shape, "rel err %.2e" % (np.linalg.norm(y - ref.T) / np.linalg.norm(ref)))
         return
     B = args.batch
-    pos = rng.integers(128, 2048, B)
+    pos = np.full(B, args.pos) if args.pos_given else rng.integers(128, 2048, B)
     nkv, nh, hd = 8, 16, 128
     pt_stride = int(max(pos)) // 16 + 2
     n_pages = int(sum(p // 16 + 1 for p in pos)) + 4
@@ -71,7 +73,9 @@ def main():
     ap.add_argument("--rows", type=int, default=1024)
     ap.add_argument("--cols", type=int, default=2048)
     ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--fmt", default="bf16", choices=["bf16", "int8"])
     args = ap.parse_args()
+    args.pos_given = "--pos" in sys.argv
     if args.stage:
         one_stage(args)
         return

@@ -47,7 +47,8 @@ class EngineDesc(C.Structure):
     _fields_ = [("talker", StackDesc), ("codec_head", _vp), ("codec_embedding", _vp), ("codec_vocab", C.c_int),
                 ("codebook", C.c_int), ("has_cp", C.c_int), ("cp", StackDesc), ("cp_norm", _vp),
                 ("cp_lm_head", Matrix * 15), ("cp_codec_emb", _vp * 15), ("cp_emb_dim", C.c_int),
-                ("cp_mtp_proj", Matrix), ("cp_mtp_fmt", C.c_int), ("cp_mtp_bias", _vp)]
+                ("cp_mtp_proj", Matrix), ("cp_mtp_fmt", C.c_int), ("cp_mtp_bias", _vp),
+                ("talker_prefill_layers", C.POINTER(Layer))]
 
 
 _lib = None
@@ -268,7 +269,9 @@ class Engine:
     """Weights of the talker (+ code predictor) resident on one device."""
 
     def __init__(self, model: HostModel, talker_fmt: int = FMT_BF16, cp_fmt: int | None = None, device: int = 0,
-                 rope=None, cp_rope=None, quantized=None):
+                 rope=None, cp_rope=None, quantized=None, prefill_bf16=True):
+        """prefill_bf16: with a quantized talker, also keep its bf16 weights for
+        qtb_prefill, as the reference prefills from bf16 in every mode."""
         L = lib()
         cfg = model.cfg
         self.cfg = cfg
@@ -302,6 +305,10 @@ class Engine:
             d.talker = stack_desc(model.talker, "t", cfg.hidden, len(model.talker.layers), cfg.heads, cfg.kv_heads,
                                   cfg.head_dim, cfg.inter, talker_fmt, rope, cfg.theta)
             d.codec_head = ptr(model.codec_head)
+            if prefill_bf16 and talker_fmt != FMT_BF16:
+                pf = stack_desc(model.talker, "pf", cfg.hidden, len(model.talker.layers), cfg.heads, cfg.kv_heads,
+                                cfg.head_dim, cfg.inter, FMT_BF16, rope, cfg.theta)
+                d.talker_prefill_layers = pf.layers
         d.codec_embedding = ptr(model.codec_embedding)
         self._keep += [model.codec_head, model.codec_embedding]
         d.codec_vocab = cfg.codec_vocab

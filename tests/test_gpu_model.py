@@ -173,24 +173,29 @@ def test_large_batch_matches_single_sessions(have_gpu, tiny):
 
 @pytest.mark.parametrize("fmt", ["bf16", "int8"])
 def test_prefill_matches_reference_prefill(have_gpu, tiny, fmt):
-    """Device prefill (qtb_prefill, 40 tokens in one 64-row chunk) against
-    the reference's own CPU prefill (qwen_talker_prefill): last-token residual
-    and the KV cache; then a 100-token prefill (two chunks) continuing from a
-    10-token prefix against single decode steps on the device."""
+    """Device prefill (qtb_prefill) against the reference's own CPU prefill
+    (qwen_talker_prefill), whose prompt tokens attend to the prompt's f32 K/V:
+    40 tokens (one 64-row chunk) and 100 tokens (two chunks, the second
+    attending to the first's f32 K/V), last-token residual and the KV cache.
+    Then a 100-token prefill continuing from a 10-token prefix of decode steps
+    against 110 decode steps (the steps attend to the bf16 cache, the prefill
+    to its prompt's f32 K/V: they differ by that rounding), and decoding
+    continues from the prefilled cache."""
     cfg, m, path = tiny
     ref = refbind.RefModel(path, cfg, use_int8=(fmt == "int8"), threads=8, cp=False)
     eng = engine_from_ref(ref, m, cfg, fmt, with_cp=False)
     rng = np.random.default_rng(31)
-    E = (0.1 * rng.standard_normal((40, cfg.hidden))).astype(np.float32)
-    dx_ref = ref.talker_prefill(E)
-    ses = Q.Session(eng, 2, 256)
-    h, dx = ses.prefill(1, E, 0)
-    assert rel_l2(dx, dx_ref) < 1e-3, rel_l2(dx, dx_ref)
-    assert list(ses.get_pos()) == [0, 40]
-    kg, vg = ses.download_kv(1, cfg.layers, cfg.kv_heads * 128, 40)
-    for l in range(cfg.layers):
-        k, v = ref.kv(l, 40)
-        assert kv_close(kg[l], k, 0.85) and kv_close(vg[l], v, 0.85), l
+    for n in (40, 100):
+        E = (0.1 * rng.standard_normal((n, cfg.hidden))).astype(np.float32)
+        dx_ref = ref.talker_prefill(E)
+        ses = Q.Session(eng, 2, 256)
+        h, dx = ses.prefill(1, E, 0)
+        assert rel_l2(dx, dx_ref) < 1e-3, (n, rel_l2(dx, dx_ref))
+        assert list(ses.get_pos()) == [0, n]
+        kg, vg = ses.download_kv(1, cfg.layers, cfg.kv_heads * 128, n)
+        for l in range(cfg.layers):
+            k, v = ref.kv(l, n)
+            assert kv_close(kg[l], k, 0.85) and kv_close(vg[l], v, 0.85), (n, l)
     ref.close()
     # prefix of 10 single steps, then 100 tokens by prefill, against 110 steps
     E2 = (0.1 * rng.standard_normal((110, cfg.hidden))).astype(np.float32)
@@ -201,14 +206,18 @@ def test_prefill_matches_reference_prefill(have_gpu, tiny, fmt):
     for p in range(10):
         bb.talker_step(E2[p], p)
     hp, _ = bb.prefill(0, E2[10:], 10)
-    assert rel_l2(hp, hs[0]) < 1e-3, rel_l2(hp, hs[0])
+    assert rel_l2(hp, hs[0]) < 2e-2, rel_l2(hp, hs[0])
     ka, va = a.download_kv(0, cfg.layers, cfg.kv_heads * 128, 110)
     kb, vb = bb.download_kv(0, cfg.layers, cfg.kv_heads * 128, 110)
-    for l in range(cfg.layers):
-        assert kv_close(kb[l], ka[l], 0.85) and kv_close(vb[l], va[l], 0.85), l
+    # layer 0's K/V depend on the embeddings alone; deeper layers carry the
+    # f32-vs-bf16 attention difference of the layers below
+    assert kv_close(kb[0], ka[0], 0.85) and kv_close(vb[0], va[0], 0.85)
+    f32 = lambda u: (u.astype(np.uint32) << 16).view(np.float32)
+    for l in range(1, cfg.layers):
+        assert rel_l2(f32(kb[l]), f32(ka[l])) < 2e-2 and rel_l2(f32(vb[l]), f32(va[l])) < 2e-2, l
     # and decoding continues from the prefilled cache
     e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
-    assert rel_l2(bb.talker_step(e, 110)[0], a.talker_step(e, 110)[0]) < 1e-3
+    assert rel_l2(bb.talker_step(e, 110)[0], a.talker_step(e, 110)[0]) < 2e-2
 
 
 def test_kv_upload_download_roundtrip(have_gpu, tiny):
