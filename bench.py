@@ -233,6 +233,11 @@ def run_b200(args, rank, world, local_rank):
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
+    # which schedule the timed program ran (qtb_session_program_grid: negative
+    # = one cluster of that many CTAs, the small-batch single-cluster schedule)
+    g = ses.program_grid(3)
+    out["config"]["schedule"] = (f"one cluster of {-g} CTAs (cluster barriers)" if g < 0
+                                 else f"{g} CTAs, grid barrier")
     return out
 
 

@@ -132,6 +132,13 @@ int64_t qtb_engine_cp_head_weight_bytes(const qtb_engine_t *e);
 int  qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n_pages, qtb_session_t **out);
 void qtb_session_destroy(qtb_session_t *s);
 int  qtb_session_batch(const qtb_session_t *s);
+/* CTAs a session's program launches with: which = 0 talker step, 1 CP pass,
+ * 2 CP frame, 3 whole frame, 4 prefill.  Negative: the program runs as one
+ * cluster of that many CTAs (the single-cluster schedule of small batches,
+ * opt-in with QTB_CL=1 in the environment at engine creation, used when the
+ * device can co-schedule the cluster and every stage of the program fits it).
+ * 0: no such program. */
+int  qtb_session_program_grid(const qtb_session_t *s, int which);
 int  qtb_session_n_pages(const qtb_session_t *s);
 
 int  qtb_session_max_ctx(const qtb_session_t *s);

@@ -46,6 +46,21 @@ static void cluster_launch_config(cudaLaunchConfig_t &cfg, cudaLaunchAttribute (
   cfg.numAttrs = 2;
 }
 
+// One cluster of CL_G CTAs (the single-cluster schedule of small batches):
+// the cluster is co-scheduled as a whole, so no cooperative attribute.
+static void cl_launch_config(cudaLaunchConfig_t &cfg, cudaLaunchAttribute (&at)[2], cudaStream_t st) {
+  cfg.gridDim = dim3(CL_G);
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CL_G;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+}
+
 static int set_err(int code, const char *fmt, ...) {
   char buf[512];
   va_list ap;
@@ -440,6 +455,7 @@ struct qtb_engine {
   int device = 0;
   int n_sm = 0;
   int pairs = 0;   // launches run in 2-CTA clusters (K-split of small-tile int8 stages)
+  int cl = 0;      // small-batch programs may run as one cluster of CL_G CTAs
   Arena ar;
   DStack talker, cp;
   int has_talker = 0, has_cp = 0;
@@ -583,6 +599,23 @@ extern "C" int qtb_engine_create(const qtb_engine_desc_t *d, int device, qtb_eng
       e->pairs = 1;
     cudaGetLastError();
   }
+  {
+    // the single-cluster schedule, opt-in (QTB_CL=1): one cluster of CL_G
+    // CTAs must fit.  Measured on B200 it is slower than the whole-GPU
+    // schedule at batch 1 (c2 6.7 vs 4.7 ms per frame): 16 SMs stream the
+    // weights at ~50 GB/s each, and the staging and epilogue latency per
+    // stage stays, so the cheaper cluster barrier does not pay for it.
+    const char *cv = getenv("QTB_CL");
+    if (cv && cv[0] == '1' && e->n_sm >= CL_G &&
+        cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute at[2];
+      cl_launch_config(cfg, at, nullptr);
+      int ncl = 0;
+      if (cudaOccupancyMaxActiveClusters(&ncl, (const void *)decode_kernel, &cfg) == cudaSuccess && ncl >= 1) e->cl = 1;
+    }
+    cudaGetLastError();
+  }
   int rc = 0;
   if ((rc = qk_rsq_table(&e->rsq_tab))) goto fail;
   e->has_talker = d->talker.n_layers > 0;
@@ -724,6 +757,8 @@ struct qtb_session {
   unsigned *tc_sem[PROG_N] = {};   // per-tile counters of the split tcgen05 stages
   int tc_sem_n[PROG_N] = {};
   int prog_n[PROG_N] = {};
+  int prog_G[PROG_N] = {};    // CTAs of each program's launch
+  int prog_cl[PROG_N] = {};   // ... launched as one cluster (single-cluster schedule)
   int has_pad = 0;
   long long *trace = nullptr;   // per-stage clock64 trace (CTA 0), profiling only
   int trace_n = 0, trace_on = 0;
@@ -788,6 +823,20 @@ static bool v2_ok(int fmt, int rows, int K, int B, int G) {
   return 256 + (size_t)nt_max * (NWARPS + 1) * 16 * B * 4 <= (size_t)(SM_PAIR_OFF - SM_R_OFF);
 }
 
+// A small-batch GEMV stage on the single-cluster schedule: the activation
+// staging of the small-batch path fits, and every CTA's unit results (and the
+// slice sums of split tiles) fit the reduction region.
+static bool cl_ok(int fmt, int rows, int K, int B) {
+  if (!v2_ok(fmt, rows, K, B, 1 << 20)) return false;   // staging only (tile count checked below)
+  if (rows % 16) return false;
+  for (int c = 0; c < CL_G; c++) {
+    const V2Plan p = cl_plan(fmt, rows, K, c, CL_G);
+    const size_t units = (size_t)p.nt * p.kb, vals = (p.kb > 1) ? (size_t)p.nt : 0;
+    if (256 + (units + vals) * 16 * B * 4 > (size_t)(SM_PAIR_OFF - SM_R_OFF)) return false;
+  }
+  return true;
+}
+
 // tcgen05 stage shape: slices of kcn K chunks (S of them) x row groups R of
 // 128-row tiles over the G CTAs, minimising the weight chunks the busiest CTA
 // streams plus the split-K fix-up.  The staged activation slice must fit
@@ -838,7 +887,10 @@ struct ProgBuilder {
   qtb_session *s;
   std::vector<Stage> st;
   int err = 0;
-  int W() const { return s->e->n_sm * NWARPS; }
+  int cl = 0;         // single-cluster schedule (CL_G CTAs in one cluster)
+  int cl_fail = 0;    // a stage this schedule cannot run was asked for
+  int grid() const { return cl ? CL_G : s->e->n_sm; }
+  int W() const { return grid() * NWARPS; }
 
   void gemv(const DMat &m, int B, const float *x, int ldx, const float *norm_w, float eps, float *y, int ldy,
             int epi, int evict_last, const float *bias = nullptr) {
@@ -849,9 +901,13 @@ struct ProgBuilder {
     GemvArgs &g = S.g;
     g.w = m.w; g.row_scale = m.row_scale; g.gsz = m.gsz; g.bias = bias;
     g.fmt = m.fmt; g.rows = m.rows; g.K = m.K;
-    g.v2 = v2_ok(m.fmt, m.rows, m.K, B, s->e->n_sm) ? 1 : 0;
+    g.v2 = v2_ok(m.fmt, m.rows, m.K, B, grid()) ? 1 : 0;
+    if (cl) {
+      if (cl_ok(m.fmt, m.rows, m.K, B)) g.v2 = g.cl = 1;
+      else cl_fail = 1;
+    }
     if (!g.v2 && tc_ok(m, B, m.fmt)) {
-      const TcShape sh = tc_choose(m.fmt, m.rows, m.K, B, s->e->n_sm);
+      const TcShape sh = tc_choose(m.fmt, m.rows, m.K, B, grid());
       g.tc = 1;
       g.wtc = m.wtc;
       g.S = sh.S;
@@ -862,7 +918,7 @@ struct ProgBuilder {
       g.ws = s->ws; g.sem = s->sem;
       g.amax_ws = s->amax_ws; g.amax_sem = s->amax_sem;
       if (sh.S < 1) { err = set_err(QTB_E_UNSUPPORTED, "no tcgen05 shape for %dx%d at B=%d", m.rows, m.K, B); return; }
-      if (tc_ws_floats(m.fmt, m.rows, m.K, B, s->e->n_sm) > s->ws_floats) { err = set_err(QTB_E_INVALID, "split-K workspace too small"); return; }
+      if (tc_ws_floats(m.fmt, m.rows, m.K, B, grid()) > s->ws_floats) { err = set_err(QTB_E_INVALID, "split-K workspace too small"); return; }
       st.push_back(S);
       return;
     }
@@ -875,7 +931,7 @@ struct ProgBuilder {
     g.y = y; g.ldy = ldy; g.epi = epi;
     g.ws = s->ws; g.sem = s->sem;
     g.amax_ws = s->amax_ws; g.amax_sem = s->amax_sem;
-    const size_t need = (size_t)(m.rows / 16) * (g.v2 ? std::max(1, s->e->n_sm / std::max(1, m.rows / 16)) : g.S) * 16 * B;
+    const size_t need = (size_t)(m.rows / 16) * (g.v2 ? std::max(1, grid() / std::max(1, m.rows / 16)) : g.S) * 16 * B;
     if (need > s->ws_floats) { err = set_err(QTB_E_INVALID, "split-K workspace too small"); return; }
     if (m.rows / 16 > s->sem_n) { err = set_err(QTB_E_INVALID, "semaphore array too small"); return; }
     st.push_back(S);
@@ -915,7 +971,8 @@ struct ProgBuilder {
       a.max_splits = 1; a.min_pps = 1 << 20;
       a.pkv = s->pkv; a.layer = layer;
     }
-    attn_schedule(a, B, s->e->n_sm);
+    if (cl) a.max_splits = std::max(1, std::min(a.max_splits, grid() / std::max(1, B * k.n_kv)));
+    attn_schedule(a, B, grid());
     if (mode == ATT_ATTEND) a.dyn = 0;   // static item order (attn_prefill_stage)
     st.push_back(S);
   }
@@ -1017,7 +1074,10 @@ static void make_plans(const std::vector<Stage> &st, int G, bool pairs, std::vec
     if (st[i].kind == ST_GEMV && st[i].g.tc)
       for (int c = 0; c < G; c++) out[i * G + c] = tc_plan(st[i].g, st[i].B, c, G);
   for (size_t i = 0; i < st.size(); i++)
-    if (st[i].kind == ST_GEMV && st[i].g.v2)
+    if (st[i].kind == ST_GEMV && st[i].g.cl)
+      for (int c = 0; c < G; c++) out[i * G + c] = cl_plan(st[i].g.fmt, st[i].g.rows, st[i].g.K, c, G);
+  for (size_t i = 0; i < st.size(); i++)
+    if (st[i].kind == ST_GEMV && st[i].g.v2 && !st[i].g.cl)
       for (int c = 0; c < G; c++)
         out[i * G + c] = v2_plan(st[i].g.fmt, st[i].g.rows, st[i].g.K, st[i].g.norm_w != nullptr, st[i].g.epi, c, G,
                                  pairs);
@@ -1050,12 +1110,14 @@ static int upload_prog(qtb_session *s, int which, ProgBuilder &pb) {
   int rc = s->ar.upload(&d, pb.st.data(), pb.st.size() * sizeof(Stage));
   if (rc) return rc;
   std::vector<V2Plan> pl;
-  make_plans(pb.st, s->e->n_sm, s->e->pairs != 0, pl);
+  make_plans(pb.st, pb.grid(), s->e->pairs != 0 && !pb.cl, pl);
   V2Plan *dp;
   if ((rc = s->ar.upload(&dp, pl.data(), pl.size() * sizeof(V2Plan)))) return rc;
   s->prog[which] = d;
   s->plan[which] = dp;
   s->prog_n[which] = (int)pb.st.size();
+  s->prog_G[which] = pb.grid();
+  s->prog_cl[which] = pb.cl;
   return 0;
 }
 
@@ -1063,12 +1125,26 @@ static int build_programs(qtb_session *s) {
   qtb_engine *e = s->e;
   const int B = s->B;
   int rc;
+  // a small-batch program runs on the single-cluster schedule when every one
+  // of its stages can; otherwise (and for large batches) on the whole GPU
+  auto make = [&](int which, const std::function<void(ProgBuilder &)> &fill) -> int {
+    if (e->cl && B <= 4) {
+      ProgBuilder pb{s};
+      pb.cl = 1;
+      fill(pb);
+      if (!pb.err && !pb.cl_fail) return upload_prog(s, which, pb);
+    }
+    ProgBuilder pb{s};
+    fill(pb);
+    return upload_prog(s, which, pb);
+  };
   if (e->has_talker) {
     const DStack &k = e->talker;
-    ProgBuilder pb{s};
-    pb.layers(k, s->tk, B, s->pos, 0, s->tk_layer_elems, 0);
-    pb.norm(s->tk.x, k.hidden, k.final_norm, s->tk.hidden, k.hidden, k.hidden, k.eps, B);
-    if ((rc = upload_prog(s, PROG_TALKER, pb))) return rc;
+    rc = make(PROG_TALKER, [&](ProgBuilder &pb) {
+      pb.layers(k, s->tk, B, s->pos, 0, s->tk_layer_elems, 0);
+      pb.norm(s->tk.x, k.hidden, k.final_norm, s->tk.hidden, k.hidden, k.hidden, k.eps, B);
+    });
+    if (rc) return rc;
     if (s->pf.x) {
       ProgBuilder pp{s};
       const DStack &kp = e->has_talker_pf ? e->talker_pf : k;
@@ -1079,30 +1155,31 @@ static int build_programs(qtb_session *s) {
   }
   if (e->has_cp) {
     const DStack &k = e->cp;
-    ProgBuilder pb{s};
-    pb.layers(k, s->cp, B, s->cp_pos, 0, s->cp_layer_elems, 1);
-    if ((rc = upload_prog(s, PROG_CP_PASS, pb))) return rc;
-    ProgBuilder pf{s};
-    build_cp_frame(pf, s, s->cp_in);
-    if ((rc = upload_prog(s, PROG_CP_FRAME, pf))) return rc;
+    rc = make(PROG_CP_PASS, [&](ProgBuilder &pb) { pb.layers(k, s->cp, B, s->cp_pos, 0, s->cp_layer_elems, 1); });
+    if (rc) return rc;
+    rc = make(PROG_CP_FRAME, [&](ProgBuilder &pb) { build_cp_frame(pb, s, s->cp_in); });
+    if (rc) return rc;
   }
   if (e->has_talker && e->codec_head.w && e->codec_emb) {
     const DStack &k = e->talker;
-    ProgBuilder pb{s};
-    pb.layers(k, s->tk, B, s->pos, 0, s->tk_layer_elems, 0);
-    pb.norm(s->tk.x, k.hidden, k.final_norm, s->tk.hidden, k.hidden, k.hidden, k.eps, B);
-    // greedy code0 over the first `codebook` rows of the codec head
-    pb.argmax(e->codec_head, B, s->tk.x, k.hidden, k.final_norm, k.eps, s->codes, 16, nullptr, 0, 0, nullptr, 0, 0);
-    pb.st.back().g.gen = s->gen;
-    if (e->has_cp) build_cp_frame(pb, s, s->tk.hidden);
-    Stage &S = pb.embed(s->tk.x, k.hidden, k.hidden, B, nullptr, 0);
-    ProgBuilder::add_tab(S, e->codec_emb, k.hidden, e->codec_vocab, s->codes, 16);
-    if (e->has_cp)
-      for (int g = 0; g < 15; g++) ProgBuilder::add_tab(S, e->cp_emb[g], e->cp_emb_dim, e->codebook, s->codes + 1 + g, 16);
-    S.e.add = s->pad;
-    pb.pos_inc(s->pos, B);
-    pb.st.back().p.gen = s->gen;
-    if ((rc = upload_prog(s, PROG_FRAME, pb))) return rc;
+    rc = make(PROG_FRAME, [&](ProgBuilder &pb) {
+      pb.layers(k, s->tk, B, s->pos, 0, s->tk_layer_elems, 0);
+      pb.norm(s->tk.x, k.hidden, k.final_norm, s->tk.hidden, k.hidden, k.hidden, k.eps, B);
+      // greedy code0 over the first `codebook` rows of the codec head
+      pb.argmax(e->codec_head, B, s->tk.x, k.hidden, k.final_norm, k.eps, s->codes, 16, nullptr, 0, 0, nullptr, 0, 0);
+      if (pb.err) return;
+      pb.st.back().g.gen = s->gen;
+      if (e->has_cp) build_cp_frame(pb, s, s->tk.hidden);
+      if (pb.err) return;
+      Stage &S = pb.embed(s->tk.x, k.hidden, k.hidden, B, nullptr, 0);
+      ProgBuilder::add_tab(S, e->codec_emb, k.hidden, e->codec_vocab, s->codes, 16);
+      if (e->has_cp)
+        for (int g = 0; g < 15; g++) ProgBuilder::add_tab(S, e->cp_emb[g], e->cp_emb_dim, e->codebook, s->codes + 1 + g, 16);
+      S.e.add = s->pad;
+      pb.pos_inc(s->pos, B);
+      pb.st.back().p.gen = s->gen;
+    });
+    if (rc) return rc;
   }
   return 0;
 }
@@ -1314,6 +1391,10 @@ fail:
 }
 
 extern "C" int qtb_session_batch(const qtb_session_t *s) { return s ? s->B : 0; }
+extern "C" int qtb_session_program_grid(const qtb_session_t *s, int which) {
+  if (!s || which < 0 || which >= PROG_N || !s->prog[which]) return 0;
+  return s->prog_cl[which] ? -s->prog_G[which] : s->prog_G[which];
+}
 extern "C" int qtb_session_n_pages(const qtb_session_t *s) { return s ? s->tk.n_pages : 0; }
 extern "C" double qtb_session_last_ms(const qtb_session_t *s) { return s ? s->last_ms : 0.0; }
 extern "C" int qtb_session_last_launches(const qtb_session_t *s) { return s ? s->last_launches : 0; }
@@ -1362,7 +1443,9 @@ static int begin_call(qtb_session *s) {
 // Launch program `which` n_iters times as ONE cooperative persistent kernel.
 static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
   if (!s->prog[which]) return set_err(QTB_E_UNSUPPORTED, "program %d not available for this engine", which);
-  if ((long long)n_iters * s->prog_n[which] * s->e->n_sm > 0x3fffffffLL)
+  const int G = s->prog_G[which] ? s->prog_G[which] : s->e->n_sm;
+  int cl = s->prog_cl[which];
+  if ((long long)n_iters * s->prog_n[which] * G > 0x3fffffffLL)
     return set_err(QTB_E_INVALID, "too many iterations for one launch");
   CUDA_TRY(cudaMemsetAsync(&s->ctl->bar_count, 0, sizeof(unsigned), s->stream));
   CUDA_TRY(cudaMemsetAsync(&s->ctl->att_work, 0, sizeof(unsigned), s->stream));
@@ -1373,9 +1456,15 @@ static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
   int n_st = s->prog_n[which];
   Ctl *ctl = s->ctl;
   long long *trace = s->trace_on ? s->trace : nullptr;
-  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_iters, (void *)&ctl, (void *)&trace};
+  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_iters, (void *)&ctl, (void *)&trace,
+                  (void *)&cl};
   if (timed) CUDA_TRY(cudaEventRecord(s->ev0, s->stream));
-  if (s->e->pairs) {
+  if (cl) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[2];
+    cl_launch_config(cfg, at, s->stream);
+    CUDA_TRY(cudaLaunchKernelExC(&cfg, (const void *)decode_kernel, args));
+  } else if (s->e->pairs) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[2];
     cluster_launch_config(cfg, at, s->e->n_sm, s->stream);
@@ -1554,7 +1643,7 @@ extern "C" int qtb_session_reset_slot(qtb_session_t *s, int b, int32_t expected_
   if (!s || b < 0 || b >= s->B) return set_err(QTB_E_INVALID, "bad slot");
   if (!s->gen_on) return set_err(QTB_E_INVALID, "qtb_session_begin_generation first");
   CUDA_TRY(cudaSetDevice(s->e->device));
-  const int32_t z = 0, d = active ? 0 : 1, bs = expected_frames > 0 ? 2 * expected_frames : -1;
+  const int32_t z = 0, d = active ? 0 : 2, bs = expected_frames > 0 ? 2 * expected_frames : -1;
   CUDA_TRY(cudaMemcpy(s->gen_h.frame + b, &z, 4, cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemcpy(s->gen_h.done + b, &d, 4, cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemcpy(s->gen_h.boost_start + b, &bs, 4, cudaMemcpyHostToDevice));
@@ -1582,6 +1671,7 @@ extern "C" int qtb_session_get_done(qtb_session_t *s, int32_t *done) {
   if (!s || !done) return set_err(QTB_E_INVALID, "null argument");
   CUDA_TRY(cudaSetDevice(s->e->device));
   CUDA_TRY(cudaMemcpy(done, s->gen_h.done, (size_t)s->B * 4, cudaMemcpyDeviceToHost));
+  for (int b = 0; b < s->B; b++) done[b] = done[b] != 0;   // 1: EOS in the last frame, 2: stopped before
   return 0;
 }
 
@@ -1726,7 +1816,8 @@ static int run_single_stage(MiniRun &mr, const Stage &S) {
   const V2Plan *plan = dplan;
   int n_st = 1, n_it = 1;
   long long *trace = nullptr;
-  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
+  int cl0 = 0;
+  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace, (void *)&cl0};
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(nsm), dim3(NTHREADS), args, SMEM_BYTES, mr.st));
   CUDA_TRY(cudaStreamSynchronize(mr.st));
   Ctl h;
@@ -1991,7 +2082,8 @@ extern "C" int qtb_attention_noalloc(const float *qkv, int batch, int n_heads, i
   int n_st = 1, n_it = 1;
   long long *trace = nullptr;
   const V2Plan *plan = nullptr;   // an attention stage reads no GEMV plan
-  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
+  int cl0 = 0;
+  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace, (void *)&cl0};
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(nsm), dim3(NTHREADS), args, SMEM_BYTES, st));
   Ctl h;
   CUDA_TRY(cudaMemcpyAsync(&h, ctl, sizeof h, cudaMemcpyDeviceToHost, st));
@@ -2099,7 +2191,8 @@ int op_matmat(OpCtx *c, float *Y, const uint16_t *W, const float *X, int rows, i
   int n_st = 1, n_it = 1;
   long long *trace = nullptr;
   Ctl *ctl = c->ctl;
-  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace};
+  int cl0 = 0;
+  void *args[] = {(void *)&prog, (void *)&plan, (void *)&n_st, (void *)&n_it, (void *)&ctl, (void *)&trace, (void *)&cl0};
   CUDA_TRY(cudaLaunchCooperativeKernel((const void *)decode_kernel, dim3(c->nsm), dim3(NTHREADS), args, SMEM_BYTES, c->st));
   Ctl h;
   CUDA_TRY(cudaMemcpyAsync(&h, c->ctl, sizeof h, cudaMemcpyDeviceToHost, c->st));

@@ -82,6 +82,14 @@ constexpr int TC_ACC_COLS = 256;         // one 128 x N (N <= 256) 32-bit accumu
 constexpr int TC_TMEM_COLS = 2 * TC_ACC_COLS;   // two: a tile is read back while the next accumulates
 static_assert(TC_X_OFF + TC_X_BYTES + 1024 <= TC_SCR_OFF && TC_SCR_OFF + 4096 <= SMEM_BYTES, "tcgen05 stage smem map");
 
+// Single-cluster schedule for small batches: the launch is one cluster of
+// CL_G CTAs (cluster barriers instead of the grid barrier), and each warp
+// streams its own GEMV weight pieces through two slots of CL_SLOT_BYTES in the
+// weight-ring region, issuing the next stage's first pieces before the barrier.
+constexpr int CL_G = 16;
+constexpr int CL_SLOT_BYTES = NWSLOT * WSLOT_BYTES / (2 * NWARPS);
+static_assert(CL_SLOT_BYTES % 1024 == 0, "per-warp weight slots");
+
 enum StageKind { ST_GEMV = 1, ST_ATTN = 2, ST_EMBED = 3, ST_NORM = 4, ST_POS_INC = 5 };
 enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 enum Fmt { FMT_BF16 = 0, FMT_INT8 = 1, FMT_Q4_0 = 2, FMT_INT4G = 3 };
@@ -102,7 +110,7 @@ struct GenState {
   float rep_pen, rep_inv;    // repetition penalty and its reciprocal (as the reference's -ffast-math build uses)
   int *frame;                // [B] frames generated so far by the slot
   int *boost_start;          // [B] 2 x expected frames, or -1: no EOS boost
-  int *done;                 // [B] the slot has sampled EOS
+  int *done;                 // [B] 0 running, 1 sampled EOS in this frame, 2 stopped (parked)
   uint16_t *rep_count;       // [B][vocab] occurrences of each code0 so far
 };
 
@@ -117,6 +125,7 @@ struct GemvArgs {
   int evict_last;            // keep these weights in L2 (code-predictor)
   int v2;                    // small-batch path: whole activation staged, weights TMA-streamed
   int tc;                    // large-batch path on tcgen05 (bf16 / int8 weights, see gemv_tc_t)
+  int cl;                    // single-cluster schedule (gemv_cl_t): per-warp weight pieces
   const uint8_t *wtc;        // weights in 128-row x 128-byte swizzled tiles (tcgen05 operand layout)
   float *ss_ws;              // tcgen05 path: per-(row group, k-slice) activation sums of squares
   int sem_off;               // tcgen05 path: this stage's per-tile counters are sem[sem_off + tile]
@@ -252,6 +261,13 @@ struct KCtx {
   unsigned tc_done;     // ... whose bulk copy has been waited for
   unsigned tc_committed;// tile accumulators committed so far (the g-th uses buffer g & 1)
   unsigned tc_waited;   // ... and waited for
+  // single-cluster schedule (a launch of one cluster of CL_G CTAs, see gemv_cl_t)
+  int cl;               // this launch runs it: cluster barriers, per-warp weight pieces
+  uint64_t *clbars;     // [2 * NWARPS] mbarriers of the warps' two weight slots
+  unsigned cl_q[NWARPS];    // weight pieces each warp has consumed (lane 0 writes)
+  unsigned cl_iss[NWARPS];  // ... and issued
+  unsigned cl_pre[NWARPS];  // the stage whose first pieces were issued ahead (or ~0u)
+  int cl_err;           // set (over distributed shared memory) by any CTA that raised an error
 };
 
 // Profiling checkpoint (CTA 0, thread 0) when stage tracing is on.
@@ -278,8 +294,25 @@ QTB_DEV void raise_err(KCtx &kc, int code, int info) {
 // persistent kernel.  Bounded: the wait gives up (and raises
 // ERR_BARRIER_TIMEOUT) after WAIT_LIMIT_CYCLES, or as soon as any CTA has
 // raised an error, so a failing launch always returns.
+QTB_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+QTB_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
 QTB_DEV void grid_arrive(KCtx &kc) {
   __syncthreads();
+  if (kc.cl) {
+    // single-cluster launch: a CTA that raised an error tells every CTA of the
+    // cluster (tag = this barrier's number + 1) before it arrives, so all of
+    // them see it when this barrier completes and leave together
+    if (kc.local_err && threadIdx.x < (unsigned)gridDim.x) {
+      uint32_t r;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(&kc.cl_err)), "r"((uint32_t)threadIdx.x));
+      asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(r), "r"((int)kc.epoch + 1) : "memory");
+    }
+    if (threadIdx.x == 0) kc.last = 0;
+    __syncwarp();
+    cluster_arrive();
+    return;
+  }
   // acq_rel: this CTA's writes (ordered before by bar.sync) happen-before every
   // CTA that acquires the final count; the CTA whose increment completes the
   // count acquires all the others' writes through the same RMW and needs no poll
@@ -1079,6 +1112,7 @@ QTB_DEV void prefetch_gemv_operands(const GemvArgs &a, const V2Plan &p) {
 // the streamer state; __syncwarp orders it for the other lanes.
 QTB_CALL void stream(KCtx &kc, char *smem, unsigned done, unsigned limit) {
   const int lane = threadIdx.x & 31;
+  if (kc.cl) return;   // the single-cluster GEMV stages stream their own weights
   // A completed stage has no fills left to issue (each GEMV stage issues its
   // own before reading them), and its descriptor slot may already hold a later
   // stage: never look behind `done`.
@@ -1136,6 +1170,13 @@ QTB_CALL void drain(KCtx &kc, unsigned cur) {
   // commit completes after all of them) before the tensor memory is freed
   for (unsigned c = kc.tc_done; c != kc.tc_issued; c++) mbar_wait(kc.tcfull + c % TC_NSLOT, (c / TC_NSLOT) & 1u, LIM);
   for (unsigned g = kc.tc_waited; g != kc.tc_committed; g++) mbar_wait(kc.tcacc + (g & 1u), (g >> 1) & 1u, LIM);
+  // single-cluster GEMV stages: the last piece issued into each warp slot
+  // (a slot's copies complete in order; a wait skipped after an error does not
+  // count as landed)
+  if (kc.cl)
+    for (int w = 0; w < NWARPS; w++)
+      for (unsigned c = kc.cl_iss[w] >= 2u ? kc.cl_iss[w] - 2u : 0u; c < kc.cl_iss[w]; c++)
+        mbar_wait(kc.clbars + 2 * w + (c & 1u), (c >> 1) & 1u, LIM);
 }
 
 QTB_CALL void argmax_finish(const GemvArgs &a, int B, KCtx &kc);
@@ -1680,6 +1721,371 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
   ckpt(kc, 5);
 }
 
+// ====================================== GEMV stage, single-cluster schedule =
+//
+// Small batches (B <= 4) when the launch is one cluster of CL_G CTAs.  A CTA
+// owns whole 16-row tiles t0 .. t0 + nt - 1; with fewer tiles than warps each
+// tile's K is cut into ks slices (a power of two) so every warp has a unit
+// (tile, slice) of kc = nck / ks chunks; warp w takes units w, w + 8, ...
+// Each warp streams its own units' weights, in pieces of up to cl_pc chunks,
+// through its two slots of the weight-ring region (one piece computing while
+// the next is in flight), and issues the first two pieces of the next GEMV
+// stage before the cluster barrier, so the weight stream does not stop at
+// stage boundaries.  The activation is staged as in the other small-batch
+// stages; each unit's 16 rows go to shared memory and the CTA adds a tile's
+// slices in slice order (deterministic) before the common epilogue.
+//
+// Host plan (V2Plan): t0, nt, kb = ks, kc = chunks per unit, L = pieces per
+// unit, the rest zero.
+template <int FMT>
+QTB_HOST_DEV constexpr int cl_pc() { return CL_SLOT_BYTES / (512 + 8 * FmtTraits<FMT>::GSZ); }
+QTB_HOST_DEV int cl_pc_fmt(int fmt) {
+  return fmt == FMT_BF16 ? cl_pc<FMT_BF16>() : fmt == FMT_INT8 ? cl_pc<FMT_INT8>()
+       : fmt == FMT_Q4_0 ? cl_pc<FMT_Q4_0>() : cl_pc<FMT_INT4G>();
+}
+
+QTB_HOST_DEV V2Plan cl_plan(int fmt, int rows, int K, int cta, int G) {
+  const int ck = fmt == FMT_BF16 ? 1 : (fmt == FMT_INT8 ? 2 : 4);
+  const int T = rows >> 4, nck = K / (16 * ck);
+  V2Plan p;
+  p.t0 = (int)((long long)cta * T / G);
+  p.nt = (int)((long long)(cta + 1) * T / G) - p.t0;
+  int ks = 1;
+  while (p.nt > 0 && 2 * ks * p.nt <= NWARPS && nck % (2 * ks) == 0 && nck / (2 * ks) >= 4) ks *= 2;
+  p.kb = ks;
+  p.kc = nck / ks;
+  const int pc = cl_pc_fmt(fmt);
+  p.L = (p.kc + pc - 1) / pc;
+  p.nfill = 0;
+  p.pair = 0;
+  p.pad = 0;
+  return p;
+}
+
+struct ClPiece { int tl, s, c0, n; };   // local tile, slice, first chunk in the tile, chunks
+
+QTB_DEV int cl_npieces(const V2Plan &p, int w) {
+  const int units = p.nt * p.kb;
+  return w < units ? ((units - 1 - w) / NWARPS + 1) * p.L : 0;
+}
+QTB_DEV ClPiece cl_piece(const V2Plan &p, int pc, int w, int q) {
+  const int j = q / p.L, pp = q - j * p.L, u = w + NWARPS * j;
+  ClPiece r;
+  r.tl = u / p.kb;
+  r.s = u - r.tl * p.kb;
+  r.c0 = r.s * p.kc + pp * pc;
+  r.n = min(pc, p.kc - pp * pc);
+  return r;
+}
+
+// Lane 0 of warp w: bulk-copy piece q of the warp's units of stage (a, p)
+// into the warp's next slot.
+template <int FMT>
+QTB_DEV void cl_issue(const GemvArgs &a, const V2Plan &p, int w, int q, KCtx &kc, char *smem) {
+  using Tr = FmtTraits<FMT>;
+  constexpr int PC = cl_pc<FMT>();
+  const ClPiece pc = cl_piece(p, PC, w, q);
+  const size_t base = (size_t)(p.t0 + pc.tl) * (p.kb * p.kc) + pc.c0;
+  const unsigned k = kc.cl_iss[w];
+  char *dst = smem + SM_W_OFF + (2 * w + (int)(k & 1u)) * CL_SLOT_BYTES;
+  uint64_t *bar = kc.clbars + 2 * w + (k & 1u);
+  const uint32_t wb = (uint32_t)pc.n * 512u, gb = (uint32_t)pc.n * 8u * Tr::GSZ;
+  const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
+  fence_proxy_async_smem();   // the slot was last read through the generic proxy
+  mbar_arrive_expect_tx(bar, wb + gb);
+  bulk_g2s_hint(dst, a.w + base * 512, wb, bar, pol);
+  if (Tr::GSZ) bulk_g2s_hint(dst + PC * 512, a.gsz + base * (8 * Tr::GSZ), gb, bar, pol);
+  kc.cl_iss[w] = k + 1u;
+}
+
+// Lane 0 of warp w, after its last piece of the current stage: the first two
+// pieces of the next GEMV stage within the landed descriptors.
+QTB_DEV void cl_issue_ahead(KCtx &kc, char *smem, int w) {
+  if (kc.local_err) return;
+  for (unsigned k = kc.seq + 1; k < kc.n_total && k <= kc.seq + STREAM_AHEAD; k++) {
+    const int slot = (int)(k % NDESC);
+    if (!mbar_test(kc.dbars + slot, (k / NDESC) & 1u)) return;
+    const Stage *st = kc.dring + slot;
+    if (st->kind != ST_GEMV) continue;
+    if (!st->g.cl) return;
+    const V2Plan &p = kc.pring[slot];
+    const int n = min(2, cl_npieces(p, w));
+    for (int q = 0; q < n; q++) {
+      switch (st->g.fmt) {
+        case FMT_BF16: cl_issue<FMT_BF16>(st->g, p, w, q, kc, smem); break;
+        case FMT_INT8: cl_issue<FMT_INT8>(st->g, p, w, q, kc, smem); break;
+        case FMT_Q4_0: cl_issue<FMT_Q4_0>(st->g, p, w, q, kc, smem); break;
+        default: cl_issue<FMT_INT4G>(st->g, p, w, q, kc, smem); break;
+      }
+    }
+    kc.cl_pre[w] = k;
+    return;
+  }
+}
+
+// Lane 0 of warp w at the start of a stage: its first pieces, unless issued
+// ahead by the previous GEMV stage.
+template <int FMT>
+QTB_DEV void cl_start(const GemvArgs &a, const V2Plan &p, int w, int np, KCtx &kc, char *smem) {
+  const int have = (kc.cl_pre[w] == kc.seq) ? (int)(kc.cl_iss[w] - kc.cl_q[w]) : 0;
+  if (kc.local_err) return;
+  for (int q = have; q < min(2, np); q++) cl_issue<FMT>(a, p, w, q, kc, smem);
+}
+
+// Every lane of the warp: wait for the warp's next piece (bounded); returns its slot.
+QTB_DEV const char *cl_wait(KCtx &kc, char *smem, int w, int q) {
+  const unsigned k = kc.cl_q[w];
+  if (!kc.local_err && !mbar_wait(kc.clbars + 2 * w + (k & 1u), (k >> 1) & 1u, WAIT_LIMIT_CYCLES))
+    raise_err(kc, ERR_MBAR_TIMEOUT, 4000 + q);
+  return smem + SM_W_OFF + (2 * w + (int)(k & 1u)) * CL_SLOT_BYTES;
+}
+// ... and after reading it: release the slot, refill it with piece q + 2.
+template <int FMT>
+QTB_DEV void cl_release(const GemvArgs &a, const V2Plan &p, int w, int q, int np, KCtx &kc, char *smem) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    kc.cl_q[w] += 1u;
+    // after an error no new copy goes out (the ones in flight are drained)
+    if (q + 2 < np && !kc.local_err) cl_issue<FMT>(a, p, w, q + 2, kc, smem);
+  }
+  __syncwarp();
+}
+
+// bf16 / q4_0 / int4 g32 weights (f16 / bf16 MMA on the staged parts).
+template <int FMT, int NCH, int P>
+__device__ __noinline__ void gemv_cl_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  using Tr = FmtTraits<FMT>;
+  constexpr bool F16 = (FMT != FMT_BF16);
+  constexpr bool XSUM = (FMT == FMT_Q4_0 || FMT == FMT_INT4G);
+  constexpr int PC = cl_pc<FMT>();
+  const V2Plan p = kc.pring[kc.seq % NDESC];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+  const int ent = 4 * min(8, P * B);
+  const int xsum_n = a.K >> 5;
+  float *s_inv = reinterpret_cast<float *>(smem + SM_R_OFF);
+  float *s_red = s_inv + 64;   // [nt * ks][16][B]
+  float *s_xsum = reinterpret_cast<float *>(smem + SM_X_OFF);
+  const int xsum_floats = XSUM ? ((B * xsum_n + 3) & ~3) : 0;
+  uint2 *s_xf = reinterpret_cast<uint2 *>(s_xsum + xsum_floats);
+  const int np = cl_npieces(p, warp);
+
+  ckpt(kc, 11);
+  if (lane == 0) cl_start<FMT>(a, p, warp, np, kc, smem);
+  __syncwarp();
+  ckpt(kc, 0);
+  if (p.nt == 0) return;
+  {
+    const int mq = (B * (a.K >> 2) + NTHREADS - 1) / NTHREADS;
+    if (mq <= 1) stage_x_fused<F16, P, 1>(a, B, ent, s_inv, s_xsum, s_xf, XSUM, kc, smem);
+    else if (mq <= 2) stage_x_fused<F16, P, 2>(a, B, ent, s_inv, s_xsum, s_xf, XSUM, kc, smem);
+    else if (mq <= 4) stage_x_fused<F16, P, 4>(a, B, ent, s_inv, s_xsum, s_xf, XSUM, kc, smem);
+    else stage_x_fused<F16, P, 8>(a, B, ent, s_inv, s_xsum, s_xf, XSUM, kc, smem);
+  }
+  __syncthreads();
+  ckpt(kc, 2);
+
+  float acc[NCH][4], acc1[NCH][4], acc2[NCH][4], acc3[NCH][4], res[NCH][2];
+#pragma unroll
+  for (int j = 0; j < NCH; j++)
+#pragma unroll
+    for (int e2 = 0; e2 < 4; e2++) { acc[j][e2] = acc1[j][e2] = acc2[j][e2] = acc3[j][e2] = 0.f; res[j][e2 & 1] = 0.f; }
+  for (int q = 0; q < np; q++) {
+    const ClPiece pc = cl_piece(p, PC, warp, q);
+    const char *slot = cl_wait(kc, smem, warp, q);
+    if (q == 0) ckpt(kc, 12);
+    auto load = [&](int i, uint4 &wv, uint4 &gv) {
+      wv = *reinterpret_cast<const uint4 *>(slot + i * 512 + lane * 16);
+      gv = make_uint4(0u, 0u, 0u, 0u);
+      if (Tr::GSZ == 8) {
+        const uint2 g = *reinterpret_cast<const uint2 *>(slot + PC * 512 + i * 64 + gid * 8);
+        gv = make_uint4(g.x, g.y, 0u, 0u);
+      } else if (Tr::GSZ == 16) {
+        gv = *reinterpret_cast<const uint4 *>(slot + PC * 512 + i * 128 + gid * 16);
+      }
+    };
+    int i = 0;
+    for (; i + 4 <= pc.n; i += 4) {
+      uint4 wv[4], gv[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) load(i + u, wv[u], gv[u]);
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        if (u & 1) mma_chunk<FMT, NCH>(wv[u], gv[u], pc.c0 + i + u, s_xf, ent, s_xsum, xsum_n, B, acc2, res, acc3);
+        else mma_chunk<FMT, NCH>(wv[u], gv[u], pc.c0 + i + u, s_xf, ent, s_xsum, xsum_n, B, acc, res, acc1);
+      }
+    }
+    for (; i < pc.n; i++) {
+      uint4 wv, gv;
+      load(i, wv, gv);
+      mma_chunk<FMT, NCH>(wv, gv, pc.c0 + i, s_xf, ent, s_xsum, xsum_n, B, acc, res, acc1);
+    }
+    cl_release<FMT>(a, p, warp, q, np, kc, smem);
+    if (pc.c0 + pc.n == (pc.s + 1) * p.kc) {   // the unit's last piece: its 16 rows out
+#pragma unroll
+      for (int j = 0; j < NCH; j++)
+#pragma unroll
+        for (int e2 = 0; e2 < 4; e2++) {
+          acc[j][e2] = (acc[j][e2] + acc1[j][e2]) + (acc2[j][e2] + acc3[j][e2]);
+          acc1[j][e2] = acc2[j][e2] = acc3[j][e2] = 0.f;
+        }
+      acc_finish<FMT, NCH, P>(acc, res);
+      const int u = pc.tl * p.kb + pc.s;
+#pragma unroll
+      for (int j = 0; j < NCH; j++) {
+        const int b = col_batch<P>(j, tig);
+        if (b < B && col_owner<P>(tig)) {
+          s_red[(u * 16 + gid) * B + b] = res[j][0];
+          s_red[(u * 16 + gid + 8) * B + b] = res[j][1];
+        }
+        acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        res[j][0] = res[j][1] = 0.f;
+      }
+    }
+  }
+  ckpt_w(kc, 24);
+  if (lane == 0) cl_issue_ahead(kc, smem, warp);
+  __syncthreads();
+  ckpt(kc, 3);
+  float *s_val = s_red;
+  if (p.kb > 1) {   // a tile's slices, in slice order
+    s_val = s_red + p.nt * p.kb * 16 * B;
+    for (int idx = tid; idx < p.nt * 16 * B; idx += NTHREADS) {
+      const int rb = idx % (16 * B), tl = idx / (16 * B);
+      float v = 0.f;
+      for (int sl = 0; sl < p.kb; sl++) v += s_red[(tl * p.kb + sl) * 16 * B + rb];
+      s_val[idx] = v;
+    }
+    __syncthreads();
+  }
+  ckpt(kc, 4);
+  v2_epilogue(a, B, p.t0, p.nt, s_val, B, kc);
+  ckpt(kc, 5);
+}
+
+// int8 weights on the s8 MMA with the four-part activation (as gemv2_s8_t).
+template <int NCH>
+__device__ __noinline__ void gemv_cl_s8_t(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  constexpr int PC = cl_pc<FMT_INT8>();
+  const V2Plan p = kc.pring[kc.seq % NDESC];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+  float *s_scl = reinterpret_cast<float *>(smem + SM_R_OFF);
+  float *s_red = s_scl + 64;   // [nt * ks][16][B]
+  uint32_t *s_xw = reinterpret_cast<uint32_t *>(smem + SM_X_OFF);
+  const uint2 *s_xf = reinterpret_cast<const uint2 *>(s_xw);
+  const int np = cl_npieces(p, warp);
+
+  ckpt(kc, 11);
+  if (lane == 0) cl_start<FMT_INT8>(a, p, warp, np, kc, smem);
+  __syncwarp();
+  ckpt(kc, 0);
+  if (p.nt == 0) return;
+  {
+    const int mq = (B * (a.K >> 2) + NTHREADS - 1) / NTHREADS;
+    if (mq <= 1) stage_x_s8<1>(a, B, NCH, 0, a.K, s_scl, s_xw, s_red, 0, kc);
+    else if (mq <= 2) stage_x_s8<2>(a, B, NCH, 0, a.K, s_scl, s_xw, s_red, 0, kc);
+    else if (mq <= 4) stage_x_s8<4>(a, B, NCH, 0, a.K, s_scl, s_xw, s_red, 0, kc);
+    else stage_x_s8<8>(a, B, NCH, 0, a.K, s_scl, s_xw, s_red, 0, kc);
+  }
+  __syncthreads();
+  ckpt(kc, 2);
+
+  // column pair (2 tig, 2 tig + 1) of chunk j = parts (2 (tig & 1), +1) of
+  // batch row 2 j + tig / 2
+  const float wlo = (tig & 1) ? (1.0f / 16384.0f) : 1.0f, whi = (tig & 1) ? (1.0f / 2097152.0f) : (1.0f / 128.0f);
+  int acc[4][NCH][4];
+#pragma unroll
+  for (int u = 0; u < 4; u++)
+#pragma unroll
+    for (int j = 0; j < NCH; j++) acc[u][j][0] = acc[u][j][1] = acc[u][j][2] = acc[u][j][3] = 0;
+  for (int q = 0; q < np; q++) {
+    const ClPiece pc = cl_piece(p, PC, warp, q);
+    const char *slot = cl_wait(kc, smem, warp, q);
+    if (q == 0) ckpt(kc, 12);
+    int i = 0;
+    for (; i + 4 <= pc.n; i += 4) {
+      uint4 wv[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) wv[u] = *reinterpret_cast<const uint4 *>(slot + (i + u) * 512 + lane * 16);
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+#pragma unroll
+        for (int j = 0; j < NCH; j++) {
+          const uint2 bx = s_xf[((pc.c0 + i + u) * NCH + j) * 32 + lane];
+          mma_s8(acc[u][j], wv[u], bx.x, bx.y);
+        }
+    }
+    for (; i < pc.n; i++) {
+      const uint4 wv = *reinterpret_cast<const uint4 *>(slot + i * 512 + lane * 16);
+#pragma unroll
+      for (int j = 0; j < NCH; j++) {
+        const uint2 bx = s_xf[((pc.c0 + i) * NCH + j) * 32 + lane];
+        mma_s8(acc[0][j], wv, bx.x, bx.y);
+      }
+    }
+    cl_release<FMT_INT8>(a, p, warp, q, np, kc, smem);
+    if (pc.c0 + pc.n == (pc.s + 1) * p.kc) {   // the unit's last piece: its 16 rows out
+      const int un = pc.tl * p.kb + pc.s;
+#pragma unroll
+      for (int j = 0; j < NCH; j++) {
+        const int i0 = acc[0][j][0] + acc[1][j][0] + acc[2][j][0] + acc[3][j][0];
+        const int i1 = acc[0][j][1] + acc[1][j][1] + acc[2][j][1] + acc[3][j][1];
+        const int i2 = acc[0][j][2] + acc[1][j][2] + acc[2][j][2] + acc[3][j][2];
+        const int i3 = acc[0][j][3] + acc[1][j][3] + acc[2][j][3] + acc[3][j][3];
+        float r0 = (float)i0 * wlo + (float)i1 * whi;   // row gid
+        float r1 = (float)i2 * wlo + (float)i3 * whi;   // row gid + 8
+        r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+        r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+        const int b = 2 * j + (tig >> 1);
+        if ((tig & 1) == 0 && b < B) {
+          const float sx = s_scl[4 + b];
+          s_red[(un * 16 + gid) * B + b] = r0 * sx;
+          s_red[(un * 16 + gid + 8) * B + b] = r1 * sx;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) acc[u][j][0] = acc[u][j][1] = acc[u][j][2] = acc[u][j][3] = 0;
+      }
+    }
+  }
+  ckpt_w(kc, 24);
+  if (lane == 0) cl_issue_ahead(kc, smem, warp);
+  __syncthreads();
+  ckpt(kc, 3);
+  float *s_val = s_red;
+  if (p.kb > 1) {   // a tile's slices, in slice order
+    s_val = s_red + p.nt * p.kb * 16 * B;
+    for (int idx = tid; idx < p.nt * 16 * B; idx += NTHREADS) {
+      const int rb = idx % (16 * B), tl = idx / (16 * B);
+      float v = 0.f;
+      for (int sl = 0; sl < p.kb; sl++) v += s_red[(tl * p.kb + sl) * 16 * B + rb];
+      s_val[idx] = v;
+    }
+    __syncthreads();
+  }
+  ckpt(kc, 4);
+  v2_epilogue(a, B, p.t0, p.nt, s_val, B, kc);
+  ckpt(kc, 5);
+}
+
+template <int FMT>
+QTB_DEV void gemv_cl_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  if (FMT == FMT_INT8 && a.parts == 4) {
+    switch (a.nch) {
+      case 1: gemv_cl_s8_t<1>(a, B, smem, kc); return;
+      case 2: gemv_cl_s8_t<2>(a, B, smem, kc); return;
+    }
+  } else if (FMT == FMT_BF16 && a.parts == 4) {
+    switch (a.nch) {
+      case 1: gemv_cl_t<FMT, 1, 4>(a, B, smem, kc); return;
+      case 2: gemv_cl_t<FMT, 2, 4>(a, B, smem, kc); return;
+    }
+  } else if (a.parts == 2 && FMT != FMT_BF16 && FMT != FMT_INT8) {
+    switch (a.nch) {
+      case 1: gemv_cl_t<FMT, 1, 2>(a, B, smem, kc); return;
+    }
+  }
+  if (threadIdx.x == 0) raise_err(kc, ERR_BAD_STAGE, 5000 + a.nch * 16 + a.parts);
+}
+
 // ============================================ GEMV stage on tcgen05 =======
 //
 // Large batches (5..64 rows) with bf16 or int8 weights.  A CTA owns one k-slice
@@ -2133,6 +2539,7 @@ QTB_DEV void gemv2_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
 
 template <int FMT>
 QTB_DEV void gemv_stage_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
+  if (a.cl) { gemv_cl_f<FMT>(a, B, smem, kc); return; }
   if (a.v2) { gemv2_stage_f<FMT>(a, B, smem, kc); return; }
   if (FMT == FMT_BF16 || FMT == FMT_INT8) {
     // large batches of bf16 / int8 weights always run on tcgen05
@@ -3122,6 +3529,36 @@ __device__ __noinline__ void norm_stage(const NormArgs &n, int B) {
 // the stage counters.
 QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
   __shared__ int s_ok;
+  if (kc.cl) {
+    // the hook once (the cluster barrier has no poll loop), then the barrier
+    if (threadIdx.x < 32) {
+      const unsigned nxt = kc.seq + 1;
+      if (nxt < kc.n_total) {
+        const int slot = (int)(nxt % NDESC);
+        const bool landed = __all_sync(0xffffffffu, mbar_test(kc.dbars + slot, (nxt / NDESC) & 1u));
+        if (landed && kc.dring[slot].kind == ST_ATTN && kc.dring[slot].a.mode == ATT_DECODE)
+          attn_prefetch(kc.dring[slot].a, kc.dring[slot].B, kc, smem);
+        __syncwarp();
+        if (threadIdx.x == 0 && landed) {
+          const Stage *nx = kc.dring + slot;
+          if (nx->kind == ST_GEMV && nx->g.v2) prefetch_gemv_operands(nx->g, kc.pring[slot]);
+        }
+        __syncwarp();
+      }
+    }
+    __syncwarp();
+    cluster_wait();
+    const int tag = kc.cl_err;
+    const bool ok = !(tag != 0 && tag <= (int)kc.epoch + 1);
+    __syncthreads();   // every thread has read the tag and the hook's state
+    if (threadIdx.x == 0) {
+      kc.epoch++;
+      kc.seq++;
+      kc.stage = (kc.stage + 1 == kc.n_stages) ? 0 : kc.stage + 1;
+    }
+    __syncthreads();
+    return ok;
+  }
   if (threadIdx.x < 32) {   // warp 0: lane 0 polls, the warp runs the hook
     const int lane = threadIdx.x;
     __syncwarp();            // kc.last, written by lane 0 in grid_arrive
@@ -3183,7 +3620,7 @@ QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
 // ====================================================== persistent kernel ==
 __global__ void __launch_bounds__(NTHREADS, 1)
 decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, int n_stages, int n_iters, Ctl *ctl,
-              long long *trace) {
+              long long *trace, int cl) {
   extern __shared__ __align__(128) char smem[];
   __shared__ __align__(8) uint64_t bars[ATT_NBUF_MAX];
   __shared__ __align__(8) uint64_t wbars[NWSLOT];
@@ -3192,6 +3629,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
   __shared__ V2Plan pring[NDESC];  // this CTA's plan entries for them ([stage][CTA] in `plan`)
   __shared__ __align__(8) uint64_t pbar;
   __shared__ __align__(8) uint64_t tcbars[2 * TC_NSLOT + 2];   // weight slot full / empty, accumulators
+  __shared__ __align__(8) uint64_t clbars[2 * NWARPS];          // single-cluster GEMV: per-warp weight slots
   __shared__ uint32_t tmem_base;
   __shared__ KCtx kc;
   if (threadIdx.x == 0) {
@@ -3233,6 +3671,14 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     kc.tc_done = 0;
     kc.tc_committed = 0;
     kc.tc_waited = 0;
+    kc.cl = cl;
+    kc.clbars = clbars;
+    for (int w = 0; w < NWARPS; w++) {
+      kc.cl_q[w] = 0u;
+      kc.cl_iss[w] = 0u;
+      kc.cl_pre[w] = ~0u;
+    }
+    kc.cl_err = 0;
   }
   // the tensor-memory accumulator of the tcgen05 GEMV stages, held for the
   // whole launch (one CTA per SM: the allocation never waits)
@@ -3250,6 +3696,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     for (int i = 0; i < NDESC; i++) mbar_init(dbars + i, 1);
     for (int i = 0; i < 2 * TC_NSLOT + 2; i++) mbar_init(tcbars + i, 1);
     mbar_init(&pbar, 1);
+    for (int i = 0; i < 2 * NWARPS; i++) mbar_init(clbars + i, 1);
     fence_mbar_init();
     for (unsigned k = 0; k < NDESC - 1 && k < kc.n_total; k++) issue_desc(k);
     kc.t_start = clock64();
@@ -3259,6 +3706,10 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
   tc_fence_after();
   if (threadIdx.x == 0) kc.tmem = tmem_base;
   __syncthreads();
+  if (cl) {   // every CTA's error word is initialised before any CTA can write to it
+    cluster_arrive();
+    cluster_wait();
+  }
   if (trace && blockIdx.x == 0 && threadIdx.x == 0) trace[(size_t)n_iters * n_stages] = clock64();
   for (int it = 0; it < n_iters; it++) {
     for (int si = 0; si < n_stages; si++) {
@@ -3281,13 +3732,19 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
         case ST_EMBED: embed_stage(st->e, B, kc); break;
         case ST_NORM: norm_stage(st->n, B); break;
         case ST_POS_INC:
-          // slots stopped at EOS keep their position and frame count
+          // done = 1: the slot sampled EOS in this frame, whose talker step
+          // did run (its position advances past it, as the reference's does),
+          // and it stops: done = 2 keeps its position and frame count
           if (blockIdx.x == 0)
             for (int b = threadIdx.x; b < B; b += NTHREADS) {
               const GenState *gs = st->p.gen;
-              if (gs && gs->enabled && __ldcg(gs->done + b)) continue;
+              const int d = (gs && gs->enabled) ? __ldcg(gs->done + b) : 0;
+              if (d >= 2) continue;
               st->p.pos[b] += 1;
-              if (gs && gs->enabled) gs->frame[b] += 1;
+              if (gs && gs->enabled) {
+                gs->frame[b] += 1;
+                if (d == 1) gs->done[b] = 2;
+              }
             }
           break;
         default:

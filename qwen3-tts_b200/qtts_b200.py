@@ -89,6 +89,7 @@ def lib():
     L.qtb_decode_frames.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp]
     L.qtb_session_begin_generation.argtypes = [_vp, _vp, C.c_float]
     L.qtb_prefill.argtypes = [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]
+    L.qtb_session_program_grid.argtypes = [_vp, C.c_int]
     L.qtb_session_reset_slot.argtypes = [_vp, C.c_int, C.c_int, C.c_int]
     L.qtb_session_set_slot_pos.argtypes = [_vp, C.c_int, C.c_int]
     L.qtb_session_set_embed.argtypes = [_vp, C.c_int, _vp]
@@ -426,6 +427,11 @@ class Session:
         hid = np.empty((self.B, cfg.hidden), np.float32)
         check(lib().qtb_decode_frames(self.h, ptr(e), ptr(pd), n_frames, ptr(codes), ptr(hid)))
         return codes, hid
+
+    def program_grid(self, which):
+        """CTAs of program `which` (0 talker, 1 CP pass, 2 CP frame, 3 frame,
+        4 prefill); negative = one cluster of that many CTAs."""
+        return lib().qtb_session_program_grid(self.h, int(which))
 
     def prefill(self, b, embeds, pos0=0):
         """Device prefill of slot b (qtb_prefill): embeds [n][hidden] at

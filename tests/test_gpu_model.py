@@ -76,6 +76,40 @@ def test_talker_steps_match_reference(have_gpu, tiny, fmt):
     ref.close()
 
 
+@pytest.mark.parametrize("fmt", ["bf16", "int8", "q4_0", "int4g32"])
+def test_single_cluster_schedule_matches_whole_gpu(have_gpu, tiny, fmt, monkeypatch):
+    """With QTB_CL=1 small-batch programs run as one 16-CTA cluster (cluster
+    barriers, per-warp weight streams), else on the whole GPU: both give the same
+    hidden states (to the rounding of their different reduction orders) and
+    the same greedy codes over whole frames, at B = 1 and B = 2 (the
+    small-batch activation staging holds B x K <= 8192 values)."""
+    cfg, m, path = tiny
+    engs = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("QTB_CL", mode)
+        engs[mode] = Q.Engine(m, Q.FMT_NAMES[fmt], Q.FMT_NAMES[fmt])
+    monkeypatch.delenv("QTB_CL")
+    for B in (1, 2):
+        a, b = Q.Session(engs["1"], B, 256), Q.Session(engs["0"], B, 256)
+        assert a.program_grid(0) == -16 and a.program_grid(3) == -16, [a.program_grid(i) for i in range(5)]
+        assert b.program_grid(0) > 16
+        rng = np.random.default_rng(40 + B)
+        for pos in range(20):
+            e = (0.1 * rng.standard_normal((B, cfg.hidden))).astype(np.float32)
+            ha = a.talker_step(e, [pos] * B)
+            hb = b.talker_step(e, [pos] * B)
+            # last-bit differences of the two reduction orders become 1-ulp
+            # bf16 K/V flips (as between the engine and the reference)
+            assert rel_l2(ha, hb) < 1e-3, (B, pos, rel_l2(ha, hb))
+        e = (0.1 * rng.standard_normal((B, cfg.hidden))).astype(np.float32)
+        ca, xa = a.decode_frames(e, 6)
+        cb, xb = b.decode_frames(e, 6)
+        assert rel_l2(xa, xb) < 1e-3
+        # greedy codes: identical unless a near-tie flips (both schedules are
+        # within f32 rounding of each other); most frames must agree exactly
+        assert (ca == cb).all(axis=2).mean() >= 0.8, (ca[:, :, :4], cb[:, :, :4])
+
+
 @pytest.mark.parametrize("fmt", ["bf16", "int8"])
 def test_cp_frame_codes_match_reference(have_gpu, tiny, fmt):
     cfg, m, path = tiny
@@ -206,18 +240,22 @@ def test_prefill_matches_reference_prefill(have_gpu, tiny, fmt):
     for p in range(10):
         bb.talker_step(E2[p], p)
     hp, _ = bb.prefill(0, E2[10:], 10)
-    assert rel_l2(hp, hs[0]) < 2e-2, rel_l2(hp, hs[0])
+    # an INT8 engine prefills from its bf16 weights (as the reference does) and
+    # decodes from the INT8 ones: the steps differ from the prefill by that too
+    tol = 2e-2 if fmt == "bf16" else 6e-2
+    assert rel_l2(hp, hs[0]) < tol, rel_l2(hp, hs[0])
     ka, va = a.download_kv(0, cfg.layers, cfg.kv_heads * 128, 110)
     kb, vb = bb.download_kv(0, cfg.layers, cfg.kv_heads * 128, 110)
-    # layer 0's K/V depend on the embeddings alone; deeper layers carry the
-    # f32-vs-bf16 attention difference of the layers below
-    assert kv_close(kb[0], ka[0], 0.85) and kv_close(vb[0], va[0], 0.85)
+    # with the same weights layer 0's K/V depend on the embeddings alone;
+    # deeper layers carry the f32-vs-bf16 attention difference of the layers below
+    if fmt == "bf16":
+        assert kv_close(kb[0], ka[0], 0.85) and kv_close(vb[0], va[0], 0.85)
     f32 = lambda u: (u.astype(np.uint32) << 16).view(np.float32)
-    for l in range(1, cfg.layers):
-        assert rel_l2(f32(kb[l]), f32(ka[l])) < 2e-2 and rel_l2(f32(vb[l]), f32(va[l])) < 2e-2, l
+    for l in range(0 if fmt != "bf16" else 1, cfg.layers):
+        assert rel_l2(f32(kb[l]), f32(ka[l])) < tol and rel_l2(f32(vb[l]), f32(va[l])) < tol, l
     # and decoding continues from the prefilled cache
     e = (0.1 * rng.standard_normal(cfg.hidden)).astype(np.float32)
-    assert rel_l2(bb.talker_step(e, 110)[0], a.talker_step(e, 110)[0]) < 2e-2
+    assert rel_l2(bb.talker_step(e, 110)[0], a.talker_step(e, 110)[0]) < tol
 
 
 def test_kv_upload_download_roundtrip(have_gpu, tiny):
