@@ -152,6 +152,23 @@ QTB_DEV void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint
       "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Tiled TMA load of a 3-D box (no multicast): coordinates x (innermost,
+// elements), y, z of the tensor map at generic address `map` (global memory).
+QTB_DEV void tma_load_3d(void *dst_smem, const void *map, int x, int y, int z, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+// Four transposed 8 x 8 b16 matrices from shared memory (lane 8i + r gives
+// row r of matrix i).
+QTB_DEV void ldsm_x4_trans(uint32_t (&r)[4], const void *row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(row_addr))
+               : "memory");
+}
 QTB_DEV void bulk_g2s_hint(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar, uint64_t pol) {
   asm volatile(
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(

@@ -9,6 +9,7 @@
 #include "../../include/qwen3tts_b200.h"
 #include "../../include/qwen_tts_cuda_b200.h"
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cmath>
@@ -59,6 +60,38 @@ static void cl_launch_config(cudaLaunchConfig_t &cfg, cudaLaunchAttribute (&at)[
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+}
+
+// Tiled tensor maps through the driver's cuTensorMapEncodeTiled (fetched at
+// run time: the library links the runtime only).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+// A KV pool [layers][rows][128] bf16 (rows = pages x kv heads x 16) as a 3-D
+// tensor of 16 x 64 boxes with the 128-byte swizzle.
+static bool kv_tensor_map(CUtensorMap *out, const uint16_t *pool, int n_layers, size_t layer_elems) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || layer_elems % 128 || (uintptr_t)pool % 16) return false;
+  const cuuint64_t dims[3] = {128, (cuuint64_t)(layer_elems / 128), (cuuint64_t)n_layers};
+  const cuuint64_t strides[2] = {256, (cuuint64_t)layer_elems * 2};
+  const cuuint32_t box[3] = {64, 16, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t *>(pool), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 static int set_err(int code, const char *fmt, ...) {
@@ -712,6 +745,7 @@ struct StackBufs {
   int *page_table = nullptr;                    // [B][pt_stride]
   int pt_stride = 0;
   int max_splits = 1, min_pps = 4;
+  const void *kmap = nullptr, *vmap = nullptr;  // TMA tensor maps of the pools (device), or null
   size_t layer_pool_elems() const { return 0; }
 };
 
@@ -842,6 +876,10 @@ static bool cl_ok(int fmt, int rows, int K, int B) {
 // streams plus the split-K fix-up.  The staged activation slice must fit
 // TC_X_BYTES (N x 128 bytes per chunk) and 2048 columns.
 struct TcShape { int S = 0, kcn = 0, R = 0; };
+static bool attn_tc_enabled() {
+  const char *v = getenv("QTB_ATTN_TC");   // read at each program build / standalone call
+  return !(v && v[0] == '0');
+}
 static bool tc_ok(const DMat &m, int B, int fmt) {
   return tc_enabled() && m.wtc && B >= 1 && B <= 64 && (fmt == FMT_BF16 || fmt == FMT_INT8) && m.rows % 128 == 0;
 }
@@ -972,6 +1010,12 @@ struct ProgBuilder {
       a.pkv = s->pkv; a.layer = layer;
     }
     if (cl) a.max_splits = std::max(1, std::min(a.max_splits, grid() / std::max(1, B * k.n_kv)));
+    a.layer = layer;
+    a.kmap = b.kmap; a.vmap = b.vmap;
+    // large-batch decode attention on the tensor cores (needs the 16 page
+    // buffers of a program without small-batch GEMV stages: upload_prog
+    // turns it off otherwise); QTB_ATTN_TC=0 keeps the CUDA-core loop
+    a.tc = (mode == ATT_DECODE && B >= 8 && b.kmap && attn_tc_enabled()) ? 1 : 0;
     attn_schedule(a, B, grid());
     if (mode == ATT_ATTEND) a.dyn = 0;   // static item order (attn_prefill_stage)
     st.push_back(S);
@@ -1091,7 +1135,7 @@ static int upload_prog(qtb_session *s, int which, ProgBuilder &pb) {
   bool streams = false;
   for (const Stage &st : pb.st) streams |= (st.kind == ST_GEMV && st.g.v2);
   for (Stage &st : pb.st)
-    if (st.kind == ST_ATTN && streams) st.a.nbuf = ATT_NBUF;
+    if (st.kind == ST_ATTN && streams) { st.a.nbuf = ATT_NBUF; st.a.tc = 0; }
   // per-tile counters of the split tcgen05 stages: a disjoint range per stage,
   // zeroed at every launch of the program
   int tc_sem_n = 0;
@@ -1208,6 +1252,18 @@ static int alloc_stack_bufs(qtb_session *s, const DStack &k, StackBufs &b, int B
   for (int i = 0; i < B; i++)
     for (int j = 0; j < b.pt_stride; j++) pt[(size_t)i * b.pt_stride + j] = (n_pages > 0) ? -1 : i * b.pt_stride + j;
   if ((rc = ar.upload(&b.page_table, pt.data(), pt.size() * 4))) return rc;
+  {
+    // tensor maps of the pools for the tensor-core decode attention (cudaMalloc
+    // memory is 256-byte aligned, as a tensor map in global memory must be 64)
+    CUtensorMap maps[2];
+    if (kv_tensor_map(&maps[0], b.kpool, k.n_layers, layer_elems) &&
+        kv_tensor_map(&maps[1], b.vpool, k.n_layers, layer_elems)) {
+      char *d;
+      if ((rc = ar.upload(&d, maps, sizeof maps))) return rc;
+      b.kmap = d;
+      b.vmap = d + sizeof(CUtensorMap);
+    }
+  }
   if (B * k.n_kv > s->e->n_sm / 2) {
     // many sequences: items of 32-64 pages taken in dynamic order keep the
     // CTAs evenly loaded whatever the length mix (pages stream across items,
@@ -1351,6 +1407,7 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
         cudaMemset(s->pkv, 0, sizeof(PromptKV));
         cudaMemset(p.page_table, 0, R * s->tk.pt_stride * 4);
         p.kpool = s->tk.kpool; p.vpool = s->tk.vpool;
+        p.kmap = s->tk.kmap; p.vmap = s->tk.vmap;
         p.n_pages = s->tk.n_pages; p.pt_stride = s->tk.pt_stride;
         p.max_splits = 16; p.min_pps = 64;
         att_splits = std::max(att_splits, p.max_splits);
@@ -1924,6 +1981,14 @@ extern "C" int qtb_attention_host(const float *qkv, int batch, int n_heads, int 
     CUDA_TRY(cudaGetDevice(&dev));
     CUDA_TRY(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
     attn_schedule(a, batch, nsm);
+  }
+  if (batch >= 8 && attn_tc_enabled()) {   // the tensor-core page loop, as large-batch sessions run it
+    CUtensorMap maps[2];
+    if (kv_tensor_map(&maps[0], dk, 1, pool) && kv_tensor_map(&maps[1], dv, 1, pool)) {
+      char *d;
+      if ((rc = mr.ar.upload(&d, maps, sizeof maps))) return rc;
+      a.kmap = d; a.vmap = d + sizeof(CUtensorMap); a.layer = 0; a.tc = 1;
+    }
   }
   if ((rc = run_single_stage(mr, st))) return rc;
   CUDA_TRY(cudaMemcpy(out, dout, (size_t)batch * qd * 4, cudaMemcpyDeviceToHost));

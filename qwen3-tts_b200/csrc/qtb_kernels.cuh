@@ -170,6 +170,10 @@ struct AttnArgs {
   // writes them there as well as into the pages; ATTEND reads positions from
   // the prompt's first one on from there, older ones from the pages.
   const struct PromptKV *pkv; int layer;
+  // tensor-core decode attention (attn_pages_tc): tensor maps of this stack's
+  // K and V pools ([layer][rows = page, kv head, position][128] bf16), pages
+  // copied as 128-byte swizzled 16 x 64 boxes
+  int tc; const void *kmap, *vmap;
 };
 enum AttnMode { ATT_DECODE = 0, ATT_APPEND = 1, ATT_ATTEND = 2 };
 
@@ -2609,6 +2613,19 @@ static_assert(ATT_COMB_OFF + NWARPS * (HD + 2) * 4 <= SM_X2_BYTES, "page ring ex
 static_assert(NWARPS == 2 * ATT_NBUF, "one warp pair (the two heads of a GQA group) per page buffer group");
 static_assert((ATT_NBUF_MAX - ATT_NBUF) * ATT_PAGE_BYTES <= NWSLOT * WSLOT_BYTES, "extra page buffers exceed the weight ring");
 
+// The tensor-core page loop (a.tc) copies pages as 128-byte swizzled TMA
+// boxes, whose destination must sit on a 1024-byte boundary: its 16 buffers
+// start at the first such boundary of the dynamic shared memory (weight-ring
+// and activation regions, idle then: a.tc is set only in programs without
+// small-batch GEMV stages), followed by its attention scratch and the
+// per-warp states of both heads.
+constexpr int ATT_TC_SM_OFF = ATT_NBUF_MAX * ATT_PAGE_BYTES + 1024;
+constexpr int ATT_TC_COMB_OFF = ATT_TC_SM_OFF + 2048;
+static_assert(ATT_TC_COMB_OFF + NWARPS * 2 * (HD + 2) * 4 <= SM_R_OFF, "tensor-core attention region");
+QTB_DEV char *att_tc_buf(char *smem, int i) {
+  return smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u) + i * ATT_PAGE_BYTES;
+}
+
 // Page buffer i (of a.nbuf): the first ATT_NBUF follow the attention scratch
 // in the activation region; the others take the weight-ring region, which is
 // idle in a program without small-batch GEMV stages.
@@ -2621,6 +2638,12 @@ struct AttnItem {
   int b, g, sp, pos, L, npages, nsp, p_begin, p_end;
   bool bad_pos;
 };
+
+// The attention scratch of a stage (where the tensor-core loop keeps it, or
+// at the start of the activation region).
+QTB_DEV AttnSmem *attn_sm(const AttnArgs &a, char *smem) {
+  return reinterpret_cast<AttnSmem *>(smem + (a.tc ? ATT_TC_SM_OFF : SM_X_OFF));
+}
 
 // Pages per split for a sequence of np pages: at least min_pps, at most
 // max_splits splits.
@@ -2782,6 +2805,17 @@ QTB_DEV void attn_issue_pg(const AttnArgs &a, int page, int g, unsigned ctr, KCt
   const int nb = a.nbuf;
   const int buf = ctr % nb;
   if (page < 0 || page >= a.n_pages) { raise_err(kc, ERR_BAD_PAGE, page); page = 0; }
+  if (a.tc) {
+    // K dims 0-63, 64-127, then V: four 16 x 64 boxes of 2 KB, swizzled
+    char *dst = att_tc_buf(smem, buf);
+    const int y = (page * a.n_kv + g) * PAGE;
+    mbar_arrive_expect_tx(kc.bars + buf, ATT_PAGE_BYTES);
+    tma_load_3d(dst, a.kmap, 0, y, a.layer, kc.bars + buf);
+    tma_load_3d(dst + 2048, a.kmap, 64, y, a.layer, kc.bars + buf);
+    tma_load_3d(dst + 4096, a.vmap, 0, y, a.layer, kc.bars + buf);
+    tma_load_3d(dst + 6144, a.vmap, 64, y, a.layer, kc.bars + buf);
+    return;
+  }
   uint16_t *dstk = att_buf(smem, buf);
   const size_t off = (((size_t)page * a.n_kv + g) * PAGE) * HD;
   mbar_arrive_expect_tx(kc.bars + buf, ATT_PAGE_BYTES);
@@ -2812,7 +2846,7 @@ QTB_DEV void attn_issue(const AttnArgs &a, const AttnItem &it, int i0, int i1, K
 // newest token is patched in from registers by the stage itself).
 QTB_CALL void attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem) {
   const int lane = threadIdx.x & 31;
-  AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem + SM_X_OFF);
+  AttnSmem *sm = attn_sm(a, smem);
   AttnItem it;
   if (a.dyn) {
     const int tot = attn_prefix(a, B, sm);
@@ -2833,9 +2867,160 @@ QTB_CALL void attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem) {
   attn_issue(a, it, 0, n, kc, smem);
 }
 
+// Tensor-core pages of one decode attention item (large batches).  Warp w
+// takes the item's pages w, w + 8, ... with both query heads of the GQA group
+// at once, on the bf16 MMA (m16n8k16, f32 accumulate):
+//  - scores S[16 tokens x 8] = K[16 x 128] q^T, the 8 MMA columns being
+//    (part p, head h) = 2 p + h: q carried as three bf16 parts (24 bits).  The
+//    K rows come from the swizzled page (lane: row gid, 16-byte chunk 2 tig +
+//    (j & 1) of box j >> 1 per step pair j; the MMA's k order follows that
+//    dimension order, and q's fragments use the same one);
+//  - the online softmax of each head over the page's tokens (reference
+//    recurrence of qwen_causal_attention_bf16kv, per page);
+//  - O[(p, h) x 128] += P[(p, h) x 16 tokens] V: P's rows are the three bf16
+//    parts of the f32 probabilities, V's fragments come from ldmatrix.trans
+//    on the swizzled page (conflict-free).
+// The warp's per-head state (max, sum, 128 outputs) goes to s_acc / s_ml
+// ([NWARPS][2][HD], [NWARPS][2][2]).  Returns false after a failed wait.
+__device__ __noinline__ bool attn_pages_tc(const AttnArgs &a, const AttnItem &it, const AttnItem &nx, int nx_n,
+                                           bool owns_new, KCtx &kc, char *smem_base, const AttnSmem *sm,
+                                           float *s_acc, float *s_ml) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+  const int NB = a.nbuf;
+  const int n = it.p_end - it.p_begin;
+  const int *pt = a.page_table + (size_t)it.b * a.pt_stride;
+  const int hq = gid & 1, pq = gid >> 1;   // this lane's MMA column / P row: head, part
+  // q fragments (B operand of the score MMAs)
+  uint32_t qf[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const float *q = sm->q[hq] + (j >> 1) * 64 + (2 * tig + (j & 1)) * 8;
+#pragma unroll
+    for (int u = 0; u < 4; u++) qf[j][u] = gid < 6 ? split_pack<false>(q[2 * u], q[2 * u + 1], pq) : 0u;
+  }
+  float m_w[2] = {-INFINITY, -INFINITY}, l_w[2] = {0.f, 0.f};
+  float oacc[16][4];
+#pragma unroll
+  for (int m = 0; m < 16; m++) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
+  bool ok = true;
+  for (int i = warp; i < n; i += NWARPS) {
+    const unsigned ctr = kc.page_ctr + i;
+    const int buf = ctr % NB;
+    const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+    if (!__all_sync(0xffffffffu, landed)) {
+      if (lane == 0) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+      ok = false;
+      break;
+    }
+    char *pg_k = att_tc_buf(smem_base, buf);
+    const char *pg_v = pg_k + 4096;
+    const int pg = it.p_begin + i;
+    const int ntok = min(PAGE, it.L - pg * PAGE);
+    if (owns_new && pg == it.npages - 1) {
+      // the newest token comes from shared memory (its copy may predate the append)
+      const int row = it.pos % PAGE, c = lane & 15;
+      const uint16_t *src = (lane < 16 ? sm->knew : sm->vnew) + c * 8;
+      char *dst = pg_k + (lane < 16 ? 0 : 4096) + (c >> 3) * 2048 + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+      __syncwarp();
+    }
+    int refill_page = -1;
+    const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
+    if (lane == 0) {
+      if (tgt < n) refill_page = __ldg(pt + it.p_begin + tgt);
+      else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+    }
+    // ---- scores ----
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const char *kb = pg_k + (j >> 1) * 2048;
+      const int cc = ((2 * tig + (j & 1)) ^ (gid & 7)) << 4;
+      const uint4 w0 = *reinterpret_cast<const uint4 *>(kb + gid * 128 + cc);
+      const uint4 w1 = *reinterpret_cast<const uint4 *>(kb + (gid + 8) * 128 + cc);
+      const uint32_t A0[4] = {w0.x, w1.x, w0.y, w1.y};
+      mma_bf16(sc, A0, qf[j][0], qf[j][1]);
+      const uint32_t A1[4] = {w0.z, w1.z, w0.w, w1.w};
+      mma_bf16(sc, A1, qf[j][2], qf[j][3]);
+    }
+    // sc: tokens gid (0, 1) and gid + 8 (2, 3), head e & 1, part tig: sum the parts
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 1);
+      sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
+    }
+    const bool v0 = gid < ntok, v1 = gid + 8 < ntok;
+    float pr[4], corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const float s0 = v0 ? sc[h] * a.scale : -INFINITY, s1 = v1 ? sc[2 + h] * a.scale : -INFINITY;
+      float mx = fmaxf(s0, s1);
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float m_new = fmaxf(m_w[h], mx);   // finite: token 0 of every page is valid
+      corr[h] = (m_w[h] == -INFINITY) ? 0.f : expf(m_w[h] - m_new);
+      pr[h] = v0 ? expf(s0 - m_new) : 0.f;
+      pr[2 + h] = v1 ? expf(s1 - m_new) : 0.f;
+      l_w[h] = l_w[h] * corr[h] + (pr[h] + pr[2 + h]);
+      m_w[h] = m_new;
+    }
+    const float cq = corr[hq];
+#pragma unroll
+    for (int m = 0; m < 16; m++) { oacc[m][0] *= cq; oacc[m][1] *= cq; }
+    // ---- P (rows (part, head), tokens) from the score layout ----
+    const float off1 = (tig & 1) ? pr[1] : pr[0], off2 = (tig & 1) ? pr[3] : pr[2];
+    const int sa = (2 * tig) * 4 + hq, sb = (2 * tig + 1) * 4 + hq;
+    const float pa = __shfl_sync(0xffffffffu, off1, sa), pb = __shfl_sync(0xffffffffu, off1, sb);
+    const float pc = __shfl_sync(0xffffffffu, off2, sa), pd = __shfl_sync(0xffffffffu, off2, sb);
+    const uint32_t PA[4] = {gid < 6 ? split_pack<false>(pa, pb, pq) : 0u, 0u,
+                            gid < 6 ? split_pack<false>(pc, pd, pq) : 0u, 0u};
+    // ---- O += P V ----
+    const int mi = lane >> 3, r = lane & 7;
+    const int tok = r + 8 * (mi & 1);
+#pragma unroll
+    for (int mt = 0; mt < 8; mt++) {
+      const int c = 2 * mt + (mi >> 1);
+      const char *addr = pg_v + (c >> 3) * 2048 + tok * 128 + (((c & 7) ^ r) << 4);
+      uint32_t vb[4];
+      ldsm_x4_trans(vb, addr);
+      mma_bf16(oacc[2 * mt], PA, vb[0], vb[1]);
+      mma_bf16(oacc[2 * mt + 1], PA, vb[2], vb[3]);
+    }
+    // the warp is done with the buffer: refill it with stream position ctr + NB
+    __syncwarp();
+    if (lane == 0 && (tgt < n || tgt - n < nx_n)) {
+      fence_proxy_async_smem();
+      attn_issue_pg(a, refill_page, tgt < n ? it.g : nx.g, ctr + NB, kc, smem_base);
+      atomicMax(&kc.att_issued, ctr + NB + 1u);
+    }
+  }
+  // ---- the warp's per-head states ----
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) l_w[h] += __shfl_xor_sync(0xffffffffu, l_w[h], o);
+#pragma unroll
+  for (int m = 0; m < 16; m++)
+#pragma unroll
+    for (int e = 0; e < 2; e++) {   // the three parts of each head (rows h, h + 2, h + 4; h + 6 is zero)
+      oacc[m][e] += __shfl_xor_sync(0xffffffffu, oacc[m][e], 8);
+      oacc[m][e] += __shfl_xor_sync(0xffffffffu, oacc[m][e], 16);
+    }
+  if (gid < 2) {
+    float *dst = s_acc + (warp * 2 + gid) * HD;
+#pragma unroll
+    for (int m = 0; m < 16; m++) *reinterpret_cast<float2 *>(dst + 8 * m + 2 * tig) = make_float2(oacc[m][0], oacc[m][1]);
+  }
+  if (lane < 2) {
+    s_ml[(warp * 2 + lane) * 2] = m_w[lane];
+    s_ml[(warp * 2 + lane) * 2 + 1] = l_w[lane];
+  }
+  return ok;
+}
+
 __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_base, KCtx &kc) {
   char *smem = smem_base + SM_X_OFF;
-  AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem);
+  AttnSmem *sm = attn_sm(a, smem_base);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NB = a.nbuf;
 
@@ -2957,320 +3142,337 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
     }
 
     // ---- main loop over this split's pages ----
-    // Warp w handles head h = w & 1 of the item's pages i = w / 2 (mod 4), so
-    // four pages are in work at once, each by the two warps of its GQA group;
-    // every warp keeps its own online softmax (running max m, sum l, output
-    // dims 4 lane .. 4 lane + 3), combined across warps in warp order at the
-    // end.  The split of pages among warps depends on the item alone, so the
-    // result does not depend on which CTA ran it.  Page i sits in ring buffer
-    // (stream position) % NB; once both warps of the pair are done with a
-    // buffer (named barrier per pair) the head-0 warp refills it with stream
-    // position + NB (this item's page i + NB, or a page of the next item).
     const int n = p_end - p_begin;
     const int tid = threadIdx.x;
-    const int h = warp & 1, pw = warp >> 1;
-    const int t = lane & 15, half = lane >> 4;
-    float m_w = -INFINITY, l_w = 0.f, acc4[4] = {0.f, 0.f, 0.f, 0.f};
-    // With 16 buffers a pair takes two of its pages per step (i and i + 4):
-    // the two pages' dot products and P.V run as independent chains and share
-    // one softmax update; with 4 buffers (small batches) one page per step.
-    float acc4b[4] = {0.f, 0.f, 0.f, 0.f};
-    if (NB >= 2 * (NWARPS / 2)) {
-      for (int i = pw; i < n; i += 2 * (NWARPS / 2)) {
-        const int i2 = i + NWARPS / 2;
-        const bool two = i2 < n;
-        const unsigned ctr = kc.page_ctr + i, ctr2 = ctr + NWARPS / 2;
-        const int buf = ctr % NB, buf2 = ctr2 % NB;
-        // every lane observes the phase flips, which makes the bulk-copied bytes
-        // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
-        // so a timeout ends both warps' loops at the same page
-        bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
-        if (two) landed = mbar_wait(kc.bars + buf2, (ctr2 / NB) & 1u, WAIT_LIMIT_CYCLES) && landed;
-        if (!bar_and_n(1 + pw, 64, landed)) {
-          if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-          break;
-        }
-        uint16_t *kb = att_buf(smem_base, buf);
-        uint16_t *vb = kb + PAGE * HD;
-        uint16_t *kb2 = att_buf(smem_base, buf2);
-        uint16_t *vb2 = kb2 + PAGE * HD;
-        const int ntok = min(PAGE, L - (p_begin + i) * PAGE);
-        const int ntok2 = two ? min(PAGE, L - (p_begin + i2) * PAGE) : 0;
-        if (owns_new && (p_begin + i == npages - 1 || (two && p_begin + i2 == npages - 1))) {
-          // the newest token comes from shared memory, not from the copy (both
-          // warps of the page write the same bytes)
-          const int slot = pos % PAGE;
-          uint16_t *kp = (p_begin + i == npages - 1) ? kb : kb2;
-          uint16_t *vp = kp + PAGE * HD;
-          *reinterpret_cast<uint2 *>(kp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
-          *reinterpret_cast<uint2 *>(vp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
-          __syncwarp();
-        }
-        // the pages that will reuse these buffers: their indices are loaded
-        // now, so the refills at the end of the step do not wait for them
-        int refill_page = -1, refill_page2 = -1;
-        if (h == 0 && lane == 0) {
-          const int tgt = i + NB, tgt2 = i2 + NB;
-          if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
-          else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
-          if (two) {
-            if (tgt2 < n) refill_page2 = __ldg(pt + p_begin + tgt2);
-            else if (tgt2 - n < nx_n) refill_page2 = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt2 - n));
+    const int hh = tid >> 7, d = tid & 127;
+    float Mh = -INFINITY, Lh = 0.f, acc = 0.f;
+    if (a.tc) {
+      // tensor-core pages: per-warp states of both heads, combined in warp order
+      float *s_acc = reinterpret_cast<float *>(smem_base + ATT_TC_COMB_OFF);   // [NWARPS][2][HD]
+      float *s_ml = s_acc + NWARPS * 2 * HD;                                    // [NWARPS][2][2]
+      attn_pages_tc(a, it, nx, nx_n, owns_new, kc, smem_base, sm, s_acc, s_ml);
+      if (__syncthreads_or(kc.local_err)) return;   // copies still in flight are drained on the way out
+      if (tid == 0) kc.page_ctr += n;
+#pragma unroll
+      for (int w = 0; w < NWARPS; w++) Mh = fmaxf(Mh, s_ml[(w * 2 + hh) * 2]);
+#pragma unroll
+      for (int w = 0; w < NWARPS; w++) {
+        const float mw = s_ml[(w * 2 + hh) * 2];
+        const float e = (mw == -INFINITY) ? 0.f : expf(mw - Mh);
+        Lh += s_ml[(w * 2 + hh) * 2 + 1] * e;
+        acc += s_acc[(w * 2 + hh) * HD + d] * e;
+      }
+    } else {
+      // Warp w handles head h = w & 1 of the item's pages i = w / 2 (mod 4), so
+      // four pages are in work at once, each by the two warps of its GQA group;
+      // every warp keeps its own online softmax (running max m, sum l, output
+      // dims 4 lane .. 4 lane + 3), combined across warps in warp order at the
+      // end.  The split of pages among warps depends on the item alone, so the
+      // result does not depend on which CTA ran it.  Page i sits in ring buffer
+      // (stream position) % NB; once both warps of the pair are done with a
+      // buffer (named barrier per pair) the head-0 warp refills it with stream
+      // position + NB (this item's page i + NB, or a page of the next item).
+      const int h = warp & 1, pw = warp >> 1;
+      const int t = lane & 15, half = lane >> 4;
+      float m_w = -INFINITY, l_w = 0.f, acc4[4] = {0.f, 0.f, 0.f, 0.f};
+      // With 16 buffers a pair takes two of its pages per step (i and i + 4):
+      // the two pages' dot products and P.V run as independent chains and share
+      // one softmax update; with 4 buffers (small batches) one page per step.
+      float acc4b[4] = {0.f, 0.f, 0.f, 0.f};
+      if (NB >= 2 * (NWARPS / 2)) {
+        for (int i = pw; i < n; i += 2 * (NWARPS / 2)) {
+          const int i2 = i + NWARPS / 2;
+          const bool two = i2 < n;
+          const unsigned ctr = kc.page_ctr + i, ctr2 = ctr + NWARPS / 2;
+          const int buf = ctr % NB, buf2 = ctr2 % NB;
+          // every lane observes the phase flips, which makes the bulk-copied bytes
+          // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
+          // so a timeout ends both warps' loops at the same page
+          bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+          if (two) landed = mbar_wait(kc.bars + buf2, (ctr2 / NB) & 1u, WAIT_LIMIT_CYCLES) && landed;
+          if (!bar_and_n(1 + pw, 64, landed)) {
+            if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+            break;
           }
-        }
-        // scores of both pages, as in the one-page loop; the q reads are shared
-        const float *qh = sm->q[h] + half * 64;
-        float sdot, sdot2 = 0.f;
-        {
-          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-          const uint16_t *kr = kb + t * HD + half * 64;
-          if (two) {
-            float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
-            const uint16_t *kr2 = kb2 + t * HD + half * 64;
-  #pragma unroll
-            for (int jj = 0; jj < 8; jj++) {
-              const int jq = (jj + t) & 7;
-              const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
-              const uint4 k2 = *reinterpret_cast<const uint4 *>(kr2 + 8 * jq);
-              const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
-              const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
-              s0 = fmaf(qa.x, bf16lo(kk.x), s0);
-              s1 = fmaf(qa.y, bf16hi(kk.x), s1);
-              s2 = fmaf(qa.z, bf16lo(kk.y), s2);
-              s3 = fmaf(qa.w, bf16hi(kk.y), s3);
-              u0 = fmaf(qa.x, bf16lo(k2.x), u0);
-              u1 = fmaf(qa.y, bf16hi(k2.x), u1);
-              u2 = fmaf(qa.z, bf16lo(k2.y), u2);
-              u3 = fmaf(qa.w, bf16hi(k2.y), u3);
-              s0 = fmaf(qb.x, bf16lo(kk.z), s0);
-              s1 = fmaf(qb.y, bf16hi(kk.z), s1);
-              s2 = fmaf(qb.z, bf16lo(kk.w), s2);
-              s3 = fmaf(qb.w, bf16hi(kk.w), s3);
-              u0 = fmaf(qb.x, bf16lo(k2.z), u0);
-              u1 = fmaf(qb.y, bf16hi(k2.z), u1);
-              u2 = fmaf(qb.z, bf16lo(k2.w), u2);
-              u3 = fmaf(qb.w, bf16hi(k2.w), u3);
-            }
-            sdot2 = (u0 + u1) + (u2 + u3);
-          } else {
-  #pragma unroll
-            for (int jj = 0; jj < 8; jj++) {
-              const int jq = (jj + t) & 7;
-              const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
-              const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
-              const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
-              s0 = fmaf(qa.x, bf16lo(kk.x), s0);
-              s1 = fmaf(qa.y, bf16hi(kk.x), s1);
-              s2 = fmaf(qa.z, bf16lo(kk.y), s2);
-              s3 = fmaf(qa.w, bf16hi(kk.y), s3);
-              s0 = fmaf(qb.x, bf16lo(kk.z), s0);
-              s1 = fmaf(qb.y, bf16hi(kk.z), s1);
-              s2 = fmaf(qb.z, bf16lo(kk.w), s2);
-              s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+          uint16_t *kb = att_buf(smem_base, buf);
+          uint16_t *vb = kb + PAGE * HD;
+          uint16_t *kb2 = att_buf(smem_base, buf2);
+          uint16_t *vb2 = kb2 + PAGE * HD;
+          const int ntok = min(PAGE, L - (p_begin + i) * PAGE);
+          const int ntok2 = two ? min(PAGE, L - (p_begin + i2) * PAGE) : 0;
+          if (owns_new && (p_begin + i == npages - 1 || (two && p_begin + i2 == npages - 1))) {
+            // the newest token comes from shared memory, not from the copy (both
+            // warps of the page write the same bytes)
+            const int slot = pos % PAGE;
+            uint16_t *kp = (p_begin + i == npages - 1) ? kb : kb2;
+            uint16_t *vp = kp + PAGE * HD;
+            *reinterpret_cast<uint2 *>(kp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
+            *reinterpret_cast<uint2 *>(vp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
+            __syncwarp();
+          }
+          // the pages that will reuse these buffers: their indices are loaded
+          // now, so the refills at the end of the step do not wait for them
+          int refill_page = -1, refill_page2 = -1;
+          if (h == 0 && lane == 0) {
+            const int tgt = i + NB, tgt2 = i2 + NB;
+            if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
+            else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+            if (two) {
+              if (tgt2 < n) refill_page2 = __ldg(pt + p_begin + tgt2);
+              else if (tgt2 - n < nx_n) refill_page2 = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt2 - n));
             }
           }
-          sdot = (s0 + s1) + (s2 + s3);
-        }
-        sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
-        sdot2 += __shfl_xor_sync(0xffffffffu, sdot2, 16);
-        const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
-        const float sc2 = (t < ntok2) ? sdot2 * a.scale : -INFINITY;
-        float mx = fmaxf(sc, sc2);
-  #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        const float m_new = fmaxf(m_w, mx);
-        const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
-        const float pr2 = (t < ntok2) ? expf(sc2 - m_new) : 0.f;
-        const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
-        l_w = l_w * corr + (pr + pr2);   // this lane's token shares; summed over the lanes after the loop
-        m_w = m_new;
-  #pragma unroll
-        for (int e = 0; e < 4; e++) {
-          acc4[e] *= corr;
-          acc4b[e] *= corr;
-        }
-        // slots past the sequence end hold whatever the pool has there: skip them
-        if (ntok == PAGE && ntok2 == PAGE) {
-  #pragma unroll
-          for (int tt = 0; tt < PAGE; tt++) {
-            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-            const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
-            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-            const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
-            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
-            acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
-            acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
-            acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
-            acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
+          // scores of both pages, as in the one-page loop; the q reads are shared
+          const float *qh = sm->q[h] + half * 64;
+          float sdot, sdot2 = 0.f;
+          {
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+            const uint16_t *kr = kb + t * HD + half * 64;
+            if (two) {
+              float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
+              const uint16_t *kr2 = kb2 + t * HD + half * 64;
+    #pragma unroll
+              for (int jj = 0; jj < 8; jj++) {
+                const int jq = (jj + t) & 7;
+                const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+                const uint4 k2 = *reinterpret_cast<const uint4 *>(kr2 + 8 * jq);
+                const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+                const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+                s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+                s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+                s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+                s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+                u0 = fmaf(qa.x, bf16lo(k2.x), u0);
+                u1 = fmaf(qa.y, bf16hi(k2.x), u1);
+                u2 = fmaf(qa.z, bf16lo(k2.y), u2);
+                u3 = fmaf(qa.w, bf16hi(k2.y), u3);
+                s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+                s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+                s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+                s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+                u0 = fmaf(qb.x, bf16lo(k2.z), u0);
+                u1 = fmaf(qb.y, bf16hi(k2.z), u1);
+                u2 = fmaf(qb.z, bf16lo(k2.w), u2);
+                u3 = fmaf(qb.w, bf16hi(k2.w), u3);
+              }
+              sdot2 = (u0 + u1) + (u2 + u3);
+            } else {
+    #pragma unroll
+              for (int jj = 0; jj < 8; jj++) {
+                const int jq = (jj + t) & 7;
+                const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+                const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+                const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+                s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+                s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+                s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+                s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+                s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+                s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+                s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+                s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+              }
+            }
+            sdot = (s0 + s1) + (s2 + s3);
           }
-        } else if (ntok == PAGE && ntok2 == 0) {
-  #pragma unroll
-          for (int tt = 0; tt < PAGE; tt++) {
-            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+          sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+          sdot2 += __shfl_xor_sync(0xffffffffu, sdot2, 16);
+          const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
+          const float sc2 = (t < ntok2) ? sdot2 * a.scale : -INFINITY;
+          float mx = fmaxf(sc, sc2);
+    #pragma unroll
+          for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          const float m_new = fmaxf(m_w, mx);
+          const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
+          const float pr2 = (t < ntok2) ? expf(sc2 - m_new) : 0.f;
+          const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
+          l_w = l_w * corr + (pr + pr2);   // this lane's token shares; summed over the lanes after the loop
+          m_w = m_new;
+    #pragma unroll
+          for (int e = 0; e < 4; e++) {
+            acc4[e] *= corr;
+            acc4b[e] *= corr;
           }
-        } else {
-          for (int tt = 0; tt < PAGE; tt++) {
-            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-            const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
-            if (tt < ntok) {
+          // slots past the sequence end hold whatever the pool has there: skip them
+          if (ntok == PAGE && ntok2 == PAGE) {
+    #pragma unroll
+            for (int tt = 0; tt < PAGE; tt++) {
+              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+              const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
+              const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+              const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
+              acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+              acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+              acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+              acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+              acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
+              acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
+              acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
+              acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
+            }
+          } else if (ntok == PAGE && ntok2 == 0) {
+    #pragma unroll
+            for (int tt = 0; tt < PAGE; tt++) {
+              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
               const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
               acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
               acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
               acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
               acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
             }
-            if (tt < ntok2) {
-              const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
-              acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
-              acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
-              acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
-              acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
+          } else {
+            for (int tt = 0; tt < PAGE; tt++) {
+              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+              const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
+              if (tt < ntok) {
+                const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+                acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+                acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+                acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+                acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+              }
+              if (tt < ntok2) {
+                const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
+                acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
+                acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
+                acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
+                acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
+              }
             }
           }
-        }
-        // both warps of the pair are done with the buffers: the head-0 warp
-        // refills each with its stream position + NB
-        bar_sync_n(1 + pw, 64);
-        if (h == 0 && lane == 0) {
-          const int tgt = i + NB, tgt2 = i2 + NB;   // item-relative; >= n: the next item's page tgt - n
-          const bool r1 = tgt < n || tgt - n < nx_n;
-          const bool r2 = two && (tgt2 < n || tgt2 - n < nx_n);
-          if (r1 || r2) fence_proxy_async_smem();
-          if (r1) attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
-          if (r2) attn_issue_pg(a, refill_page2, tgt2 < n ? g : nx.g, ctr2 + NB, kc, smem_base);
-          if (r1 || r2) atomicMax(&kc.att_issued, (r2 ? ctr2 : ctr) + NB + 1u);
-        }
-      }
-    } else {
-      for (int i = pw; i < n; i += NWARPS / 2) {
-        const unsigned ctr = kc.page_ctr + i;
-        const int buf = ctr % NB;
-        // every lane observes the phase flip, which makes the bulk-copied bytes
-        // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
-        // so a timeout ends both warps' loops at the same page
-        const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
-        if (!bar_and_n(1 + pw, 64, landed)) {
-          if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-          break;
-        }
-        uint16_t *kb = att_buf(smem_base, buf);
-        uint16_t *vb = kb + PAGE * HD;
-        const int pg = p_begin + i;
-        const int ntok = min(PAGE, L - pg * PAGE);
-        if (pg == npages - 1 && owns_new) {
-          // the newest token comes from shared memory, not from the copy (both
-          // warps of the page write the same bytes)
-          const int slot = pos % PAGE;
-          *reinterpret_cast<uint2 *>(kb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
-          *reinterpret_cast<uint2 *>(vb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
-          __syncwarp();
-        }
-        // the page that will reuse this buffer: its index is loaded now, so
-        // the refill at the end of the page does not wait for it
-        int refill_page = -1;
-        if (h == 0 && lane == 0) {
-          const int tgt = i + NB;
-          if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
-          else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
-        }
-        // score of token t: lanes t and t + 16 each take half of the 128 dims
-        // in 16-byte groups, walking them from a token-dependent start so each
-        // 8-lane phase of a 16-byte read hits 8 distinct bank groups; four
-        // partial sums
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        const float *qh = sm->q[h] + half * 64;
-        const uint16_t *kr = kb + t * HD + half * 64;
-  #pragma unroll
-        for (int jj = 0; jj < 8; jj++) {
-          const int jq = (jj + t) & 7;
-          const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
-          const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
-          const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
-          s0 = fmaf(qa.x, bf16lo(kk.x), s0);
-          s1 = fmaf(qa.y, bf16hi(kk.x), s1);
-          s2 = fmaf(qa.z, bf16lo(kk.y), s2);
-          s3 = fmaf(qa.w, bf16hi(kk.y), s3);
-          s0 = fmaf(qb.x, bf16lo(kk.z), s0);
-          s1 = fmaf(qb.y, bf16hi(kk.z), s1);
-          s2 = fmaf(qb.z, bf16lo(kk.w), s2);
-          s3 = fmaf(qb.w, bf16hi(kk.w), s3);
-        }
-        float sdot = (s0 + s1) + (s2 + s3);
-        sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
-        const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
-        float mx = sc;
-  #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        const float m_new = fmaxf(m_w, mx);
-        const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
-        const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
-        l_w = l_w * corr + pr;   // this lane's token share; summed over the lanes after the loop
-        m_w = m_new;
-  #pragma unroll
-        for (int e = 0; e < 4; e++) acc4[e] *= corr;
-        // slots past the sequence end hold whatever the pool has there: skip them
-        if (ntok == PAGE) {
-  #pragma unroll
-          for (int tt = 0; tt < PAGE; tt++) {
-            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
-          }
-        } else {
-          for (int tt = 0; tt < ntok; tt++) {
-            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+          // both warps of the pair are done with the buffers: the head-0 warp
+          // refills each with its stream position + NB
+          bar_sync_n(1 + pw, 64);
+          if (h == 0 && lane == 0) {
+            const int tgt = i + NB, tgt2 = i2 + NB;   // item-relative; >= n: the next item's page tgt - n
+            const bool r1 = tgt < n || tgt - n < nx_n;
+            const bool r2 = two && (tgt2 < n || tgt2 - n < nx_n);
+            if (r1 || r2) fence_proxy_async_smem();
+            if (r1) attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
+            if (r2) attn_issue_pg(a, refill_page2, tgt2 < n ? g : nx.g, ctr2 + NB, kc, smem_base);
+            if (r1 || r2) atomicMax(&kc.att_issued, (r2 ? ctr2 : ctr) + NB + 1u);
           }
         }
-        // both warps of the pair are done with the buffer: the head-0 warp
-        // refills it with stream position ctr + NB
-        bar_sync_n(1 + pw, 64);
-        const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
-        if (h == 0 && lane == 0 && (tgt < n || tgt - n < nx_n)) {
-          fence_proxy_async_smem();
-          attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
-          atomicMax(&kc.att_issued, ctr + NB + 1u);
+      } else {
+        for (int i = pw; i < n; i += NWARPS / 2) {
+          const unsigned ctr = kc.page_ctr + i;
+          const int buf = ctr % NB;
+          // every lane observes the phase flip, which makes the bulk-copied bytes
+          // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
+          // so a timeout ends both warps' loops at the same page
+          const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+          if (!bar_and_n(1 + pw, 64, landed)) {
+            if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+            break;
+          }
+          uint16_t *kb = att_buf(smem_base, buf);
+          uint16_t *vb = kb + PAGE * HD;
+          const int pg = p_begin + i;
+          const int ntok = min(PAGE, L - pg * PAGE);
+          if (pg == npages - 1 && owns_new) {
+            // the newest token comes from shared memory, not from the copy (both
+            // warps of the page write the same bytes)
+            const int slot = pos % PAGE;
+            *reinterpret_cast<uint2 *>(kb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
+            *reinterpret_cast<uint2 *>(vb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
+            __syncwarp();
+          }
+          // the page that will reuse this buffer: its index is loaded now, so
+          // the refill at the end of the page does not wait for it
+          int refill_page = -1;
+          if (h == 0 && lane == 0) {
+            const int tgt = i + NB;
+            if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
+            else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+          }
+          // score of token t: lanes t and t + 16 each take half of the 128 dims
+          // in 16-byte groups, walking them from a token-dependent start so each
+          // 8-lane phase of a 16-byte read hits 8 distinct bank groups; four
+          // partial sums
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+          const float *qh = sm->q[h] + half * 64;
+          const uint16_t *kr = kb + t * HD + half * 64;
+    #pragma unroll
+          for (int jj = 0; jj < 8; jj++) {
+            const int jq = (jj + t) & 7;
+            const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+            const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+            const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+            s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+            s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+            s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+            s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+            s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+            s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+            s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+            s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+          }
+          float sdot = (s0 + s1) + (s2 + s3);
+          sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+          const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
+          float mx = sc;
+    #pragma unroll
+          for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          const float m_new = fmaxf(m_w, mx);
+          const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
+          const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
+          l_w = l_w * corr + pr;   // this lane's token share; summed over the lanes after the loop
+          m_w = m_new;
+    #pragma unroll
+          for (int e = 0; e < 4; e++) acc4[e] *= corr;
+          // slots past the sequence end hold whatever the pool has there: skip them
+          if (ntok == PAGE) {
+    #pragma unroll
+            for (int tt = 0; tt < PAGE; tt++) {
+              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+              const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+              acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+              acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+              acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+              acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+            }
+          } else {
+            for (int tt = 0; tt < ntok; tt++) {
+              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+              const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+              acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+              acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+              acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+              acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+            }
+          }
+          // both warps of the pair are done with the buffer: the head-0 warp
+          // refills it with stream position ctr + NB
+          bar_sync_n(1 + pw, 64);
+          const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
+          if (h == 0 && lane == 0 && (tgt < n || tgt - n < nx_n)) {
+            fence_proxy_async_smem();
+            attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
+            atomicMax(&kc.att_issued, ctr + NB + 1u);
+          }
         }
       }
-    }
-#pragma unroll
-    for (int e = 0; e < 4; e++) acc4[e] += acc4b[e];
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) l_w += __shfl_xor_sync(0xffffffffu, l_w, o);
-    // per-warp states -> per-head totals, in warp order
-    float *s_acc = reinterpret_cast<float *>(smem + ATT_COMB_OFF);   // [NWARPS][HD]
-    float *s_ml = s_acc + NWARPS * HD;                                // [NWARPS][2]
-    *reinterpret_cast<float4 *>(s_acc + warp * HD + 4 * lane) = make_float4(acc4[0], acc4[1], acc4[2], acc4[3]);
-    if (lane == 0) { s_ml[2 * warp] = m_w; s_ml[2 * warp + 1] = l_w; }
-    if (__syncthreads_or(kc.local_err)) return;   // copies still in flight are drained on the way out
-    if (tid == 0) kc.page_ctr += n;
-    const int hh = tid >> 7, d = tid & 127;
-    float Mh = -INFINITY;
-#pragma unroll
-    for (int q = 0; q < NWARPS / 2; q++) Mh = fmaxf(Mh, s_ml[2 * (2 * q + hh)]);
-    float Lh = 0.f, acc = 0.f;
-#pragma unroll
-    for (int q = 0; q < NWARPS / 2; q++) {
-      const int w = 2 * q + hh;
-      const float mw = s_ml[2 * w];
-      const float e = (mw == -INFINITY) ? 0.f : expf(mw - Mh);
-      Lh += s_ml[2 * w + 1] * e;
-      acc += s_acc[w * HD + d] * e;
+  #pragma unroll
+      for (int e = 0; e < 4; e++) acc4[e] += acc4b[e];
+  #pragma unroll
+      for (int o = 8; o > 0; o >>= 1) l_w += __shfl_xor_sync(0xffffffffu, l_w, o);
+      // per-warp states -> per-head totals, in warp order
+      float *s_acc = reinterpret_cast<float *>(smem + ATT_COMB_OFF);   // [NWARPS][HD]
+      float *s_ml = s_acc + NWARPS * HD;                                // [NWARPS][2]
+      *reinterpret_cast<float4 *>(s_acc + warp * HD + 4 * lane) = make_float4(acc4[0], acc4[1], acc4[2], acc4[3]);
+      if (lane == 0) { s_ml[2 * warp] = m_w; s_ml[2 * warp + 1] = l_w; }
+      if (__syncthreads_or(kc.local_err)) return;   // copies still in flight are drained on the way out
+      if (tid == 0) kc.page_ctr += n;
+  #pragma unroll
+      for (int q = 0; q < NWARPS / 2; q++) Mh = fmaxf(Mh, s_ml[2 * (2 * q + hh)]);
+  #pragma unroll
+      for (int q = 0; q < NWARPS / 2; q++) {
+        const int w = 2 * q + hh;
+        const float mw = s_ml[2 * w];
+        const float e = (mw == -INFINITY) ? 0.f : expf(mw - Mh);
+        Lh += s_ml[2 * w + 1] * e;
+        acc += s_acc[w * HD + d] * e;
+      }
     }
     ckpt(kc, 2);
 

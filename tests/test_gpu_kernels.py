@@ -117,6 +117,35 @@ def test_attention_append_matches_oracle(have_gpu, pos, max_splits):
                 assert np.array_equal(vp[page, :, slot], vp0[page, :, slot])
 
 
+def test_attention_tensor_cores_match_cuda_cores(have_gpu, monkeypatch):
+    """Batch >= 8 decode attention runs its pages on the tensor cores (bf16 MMA,
+    q and p as three bf16 parts, pages copied as swizzled TMA boxes); the
+    CUDA-core page loop (QTB_ATTN_TC=0) gives the same outputs to f32 rounding
+    and the same appended K/V bytes.  64 slots, lengths across page edges,
+    splits in dynamic order."""
+    rng = np.random.default_rng(91)
+    pos = [15, 16, 17, 31, 32, 0, 1, 4095] + [int(v) for v in rng.integers(0, 3000, 56)]
+    B, nh, nkv, hd, eps = len(pos), 16, 8, 128, 1e-6
+    n_pages = sum(p // 16 + 1 for p in pos) + 3
+    qkv, kp, vp, pt, qn, kn, cs, sn = make_attention_case(rng, B, pos, n_pages)
+    outs, pools = {}, {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("QTB_ATTN_TC", mode)
+        k2, v2 = kp.copy(), vp.copy()
+        outs[mode] = Q.attention(qkv, nh, nkv, qn, kn, eps, cs, sn, k2, v2, pt, np.array(pos, np.int32), 16)
+        pools[mode] = (k2, v2)
+    assert np.array_equal(pools["1"][0], pools["0"][0]) and np.array_equal(pools["1"][1], pools["0"][1])
+    for b in range(B):
+        assert rel_l2(outs["1"][b], outs["0"][b]) < 1e-5, (b, pos[b], rel_l2(outs["1"][b], outs["0"][b]))
+    # and against the restatement for a few slots
+    for b in (0, 1, 7, 20):
+        p = pos[b]
+        q = O.rope_neox(O.rms_norm_per_head(qkv[b, :nh * hd], qn, nh, hd, eps), nh, hd, cs, sn, p)
+        K, V = O.gather_pages(pools["1"][0], pools["1"][1], pt[b], p + 1)
+        ref = O.attention_bf16kv(q, K, V, nh, nkv, hd, p + 1)
+        assert rel_l2(outs["1"][b], ref) < 1e-5, (b, rel_l2(outs["1"][b], ref))
+
+
 @pytest.mark.parametrize("scale", [1.0, 300.0, 1e-3])
 def test_kv_append_bit_exact_vs_reference(have_gpu, scale):
     """Identical f32 q/k/v rows into the reference's own K/V append (its
