@@ -1015,7 +1015,9 @@ struct ProgBuilder {
     // large-batch decode attention on the tensor cores (needs the 16 page
     // buffers of a program without small-batch GEMV stages: upload_prog
     // turns it off otherwise); QTB_ATTN_TC=0 keeps the CUDA-core loop
-    a.tc = (mode == ATT_DECODE && B >= 8 && b.kmap && attn_tc_enabled()) ? 1 : 0;
+    // (not the code predictor's: its items are one page of at most 16
+    // positions, where the per-item set-up outweighs the page loop)
+    a.tc = (mode == ATT_DECODE && B >= 8 && b.kmap && &k != &s->e->cp && attn_tc_enabled()) ? 1 : 0;
     attn_schedule(a, B, grid());
     if (mode == ATT_ATTEND) a.dyn = 0;   // static item order (attn_prefill_stage)
     st.push_back(S);

@@ -2868,18 +2868,20 @@ QTB_CALL void attn_prefetch(const AttnArgs &a, int B, KCtx &kc, char *smem) {
 }
 
 // Tensor-core pages of one decode attention item (large batches).  Warp w
-// takes the item's pages w, w + 8, ... with both query heads of the GQA group
-// at once, on the bf16 MMA (m16n8k16, f32 accumulate):
+// takes the item's pages w, w + 16, ... and w + 8, w + 24, ..., two per step
+// (independent chains sharing one softmax update), with both query heads of
+// the GQA group at once, on the bf16 MMA (m16n8k16, f32 accumulate):
 //  - scores S[16 tokens x 8] = K[16 x 128] q^T, the 8 MMA columns being
 //    (part p, head h) = 2 p + h: q carried as three bf16 parts (24 bits).  The
 //    K rows come from the swizzled page (lane: row gid, 16-byte chunk 2 tig +
 //    (j & 1) of box j >> 1 per step pair j; the MMA's k order follows that
-//    dimension order, and q's fragments use the same one);
-//  - the online softmax of each head over the page's tokens (reference
-//    recurrence of qwen_causal_attention_bf16kv, per page);
-//  - O[(p, h) x 128] += P[(p, h) x 16 tokens] V: P's rows are the three bf16
-//    parts of the f32 probabilities, V's fragments come from ldmatrix.trans
-//    on the swizzled page (conflict-free).
+//    dimension order, and q's fragments use the same one), in two chains;
+//  - the online softmax of each head over the pages' tokens (reference
+//    recurrence of qwen_causal_attention_bf16kv, per step);
+//  - O^T[128 x (p, h)] += V^T[128 x 16 tokens] P^T: A = V^T from
+//    ldmatrix.trans on the swizzled V box (conflict-free), B = the three bf16
+//    parts of the f32 probabilities, rebuilt from the score layout with four
+//    shuffles; all four accumulator registers of a tile are used.
 // The warp's per-head state (max, sum, 128 outputs) goes to s_acc / s_ml
 // ([NWARPS][2][HD], [NWARPS][2][2]).  Returns false after a failed wait.
 __device__ __noinline__ bool attn_pages_tc(const AttnArgs &a, const AttnItem &it, const AttnItem &nx, int nx_n,
@@ -2899,39 +2901,15 @@ __device__ __noinline__ bool attn_pages_tc(const AttnArgs &a, const AttnItem &it
     for (int u = 0; u < 4; u++) qf[j][u] = gid < 6 ? split_pack<false>(q[2 * u], q[2 * u + 1], pq) : 0u;
   }
   float m_w[2] = {-INFINITY, -INFINITY}, l_w[2] = {0.f, 0.f};
-  float oacc[16][4];
+  // O^T tile m: dims 16 m + gid (0, 1) and 16 m + gid + 8 (2, 3), columns
+  // (part tig, head 0 / 1)
+  float oacc[8][4];
 #pragma unroll
-  for (int m = 0; m < 16; m++) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
+  for (int m = 0; m < 8; m++) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
   bool ok = true;
-  for (int i = warp; i < n; i += NWARPS) {
-    const unsigned ctr = kc.page_ctr + i;
-    const int buf = ctr % NB;
-    const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
-    if (!__all_sync(0xffffffffu, landed)) {
-      if (lane == 0) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-      ok = false;
-      break;
-    }
-    char *pg_k = att_tc_buf(smem_base, buf);
-    const char *pg_v = pg_k + 4096;
-    const int pg = it.p_begin + i;
-    const int ntok = min(PAGE, it.L - pg * PAGE);
-    if (owns_new && pg == it.npages - 1) {
-      // the newest token comes from shared memory (its copy may predate the append)
-      const int row = it.pos % PAGE, c = lane & 15;
-      const uint16_t *src = (lane < 16 ? sm->knew : sm->vnew) + c * 8;
-      char *dst = pg_k + (lane < 16 ? 0 : 4096) + (c >> 3) * 2048 + row * 128 + (((c & 7) ^ (row & 7)) << 4);
-      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
-      __syncwarp();
-    }
-    int refill_page = -1;
-    const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
-    if (lane == 0) {
-      if (tgt < n) refill_page = __ldg(pt + it.p_begin + tgt);
-      else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
-    }
-    // ---- scores ----
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+  // the scores of one page: two independent chains (dims 0-63, 64-127), parts summed
+  auto scores = [&](const char *pg_k, float (&sc)[4]) {
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const char *kb = pg_k + (j >> 1) * 2048;
@@ -2939,59 +2917,128 @@ __device__ __noinline__ bool attn_pages_tc(const AttnArgs &a, const AttnItem &it
       const uint4 w0 = *reinterpret_cast<const uint4 *>(kb + gid * 128 + cc);
       const uint4 w1 = *reinterpret_cast<const uint4 *>(kb + (gid + 8) * 128 + cc);
       const uint32_t A0[4] = {w0.x, w1.x, w0.y, w1.y};
-      mma_bf16(sc, A0, qf[j][0], qf[j][1]);
       const uint32_t A1[4] = {w0.z, w1.z, w0.w, w1.w};
-      mma_bf16(sc, A1, qf[j][2], qf[j][3]);
+      if (j < 2) {
+        mma_bf16(s0, A0, qf[j][0], qf[j][1]);
+        mma_bf16(s0, A1, qf[j][2], qf[j][3]);
+      } else {
+        mma_bf16(s1, A0, qf[j][0], qf[j][1]);
+        mma_bf16(s1, A1, qf[j][2], qf[j][3]);
+      }
     }
-    // sc: tokens gid (0, 1) and gid + 8 (2, 3), head e & 1, part tig: sum the parts
 #pragma unroll
     for (int e = 0; e < 4; e++) {
+      sc[e] = s0[e] + s1[e];
       sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 1);
       sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
     }
-    const bool v0 = gid < ntok, v1 = gid + 8 < ntok;
-    float pr[4], corr[2];
+  };
+  // P^T fragments (tokens x (part, head)) of one page from its probabilities
+  // in the score layout: lane (gid, tig) holds P[gid][2 tig, 2 tig + 1] in pb[0]
+  // and P[gid][2 tig + 8, 2 tig + 9] in pb[1]
+  auto pfrag = [&](const float (&pr)[4], uint32_t (&pb)[2]) {
+    const float off1 = (tig & 1) ? pr[1] : pr[0], off2 = (tig & 1) ? pr[3] : pr[2];
+    const int sa = (2 * tig) * 4 + hq, sb = (2 * tig + 1) * 4 + hq;
+    const float pa = __shfl_sync(0xffffffffu, off1, sa), p2 = __shfl_sync(0xffffffffu, off1, sb);
+    const float pc = __shfl_sync(0xffffffffu, off2, sa), pd = __shfl_sync(0xffffffffu, off2, sb);
+    pb[0] = gid < 6 ? split_pack<false>(pa, p2, pq) : 0u;
+    pb[1] = gid < 6 ? split_pack<false>(pc, pd, pq) : 0u;
+  };
+  // the newest token comes from shared memory (its copy may predate the append)
+  auto patch = [&](char *pg_k) {
+    const int row = it.pos % PAGE, c = lane & 15;
+    const uint16_t *src = (lane < 16 ? sm->knew : sm->vnew) + c * 8;
+    char *dst = pg_k + (lane < 16 ? 0 : 4096) + (c >> 3) * 2048 + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+    *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+    __syncwarp();
+  };
+  // Pages i and i + NWARPS per step: the two pages' chains are independent
+  // and share one softmax update.
+  for (int i = warp; i < n; i += 2 * NWARPS) {
+    const int i2 = i + NWARPS;
+    const bool two = i2 < n;
+    const unsigned ctr = kc.page_ctr + i, ctr2 = ctr + NWARPS;
+    const int buf = ctr % NB, buf2 = ctr2 % NB;
+    bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+    if (two) landed = mbar_wait(kc.bars + buf2, (ctr2 / NB) & 1u, WAIT_LIMIT_CYCLES) && landed;
+    if (!__all_sync(0xffffffffu, landed)) {
+      if (lane == 0) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+      ok = false;
+      break;
+    }
+    char *pk1 = att_tc_buf(smem_base, buf), *pk2 = att_tc_buf(smem_base, buf2);
+    const int pg = it.p_begin + i, pg2 = it.p_begin + i2;
+    const int ntok = min(PAGE, it.L - pg * PAGE), ntok2 = two ? min(PAGE, it.L - pg2 * PAGE) : 0;
+    if (owns_new && pg == it.npages - 1) patch(pk1);
+    if (owns_new && two && pg2 == it.npages - 1) patch(pk2);
+    int refill_page = -1, refill_page2 = -1;
+    const int tgt = i + NB, tgt2 = i2 + NB;   // item-relative; >= n: the next item's page tgt - n
+    if (lane == 0) {
+      if (tgt < n) refill_page = __ldg(pt + it.p_begin + tgt);
+      else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+      if (two) {
+        if (tgt2 < n) refill_page2 = __ldg(pt + it.p_begin + tgt2);
+        else if (tgt2 - n < nx_n)
+          refill_page2 = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt2 - n));
+      }
+    }
+    float sc1[4], sc2[4] = {0.f, 0.f, 0.f, 0.f};
+    scores(pk1, sc1);
+    if (two) scores(pk2, sc2);
+    // sc: tokens gid (e = 0, 1) and gid + 8 (e = 2, 3) of head e & 1
+    const bool va = gid < ntok, vb = gid + 8 < ntok, vc = gid < ntok2, vd = gid + 8 < ntok2;
+    float pr1[4], pr2[4], corr[2];
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-      const float s0 = v0 ? sc[h] * a.scale : -INFINITY, s1 = v1 ? sc[2 + h] * a.scale : -INFINITY;
-      float mx = fmaxf(s0, s1);
+      const float x0 = va ? sc1[h] * a.scale : -INFINITY, x1 = vb ? sc1[2 + h] * a.scale : -INFINITY;
+      const float y0 = vc ? sc2[h] * a.scale : -INFINITY, y1 = vd ? sc2[2 + h] * a.scale : -INFINITY;
+      float mx = fmaxf(fmaxf(x0, x1), fmaxf(y0, y1));
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float m_new = fmaxf(m_w[h], mx);   // finite: token 0 of every page is valid
       corr[h] = (m_w[h] == -INFINITY) ? 0.f : expf(m_w[h] - m_new);
-      pr[h] = v0 ? expf(s0 - m_new) : 0.f;
-      pr[2 + h] = v1 ? expf(s1 - m_new) : 0.f;
-      l_w[h] = l_w[h] * corr[h] + (pr[h] + pr[2 + h]);
+      pr1[h] = va ? expf(x0 - m_new) : 0.f;
+      pr1[2 + h] = vb ? expf(x1 - m_new) : 0.f;
+      pr2[h] = vc ? expf(y0 - m_new) : 0.f;
+      pr2[2 + h] = vd ? expf(y1 - m_new) : 0.f;
+      l_w[h] = l_w[h] * corr[h] + ((pr1[h] + pr1[2 + h]) + (pr2[h] + pr2[2 + h]));
       m_w[h] = m_new;
     }
-    const float cq = corr[hq];
 #pragma unroll
-    for (int m = 0; m < 16; m++) { oacc[m][0] *= cq; oacc[m][1] *= cq; }
-    // ---- P (rows (part, head), tokens) from the score layout ----
-    const float off1 = (tig & 1) ? pr[1] : pr[0], off2 = (tig & 1) ? pr[3] : pr[2];
-    const int sa = (2 * tig) * 4 + hq, sb = (2 * tig + 1) * 4 + hq;
-    const float pa = __shfl_sync(0xffffffffu, off1, sa), pb = __shfl_sync(0xffffffffu, off1, sb);
-    const float pc = __shfl_sync(0xffffffffu, off2, sa), pd = __shfl_sync(0xffffffffu, off2, sb);
-    const uint32_t PA[4] = {gid < 6 ? split_pack<false>(pa, pb, pq) : 0u, 0u,
-                            gid < 6 ? split_pack<false>(pc, pd, pq) : 0u, 0u};
-    // ---- O += P V ----
-    const int mi = lane >> 3, r = lane & 7;
-    const int tok = r + 8 * (mi & 1);
-#pragma unroll
-    for (int mt = 0; mt < 8; mt++) {
-      const int c = 2 * mt + (mi >> 1);
-      const char *addr = pg_v + (c >> 3) * 2048 + tok * 128 + (((c & 7) ^ r) << 4);
-      uint32_t vb[4];
-      ldsm_x4_trans(vb, addr);
-      mma_bf16(oacc[2 * mt], PA, vb[0], vb[1]);
-      mma_bf16(oacc[2 * mt + 1], PA, vb[2], vb[3]);
+    for (int m = 0; m < 8; m++) {
+      oacc[m][0] *= corr[0];
+      oacc[m][1] *= corr[1];
+      oacc[m][2] *= corr[0];
+      oacc[m][3] *= corr[1];
     }
-    // the warp is done with the buffer: refill it with stream position ctr + NB
+    uint32_t pb1[2], pb2[2];
+    pfrag(pr1, pb1);
+    pfrag(pr2, pb2);   // zeros for a missing second page
+    // ---- O^T += V^T P^T: A = V^T (ldmatrix.trans of the swizzled V box),
+    // B = P^T; matrix j of a tile: tokens 8 (j >> 1) .., dims 16 m + 8 (j & 1) ..
+    const int mj = lane >> 3, r = lane & 7;
+    const int tok = r + 8 * (mj >> 1);
+#pragma unroll
+    for (int m = 0; m < 8; m++) {
+      const int c = 2 * m + (mj & 1);
+      const int off = 4096 + (c >> 3) * 2048 + tok * 128 + (((c & 7) ^ r) << 4);
+      uint32_t va4[4];
+      ldsm_x4_trans(va4, pk1 + off);
+      mma_bf16(oacc[m], va4, pb1[0], pb1[1]);
+      if (two) {
+        ldsm_x4_trans(va4, pk2 + off);
+        mma_bf16(oacc[m], va4, pb2[0], pb2[1]);
+      }
+    }
+    // the warp is done with both buffers: refill each with its stream position + NB
     __syncwarp();
-    if (lane == 0 && (tgt < n || tgt - n < nx_n)) {
-      fence_proxy_async_smem();
-      attn_issue_pg(a, refill_page, tgt < n ? it.g : nx.g, ctr + NB, kc, smem_base);
-      atomicMax(&kc.att_issued, ctr + NB + 1u);
+    if (lane == 0) {
+      const bool r1 = tgt < n || tgt - n < nx_n;
+      const bool r2 = two && (tgt2 < n || tgt2 - n < nx_n);
+      if (r1 || r2) fence_proxy_async_smem();
+      if (r1) attn_issue_pg(a, refill_page, tgt < n ? it.g : nx.g, ctr + NB, kc, smem_base);
+      if (r2) attn_issue_pg(a, refill_page2, tgt2 < n ? it.g : nx.g, ctr2 + NB, kc, smem_base);
+      if (r1 || r2) atomicMax(&kc.att_issued, (r2 ? ctr2 : ctr) + NB + 1u);
     }
   }
   // ---- the warp's per-head states ----
@@ -3000,25 +3047,32 @@ __device__ __noinline__ bool attn_pages_tc(const AttnArgs &a, const AttnItem &it
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) l_w[h] += __shfl_xor_sync(0xffffffffu, l_w[h], o);
 #pragma unroll
-  for (int m = 0; m < 16; m++)
+  for (int m = 0; m < 8; m++)
 #pragma unroll
-    for (int e = 0; e < 2; e++) {   // the three parts of each head (rows h, h + 2, h + 4; h + 6 is zero)
-      oacc[m][e] += __shfl_xor_sync(0xffffffffu, oacc[m][e], 8);
-      oacc[m][e] += __shfl_xor_sync(0xffffffffu, oacc[m][e], 16);
+    for (int e = 0; e < 4; e++) {   // the three parts of each head (columns tig = 0, 1, 2; 3 is zero)
+      oacc[m][e] += __shfl_xor_sync(0xffffffffu, oacc[m][e], 1);
+      oacc[m][e] += __shfl_xor_sync(0xffffffffu, oacc[m][e], 2);
     }
-  if (gid < 2) {
-    float *dst = s_acc + (warp * 2 + gid) * HD;
+  if (tig == 0) {
+    float *d0 = s_acc + (warp * 2) * HD, *d1 = d0 + HD;
 #pragma unroll
-    for (int m = 0; m < 16; m++) *reinterpret_cast<float2 *>(dst + 8 * m + 2 * tig) = make_float2(oacc[m][0], oacc[m][1]);
+    for (int m = 0; m < 8; m++) {
+      d0[16 * m + gid] = oacc[m][0];
+      d1[16 * m + gid] = oacc[m][1];
+      d0[16 * m + gid + 8] = oacc[m][2];
+      d1[16 * m + gid + 8] = oacc[m][3];
+    }
   }
   if (lane < 2) {
-    s_ml[(warp * 2 + lane) * 2] = m_w[lane];
-    s_ml[(warp * 2 + lane) * 2 + 1] = l_w[lane];
+    s_ml[(warp * 2 + lane) * 2] = lane ? m_w[1] : m_w[0];
+    s_ml[(warp * 2 + lane) * 2 + 1] = lane ? l_w[1] : l_w[0];
   }
   return ok;
 }
 
-__device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_base, KCtx &kc) {
+// The decode attention stage with the tensor-core page loop (a.tc: batch >= 8
+// talker stages); same items, prologue and split combine as attn_stage.
+__device__ __noinline__ void attn_stage_tc(const AttnArgs &a, int B, char *smem_base, KCtx &kc) {
   char *smem = smem_base + SM_X_OFF;
   AttnSmem *sm = attn_sm(a, smem_base);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -3146,7 +3200,7 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
     const int tid = threadIdx.x;
     const int hh = tid >> 7, d = tid & 127;
     float Mh = -INFINITY, Lh = 0.f, acc = 0.f;
-    if (a.tc) {
+    {
       // tensor-core pages: per-warp states of both heads, combined in warp order
       float *s_acc = reinterpret_cast<float *>(smem_base + ATT_TC_COMB_OFF);   // [NWARPS][2][HD]
       float *s_ml = s_acc + NWARPS * 2 * HD;                                    // [NWARPS][2][2]
@@ -3162,317 +3216,487 @@ __device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_bas
         Lh += s_ml[(w * 2 + hh) * 2 + 1] * e;
         acc += s_acc[(w * 2 + hh) * HD + d] * e;
       }
+    }
+    ckpt(kc, 2);
+
+    // ---- output / split combine ----
+    const int head = 2 * g + hh;
+    if (nsp == 1) {
+      __stcg(a.out + (size_t)b * a.ld_out + head * HD + d, acc * (1.0f / Lh));
     } else {
-      // Warp w handles head h = w & 1 of the item's pages i = w / 2 (mod 4), so
-      // four pages are in work at once, each by the two warps of its GQA group;
-      // every warp keeps its own online softmax (running max m, sum l, output
-      // dims 4 lane .. 4 lane + 3), combined across warps in warp order at the
-      // end.  The split of pages among warps depends on the item alone, so the
-      // result does not depend on which CTA ran it.  Page i sits in ring buffer
-      // (stream position) % NB; once both warps of the pair are done with a
-      // buffer (named barrier per pair) the head-0 warp refills it with stream
-      // position + NB (this item's page i + NB, or a page of the next item).
-      const int h = warp & 1, pw = warp >> 1;
-      const int t = lane & 15, half = lane >> 4;
-      float m_w = -INFINITY, l_w = 0.f, acc4[4] = {0.f, 0.f, 0.f, 0.f};
-      // With 16 buffers a pair takes two of its pages per step (i and i + 4):
-      // the two pages' dot products and P.V run as independent chains and share
-      // one softmax update; with 4 buffers (small batches) one page per step.
-      float acc4b[4] = {0.f, 0.f, 0.f, 0.f};
-      if (NB >= 2 * (NWARPS / 2)) {
-        for (int i = pw; i < n; i += 2 * (NWARPS / 2)) {
-          const int i2 = i + NWARPS / 2;
-          const bool two = i2 < n;
-          const unsigned ctr = kc.page_ctr + i, ctr2 = ctr + NWARPS / 2;
-          const int buf = ctr % NB, buf2 = ctr2 % NB;
-          // every lane observes the phase flips, which makes the bulk-copied bytes
-          // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
-          // so a timeout ends both warps' loops at the same page
-          bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
-          if (two) landed = mbar_wait(kc.bars + buf2, (ctr2 / NB) & 1u, WAIT_LIMIT_CYCLES) && landed;
-          if (!bar_and_n(1 + pw, 64, landed)) {
-            if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-            break;
+      float *wsi = a.ws + ((((size_t)b * a.n_kv + g) * a.max_splits + sp) * 2 + hh) * (HD + 2);
+      __stcg(wsi + d, acc);
+      if (d == 0) { __stcg(wsi + HD, Mh); __stcg(wsi + HD + 1, Lh); }
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) sm->flag = (atomicAdd(a.sem + (size_t)b * a.n_kv + g, 1u) == (unsigned)(nsp - 1));
+      __syncthreads();
+      if (sm->flag) {
+        __threadfence();
+        const float *w0 = a.ws + ((((size_t)b * a.n_kv + g) * a.max_splits) * 2 + hh) * (HD + 2);
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < nsp; s2++) M = fmaxf(M, __ldcg(w0 + (size_t)s2 * 2 * (HD + 2) + HD));
+        float Ls = 0.f, O = 0.f;
+        for (int s2 = 0; s2 < nsp; s2++) {
+          const float *wsp = w0 + (size_t)s2 * 2 * (HD + 2);
+          const float e = expf(__ldcg(wsp + HD) - M);
+          Ls += __ldcg(wsp + HD + 1) * e;
+          O += __ldcg(wsp + d) * e;
+        }
+        __stcg(a.out + (size_t)b * a.ld_out + head * HD + d, O * (1.0f / Ls));
+        if (tid == 0) a.sem[(size_t)b * a.n_kv + g] = 0u;
+      }
+    }
+    __syncthreads();
+    item = next;
+  }
+  // every CTA took exactly one item past the end: the counter now stands at
+  // the next dynamic stage's base
+  if (a.dyn && threadIdx.x == 0) kc.att_base += (unsigned)n_items + gridDim.x;
+}
+
+__device__ __noinline__ void attn_stage(const AttnArgs &a, int B, char *smem_base, KCtx &kc) {
+  if (a.tc) {
+    attn_stage_tc(a, B, smem_base, kc);
+    return;
+  }
+  char *smem = smem_base + SM_X_OFF;
+  AttnSmem *sm = reinterpret_cast<AttnSmem *>(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NB = a.nbuf;
+
+  // ---- this CTA's first item ----
+  int n_items, item;
+  if (a.dyn) {
+    if (kc.att_first < 0) {   // not taken before the barrier
+      if (warp == 0) {
+        const int tot = attn_prefix(a, B, sm);
+        if (lane == 0) {
+          sm->flag = tot;
+          if (tot >= 0) sm->next = attn_take(kc);
+        }
+      }
+      __syncthreads();
+      n_items = sm->flag;
+      item = sm->next;
+      if (n_items < 0) {
+        if (threadIdx.x == 0) raise_err(kc, ERR_BAD_POS, -1);
+        return;
+      }
+    } else {
+      n_items = kc.att_tot;
+      item = kc.att_first;
+    }
+  } else {
+    n_items = B * a.n_kv * a.max_splits;
+    item = blockIdx.x;
+  }
+  __syncthreads();   // every thread has read the first item before it changes
+  if (threadIdx.x == 0) { kc.att_first = -1; kc.att_nbuf = NB; }
+
+  while (item < n_items) {
+    AttnItem it;
+    if (a.dyn) {
+      attn_item_dyn(a, B, item, sm, it);
+    } else if (!attn_item(a, item, it)) {
+      if (it.bad_pos) {
+        if (threadIdx.x == 0) raise_err(kc, ERR_BAD_POS, it.pos);
+        return;
+      }
+      item += gridDim.x;
+      continue;
+    }
+    const int b = it.b, g = it.g, sp = it.sp, pos = it.pos, L = it.L, npages = it.npages, nsp = it.nsp;
+    const int p_begin = it.p_begin, p_end = it.p_end;
+    // the item that holds the newest page appends the token (decode, append)
+    // and patches it into its page buffer from registers (decode only)
+    const bool owns_new = (p_end == npages) && a.mode != ATT_ATTEND;
+    const int *pt = a.page_table + (size_t)b * a.pt_stride;
+    // pages first: the stream positions issued so far are a prefix (the hook
+    // before the barrier, or the previous item's refills, may have covered
+    // the first ones)
+    if (warp == 7 && a.mode != ATT_APPEND) {
+      const int done = (int)min(kc.att_issued - kc.page_ctr, (unsigned)NB);
+      attn_issue(a, it, done, min(p_end - p_begin, NB), kc, smem_base);
+    }
+    // dynamic order: take the next item now (the atomic's latency hides behind
+    // this one), from a warp that is idle in the prologue
+    if (a.dyn && threadIdx.x == 4 * 32) sm->next = attn_take(kc);
+    ckpt(kc, 0);
+
+    // ---- prologue: QK RMSNorm + RoPE (+ KV append) ----
+    if (warp < 4) {
+      float v[4];
+      attn_row(a, b, g, warp, pos, lane, v);
+      if (warp < 2) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) sm->q[warp][lane + 32 * i] = v[i];
+      } else {
+        uint16_t *dst = (warp == 2) ? sm->knew : sm->vnew;
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[lane + 32 * i] = (uint16_t)f32_to_bf16_trunc(v[i]);
+        if (a.mode == ATT_APPEND && a.pkv) {   // a prefill's prompt K/V, unrounded
+          const PromptKV P = *a.pkv;
+          const int r = pos - P.p0;
+          if (r < 0 || r >= P.cap) {
+            if (lane == 0) raise_err(kc, ERR_BAD_POS, pos);
+          } else {
+            float *dstf = (warp == 2 ? P.k : P.v) + (((size_t)a.layer * a.n_kv + g) * P.cap + r) * HD;
+#pragma unroll
+            for (int i = 0; i < 4; i++) __stcg(dstf + lane + 32 * i, v[i]);
           }
-          uint16_t *kb = att_buf(smem_base, buf);
-          uint16_t *vb = kb + PAGE * HD;
-          uint16_t *kb2 = att_buf(smem_base, buf2);
-          uint16_t *vb2 = kb2 + PAGE * HD;
-          const int ntok = min(PAGE, L - (p_begin + i) * PAGE);
-          const int ntok2 = two ? min(PAGE, L - (p_begin + i2) * PAGE) : 0;
-          if (owns_new && (p_begin + i == npages - 1 || (two && p_begin + i2 == npages - 1))) {
-            // the newest token comes from shared memory, not from the copy (both
-            // warps of the page write the same bytes)
-            const int slot = pos % PAGE;
-            uint16_t *kp = (p_begin + i == npages - 1) ? kb : kb2;
-            uint16_t *vp = kp + PAGE * HD;
-            *reinterpret_cast<uint2 *>(kp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
-            *reinterpret_cast<uint2 *>(vp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
-            __syncwarp();
+        }
+      }
+    }
+    __syncthreads();
+    if (owns_new && threadIdx.x < 32) {
+      const int page = __ldg(pt + pos / PAGE);
+      if (page < 0 || page >= a.n_pages) {
+        if (threadIdx.x == 0) raise_err(kc, ERR_BAD_PAGE, page);
+      } else {
+        const int half = threadIdx.x >> 4, part = threadIdx.x & 15;   // 16 x 16 B per K / V row
+        uint16_t *pool = half ? a.vpool : a.kpool;
+        const uint16_t *srcv = half ? sm->vnew : sm->knew;
+        uint4 val = *reinterpret_cast<const uint4 *>(srcv + part * 8);
+        uint16_t *dst = pool + (((size_t)page * a.n_kv + g) * PAGE + (pos % PAGE)) * HD + part * 8;
+        __stcg(reinterpret_cast<uint4 *>(dst), val);
+      }
+    }
+    if (__syncthreads_or(kc.local_err)) return;
+    ckpt(kc, 1);
+    const int next = a.dyn ? sm->next : item + (int)gridDim.x;
+    if (a.mode == ATT_APPEND) {   // no attention in this stage
+      __syncthreads();   // every thread has read sm->next and the new K/V rows
+      item = next;
+      continue;
+    }
+    // dynamic order: the next item's pages follow this one's in the stream, so
+    // buffers freed near the end of this item already take the next one's
+    // pages.  Only from an item of at least NB pages: then the refills cover
+    // the next item's first positions without a gap (the issued positions stay
+    // a prefix of the stream, which the next item's first issue relies on).
+    AttnItem nx;
+    int nx_n = 0;
+    if (a.dyn && next < n_items && p_end - p_begin >= NB) {
+      attn_item_dyn(a, B, next, sm, nx);
+      nx_n = nx.p_end - nx.p_begin;
+    }
+
+    // ---- main loop over this split's pages ----
+    // Warp w handles head h = w & 1 of the item's pages i = w / 2 (mod 4), so
+    // four pages are in work at once, each by the two warps of its GQA group;
+    // every warp keeps its own online softmax (running max m, sum l, output
+    // dims 4 lane .. 4 lane + 3), combined across warps in warp order at the
+    // end.  The split of pages among warps depends on the item alone, so the
+    // result does not depend on which CTA ran it.  Page i sits in ring buffer
+    // (stream position) % NB; once both warps of the pair are done with a
+    // buffer (named barrier per pair) the head-0 warp refills it with stream
+    // position + NB (this item's page i + NB, or a page of the next item).
+    const int n = p_end - p_begin;
+    const int tid = threadIdx.x;
+    const int h = warp & 1, pw = warp >> 1;
+    const int t = lane & 15, half = lane >> 4;
+    float m_w = -INFINITY, l_w = 0.f, acc4[4] = {0.f, 0.f, 0.f, 0.f};
+    // With 16 buffers a pair takes two of its pages per step (i and i + 4):
+    // the two pages' dot products and P.V run as independent chains and share
+    // one softmax update; with 4 buffers (small batches) one page per step.
+    float acc4b[4] = {0.f, 0.f, 0.f, 0.f};
+    if (NB >= 2 * (NWARPS / 2)) {
+      for (int i = pw; i < n; i += 2 * (NWARPS / 2)) {
+        const int i2 = i + NWARPS / 2;
+        const bool two = i2 < n;
+        const unsigned ctr = kc.page_ctr + i, ctr2 = ctr + NWARPS / 2;
+        const int buf = ctr % NB, buf2 = ctr2 % NB;
+        // every lane observes the phase flips, which makes the bulk-copied bytes
+        // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
+        // so a timeout ends both warps' loops at the same page
+        bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+        if (two) landed = mbar_wait(kc.bars + buf2, (ctr2 / NB) & 1u, WAIT_LIMIT_CYCLES) && landed;
+        if (!bar_and_n(1 + pw, 64, landed)) {
+          if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+          break;
+        }
+        uint16_t *kb = att_buf(smem_base, buf);
+        uint16_t *vb = kb + PAGE * HD;
+        uint16_t *kb2 = att_buf(smem_base, buf2);
+        uint16_t *vb2 = kb2 + PAGE * HD;
+        const int ntok = min(PAGE, L - (p_begin + i) * PAGE);
+        const int ntok2 = two ? min(PAGE, L - (p_begin + i2) * PAGE) : 0;
+        if (owns_new && (p_begin + i == npages - 1 || (two && p_begin + i2 == npages - 1))) {
+          // the newest token comes from shared memory, not from the copy (both
+          // warps of the page write the same bytes)
+          const int slot = pos % PAGE;
+          uint16_t *kp = (p_begin + i == npages - 1) ? kb : kb2;
+          uint16_t *vp = kp + PAGE * HD;
+          *reinterpret_cast<uint2 *>(kp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
+          *reinterpret_cast<uint2 *>(vp + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
+          __syncwarp();
+        }
+        // the pages that will reuse these buffers: their indices are loaded
+        // now, so the refills at the end of the step do not wait for them
+        int refill_page = -1, refill_page2 = -1;
+        if (h == 0 && lane == 0) {
+          const int tgt = i + NB, tgt2 = i2 + NB;
+          if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
+          else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+          if (two) {
+            if (tgt2 < n) refill_page2 = __ldg(pt + p_begin + tgt2);
+            else if (tgt2 - n < nx_n) refill_page2 = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt2 - n));
           }
-          // the pages that will reuse these buffers: their indices are loaded
-          // now, so the refills at the end of the step do not wait for them
-          int refill_page = -1, refill_page2 = -1;
-          if (h == 0 && lane == 0) {
-            const int tgt = i + NB, tgt2 = i2 + NB;
-            if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
-            else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
-            if (two) {
-              if (tgt2 < n) refill_page2 = __ldg(pt + p_begin + tgt2);
-              else if (tgt2 - n < nx_n) refill_page2 = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt2 - n));
+        }
+        // scores of both pages, as in the one-page loop; the q reads are shared
+        const float *qh = sm->q[h] + half * 64;
+        float sdot, sdot2 = 0.f;
+        {
+          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+          const uint16_t *kr = kb + t * HD + half * 64;
+          if (two) {
+            float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
+            const uint16_t *kr2 = kb2 + t * HD + half * 64;
+  #pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+              const int jq = (jj + t) & 7;
+              const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+              const uint4 k2 = *reinterpret_cast<const uint4 *>(kr2 + 8 * jq);
+              const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+              const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+              s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+              s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+              s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+              s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+              u0 = fmaf(qa.x, bf16lo(k2.x), u0);
+              u1 = fmaf(qa.y, bf16hi(k2.x), u1);
+              u2 = fmaf(qa.z, bf16lo(k2.y), u2);
+              u3 = fmaf(qa.w, bf16hi(k2.y), u3);
+              s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+              s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+              s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+              s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+              u0 = fmaf(qb.x, bf16lo(k2.z), u0);
+              u1 = fmaf(qb.y, bf16hi(k2.z), u1);
+              u2 = fmaf(qb.z, bf16lo(k2.w), u2);
+              u3 = fmaf(qb.w, bf16hi(k2.w), u3);
+            }
+            sdot2 = (u0 + u1) + (u2 + u3);
+          } else {
+  #pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+              const int jq = (jj + t) & 7;
+              const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+              const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+              const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+              s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+              s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+              s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+              s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+              s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+              s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+              s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+              s3 = fmaf(qb.w, bf16hi(kk.w), s3);
             }
           }
-          // scores of both pages, as in the one-page loop; the q reads are shared
-          const float *qh = sm->q[h] + half * 64;
-          float sdot, sdot2 = 0.f;
-          {
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-            const uint16_t *kr = kb + t * HD + half * 64;
-            if (two) {
-              float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
-              const uint16_t *kr2 = kb2 + t * HD + half * 64;
-    #pragma unroll
-              for (int jj = 0; jj < 8; jj++) {
-                const int jq = (jj + t) & 7;
-                const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
-                const uint4 k2 = *reinterpret_cast<const uint4 *>(kr2 + 8 * jq);
-                const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
-                const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
-                s0 = fmaf(qa.x, bf16lo(kk.x), s0);
-                s1 = fmaf(qa.y, bf16hi(kk.x), s1);
-                s2 = fmaf(qa.z, bf16lo(kk.y), s2);
-                s3 = fmaf(qa.w, bf16hi(kk.y), s3);
-                u0 = fmaf(qa.x, bf16lo(k2.x), u0);
-                u1 = fmaf(qa.y, bf16hi(k2.x), u1);
-                u2 = fmaf(qa.z, bf16lo(k2.y), u2);
-                u3 = fmaf(qa.w, bf16hi(k2.y), u3);
-                s0 = fmaf(qb.x, bf16lo(kk.z), s0);
-                s1 = fmaf(qb.y, bf16hi(kk.z), s1);
-                s2 = fmaf(qb.z, bf16lo(kk.w), s2);
-                s3 = fmaf(qb.w, bf16hi(kk.w), s3);
-                u0 = fmaf(qb.x, bf16lo(k2.z), u0);
-                u1 = fmaf(qb.y, bf16hi(k2.z), u1);
-                u2 = fmaf(qb.z, bf16lo(k2.w), u2);
-                u3 = fmaf(qb.w, bf16hi(k2.w), u3);
-              }
-              sdot2 = (u0 + u1) + (u2 + u3);
-            } else {
-    #pragma unroll
-              for (int jj = 0; jj < 8; jj++) {
-                const int jq = (jj + t) & 7;
-                const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
-                const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
-                const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
-                s0 = fmaf(qa.x, bf16lo(kk.x), s0);
-                s1 = fmaf(qa.y, bf16hi(kk.x), s1);
-                s2 = fmaf(qa.z, bf16lo(kk.y), s2);
-                s3 = fmaf(qa.w, bf16hi(kk.y), s3);
-                s0 = fmaf(qb.x, bf16lo(kk.z), s0);
-                s1 = fmaf(qb.y, bf16hi(kk.z), s1);
-                s2 = fmaf(qb.z, bf16lo(kk.w), s2);
-                s3 = fmaf(qb.w, bf16hi(kk.w), s3);
-              }
-            }
-            sdot = (s0 + s1) + (s2 + s3);
+          sdot = (s0 + s1) + (s2 + s3);
+        }
+        sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+        sdot2 += __shfl_xor_sync(0xffffffffu, sdot2, 16);
+        const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
+        const float sc2 = (t < ntok2) ? sdot2 * a.scale : -INFINITY;
+        float mx = fmaxf(sc, sc2);
+  #pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float m_new = fmaxf(m_w, mx);
+        const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
+        const float pr2 = (t < ntok2) ? expf(sc2 - m_new) : 0.f;
+        const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
+        l_w = l_w * corr + (pr + pr2);   // this lane's token shares; summed over the lanes after the loop
+        m_w = m_new;
+  #pragma unroll
+        for (int e = 0; e < 4; e++) {
+          acc4[e] *= corr;
+          acc4b[e] *= corr;
+        }
+        // slots past the sequence end hold whatever the pool has there: skip them
+        if (ntok == PAGE && ntok2 == PAGE) {
+  #pragma unroll
+          for (int tt = 0; tt < PAGE; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+            const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
+            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+            acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
+            acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
+            acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
+            acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
           }
-          sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
-          sdot2 += __shfl_xor_sync(0xffffffffu, sdot2, 16);
-          const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
-          const float sc2 = (t < ntok2) ? sdot2 * a.scale : -INFINITY;
-          float mx = fmaxf(sc, sc2);
-    #pragma unroll
-          for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          const float m_new = fmaxf(m_w, mx);
-          const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
-          const float pr2 = (t < ntok2) ? expf(sc2 - m_new) : 0.f;
-          const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
-          l_w = l_w * corr + (pr + pr2);   // this lane's token shares; summed over the lanes after the loop
-          m_w = m_new;
-    #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            acc4[e] *= corr;
-            acc4b[e] *= corr;
+        } else if (ntok == PAGE && ntok2 == 0) {
+  #pragma unroll
+          for (int tt = 0; tt < PAGE; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
           }
-          // slots past the sequence end hold whatever the pool has there: skip them
-          if (ntok == PAGE && ntok2 == PAGE) {
-    #pragma unroll
-            for (int tt = 0; tt < PAGE; tt++) {
-              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-              const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
+        } else {
+          for (int tt = 0; tt < PAGE; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
+            if (tt < ntok) {
               const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-              const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
               acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
               acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
               acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
               acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+            }
+            if (tt < ntok2) {
+              const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
               acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
               acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
               acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
               acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
             }
-          } else if (ntok == PAGE && ntok2 == 0) {
-    #pragma unroll
-            for (int tt = 0; tt < PAGE; tt++) {
-              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-              const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-              acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-              acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-              acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-              acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
-            }
-          } else {
-            for (int tt = 0; tt < PAGE; tt++) {
-              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-              const float p2_t = __shfl_sync(0xffffffffu, pr2, tt);
-              if (tt < ntok) {
-                const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-                acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-                acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-                acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-                acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
-              }
-              if (tt < ntok2) {
-                const uint2 v2 = *reinterpret_cast<const uint2 *>(vb2 + tt * HD + 4 * lane);
-                acc4b[0] = fmaf(p2_t, bf16lo(v2.x), acc4b[0]);
-                acc4b[1] = fmaf(p2_t, bf16hi(v2.x), acc4b[1]);
-                acc4b[2] = fmaf(p2_t, bf16lo(v2.y), acc4b[2]);
-                acc4b[3] = fmaf(p2_t, bf16hi(v2.y), acc4b[3]);
-              }
-            }
-          }
-          // both warps of the pair are done with the buffers: the head-0 warp
-          // refills each with its stream position + NB
-          bar_sync_n(1 + pw, 64);
-          if (h == 0 && lane == 0) {
-            const int tgt = i + NB, tgt2 = i2 + NB;   // item-relative; >= n: the next item's page tgt - n
-            const bool r1 = tgt < n || tgt - n < nx_n;
-            const bool r2 = two && (tgt2 < n || tgt2 - n < nx_n);
-            if (r1 || r2) fence_proxy_async_smem();
-            if (r1) attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
-            if (r2) attn_issue_pg(a, refill_page2, tgt2 < n ? g : nx.g, ctr2 + NB, kc, smem_base);
-            if (r1 || r2) atomicMax(&kc.att_issued, (r2 ? ctr2 : ctr) + NB + 1u);
           }
         }
-      } else {
-        for (int i = pw; i < n; i += NWARPS / 2) {
-          const unsigned ctr = kc.page_ctr + i;
-          const int buf = ctr % NB;
-          // every lane observes the phase flip, which makes the bulk-copied bytes
-          // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
-          // so a timeout ends both warps' loops at the same page
-          const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
-          if (!bar_and_n(1 + pw, 64, landed)) {
-            if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
-            break;
-          }
-          uint16_t *kb = att_buf(smem_base, buf);
-          uint16_t *vb = kb + PAGE * HD;
-          const int pg = p_begin + i;
-          const int ntok = min(PAGE, L - pg * PAGE);
-          if (pg == npages - 1 && owns_new) {
-            // the newest token comes from shared memory, not from the copy (both
-            // warps of the page write the same bytes)
-            const int slot = pos % PAGE;
-            *reinterpret_cast<uint2 *>(kb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
-            *reinterpret_cast<uint2 *>(vb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
-            __syncwarp();
-          }
-          // the page that will reuse this buffer: its index is loaded now, so
-          // the refill at the end of the page does not wait for it
-          int refill_page = -1;
-          if (h == 0 && lane == 0) {
-            const int tgt = i + NB;
-            if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
-            else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
-          }
-          // score of token t: lanes t and t + 16 each take half of the 128 dims
-          // in 16-byte groups, walking them from a token-dependent start so each
-          // 8-lane phase of a 16-byte read hits 8 distinct bank groups; four
-          // partial sums
-          float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-          const float *qh = sm->q[h] + half * 64;
-          const uint16_t *kr = kb + t * HD + half * 64;
-    #pragma unroll
-          for (int jj = 0; jj < 8; jj++) {
-            const int jq = (jj + t) & 7;
-            const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
-            const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
-            const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
-            s0 = fmaf(qa.x, bf16lo(kk.x), s0);
-            s1 = fmaf(qa.y, bf16hi(kk.x), s1);
-            s2 = fmaf(qa.z, bf16lo(kk.y), s2);
-            s3 = fmaf(qa.w, bf16hi(kk.y), s3);
-            s0 = fmaf(qb.x, bf16lo(kk.z), s0);
-            s1 = fmaf(qb.y, bf16hi(kk.z), s1);
-            s2 = fmaf(qb.z, bf16lo(kk.w), s2);
-            s3 = fmaf(qb.w, bf16hi(kk.w), s3);
-          }
-          float sdot = (s0 + s1) + (s2 + s3);
-          sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
-          const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
-          float mx = sc;
-    #pragma unroll
-          for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          const float m_new = fmaxf(m_w, mx);
-          const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
-          const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
-          l_w = l_w * corr + pr;   // this lane's token share; summed over the lanes after the loop
-          m_w = m_new;
-    #pragma unroll
-          for (int e = 0; e < 4; e++) acc4[e] *= corr;
-          // slots past the sequence end hold whatever the pool has there: skip them
-          if (ntok == PAGE) {
-    #pragma unroll
-            for (int tt = 0; tt < PAGE; tt++) {
-              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-              const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-              acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-              acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-              acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-              acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
-            }
-          } else {
-            for (int tt = 0; tt < ntok; tt++) {
-              const float p_t = __shfl_sync(0xffffffffu, pr, tt);
-              const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
-              acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
-              acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
-              acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
-              acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
-            }
-          }
-          // both warps of the pair are done with the buffer: the head-0 warp
-          // refills it with stream position ctr + NB
-          bar_sync_n(1 + pw, 64);
-          const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
-          if (h == 0 && lane == 0 && (tgt < n || tgt - n < nx_n)) {
-            fence_proxy_async_smem();
-            attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
-            atomicMax(&kc.att_issued, ctr + NB + 1u);
-          }
+        // both warps of the pair are done with the buffers: the head-0 warp
+        // refills each with its stream position + NB
+        bar_sync_n(1 + pw, 64);
+        if (h == 0 && lane == 0) {
+          const int tgt = i + NB, tgt2 = i2 + NB;   // item-relative; >= n: the next item's page tgt - n
+          const bool r1 = tgt < n || tgt - n < nx_n;
+          const bool r2 = two && (tgt2 < n || tgt2 - n < nx_n);
+          if (r1 || r2) fence_proxy_async_smem();
+          if (r1) attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
+          if (r2) attn_issue_pg(a, refill_page2, tgt2 < n ? g : nx.g, ctr2 + NB, kc, smem_base);
+          if (r1 || r2) atomicMax(&kc.att_issued, (r2 ? ctr2 : ctr) + NB + 1u);
         }
       }
+    } else {
+      for (int i = pw; i < n; i += NWARPS / 2) {
+        const unsigned ctr = kc.page_ctr + i;
+        const int buf = ctr % NB;
+        // every lane observes the phase flip, which makes the bulk-copied bytes
+        // visible to it; the pair agrees on the outcome (named barrier 1 + pw),
+        // so a timeout ends both warps' loops at the same page
+        const bool landed = mbar_wait(kc.bars + buf, (ctr / NB) & 1u, WAIT_LIMIT_CYCLES);
+        if (!bar_and_n(1 + pw, 64, landed)) {
+          if (lane == 0 && !landed) raise_err(kc, ERR_MBAR_TIMEOUT, i);
+          break;
+        }
+        uint16_t *kb = att_buf(smem_base, buf);
+        uint16_t *vb = kb + PAGE * HD;
+        const int pg = p_begin + i;
+        const int ntok = min(PAGE, L - pg * PAGE);
+        if (pg == npages - 1 && owns_new) {
+          // the newest token comes from shared memory, not from the copy (both
+          // warps of the page write the same bytes)
+          const int slot = pos % PAGE;
+          *reinterpret_cast<uint2 *>(kb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->knew + 4 * lane);
+          *reinterpret_cast<uint2 *>(vb + slot * HD + 4 * lane) = *reinterpret_cast<const uint2 *>(sm->vnew + 4 * lane);
+          __syncwarp();
+        }
+        // the page that will reuse this buffer: its index is loaded now, so
+        // the refill at the end of the page does not wait for it
+        int refill_page = -1;
+        if (h == 0 && lane == 0) {
+          const int tgt = i + NB;
+          if (tgt < n) refill_page = __ldg(pt + p_begin + tgt);
+          else if (tgt - n < nx_n) refill_page = __ldg(a.page_table + (size_t)nx.b * a.pt_stride + nx.p_begin + (tgt - n));
+        }
+        // score of token t: lanes t and t + 16 each take half of the 128 dims
+        // in 16-byte groups, walking them from a token-dependent start so each
+        // 8-lane phase of a 16-byte read hits 8 distinct bank groups; four
+        // partial sums
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        const float *qh = sm->q[h] + half * 64;
+        const uint16_t *kr = kb + t * HD + half * 64;
   #pragma unroll
-      for (int e = 0; e < 4; e++) acc4[e] += acc4b[e];
+        for (int jj = 0; jj < 8; jj++) {
+          const int jq = (jj + t) & 7;
+          const uint4 kk = *reinterpret_cast<const uint4 *>(kr + 8 * jq);
+          const float4 qa = *reinterpret_cast<const float4 *>(qh + 8 * jq);
+          const float4 qb = *reinterpret_cast<const float4 *>(qh + 8 * jq + 4);
+          s0 = fmaf(qa.x, bf16lo(kk.x), s0);
+          s1 = fmaf(qa.y, bf16hi(kk.x), s1);
+          s2 = fmaf(qa.z, bf16lo(kk.y), s2);
+          s3 = fmaf(qa.w, bf16hi(kk.y), s3);
+          s0 = fmaf(qb.x, bf16lo(kk.z), s0);
+          s1 = fmaf(qb.y, bf16hi(kk.z), s1);
+          s2 = fmaf(qb.z, bf16lo(kk.w), s2);
+          s3 = fmaf(qb.w, bf16hi(kk.w), s3);
+        }
+        float sdot = (s0 + s1) + (s2 + s3);
+        sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+        const float sc = (t < ntok) ? sdot * a.scale : -INFINITY;
+        float mx = sc;
   #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) l_w += __shfl_xor_sync(0xffffffffu, l_w, o);
-      // per-warp states -> per-head totals, in warp order
-      float *s_acc = reinterpret_cast<float *>(smem + ATT_COMB_OFF);   // [NWARPS][HD]
-      float *s_ml = s_acc + NWARPS * HD;                                // [NWARPS][2]
-      *reinterpret_cast<float4 *>(s_acc + warp * HD + 4 * lane) = make_float4(acc4[0], acc4[1], acc4[2], acc4[3]);
-      if (lane == 0) { s_ml[2 * warp] = m_w; s_ml[2 * warp + 1] = l_w; }
-      if (__syncthreads_or(kc.local_err)) return;   // copies still in flight are drained on the way out
-      if (tid == 0) kc.page_ctr += n;
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float m_new = fmaxf(m_w, mx);
+        const float pr = (t < ntok) ? expf(sc - m_new) : 0.f;
+        const float corr = (m_w == -INFINITY) ? 0.f : expf(m_w - m_new);
+        l_w = l_w * corr + pr;   // this lane's token share; summed over the lanes after the loop
+        m_w = m_new;
   #pragma unroll
-      for (int q = 0; q < NWARPS / 2; q++) Mh = fmaxf(Mh, s_ml[2 * (2 * q + hh)]);
+        for (int e = 0; e < 4; e++) acc4[e] *= corr;
+        // slots past the sequence end hold whatever the pool has there: skip them
+        if (ntok == PAGE) {
   #pragma unroll
-      for (int q = 0; q < NWARPS / 2; q++) {
-        const int w = 2 * q + hh;
-        const float mw = s_ml[2 * w];
-        const float e = (mw == -INFINITY) ? 0.f : expf(mw - Mh);
-        Lh += s_ml[2 * w + 1] * e;
-        acc += s_acc[w * HD + d] * e;
+          for (int tt = 0; tt < PAGE; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+          }
+        } else {
+          for (int tt = 0; tt < ntok; tt++) {
+            const float p_t = __shfl_sync(0xffffffffu, pr, tt);
+            const uint2 vv = *reinterpret_cast<const uint2 *>(vb + tt * HD + 4 * lane);
+            acc4[0] = fmaf(p_t, bf16lo(vv.x), acc4[0]);
+            acc4[1] = fmaf(p_t, bf16hi(vv.x), acc4[1]);
+            acc4[2] = fmaf(p_t, bf16lo(vv.y), acc4[2]);
+            acc4[3] = fmaf(p_t, bf16hi(vv.y), acc4[3]);
+          }
+        }
+        // both warps of the pair are done with the buffer: the head-0 warp
+        // refills it with stream position ctr + NB
+        bar_sync_n(1 + pw, 64);
+        const int tgt = i + NB;   // item-relative; >= n: the next item's page tgt - n
+        if (h == 0 && lane == 0 && (tgt < n || tgt - n < nx_n)) {
+          fence_proxy_async_smem();
+          attn_issue_pg(a, refill_page, tgt < n ? g : nx.g, ctr + NB, kc, smem_base);
+          atomicMax(&kc.att_issued, ctr + NB + 1u);
+        }
       }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc4[e] += acc4b[e];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) l_w += __shfl_xor_sync(0xffffffffu, l_w, o);
+    // per-warp states -> per-head totals, in warp order
+    float *s_acc = reinterpret_cast<float *>(smem + ATT_COMB_OFF);   // [NWARPS][HD]
+    float *s_ml = s_acc + NWARPS * HD;                                // [NWARPS][2]
+    *reinterpret_cast<float4 *>(s_acc + warp * HD + 4 * lane) = make_float4(acc4[0], acc4[1], acc4[2], acc4[3]);
+    if (lane == 0) { s_ml[2 * warp] = m_w; s_ml[2 * warp + 1] = l_w; }
+    if (__syncthreads_or(kc.local_err)) return;   // copies still in flight are drained on the way out
+    if (tid == 0) kc.page_ctr += n;
+    const int hh = tid >> 7, d = tid & 127;
+    float Mh = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < NWARPS / 2; q++) Mh = fmaxf(Mh, s_ml[2 * (2 * q + hh)]);
+    float Lh = 0.f, acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < NWARPS / 2; q++) {
+      const int w = 2 * q + hh;
+      const float mw = s_ml[2 * w];
+      const float e = (mw == -INFINITY) ? 0.f : expf(mw - Mh);
+      Lh += s_ml[2 * w + 1] * e;
+      acc += s_acc[w * HD + d] * e;
     }
     ckpt(kc, 2);
 
@@ -3768,7 +3992,15 @@ QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
     if (ok && !kc.last) {
       const unsigned target = (kc.epoch + 1u) * gridDim.x;
       const unsigned nxt = kc.seq + 1;
+      // hook steps: 0 the coming attention stage's first pages, 1 weights two
+      // stages ahead, 2 the coming GEMV stage's small operands; before a GEMV
+      // stage the weights go first (a short wait may allow one step only)
       int phase = (nxt < kc.n_total) ? 0 : 3;
+      if (phase == 0) {   // warp-uniform: every lane tests the descriptor's barrier
+        const int s0 = (int)(nxt % NDESC);
+        if (__all_sync(0xffffffffu, mbar_test(kc.dbars + s0, (nxt / NDESC) & 1u)) && kc.dring[s0].kind == ST_GEMV)
+          phase = 1;
+      }
       const long long t0 = clock64();
       unsigned spins = 0;
       while (true) {
