@@ -876,9 +876,12 @@ static bool cl_ok(int fmt, int rows, int K, int B) {
 // streams plus the split-K fix-up.  The staged activation slice must fit
 // TC_X_BYTES (N x 128 bytes per chunk) and 2048 columns.
 struct TcShape { int S = 0, kcn = 0, R = 0; };
+// The tensor-core page loop is opt-in (QTB_ATTN_TC=1, read at each program
+// build / standalone call): measured on B200 it is slower than the CUDA-core
+// loop (a 0.6B talker layer at 64 requests of 128-2048 positions: 202 vs 144 us).
 static bool attn_tc_enabled() {
-  const char *v = getenv("QTB_ATTN_TC");   // read at each program build / standalone call
-  return !(v && v[0] == '0');
+  const char *v = getenv("QTB_ATTN_TC");
+  return v && v[0] == '1';
 }
 static bool tc_ok(const DMat &m, int B, int fmt) {
   return tc_enabled() && m.wtc && B >= 1 && B <= 64 && (fmt == FMT_BF16 || fmt == FMT_INT8) && m.rows % 128 == 0;
@@ -1012,9 +1015,9 @@ struct ProgBuilder {
     if (cl) a.max_splits = std::max(1, std::min(a.max_splits, grid() / std::max(1, B * k.n_kv)));
     a.layer = layer;
     a.kmap = b.kmap; a.vmap = b.vmap;
-    // large-batch decode attention on the tensor cores (needs the 16 page
-    // buffers of a program without small-batch GEMV stages: upload_prog
-    // turns it off otherwise); QTB_ATTN_TC=0 keeps the CUDA-core loop
+    // large-batch decode attention on the tensor cores, opt-in (needs the 16
+    // page buffers of a program without small-batch GEMV stages: upload_prog
+    // turns it off otherwise)
     // (not the code predictor's: its items are one page of at most 16
     // positions, where the per-item set-up outweighs the page loop)
     a.tc = (mode == ATT_DECODE && B >= 8 && b.kmap && &k != &s->e->cp && attn_tc_enabled()) ? 1 : 0;

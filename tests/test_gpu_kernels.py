@@ -118,11 +118,11 @@ def test_attention_append_matches_oracle(have_gpu, pos, max_splits):
 
 
 def test_attention_tensor_cores_match_cuda_cores(have_gpu, monkeypatch):
-    """Batch >= 8 decode attention runs its pages on the tensor cores (bf16 MMA,
-    q and p as three bf16 parts, pages copied as swizzled TMA boxes); the
-    CUDA-core page loop (QTB_ATTN_TC=0) gives the same outputs to f32 rounding
-    and the same appended K/V bytes.  64 slots, lengths across page edges,
-    splits in dynamic order."""
+    """With QTB_ATTN_TC=1 batch >= 8 decode attention runs its pages on the
+    tensor cores (bf16 MMA, q and p as three bf16 parts, pages copied as
+    swizzled TMA boxes); it gives the outputs of the CUDA-core page loop (the
+    default) to f32 rounding and the same appended K/V bytes.  64 slots,
+    lengths across page edges, splits in dynamic order."""
     rng = np.random.default_rng(91)
     pos = [15, 16, 17, 31, 32, 0, 1, 4095] + [int(v) for v in rng.integers(0, 3000, 56)]
     B, nh, nkv, hd, eps = len(pos), 16, 8, 128, 1e-6
