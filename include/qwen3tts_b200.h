@@ -223,6 +223,26 @@ int qtb_session_set_slot_pos(qtb_session_t *s, int b, int32_t pos);
  * embeds == NULL then consumes it: the embedding of an admitted request's last
  * prompt token, while the other slots keep the inputs their last frame made. */
 int qtb_session_set_embed(qtb_session_t *s, int b, const float *embed);
+/* Sampling of slot b's code0 (the reference's qwen_tts_sample,
+ * qwen_tts_sampling.c:160-202, as its generation loop calls it at
+ * qwen_tts.c:1694): temperature (< 1e-6: greedy, the default after
+ * qtb_session_begin_generation / qtb_session_reset_slot), top-k (<= 0 or >=
+ * the vocabulary: off), top-p (>= 1: off) and the seed of the reference's
+ * per-slot LCG (qwen_set_seed; the engine keeps each slot's state across
+ * frames, as the reference's batched loop does with qwen_get_seed, qwen_tts.c:
+ * 2641-2643).  Softmax, top-k, top-p and the draw run on the device after the
+ * codec head's rules (clip, mask, EOS, repetition penalty); sums run in another
+ * order than the reference's loops, so a draw can differ from the reference's
+ * only when its uniform falls within f32 rounding of a cumulative boundary.
+ * The code predictor's heads stay greedy, as in the reference. */
+int qtb_session_set_sampling(qtb_session_t *s, int b, float temperature, int32_t top_k, float top_p, uint32_t seed);
+/* Every slot's LCG state, host [batch] (qwen_get_seed per slot). */
+int qtb_session_get_rng(qtb_session_t *s, uint32_t *state);
+/* The device sampler alone on host logits [batch][n] (n <= 2176; row n - 1
+ * plays the EOS row): per row temperature, top_k, top_p and LCG state rng
+ * (updated in place); out [batch] = the row drawn. */
+int qtb_codec_sample_host(const float *logits, int batch, int n, const float *temperature, const int32_t *top_k,
+                          const float *top_p, uint32_t *rng, int32_t *out);
 
 /* KV pages <-> contiguous bf16 ([layer][len][kv_dim] with per-layer stride
  * layer_stride positions, the reference's host layout qwen_tts_talker.c:454-460). */

@@ -307,3 +307,55 @@ def cp_predict(cp: Stack, cp_norm, lm_heads, cp_emb, codec_emb, talker_hidden, c
             break
         x = stack_step(cp, proj(cp_emb[g][c]), caches, g + 2)
     return np.array(codes, np.int32), caches
+
+
+def lcg_next(state):
+    """The reference's rand_uniform (qwen_tts_sampling.c:38-42): new state and draw."""
+    state = (state * 1103515245 + 12345) & 0xFFFFFFFF
+    return state, np.float32(((state >> 16) & 0x7FFF) / 32768.0)
+
+
+def sample(logits, temp, top_k, top_p, seed):
+    """qwen_tts_sample (qwen_tts_sampling.c:160-202) without the repetition
+    penalty, in f32 with the reference's loop orders: softmax (max, exp of
+    (x - max) * (1 / T), sequential sum, x * (1 / sum)), top-k (values below
+    the k-th largest zeroed), top-p (descending until the running sum passes
+    p), renormalisation, one LCG draw against the running sum in index order.
+    Returns (token, LCG state, draw, the running sums) for boundary checks."""
+    x = np.asarray(logits, np.float32).copy()
+    n = x.shape[0]
+    if temp < 1e-6:
+        return int(np.argmax(x)), seed, None, None
+    mx = np.float32(x.max())
+    inv_t = np.float32(np.float32(1.0) / np.float32(temp))
+    p = np.exp((x - mx) * inv_t).astype(np.float32)
+    s = np.float32(0)
+    for v in p:
+        s = np.float32(s + v)
+    p = (p * np.float32(np.float32(1.0) / s)).astype(np.float32)
+    if 0 < top_k < n:
+        thr = np.sort(p)[::-1][top_k - 1]
+        p[p < thr] = 0
+    if 0 < top_p < 1:
+        order = sorted(range(n), key=lambda i: (-float(p[i]), i))
+        cum = np.float32(0)
+        keep = np.zeros(n, bool)
+        for i in order:
+            cum = np.float32(cum + p[i])
+            keep[i] = True
+            if cum > np.float32(top_p):
+                break
+        p[~keep] = 0
+    s = np.float32(0)
+    for v in p:
+        s = np.float32(s + v)
+    if s > 0:
+        p = (p * np.float32(np.float32(1.0) / s)).astype(np.float32)
+    seed, u = lcg_next(seed)
+    cums = np.cumsum(p.astype(np.float64))
+    run = np.float32(0)
+    for i in range(n):
+        run = np.float32(run + p[i])
+        if u < run:
+            return i, seed, float(u), cums
+    return n - 1, seed, float(u), cums

@@ -29,6 +29,7 @@
 #include "qwen_tts_kernels.h"
 #include "ingot/safetensors.h"
 
+#include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -165,6 +166,8 @@ int qref_codec_argmax(void *h, const float *hidden, int limit) {
 
 int qwen_tts_sample(float *logits, int vocab_size, float temp, int top_k, float top_p,
                     float rep_penalty, int *prev_tokens, int n_prev);
+void qwen_set_seed(uint32_t seed);
+uint32_t qwen_get_seed(void);
 
 /* code0 of one frame of the reference's generation loop with greedy sampling:
  * the codec-head logits over the whole vocabulary (qwen_tts.c:1650), the
@@ -172,8 +175,11 @@ int qwen_tts_sample(float *logits, int vocab_size, float temp, int top_k, float 
  * qwen_tts_generate is not part of this harness), then the reference's own
  * qwen_tts_sample at temperature 0 with the repetition penalty over the
  * earlier code0 tokens (qwen_tts_sampling.c:160-181).  2150 = EOS. */
-int qref_codec_sample(void *h, const float *hidden, int frame, int expected_frames, float rep_penalty,
-                      int *prev_tokens, int n_prev) {
+/* The same with the reference's sampling (temperature, top-k, top-p) and its
+ * LCG state in and out (qwen_set_seed / qwen_get_seed around the draw, as its
+ * batched loop does per slot, qwen_tts.c:2641-2643). */
+int qref_codec_sample_t(void *h, const float *hidden, int frame, int expected_frames, float rep_penalty,
+                        int *prev_tokens, int n_prev, float temp, int top_k, float top_p, uint32_t *seed) {
     qwen_tts_ctx_t *ctx = (qwen_tts_ctx_t *)h;
     const int V = ctx->config.codec_vocab_size, H = ctx->config.hidden_size;
     float *logits = (float *)malloc((size_t)V * sizeof(float));
@@ -193,7 +199,27 @@ int qref_codec_sample(void *h, const float *hidden, int frame, int expected_fram
             logits[2150] += boost;
         }
     }
-    int c = qwen_tts_sample(logits, V, 0.0f, 50, 1.0f, rep_penalty, prev_tokens, n_prev);
+    qwen_set_seed(*seed);
+    int c = qwen_tts_sample(logits, V, temp, top_k, top_p, rep_penalty, prev_tokens, n_prev);
+    *seed = qwen_get_seed();
+    free(logits);
+    return c;
+}
+
+int qref_codec_sample(void *h, const float *hidden, int frame, int expected_frames, float rep_penalty,
+                      int *prev_tokens, int n_prev) {
+    uint32_t seed = 12345;
+    return qref_codec_sample_t(h, hidden, frame, expected_frames, rep_penalty, prev_tokens, n_prev, 0.0f, 50, 1.0f,
+                               &seed);
+}
+
+/* The reference's sampler alone on given logits (no repetition penalty). */
+int qref_sample_logits(const float *logits_in, int n, float temp, int top_k, float top_p, uint32_t *seed) {
+    float *logits = (float *)malloc((size_t)n * sizeof(float));
+    memcpy(logits, logits_in, (size_t)n * sizeof(float));
+    qwen_set_seed(*seed);
+    int c = qwen_tts_sample(logits, n, temp, top_k, top_p, 1.0f, NULL, 0);
+    *seed = qwen_get_seed();
     free(logits);
     return c;
 }

@@ -75,6 +75,9 @@ def ref_lib(flavour: str | None = None, dropin: bool = False, refcuda: bool = Fa
     L.qref_codec_argmax.argtypes = [vp, vp, C.c_int]
     L.qref_codec_embed.argtypes = [vp, C.c_int, vp]
     L.qref_codec_sample.argtypes = [vp, vp, C.c_int, C.c_int, C.c_float, vp, C.c_int]
+    L.qref_codec_sample_t.argtypes = [vp, vp, C.c_int, C.c_int, C.c_float, vp, C.c_int, C.c_float, C.c_int,
+                                      C.c_float, vp]
+    L.qref_sample_logits.argtypes = [vp, C.c_int, C.c_float, C.c_int, C.c_float, vp]
     L.qref_talker_prefill.argtypes = [vp, vp, C.c_int, vp]
     L.qref_weight.restype = vp
     L.qref_weight.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int]
@@ -252,6 +255,16 @@ class RefModel:
         return self.L.qref_codec_sample(self.h, p(hh), int(frame), int(expected_frames), C.c_float(rep_penalty),
                                         p(prev), len(prev_tokens))
 
+    def codec_sample_t(self, hidden, frame, expected_frames, rep_penalty, prev_tokens, temp, top_k, top_p, seed):
+        """code0 with the reference's sampling; returns (code, LCG state after the draw)."""
+        hh = np.ascontiguousarray(hidden, np.float32)
+        prev = np.ascontiguousarray(prev_tokens if len(prev_tokens) else [0], np.int32)
+        st = np.array([seed], np.uint32)
+        c = self.L.qref_codec_sample_t(self.h, p(hh), int(frame), int(expected_frames), C.c_float(rep_penalty),
+                                       p(prev), len(prev_tokens), C.c_float(temp), int(top_k), C.c_float(top_p),
+                                       p(st))
+        return c, int(st[0])
+
     def codec_embed(self, code):
         out = np.empty(self.cfg.hidden, np.float32)
         self.L.qref_codec_embed(self.h, int(code), p(out))
@@ -287,3 +300,13 @@ class RefModel:
 
     def ctx(self):
         return self.L.qref_ctx(self.h)
+
+
+def sample_logits(logits, temp, top_k, top_p, seed, flavour=None):
+    """The reference's qwen_tts_sample on given logits (no repetition
+    penalty); returns (token, LCG state after the draw)."""
+    L = ref_lib(flavour)
+    lg = np.ascontiguousarray(logits, np.float32)
+    st = np.array([seed], np.uint32)
+    c = L.qref_sample_logits(p(lg), lg.shape[0], C.c_float(temp), int(top_k), C.c_float(top_p), p(st))
+    return c, int(st[0])

@@ -16,6 +16,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <cstddef>
 #include <cstring>
 #include <string>
 #include <mutex>
@@ -1301,6 +1302,20 @@ extern "C" void qtb_session_destroy(qtb_session_t *s) {
   delete s;
 }
 
+// Slots b0 .. b1 - 1 back to greedy decoding with the reference's defaults
+// (top-k 50, top-p 1, LCG seed 12345: qwen_tts.c:559, qwen_tts_sampling.c:38).
+static int reset_sampling(const GenState &g, int b0, int b1) {
+  const int n = b1 - b0;
+  std::vector<float> t(n, 0.0f), tp(n, 1.0f);
+  std::vector<int32_t> tk(n, 50);
+  std::vector<uint32_t> r(n, 12345u);
+  CUDA_TRY(cudaMemcpy(g.temp + b0, t.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(g.top_k + b0, tk.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(g.top_p + b0, tp.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(g.rng + b0, r.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+  return 0;
+}
+
 extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n_pages, qtb_session_t **out) {
   if (!e || !out) return set_err(QTB_E_INVALID, "null argument");
   *out = nullptr;
@@ -1377,6 +1392,16 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
       cudaMemset(g.boost_start, 0xff, (size_t)B * 4);
       cudaMemset(g.done, 0, (size_t)B * 4);
       cudaMemset(g.rep_count, 0, (size_t)B * g.vocab * 2);
+      // sampling state: greedy (temperature 0) until qtb_session_set_sampling
+      g.sampling = 0;
+      g.ld = (g.eos_row + 1 + 3) & ~3;
+      if (g.eos_row + 1 > SAMPLE_MAX_ROWS) { rc = set_err(QTB_E_UNSUPPORTED, "codec head of %d rows", g.eos_row + 1); goto fail; }
+      if ((rc = s->ar.alloc((void **)&g.logits, (size_t)B * g.ld * 4))) goto fail;
+      if ((rc = s->ar.alloc((void **)&g.temp, (size_t)B * 4))) goto fail;
+      if ((rc = s->ar.alloc((void **)&g.top_k, (size_t)B * 4))) goto fail;
+      if ((rc = s->ar.alloc((void **)&g.top_p, (size_t)B * 4))) goto fail;
+      if ((rc = s->ar.alloc((void **)&g.rng, (size_t)B * 4))) goto fail;
+      if ((rc = reset_sampling(g, 0, B))) goto fail;
       if ((rc = s->ar.upload(&s->gen, &g, sizeof g))) goto fail;
     }
     cudaMemset(s->sem, 0, (size_t)sem_n * 4);
@@ -1692,6 +1717,8 @@ extern "C" int qtb_session_begin_generation(qtb_session_t *s, const int32_t *exp
   CUDA_TRY(cudaMemset(s->gen_h.frame, 0, (size_t)B * 4));
   CUDA_TRY(cudaMemset(s->gen_h.done, 0, (size_t)B * 4));
   CUDA_TRY(cudaMemset(s->gen_h.rep_count, 0, (size_t)B * s->gen_h.vocab * 2));
+  { int rc = reset_sampling(s->gen_h, 0, B); if (rc) return rc; }
+  s->gen_h.sampling = 0;
   GenState g = s->gen_h;
   g.enabled = 1;
   g.rep_pen = rep_penalty;
@@ -1710,6 +1737,34 @@ extern "C" int qtb_session_reset_slot(qtb_session_t *s, int b, int32_t expected_
   CUDA_TRY(cudaMemcpy(s->gen_h.done + b, &d, 4, cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemcpy(s->gen_h.boost_start + b, &bs, 4, cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemset(s->gen_h.rep_count + (size_t)b * s->gen_h.vocab, 0, (size_t)s->gen_h.vocab * 2));
+  return reset_sampling(s->gen_h, b, b + 1);
+}
+
+extern "C" int qtb_session_set_sampling(qtb_session_t *s, int b, float temperature, int32_t top_k, float top_p,
+                                        uint32_t seed) {
+  if (!s || b < 0 || b >= s->B) return set_err(QTB_E_INVALID, "bad slot");
+  if (!s->gen_on) return set_err(QTB_E_INVALID, "qtb_session_begin_generation first");
+  if (!(temperature >= 0.0f) || !(top_p > 0.0f))
+    return set_err(QTB_E_INVALID, "temperature %g, top-p %g", (double)temperature, (double)top_p);
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  const GenState &g = s->gen_h;
+  CUDA_TRY(cudaMemcpy(g.temp + b, &temperature, 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(g.top_k + b, &top_k, 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(g.top_p + b, &top_p, 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(g.rng + b, &seed, 4, cudaMemcpyHostToDevice));
+  if (temperature >= 1e-6f && !s->gen_h.sampling) {   // the codec head keeps its logits from now on
+    s->gen_h.sampling = 1;
+    const int one = 1;
+    CUDA_TRY(cudaMemcpy(reinterpret_cast<char *>(s->gen) + offsetof(GenState, sampling), &one, sizeof one,
+                        cudaMemcpyHostToDevice));
+  }
+  return 0;
+}
+
+extern "C" int qtb_session_get_rng(qtb_session_t *s, uint32_t *state) {
+  if (!s || !state) return set_err(QTB_E_INVALID, "null argument");
+  CUDA_TRY(cudaSetDevice(s->e->device));
+  CUDA_TRY(cudaMemcpy(state, s->gen_h.rng, (size_t)s->B * 4, cudaMemcpyDeviceToHost));
   return 0;
 }
 
@@ -1858,6 +1913,33 @@ struct MiniRun {
     ar.release();
   }
 };
+
+extern "C" int qtb_codec_sample_host(const float *logits, int batch, int n, const float *temperature,
+                                     const int32_t *top_k, const float *top_p, uint32_t *rng, int32_t *out) {
+  if (!logits || !temperature || !top_k || !top_p || !rng || !out) return set_err(QTB_E_INVALID, "null argument");
+  if (batch < 1 || batch > 64 || n < 1 || n > SAMPLE_MAX_ROWS) return set_err(QTB_E_INVALID, "batch %d, %d rows", batch, n);
+  MiniRun mr;
+  CUDA_TRY(cudaStreamCreateWithFlags(&mr.st, cudaStreamDefault));
+  GenState g = {};
+  g.eos_row = n - 1;
+  g.ld = n;
+  int rc;
+  int32_t *dout;
+  GenState *dg;
+  if ((rc = mr.ar.upload(&g.logits, logits, (size_t)batch * n * 4))) return rc;
+  if ((rc = mr.ar.upload(&g.temp, temperature, (size_t)batch * 4))) return rc;
+  if ((rc = mr.ar.upload(&g.top_k, top_k, (size_t)batch * 4))) return rc;
+  if ((rc = mr.ar.upload(&g.top_p, top_p, (size_t)batch * 4))) return rc;
+  if ((rc = mr.ar.upload(&g.rng, rng, (size_t)batch * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&dout, (size_t)batch * 4))) return rc;
+  if ((rc = mr.ar.upload(&dg, &g, sizeof g))) return rc;
+  sample_kernel<<<batch, 32, 0, mr.st>>>(dg, dout);
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaStreamSynchronize(mr.st));
+  CUDA_TRY(cudaMemcpy(out, dout, (size_t)batch * 4, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemcpy(rng, g.rng, (size_t)batch * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
 
 static int run_single_stage(MiniRun &mr, const Stage &S) {
   int rc;

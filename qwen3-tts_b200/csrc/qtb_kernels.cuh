@@ -112,6 +112,16 @@ struct GenState {
   int *boost_start;          // [B] 2 x expected frames, or -1: no EOS boost
   int *done;                 // [B] 0 running, 1 sampled EOS in this frame, 2 stopped (parked)
   uint16_t *rep_count;       // [B][vocab] occurrences of each code0 so far
+  // sampling (qwen_tts_sample): slots with temperature >= 1e-6 sample, the
+  // others take the greedy maximum; `sampling` makes the codec head keep its
+  // logits (after the rules above) for the sampler
+  int sampling;
+  int ld;                    // logits row stride (>= eos_row + 1)
+  float *logits;             // [B][ld] codec-head logits of this frame
+  float *temp;               // [B] temperature
+  int *top_k;                // [B] top-k (<= 0: off)
+  float *top_p;              // [B] top-p (>= 1: off)
+  unsigned *rng;             // [B] state of the reference's LCG (qwen_set_seed / qwen_get_seed)
 };
 
 struct GemvArgs {
@@ -760,9 +770,7 @@ QTB_DEV unsigned long long amax_key(float v, int row) {
 // slot's first two frames and boosted by min(0.5 (frame - boost_start), 10)
 // after its boost start; then every earlier occurrence of the token scales it
 // by 1 / penalty (positive) or penalty (otherwise), one rounding each.
-QTB_DEV float codec_logit(const GenState *gs, int b, int row, float v) {
-  if (row > gs->eos_row) return -1e30f;
-  if (!gs->enabled) return row == gs->eos_row ? -1e30f : v;
+QTB_DEV float codec_rules(const GenState *gs, int b, int row, float v) {
   if (v > 100.0f) v = 100.0f;
   if (v < -100.0f) v = -100.0f;
   const int frame = __ldcg(gs->frame + b);
@@ -779,6 +787,117 @@ QTB_DEV float codec_logit(const GenState *gs, int b, int row, float v) {
   const int c = __ldcg(gs->rep_count + (size_t)b * gs->vocab + row);
   for (int i = 0; i < c; i++) v = (v > 0.0f) ? __fmul_rn(v, gs->rep_inv) : __fmul_rn(v, gs->rep_pen);
   return v;
+}
+QTB_DEV float codec_logit(const GenState *gs, int b, int row, float v) {
+  if (row > gs->eos_row) return -1e30f;
+  if (!gs->enabled) return row == gs->eos_row ? -1e30f : v;
+  v = codec_rules(gs, b, row, v);
+  if (gs->sampling) __stcg(gs->logits + (size_t)b * gs->ld + row, v);
+  return v;
+}
+
+// Temperature / top-k / top-p sampling of slot b's codec-head logits (rows
+// 0 .. eos_row, the rules above applied), as the reference's qwen_tts_sample
+// does it after its repetition penalty (qwen_tts_sampling.c:52-202): softmax
+// at the temperature (x * (1 / T), exp, x * (1 / sum)), top-k keeping every
+// value >= the k-th largest, top-p keeping the largest values up to the first
+// whose running sum passes p, renormalisation, then one draw of the
+// reference's LCG (state * 1103515245 + 12345, 15 bits / 32768) against the
+// running sum in row order.  One warp; row i sits in lane i % 32, register
+// i / 32.  The sums run in a different order than the reference's loops (to
+// the last bits of f32); the k-th largest and the top-p cut are found by a
+// bitwise search over the non-negative probabilities' bit patterns.  Returns
+// the row drawn (eos_row = EOS).
+constexpr int SAMPLE_MAX_ROWS = 2176;
+QTB_DEV int sample_codec(const GenState *gs, int b) {
+  constexpr int PER = SAMPLE_MAX_ROWS / 32;
+  const int lane = threadIdx.x & 31;
+  const int n = gs->eos_row + 1;
+  const float *lg = gs->logits + (size_t)b * gs->ld;
+  const float temp = __ldcg(gs->temp + b);
+  const int top_k = __ldcg(gs->top_k + b);
+  const float top_p = __ldcg(gs->top_p + b);
+  float p[PER];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    const int r = i * 32 + lane;
+    p[i] = r < n ? __ldcg(lg + r) : -INFINITY;
+    mx = fmaxf(mx, p[i]);
+  }
+  mx = warp_max(mx);
+  const float inv_t = 1.0f / temp;
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    const int r = i * 32 + lane;
+    p[i] = r < n ? expf((p[i] - mx) * inv_t) : 0.f;
+    sum += p[i];
+  }
+  sum = warp_sum(sum);
+  float inv = 1.0f / sum;
+#pragma unroll
+  for (int i = 0; i < PER; i++) p[i] *= inv;
+  // the largest bit pattern t whose count / mass of {p >= t} still meets the bar
+  auto search = [&](bool by_mass, float bar) -> unsigned {
+    unsigned thr = 0u;
+    for (int bit = 30; bit >= 0; bit--) {
+      const unsigned cand = thr | (1u << bit);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < PER; i++)
+        if (__float_as_uint(p[i]) >= cand) acc += by_mass ? p[i] : 1.0f;
+      acc = warp_sum(acc);
+      if (by_mass ? (acc > bar) : (acc >= bar)) thr = cand;
+    }
+    return thr;
+  };
+  if (top_k > 0 && top_k < n) {
+    const unsigned thr = search(false, (float)top_k);
+#pragma unroll
+    for (int i = 0; i < PER; i++)
+      if (__float_as_uint(p[i]) < thr) p[i] = 0.f;
+  }
+  if (top_p < 1.0f && top_p > 0.0f) {
+    const unsigned thr = search(true, top_p);
+#pragma unroll
+    for (int i = 0; i < PER; i++)
+      if (__float_as_uint(p[i]) < thr) p[i] = 0.f;
+  }
+  sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; i++) sum += p[i];
+  sum = warp_sum(sum);
+  if (sum > 0.f) {
+    inv = 1.0f / sum;
+#pragma unroll
+    for (int i = 0; i < PER; i++) p[i] *= inv;
+  }
+  unsigned st = __ldcg(gs->rng + b);
+  st = st * 1103515245u + 12345u;
+  const float u = (float)((st >> 16) & 0x7FFFu) / 32768.0f;
+  // the first row whose running sum passes u; past the end, the last row
+  // with a non-zero probability (the reference then returns its last row)
+  float run = 0.f;
+  int pick = -1, last_nz = -1;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    float c = p[i];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float t = __shfl_up_sync(0xffffffffu, c, o);
+      if (lane >= o) c += t;
+    }
+    const float tot = run + c;
+    const unsigned hit = __ballot_sync(0xffffffffu, pick < 0 && u < tot);
+    if (pick < 0 && hit) pick = i * 32 + (__ffs(hit) - 1);
+    const unsigned nz = __ballot_sync(0xffffffffu, p[i] > 0.f);
+    if (nz) last_nz = i * 32 + (31 - __clz(nz));
+    run += __shfl_sync(0xffffffffu, c, 31);
+  }
+  if (lane == 0) gs->rng[b] = st;
+  __syncwarp();
+  return pick >= 0 ? pick : last_nz;
 }
 
 QTB_DEV unsigned long long shfl_xor_u64(unsigned long long v, int m) {
@@ -1262,6 +1381,9 @@ QTB_CALL void argmax_finish(const GemvArgs &a, int B, KCtx &kc) {
         best = o > best ? o : best;
       }
       int code = (int)(0xffffffffu - (unsigned)(best & 0xffffffffull));
+      // a running slot with a temperature samples instead of taking the maximum
+      if (a.gen && a.gen->enabled && a.gen->sampling && !__ldcg(a.gen->done + b) && __ldcg(a.gen->temp + b) >= 1e-6f)
+        code = sample_codec(a.gen, b);
       if (lane == 0) {
         if (a.gen && a.gen->enabled && !__ldcg(a.gen->done + b)) {
           // the codec head of a running slot: EOS stops it; other codes count
@@ -4049,6 +4171,13 @@ QTB_DEV bool grid_wait(KCtx &kc, char *smem) {
   }
   __syncthreads();
   return s_ok != 0;
+}
+
+// The codec-head sampler alone (qtb_codec_sample_host): block b, one warp,
+// samples row b of the logits in g.
+__global__ void __launch_bounds__(32) sample_kernel(const GenState *g, int *out) {
+  const int r = sample_codec(g, blockIdx.x);
+  if (threadIdx.x == 0) out[blockIdx.x] = r;
 }
 
 // ====================================================== persistent kernel ==

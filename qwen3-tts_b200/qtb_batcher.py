@@ -16,8 +16,10 @@ paged session of up to 64 slots:
   its pages and is parked on its own scratch page, so its idle talker step
   never touches pages that another request now owns.
 
-Greedy sampling only (the device codec head); every code of a request equals
-the codes of the same request run alone in a session of the same batch width.
+Each request decodes greedily or samples its code0 with its own temperature,
+top-k, top-p and seed (the device sampler, qtb_session_set_sampling); every
+code of a request equals the codes of the same request run alone in a session
+of the same batch width.
 """
 from __future__ import annotations
 
@@ -37,6 +39,10 @@ class GenRequest:
     prompt: np.ndarray          # [n][hidden] prompt embeddings (n >= 1)
     max_frames: int
     expected_frames: int = 0    # 3 x text tokens in the reference (EOS boost); 0 = none
+    temperature: float = 0.0    # code0 sampling (qtb_session_set_sampling); 0 = greedy
+    top_k: int = 50
+    top_p: float = 1.0
+    seed: int = 12345           # the request's own LCG seed, as the reference's per-slot seed
 
 
 class ContinuousBatcher:
@@ -87,6 +93,8 @@ class ContinuousBatcher:
                     s.prefill(b, r.prompt[:n - 1], 0)
                 s.set_slot_pos(b, n - 1)
                 s.reset_slot(b, r.expected_frames, active=True)
+                if r.temperature > 0.0:
+                    s.set_sampling(b, r.temperature, r.top_k, r.top_p, r.seed)
                 s.set_embed(b, r.prompt[n - 1])
                 slot_req[b], slot_pages[b] = r, pages
                 out[r.rid] = []

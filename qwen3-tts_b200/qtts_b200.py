@@ -90,6 +90,9 @@ def lib():
     L.qtb_session_begin_generation.argtypes = [_vp, _vp, C.c_float]
     L.qtb_prefill.argtypes = [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]
     L.qtb_session_program_grid.argtypes = [_vp, C.c_int]
+    L.qtb_session_set_sampling.argtypes = [_vp, C.c_int, C.c_float, C.c_int, C.c_float, C.c_uint32]
+    L.qtb_session_get_rng.argtypes = [_vp, _vp]
+    L.qtb_codec_sample_host.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp]
     L.qtb_session_reset_slot.argtypes = [_vp, C.c_int, C.c_int, C.c_int]
     L.qtb_session_set_slot_pos.argtypes = [_vp, C.c_int, C.c_int]
     L.qtb_session_set_embed.argtypes = [_vp, C.c_int, _vp]
@@ -428,6 +431,16 @@ class Session:
         check(lib().qtb_decode_frames(self.h, ptr(e), ptr(pd), n_frames, ptr(codes), ptr(hid)))
         return codes, hid
 
+    def set_sampling(self, b, temperature, top_k=50, top_p=1.0, seed=12345):
+        """Slot b samples code0 (qtb_session_set_sampling); temperature 0 = greedy."""
+        check(lib().qtb_session_set_sampling(self.h, int(b), float(temperature), int(top_k), float(top_p),
+                                             int(seed) & 0xffffffff))
+
+    def get_rng(self):
+        st = np.zeros(self.B, np.uint32)
+        check(lib().qtb_session_get_rng(self.h, ptr(st)))
+        return st
+
     def program_grid(self, which):
         """CTAs of program `which` (0 talker, 1 CP pass, 2 CP frame, 3 frame,
         4 prefill); negative = one cluster of that many CTAs."""
@@ -518,3 +531,17 @@ def attention(qkv, n_heads, n_kv, q_norm, k_norm, eps, rope_cos, rope_sin, kpage
                                    rope_cos.shape[0], ptr(kpages), ptr(vpages), kpages.shape[0], ptr(pt), pt.shape[1],
                                    ptr(np.ascontiguousarray(pos, np.int32)), max_splits, ptr(out)))
     return out
+
+
+def codec_sample(logits, temperature, top_k, top_p, rng):
+    """The device sampler on host logits [batch][n] (qtb_codec_sample_host);
+    returns (rows drawn, updated LCG states)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    B, n = lg.shape
+    t = np.ascontiguousarray(np.broadcast_to(temperature, (B,)), np.float32)
+    k = np.ascontiguousarray(np.broadcast_to(top_k, (B,)), np.int32)
+    p = np.ascontiguousarray(np.broadcast_to(top_p, (B,)), np.float32)
+    st = np.array(np.broadcast_to(rng, (B,)), np.uint32)
+    out = np.zeros(B, np.int32)
+    check(lib().qtb_codec_sample_host(ptr(lg), B, n, ptr(t), ptr(k), ptr(p), ptr(st), ptr(out)))
+    return out, st

@@ -255,3 +255,33 @@ def test_backend_vtable_matmat_bf16(have_gpu):
         assert rel_l2(y, O.f32_from_bf16(W).astype(np.float64) @ x) < GEMV_TOL
     finally:
         L.qwen_cuda_free(ctx)
+
+
+def test_codec_sampler_matches_reference(have_gpu):
+    """The device sampler of the codec head (softmax at a temperature, top-k,
+    top-p, one draw of the reference's LCG) against the reference's
+    qwen_tts_sample on the same logits: the LCG state always equal, the token
+    equal except where the draw falls within f32 rounding (1e-5) of a
+    cumulative-probability boundary (the sums run in another order)."""
+    import refbind
+    rng = np.random.default_rng(8)
+    rows, n = 64, 2049
+    for rep in range(4):
+        lg = (rng.standard_normal((rows, n)) * rng.uniform(0.5, 4, (rows, 1))).astype(np.float32)
+        lg[:, n - 1] = rng.choice([-1e30, 2.0], rows)          # the EOS row, masked or live
+        temp = rng.choice([0.5, 0.9, 1.3], rows).astype(np.float32)
+        top_k = rng.choice([0, 1, 20, 50, 5000], rows).astype(np.int32)
+        top_p = rng.choice([1.0, 0.9, 0.5], rows).astype(np.float32)
+        seed = rng.integers(0, 2 ** 32, rows, dtype=np.uint64).astype(np.uint32)
+        got, st = Q.codec_sample(lg, temp, top_k, top_p, seed)
+        near = 0
+        for b in range(rows):
+            want, wst = refbind.sample_logits(lg[b], float(temp[b]), int(top_k[b]), float(top_p[b]), int(seed[b]))
+            assert int(st[b]) == wst, b
+            if int(got[b]) != want:
+                tok, _, u, cums = O.sample(lg[b], float(temp[b]), int(top_k[b]), float(top_p[b]), int(seed[b]))
+                assert tok == want
+                lo, hi = sorted((int(got[b]), want))
+                assert np.min(np.abs(cums[lo:hi + 1] - u)) < 1e-5, (b, got[b], want)
+                near += 1
+        assert near <= 2, near

@@ -414,6 +414,60 @@ def test_generation_rules_eos_and_repetition_match_reference(have_gpu, tmp_path)
     assert list(ses.get_pos()) == [8 + len(want[0]) - 1 + 1, 8 + len(want[1]) - 1 + 1]
 
 
+def test_sampling_frames_match_reference(have_gpu, tmp_path):
+    """Sampled generation on the device (qtb_session_set_sampling): two slots
+    with their own temperature / top-k / top-p and LCG seed, against the
+    reference's loop sampling code0 with qwen_tts_sample under the same
+    seeds (its per-slot seed swap, qwen_tts.c:2641-2643).  Every code up to
+    each slot's EOS matches, and the LCG states after the last frame do."""
+    cfg, m = biased_head_model()
+    path = str(tmp_path / "samp.safetensors")
+    refbind.write_safetensors(path, refbind.model_tensors(m))
+    rep, expected = 1.05, [4, 6]
+    params = [(0.9, 50, 1.0, 777), (0.7, 20, 0.9, 4242)]
+    rng = np.random.default_rng(23)
+    prompt = (0.1 * rng.standard_normal((9, cfg.hidden))).astype(np.float32)
+    cpe = [O.f32_from_bf16(t) for t in m.cp_codec_emb]
+    want, seeds = [], []
+    for b in range(2):
+        ref = refbind.RefModel(path, cfg, threads=8)
+        for pos in range(8):
+            ref.talker_step(prompt[pos])
+        t, k, p, seed = params[b]
+        h = ref.talker_step(prompt[8])
+        prev, out = [], []
+        for f in range(40):
+            c0, seed = ref.codec_sample_t(h, f, expected[b], rep, prev, t, k, p, seed)
+            if c0 == Q.CODEC_EOS:
+                out.append([Q.CODEC_EOS] + [-1] * 15)
+                break
+            prev.append(c0)
+            codes = ref.cp_predict(h, c0)
+            out.append([c0] + list(codes))
+            nxt = ref.codec_embed(c0)
+            for g in range(15):
+                nxt = (nxt + cpe[g][codes[g]]).astype(np.float32)
+            h = ref.talker_step(nxt)
+        want.append(np.array(out, np.int32))
+        seeds.append(seed)
+        if b == 0:
+            eng = engine_from_ref(ref, m, cfg, "bf16", with_cp=True)
+        ref.close()
+    ses = Q.Session(eng, 2, 256)
+    for pos in range(8):
+        ses.talker_step(np.stack([prompt[pos]] * 2), pos)
+    ses.set_pos([8, 8])
+    ses.begin_generation(expected, rep)
+    for b in range(2):
+        ses.set_sampling(b, *params[b])
+    got, _ = ses.decode_frames(np.stack([prompt[8]] * 2), 40)
+    for b in range(2):
+        n = len(want[b])
+        assert np.array_equal(got[:n, b, :], want[b]), (b, got[:n, b, :4], want[b][:, :4])
+    if all(w[-1, 0] == Q.CODEC_EOS for w in want):
+        assert list(ses.get_rng()) == seeds
+
+
 def test_continuous_batching_admit_evict(have_gpu):
     """Continuous batching (qtb_batcher): 6 requests of different prompt
     lengths and expected lengths through 2 slots of a paged session; slots are

@@ -157,3 +157,19 @@ def test_cp_predict_matches_reference(tiny):
         codes_or, _ = O.cp_predict(cp, m.cp_norm, lm, emb, cemb, hidden, code0)
         assert np.array_equal(codes_ref, codes_or), (it, codes_ref, codes_or)
     ref.close()
+
+
+def test_sampler_matches_reference():
+    """The restated sampler (qtts_oracle.sample) draws the reference's
+    qwen_tts_sample token and leaves its LCG in the same state, over random
+    logits, temperatures, top-k and top-p settings."""
+    rng = np.random.default_rng(1)
+    for _ in range(120):
+        lg = (rng.standard_normal(2049) * rng.uniform(0.5, 4)).astype(np.float32)
+        temp = float(rng.choice([0.0, 0.5, 0.9, 1.3]))
+        k = int(rng.choice([0, 1, 20, 50, 3000]))
+        p = float(rng.choice([1.0, 0.9, 0.5]))
+        seed = int(rng.integers(0, 2 ** 32))
+        want = refbind.sample_logits(lg, temp, k, p, seed)
+        got = O.sample(lg, temp, k, p, seed)
+        assert (got[0], got[1]) == want, (temp, k, p, seed, got[:2], want)
