@@ -773,7 +773,9 @@ struct qtb_session {
   float *cp_in = nullptr;    // [B][talker hidden] input of qtb_cp_frame
   float *pad = nullptr;      // [hidden]
   float *ws = nullptr; size_t ws_floats = 0;
-  float *ss_ws = nullptr;    // tcgen05 stages: per-(row group, slice) sums of squares [G][64]
+  float *xsc = nullptr;      // tcgen05 stages: per-batch-row part scale and 1/rms [2][64]
+  uint8_t *xop = nullptr;    // tcgen05 stages: the activation in the MMA's B-operand layout
+  size_t xop_bytes = 0;
   StackBufs pf;              // prefill chunk buffers (PREFILL_CHUNK rows) over the talker's KV pools
   int *pf_pos = nullptr;     // [PREFILL_CHUNK] positions of the chunk's tokens
   PromptKV *pkv = nullptr;   // device descriptor of the prompt's f32 K/V (pkv_h: its host copy)
@@ -872,10 +874,13 @@ static bool cl_ok(int fmt, int rows, int K, int B) {
   return true;
 }
 
-// tcgen05 stage shape: slices of kcn K chunks (S of them) x row groups R of
-// 128-row tiles over the G CTAs, minimising the weight chunks the busiest CTA
-// streams plus the split-K fix-up.  The staged activation slice must fit
-// TC_X_BYTES (N x 128 bytes per chunk) and 2048 columns.
+// tcgen05 stage shape: S k-slices of kcn chunks x R row groups of 128-row tiles
+// over the G CTAs, minimising the busiest CTA's copy time (a chunk is a 16 KB
+// weight tile plus its N x 128-byte operand block; three chunks in flight
+// stream at ~60 GB/s into one SM, measured) plus the split-K fix-up: a wait
+// on the tile's other slices (~2 us) and ~1.5 us per 16-row sub-tile the CTA
+// then adds up over the slices (8 sub-tiles per tile, shared by the first
+// min(S, 8) slices).
 struct TcShape { int S = 0, kcn = 0, R = 0; };
 // The tensor-core page loop is opt-in (QTB_ATTN_TC=1, read at each program
 // build / standalone call): measured on B200 it is slower than the CUDA-core
@@ -885,20 +890,21 @@ static bool attn_tc_enabled() {
   return v && v[0] == '1';
 }
 static bool tc_ok(const DMat &m, int B, int fmt) {
-  return tc_enabled() && m.wtc && B >= 1 && B <= 64 && (fmt == FMT_BF16 || fmt == FMT_INT8) && m.rows % 128 == 0;
+  return tc_enabled() && m.wtc && B >= 1 && B <= 64 && (fmt == FMT_BF16 || fmt == FMT_INT8) && m.rows % 128 == 0 &&
+         (size_t)m.K * 4 <= (size_t)TC_NSLOT * TC_XSLOT_BYTES;   // the prep phase's row buffer
 }
 static TcShape tc_choose(int fmt, int rows, int K, int B, int G) {
   const int T = rows / 128, NKC = K * (fmt == FMT_INT8 ? 1 : 2) / 128;
   const int N = tc_parts(fmt) * tc_bpad(fmt, B);
-  const int kcmax = std::max(1, std::min(TC_X_BYTES / (N * 128), 2048 / tc_kchunk(fmt)));
+  const double chunk_us = (TC_SLOT_BYTES + (double)N * 128) / 60e3;
   TcShape best;
   double best_cost = 1e30;
-  for (int kcn = 1; kcn <= std::min(kcmax, NKC); kcn *= 2) {   // powers of two (activation staging)
-    const int S = (NKC + kcn - 1) / kcn;
-    if (S > G) continue;
-    const int R = std::max(1, G / S);
+  for (int S = 1; S <= std::min(NKC, G); S++) {
+    const int kcn = (NKC + S - 1) / S;
+    if ((S - 1) * kcn >= NKC) continue;   // the last slice would be empty
+    const int R = std::min(T, std::max(1, G / S));
     const int tpg = (T + R - 1) / R;
-    const double cost = (double)tpg * kcn + (S > 1 ? 2.0 + 0.1 * S : 0.0);
+    const double cost = tpg * kcn * chunk_us + (S > 1 ? 2.0 + 1.5 * tpg * ((8 + S - 1) / S) : 0.0);
     if (cost < best_cost - 1e-9) { best_cost = cost; best.S = S; best.kcn = kcn; best.R = R; }
   }
   return best;
@@ -953,7 +959,7 @@ struct ProgBuilder {
       g.tc = 1;
       g.wtc = m.wtc;
       g.S = sh.S;
-      g.ss_ws = s->ss_ws;
+      g.xsc = s->xsc; g.xop = s->xop;
       g.evict_last = evict_last;
       g.x = x; g.ldx = ldx; g.norm_w = norm_w; g.eps = eps;
       g.y = y; g.ldy = ldy; g.epi = epi;
@@ -961,6 +967,10 @@ struct ProgBuilder {
       g.amax_ws = s->amax_ws; g.amax_sem = s->amax_sem;
       if (sh.S < 1) { err = set_err(QTB_E_UNSUPPORTED, "no tcgen05 shape for %dx%d at B=%d", m.rows, m.K, B); return; }
       if (tc_ws_floats(m.fmt, m.rows, m.K, B, grid()) > s->ws_floats) { err = set_err(QTB_E_INVALID, "split-K workspace too small"); return; }
+      if (tc_xop_bytes(m.fmt, m.K) > s->xop_bytes || B > grid() || (size_t)m.K * 4 > (size_t)TC_NSLOT * TC_XSLOT_BYTES) {
+        err = set_err(QTB_E_INVALID, "tcgen05 operand staging too small (K=%d, B=%d)", m.K, B);
+        return;
+      }
       st.push_back(S);
       return;
     }
@@ -1342,7 +1352,7 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
   {
     // workspaces sized for the largest GEMV stage of either stack
     const int W = e->n_sm * NWARPS;
-    size_t ws = 16;
+    size_t ws = 16, xop = 16;
     int sem_n = 16;
     auto acc_b = [&](const DMat &m, int Bx) {
       if (!m.w) return;
@@ -1350,7 +1360,10 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
       const int S = choose_S(T, m.K, Bx, W, m.fmt);
       if (S > 0) ws = std::max(ws, (size_t)T * S * 16 * Bx);
       ws = std::max(ws, (size_t)T * std::max(1, e->n_sm / std::max(1, T)) * 16 * Bx);
-      if (tc_ok(m, Bx, m.fmt)) ws = std::max(ws, tc_ws_floats(m.fmt, m.rows, m.K, Bx, e->n_sm));
+      if (tc_ok(m, Bx, m.fmt)) {
+        ws = std::max(ws, tc_ws_floats(m.fmt, m.rows, m.K, Bx, e->n_sm));
+        xop = std::max(xop, tc_xop_bytes(m.fmt, m.K));
+      }
       sem_n = std::max(sem_n, T);
     };
     auto acc = [&](const DMat &m) { acc_b(m, B); };
@@ -1358,7 +1371,7 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
       for (const DLayer &L : k.layers) { acc(L.qkv); acc(L.o); acc(L.gu); acc(L.down); }
     };
     acc_stack(e->talker);
-    for (const DLayer &L : e->talker.layers) {   // the prefill program's chunks
+    for (const DLayer &L : (e->has_talker_pf ? e->talker_pf : e->talker).layers) {   // the prefill program's chunks
       acc_b(L.qkv, PREFILL_CHUNK); acc_b(L.o, PREFILL_CHUNK); acc_b(L.gu, PREFILL_CHUNK); acc_b(L.down, PREFILL_CHUNK);
     }
     acc_stack(e->cp);
@@ -1372,7 +1385,9 @@ extern "C" int qtb_session_create(qtb_engine_t *e, int batch, int max_ctx, int n
     if ((rc = s->ar.alloc((void **)&s->amax_ws, (size_t)sem_n * B * 8))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->amax_sem, 64))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->ctl, sizeof(Ctl)))) goto fail;
-    if ((rc = s->ar.alloc((void **)&s->ss_ws, (size_t)e->n_sm * 64 * 4))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->xsc, 128 * 4))) goto fail;
+    if ((rc = s->ar.alloc((void **)&s->xop, xop))) goto fail;
+    s->xop_bytes = xop;
     if ((rc = s->ar.alloc((void **)&s->pos, B * 4))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->cp_pos, B * 4))) goto fail;
     if ((rc = s->ar.alloc((void **)&s->codes, (size_t)B * 16 * 4))) goto fail;
@@ -1535,7 +1550,7 @@ static int launch_prog(qtb_session *s, int which, int n_iters, bool timed) {
   if ((long long)n_iters * s->prog_n[which] * G > 0x3fffffffLL)
     return set_err(QTB_E_INVALID, "too many iterations for one launch");
   CUDA_TRY(cudaMemsetAsync(&s->ctl->bar_count, 0, sizeof(unsigned), s->stream));
-  CUDA_TRY(cudaMemsetAsync(&s->ctl->att_work, 0, sizeof(unsigned), s->stream));
+  CUDA_TRY(cudaMemsetAsync(&s->ctl->att_work, 0, 2 * sizeof(unsigned), s->stream));   // att_work, ibar
   if (s->tc_sem_n[which] > 0)
     CUDA_TRY(cudaMemsetAsync(s->tc_sem[which], 0, (size_t)s->tc_sem_n[which] * sizeof(unsigned), s->stream));
   const Stage *prog = s->prog[which];
@@ -1982,7 +1997,8 @@ extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols,
   const int re[1] = {rows};
   int rc = upload_matrix(mr.ar, fmt, ms, re, 1, cols, m);
   if (rc) return rc;
-  float *dx, *dy, *ws, *ss_ws;
+  float *dx, *dy, *ws, *xsc;
+  uint8_t *xop;
   unsigned *sem;
   const int T = rows / 16;
   const bool v2 = v2_ok(fmt, rows, cols, batch, nsm);
@@ -1994,7 +2010,8 @@ extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols,
   if ((rc = mr.ar.upload(&dx, x, (size_t)batch * cols * 4))) return rc;
   if ((rc = mr.ar.alloc((void **)&dy, (size_t)batch * rows * 4))) return rc;
   if ((rc = mr.ar.alloc((void **)&ws, ws_floats * 4))) return rc;
-  if ((rc = mr.ar.alloc((void **)&ss_ws, (size_t)nsm * 64 * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&xsc, 128 * 4))) return rc;
+  if ((rc = mr.ar.alloc((void **)&xop, tc ? tc_xop_bytes(fmt, cols) : 16))) return rc;
   if ((rc = mr.ar.alloc((void **)&sem, (size_t)T * 4))) return rc;
   CUDA_TRY(cudaMemset(sem, 0, (size_t)T * 4));
   Stage st;
@@ -2007,7 +2024,7 @@ extern "C" int qtb_gemv_host(int fmt, const qtb_matrix_t *w, int rows, int cols,
   g.v2 = v2 ? 1 : 0;
   g.tc = tc ? 1 : 0;
   g.wtc = m.wtc;
-  g.ss_ws = ss_ws;
+  g.xsc = xsc; g.xop = xop;
   g.x = dx; g.ldx = cols; g.y = dy; g.ldy = rows; g.epi = EPI_STORE; g.ws = ws; g.sem = sem;
   if ((rc = run_single_stage(mr, st))) return rc;
   CUDA_TRY(cudaMemcpy(y, dy, (size_t)batch * rows * 4, cudaMemcpyDeviceToHost));
@@ -2105,6 +2122,10 @@ extern "C" int qtb_session_profile(qtb_session_t *s, int which, long long *cycle
   }
   CUDA_TRY(cudaMemset(s->trace, 0, (size_t)need * 8));
   { int rc0 = begin_call(s); if (rc0) return rc0; }
+  if (const char *tc = getenv("QTB_TRACE_CTA")) {   // checkpoints of another CTA than 0
+    const int cta = atoi(tc);
+    CUDA_TRY(cudaMemcpyAsync(&s->ctl->trace_cta, &cta, sizeof cta, cudaMemcpyHostToDevice, s->stream));
+  }
   s->trace_on = 1;
   int rc = launch_prog(s, which, 1, true);
   s->trace_on = 0;
@@ -2126,7 +2147,8 @@ extern "C" int qtb_session_profile(qtb_session_t *s, int which, long long *cycle
   return n;
 }
 
-// Intra-stage checkpoints (NCKPT per stage, CTA 0 clock64, 0 = not reached) of the
+// Intra-stage checkpoints (NCKPT per stage, clock64 of CTA 0 or of CTA $QTB_TRACE_CTA,
+// 0 = not reached) of the
 // last qtb_session_profile call.
 extern "C" int qtb_session_profile_checkpoints(qtb_session_t *s, long long *out, int max_vals) {
   if (!s) return set_err(QTB_E_INVALID, "null session");
@@ -2264,12 +2286,13 @@ struct OpCtx {
   Arena weights;
   std::vector<OpWeight> cache;
   cudaStream_t st = nullptr;
-  float *dx = nullptr, *dy = nullptr, *ws = nullptr, *ss_ws = nullptr;
+  float *dx = nullptr, *dy = nullptr, *ws = nullptr, *xsc = nullptr;
+  uint8_t *xop = nullptr;
   unsigned *sem = nullptr;
   Ctl *ctl = nullptr;
   Stage *dstage = nullptr;
   V2Plan *dplan = nullptr;
-  size_t x_cap = 0, y_cap = 0, ws_cap = 0, sem_cap = 0, ss_cap = 0;
+  size_t x_cap = 0, y_cap = 0, ws_cap = 0, sem_cap = 0, xsc_cap = 0, xop_cap = 0;
 };
 
 int op_grow(void **p, size_t *cap, size_t need) {
@@ -2316,7 +2339,8 @@ int op_matmat(OpCtx *c, float *Y, const uint16_t *W, const float *X, int rows, i
   if ((rc = op_grow((void **)&c->dx, &c->x_cap, (size_t)B * cp * 4))) return rc;
   if ((rc = op_grow((void **)&c->dy, &c->y_cap, (size_t)B * rp * 4))) return rc;
   if ((rc = op_grow((void **)&c->ws, &c->ws_cap, ws_floats * 4))) return rc;
-  if ((rc = op_grow((void **)&c->ss_ws, &c->ss_cap, (size_t)c->nsm * 64 * 4))) return rc;
+  if ((rc = op_grow((void **)&c->xsc, &c->xsc_cap, 128 * 4))) return rc;
+  if ((rc = op_grow((void **)&c->xop, &c->xop_cap, tc ? tc_xop_bytes(FMT_BF16, cp) : 16))) return rc;
   if ((rc = op_grow((void **)&c->sem, &c->sem_cap, (size_t)T * 4))) return rc;
   // X [cols][B] -> [B][cp] (zero-padded columns)
   std::vector<float> xt((size_t)B * cp, 0.f), yt((size_t)B * rp);
@@ -2332,7 +2356,7 @@ int op_matmat(OpCtx *c, float *Y, const uint16_t *W, const float *X, int rows, i
   GemvArgs &g = s.g;
   g.w = ow->m.w; g.fmt = FMT_BF16; g.rows = rp; g.K = cp; g.S = v2 ? 1 : S;
   g.nch = nch_for(FMT_BF16, B, v2); g.parts = parts_for(FMT_BF16, B, v2); g.v2 = v2 ? 1 : 0;
-  g.tc = tc ? 1 : 0; g.wtc = ow->m.wtc; g.ss_ws = c->ss_ws;
+  g.tc = tc ? 1 : 0; g.wtc = ow->m.wtc; g.xsc = c->xsc; g.xop = c->xop;
   g.x = c->dx; g.ldx = cp; g.y = c->dy; g.ldy = rp; g.epi = EPI_STORE; g.ws = c->ws; g.sem = c->sem;
   CUDA_TRY(cudaMemcpyAsync(c->dstage, &s, sizeof s, cudaMemcpyHostToDevice, c->st));
   std::vector<V2Plan> pl;
@@ -2398,7 +2422,7 @@ extern "C" void qwen_cuda_free(void *ctx) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->st) cudaStreamSynchronize(c->st);
-  for (void *p : {(void *)c->dx, (void *)c->dy, (void *)c->ws, (void *)c->sem, (void *)c->ss_ws})
+  for (void *p : {(void *)c->dx, (void *)c->dy, (void *)c->ws, (void *)c->sem, (void *)c->xsc, (void *)c->xop})
     if (p) cudaFree(p);
   if (c->st) cudaStreamDestroy(c->st);
   c->weights.release();

@@ -70,17 +70,19 @@ constexpr int SMEM_X_BYTES = 96 * 1024;
 
 // tcgen05 GEMV stages (large batches, bf16 / int8 weights): the dynamic shared
 // memory, from its first 1024-byte aligned byte, holds TC_NSLOT weight slots
-// of one 128-row x 128-byte operand tile each, then the staged activation
-// (the B operand, up to TC_X_BYTES); a little scratch sits at TC_SCR_OFF.
-// These stages never share a program with the small-batch weight ring.
-constexpr int TC_NSLOT = 5;
+// of one 128-row x 128-byte operand tile each, then TC_NSLOT activation slots
+// of one N x 128-byte operand block each (before them, the prep phase's row
+// buffer); a little scratch sits at TC_SCR_OFF.  These stages never share a
+// program with the small-batch weight ring.
+constexpr int TC_NSLOT = 3;
 constexpr int TC_SLOT_BYTES = 16384;
-constexpr int TC_X_OFF = TC_NSLOT * TC_SLOT_BYTES;
-constexpr int TC_X_BYTES = 64 * 1024;
-constexpr int TC_SCR_OFF = 146 * 1024;   // past TC_X_OFF + TC_X_BYTES + the 1 KB alignment slack
+constexpr int TC_XSLOT_BYTES = 32768;    // N <= 256 operand rows
+constexpr int TC_XR_OFF = TC_NSLOT * TC_SLOT_BYTES;
+constexpr int TC_SCR_OFF = 146 * 1024;   // past the slots + the 1 KB alignment slack
 constexpr int TC_ACC_COLS = 256;         // one 128 x N (N <= 256) 32-bit accumulator
 constexpr int TC_TMEM_COLS = 2 * TC_ACC_COLS;   // two: a tile is read back while the next accumulates
-static_assert(TC_X_OFF + TC_X_BYTES + 1024 <= TC_SCR_OFF && TC_SCR_OFF + 4096 <= SMEM_BYTES, "tcgen05 stage smem map");
+static_assert(TC_XR_OFF + TC_NSLOT * TC_XSLOT_BYTES + 1024 <= TC_SCR_OFF && TC_SCR_OFF + 4096 <= SMEM_BYTES,
+              "tcgen05 stage smem map");
 
 // Single-cluster schedule for small batches: the launch is one cluster of
 // CL_G CTAs (cluster barriers instead of the grid barrier), and each warp
@@ -137,7 +139,8 @@ struct GemvArgs {
   int tc;                    // large-batch path on tcgen05 (bf16 / int8 weights, see gemv_tc_t)
   int cl;                    // single-cluster schedule (gemv_cl_t): per-warp weight pieces
   const uint8_t *wtc;        // weights in 128-row x 128-byte swizzled tiles (tcgen05 operand layout)
-  float *ss_ws;              // tcgen05 path: per-(row group, k-slice) activation sums of squares
+  uint8_t *xop;              // tcgen05 path: the activation as the MMA's B operand (tc_prep_row)
+  float *xsc;                // tcgen05 path: [64] part scale sx, [64] 1/rms of each batch row
   int sem_off;               // tcgen05 path: this stage's per-tile counters are sem[sem_off + tile]
   const float *x; int ldx;   // activation [B][ldx]
   const float *norm_w;       // RMSNorm gain [K] or null
@@ -226,7 +229,9 @@ struct Ctl {
   int err_stage;        // stage index that raised it
   int err_info;
   unsigned att_work;    // attention work items taken (dynamic order; zeroed before each launch)
-  int pad[59];
+  unsigned ibar;        // tcgen05 stages: activation rows prepared (monotonic; zeroed before each launch)
+  int trace_cta;        // the CTA whose intra-stage checkpoints a stage profile records
+  int pad[57];
 };
 
 // Per-CTA kernel state, one copy in shared memory.  Fields are written by
@@ -249,7 +254,8 @@ struct KCtx {
   uint64_t *wbars;      // NWSLOT weight-slot mbarriers
   Ctl *ctl;
   int stage;
-  long long *trace2;    // optional intra-stage checkpoints: [stage][8] clock64 of CTA 0
+  long long *trace2;    // optional intra-stage checkpoints: [stage][NCKPT] clock64 of CTA trace_cta
+  int trace_cta;
   unsigned long long *gtrace;  // optional [stage][cta] global time at arrival
   long long t_start;    // clock64 when this CTA left the last barrier
   // stage program and the weight streamer (streamer fields: thread 0 only)
@@ -275,6 +281,7 @@ struct KCtx {
   unsigned tc_done;     // ... whose bulk copy has been waited for
   unsigned tc_committed;// tile accumulators committed so far (the g-th uses buffer g & 1)
   unsigned tc_waited;   // ... and waited for
+  unsigned ibar_target; // ctl->ibar count that the current tcgen05 stage's prep completes
   // single-cluster schedule (a launch of one cluster of CL_G CTAs, see gemv_cl_t)
   int cl;               // this launch runs it: cluster barriers, per-warp weight pieces
   uint64_t *clbars;     // [2 * NWARPS] mbarriers of the warps' two weight slots
@@ -286,11 +293,11 @@ struct KCtx {
 
 // Profiling checkpoint (CTA 0, thread 0) when stage tracing is on.
 QTB_DEV void ckpt(const KCtx &kc, int i) {
-  if (kc.trace2 && blockIdx.x == 0 && threadIdx.x == 0) kc.trace2[(size_t)kc.stage * NCKPT + i] = clock64();
+  if (kc.trace2 && blockIdx.x == (unsigned)kc.trace_cta && threadIdx.x == 0) kc.trace2[(size_t)kc.stage * NCKPT + i] = clock64();
 }
 // Per-warp checkpoint (CTA 0, lane 0 of each warp): slot base + warp.
 QTB_DEV void ckpt_w(const KCtx &kc, int base) {
-  if (kc.trace2 && blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+  if (kc.trace2 && blockIdx.x == (unsigned)kc.trace_cta && (threadIdx.x & 31) == 0)
     kc.trace2[(size_t)kc.stage * NCKPT + base + (threadIdx.x >> 5)] = clock64();
 }
 
@@ -1611,6 +1618,7 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, int k
     }
   }
   ckpt(kc, 8);
+  ckpt_w(kc, 16);
 #pragma unroll
   for (int bb = 0; bb < 4; bb++) {
     if (bb < B) {   // warp-uniform
@@ -1619,7 +1627,9 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, int k
     }
   }
   for (int i = tid; i < n_zero; i += NTHREADS) s_zero[i] = 0.f;   // the caller's partial sums
+  ckpt(kc, 12);
   __syncthreads();
+  ckpt(kc, 13);
   // every thread derives the scales itself (broadcast reads): no second barrier
   float inv[4], rsx[4];
 #pragma unroll
@@ -1637,6 +1647,7 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, int k
       if (tid == 0) s_scl[4 + bb] = sx;   // part scale, read after the caller's barrier
     }
   }
+  ckpt(kc, 14);
 #pragma unroll
   for (int i = 0; i < MAXQ; i++) {
     const int t = tid + i * NTHREADS;
@@ -1673,6 +1684,7 @@ __device__ __noinline__ void stage_x_s8(const GemvArgs &a, int B, int nch, int k
       }
     }
   }
+  ckpt(kc, 15);
 }
 
 // The two halves of a split stage (2-CTA cluster): the second half stores its
@@ -1835,6 +1847,7 @@ __device__ __noinline__ void gemv2_s8_t(const GemvArgs &a, int B, char *smem, KC
   __syncthreads();
   ckpt(kc, 4);
   if (role && !pair_combine(s_val, 16 * B, role, smem, kc)) return;
+  ckpt(kc, 24);
   if (fast_epi) {
     if (tid < s.nt * 16 * B) {
       const int b = tid % B, r = (tid / B) % 16, tl = tid / (16 * B);
@@ -2214,133 +2227,126 @@ QTB_DEV void gemv_cl_f(const GemvArgs &a, int B, char *smem, KCtx &kc) {
 
 // ============================================ GEMV stage on tcgen05 =======
 //
-// Large batches (5..64 rows) with bf16 or int8 weights.  A CTA owns one k-slice
-// of the activation and a run of 128-row tiles (its row group): the host plan
-// (V2Plan: t0, nt, L = nt * kc weight fills, nfill = row group, kb / kc = first
-// 128-byte chunk and chunk count of the slice, pair = slice, pad = row groups)
-// spreads tiles x slices over the grid.
-//  1. Thread 0 bulk-copies the first weight tiles -- 128 rows x one 128-byte K
-//     chunk, stored pre-swizzled in HBM (16 KB each) -- into TC_NSLOT slots.
-//  2. Every warp stages whole activation rows of the slice into the B operand
-//     (K-major, 128-byte swizzle), with the RMSNorm gain applied: int8 weights
-//     take four signed 8-bit parts per value, x g = sx (a0 + a1 2^-7 + a2 2^-14 +
-//     a3 2^-21) with sx = max|x g| / 127 over the row's slice (MMA column 4 b + p,
-//     kind::i8, exact s32 sums); bf16 weights take bf16 hi + lo parts (column
-//     2 b + p, kind::f16, f32 sums).  The RMSNorm's 1/rms multiplies each
-//     batch row's results afterwards, from the slices' sums of squares.
-//  3. Per tile, thread 0 issues four MMAs (M 128, N = parts x padded batch,
-//     32 bytes of K each) per chunk into the TMEM accumulator and refills each
-//     slot once the MMAs reading it have completed (tcgen05.commit ->
-//     mbarrier); all warps then read the accumulator (warp w: TMEM lanes
-//     32 (w % 4) .., batch half w / 4).
-//  4. With one slice the epilogue runs at once; with several, partial sums go
-//     to ws and the CTA completing a tile's count adds them in slice order
-//     (deterministic) and runs it.
+// Large batches (5..64 rows) with bf16 or int8 weights, in two phases.
+//  1. Prep: CTA b (b < B) turns activation row b into rows of the B operand in
+//     a global staging buffer `xop` (K-major, 128-byte swizzle, one block of
+//     N x 128 bytes per 128-byte K chunk), with the RMSNorm gain applied: int8
+//     weights take four signed 8-bit parts per value, x g = sx (a0 + a1 2^-7 +
+//     a2 2^-14 + a3 2^-21) with sx = max|x g| / 127 over the row (operand row
+//     4 b + p, kind::i8, exact s32 sums); bf16 weights take bf16 hi + lo parts
+//     (operand row 2 b + p, kind::f16, f32 sums).  It stores sx and the row's
+//     1/rms (1 without a norm) in xsc[b], xsc[64 + b], then counts itself on
+//     ctl->ibar.  Every other CTA meanwhile bulk-copies its first weight
+//     chunks.  The row goes through shared memory in rolled loops: the phase
+//     runs once per stage, and straight-line code that runs once is fetched
+//     into a cold instruction cache line by line.
+//  2. Stream: once B rows are counted, a CTA owns a run of 128-row tiles (its
+//     row group) over one k-slice (host plan V2Plan: t0, nt, kb / kc = first
+//     128-byte chunk and chunk count, pair = slice).  Thread 0 bulk-copies each
+//     chunk's pre-swizzled weight tile (128 rows x 128 bytes, 16 KB) and the
+//     matching operand block (N x 128 bytes) into one of TC_NSLOT slots and
+//     issues four MMAs (M 128, N = parts x padded batch, 32 bytes of K each)
+//     into the TMEM accumulator; a slot is refilled once the MMAs reading it
+//     have completed (tcgen05.commit -> mbarrier).  All warps read the
+//     accumulator back (warp w: TMEM lanes 32 (w % 4) .., batch half w / 4).
+//  3. With one slice the epilogue runs at once; with several, partial sums go
+//     to ws and the slices of a tile add them in slice order (deterministic)
+//     and run it.
 QTB_HOST_DEV constexpr int tc_parts(int fmt) { return fmt == FMT_INT8 ? 4 : 2; }
 QTB_HOST_DEV constexpr int tc_kchunk(int fmt) { return fmt == FMT_INT8 ? 128 : 64; }   // K per 128-byte chunk
 // Batch rows padded to a multiple of 8 (N = parts x rows a multiple of 16,
 // each warp's half of the batch a whole number of float4s).
 QTB_HOST_DEV constexpr int tc_bpad(int fmt, int B) { return (void)fmt, (B + 7) & ~7; }
+// Bytes of the operand staging buffer for K columns (B <= 64).
+QTB_HOST_DEV constexpr size_t tc_xop_bytes(int fmt, int K) {
+  return (size_t)(K / tc_kchunk(fmt)) * tc_parts(fmt) * 64 * 128;
+}
 
-QTB_DEV uint32_t tc_sw128(int n, int kb) {   // byte offset of (row n, byte kb of a 128-byte K chunk)
+QTB_HOST_DEV uint32_t tc_sw128(int n, int kb) {   // byte offset of (row n, byte kb of a 128-byte K chunk)
   return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((((kb >> 4) ^ (n & 7)) << 4) | (kb & 15)));
 }
 
-// Step 2: rows b = warp, warp + 8, ... of the slice [k0, k0 + KL).  A warp
-// takes 16 / N4 rows per pass (N4 = float4 per lane per row), all their loads
-// in flight together, then reduces and converts each row.
-template <int FMT, int N4>
-__device__ __noinline__ void tc_stage_x(const GemvArgs &a, int B, int N, int k0, int KL, char *xreg, float *s_sx,
-                                        float *s_ss) {
-  constexpr int RPP = 16 / N4;                  // rows per pass
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nq = KL >> 2;                       // float4 per row
-  // the RMSNorm gains of this lane's columns (the same for every row)
-  float4 gn[N4];
-#pragma unroll
-  for (int j = 0; j < N4; j++) {
-    const int q = lane + 32 * j;
-    gn[j] = (a.norm_w && q < nq) ? __ldg(reinterpret_cast<const float4 *>(a.norm_w + k0 + 4 * q))
-                                 : make_float4(1.f, 1.f, 1.f, 1.f);
-  }
-  for (int b0 = warp; b0 < B; b0 += NWARPS * RPP) {
-    float4 v[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const int b = b0 + NWARPS * (i / N4), q = lane + 32 * (i % N4);
-      v[i] = (b < B && q < nq) ? ld_cg4(a.x + (size_t)b * a.ldx + k0 + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    float ss[RPP], rs[RPP];
-#pragma unroll
-    for (int rr = 0; rr < RPP; rr++) {
-      float s2 = 0.f, m = 0.f;
-#pragma unroll
-      for (int j = 0; j < N4; j++) {
-        float4 &x = v[rr * N4 + j];
-        s2 += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
-        const float4 g = gn[j];
-        x.x *= g.x; x.y *= g.y; x.z *= g.z; x.w *= g.w;
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-      }
-      ss[rr] = warp_sum(s2);
-      const float sx = fmaxf(warp_max(m), 1e-30f) * (1.0f / 127.0f);
-      rs[rr] = __frcp_rn(sx);
-      const int b = b0 + NWARPS * rr;
-      if (lane == 0 && b < B) { s_ss[b] = ss[rr]; s_sx[b] = sx; }
-    }
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const int rr = i / N4, b = b0 + NWARPS * rr, q = lane + 32 * (i % N4);
-      if (b >= B || q >= nq) continue;
-      const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-      if (FMT == FMT_INT8) {
-        uint32_t w[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-          const float r = fminf(fmaxf(e[k] * rs[rr], -127.f), 127.f);
-          // fixed point r 2^21 as a leading part and three balanced base-128 digits
-          int I = __float2int_rn(r * 2097152.f);
-          const int d3 = ((I + 64) & 127) - 64;
-          I = (I - d3) >> 7;
-          const int d2 = ((I + 64) & 127) - 64;
-          I = (I - d2) >> 7;
-          const int d1 = ((I + 64) & 127) - 64;
-          const int a0 = (I - d1) >> 7;
-          w[0] |= ((uint32_t)a0 & 0xffu) << (8 * k);
-          w[1] |= ((uint32_t)d1 & 0xffu) << (8 * k);
-          w[2] |= ((uint32_t)d2 & 0xffu) << (8 * k);
-          w[3] |= ((uint32_t)d3 & 0xffu) << (8 * k);
-        }
-        const int kl = 4 * q, c = kl >> 7, kb = kl & 127;
-#pragma unroll
-        for (int p = 0; p < 4; p++)
-          *reinterpret_cast<uint32_t *>(xreg + (size_t)c * N * 128 + tc_sw128(4 * b + p, kb)) = w[p];
-      } else {
-        uint32_t hi[2], lo[2];
-#pragma unroll
-        for (int k = 0; k < 2; k++) {
-          const uint32_t h0 = f32_to_bf16_rn(e[2 * k]), h1 = f32_to_bf16_rn(e[2 * k + 1]);
-          const uint32_t l0 = f32_to_bf16_rn(e[2 * k] - __uint_as_float(h0 << 16));
-          const uint32_t l1 = f32_to_bf16_rn(e[2 * k + 1] - __uint_as_float(h1 << 16));
-          hi[k] = h0 | (h1 << 16);
-          lo[k] = l0 | (l1 << 16);
-        }
-        const int kbyte = 8 * q, c = kbyte >> 7, kb = kbyte & 127;
-        *reinterpret_cast<uint2 *>(xreg + (size_t)c * N * 128 + tc_sw128(2 * b, kb)) = make_uint2(hi[0], hi[1]);
-        *reinterpret_cast<uint2 *>(xreg + (size_t)c * N * 128 + tc_sw128(2 * b + 1, kb)) = make_uint2(lo[0], lo[1]);
-      }
-    }
-  }
+QTB_DEV void cp_async16(void *dst_smem, const void *src_gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
 }
+QTB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// Phase 1 for row b (the whole CTA): see the comment above.  `row` is K floats
+// of shared memory, s_red 16 floats.
 template <int FMT>
-QTB_DEV void tc_stage_x_f(const GemvArgs &a, int B, int N, int k0, int KL, char *xreg, float *s_sx, float *s_ss) {
-  const int n4 = ((KL >> 2) + 31) >> 5;
-  if (n4 <= 1) tc_stage_x<FMT, 1>(a, B, N, k0, KL, xreg, s_sx, s_ss);
-  else if (n4 <= 2) tc_stage_x<FMT, 2>(a, B, N, k0, KL, xreg, s_sx, s_ss);
-  else if (n4 <= 4) tc_stage_x<FMT, 4>(a, B, N, k0, KL, xreg, s_sx, s_ss);
-  else if (n4 <= 8) tc_stage_x<FMT, 8>(a, B, N, k0, KL, xreg, s_sx, s_ss);
-  else tc_stage_x<FMT, 16>(a, B, N, k0, KL, xreg, s_sx, s_ss);
+__device__ __noinline__ void tc_prep_row(const GemvArgs &a, int b, int N, float *row, float *s_red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nq = a.K >> 2;
+  const float *src = a.x + (size_t)b * a.ldx;
+#pragma unroll 1
+  for (int q = tid; q < nq; q += NTHREADS) cp_async16(row + 4 * q, src + 4 * q);
+  cp_async_wait_all();
+  __syncthreads();
+  float ss = 0.f, m = 0.f;
+#pragma unroll 1
+  for (int q = tid; q < nq; q += NTHREADS) {
+    const float4 v = *reinterpret_cast<const float4 *>(row + 4 * q);
+    const float4 g = a.norm_w ? __ldg(reinterpret_cast<const float4 *>(a.norm_w) + q) : make_float4(1.f, 1.f, 1.f, 1.f);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x * g.x), fabsf(v.y * g.y)), fmaxf(fabsf(v.z * g.z), fabsf(v.w * g.w))));
+  }
+  ss = warp_sum(ss);
+  m = warp_max(m);
+  if (lane == 0) { s_red[warp] = ss; s_red[NWARPS + warp] = m; }
+  __syncthreads();
+  float tot = 0.f, mx = 0.f;
+#pragma unroll
+  for (int w = 0; w < NWARPS; w++) { tot += s_red[w]; mx = fmaxf(mx, s_red[NWARPS + w]); }
+  const float sx = fmaxf(mx, 1e-30f) * (1.0f / 127.0f), rs = __frcp_rn(sx);
+  if (tid == 0) {
+    a.xsc[b] = sx;
+    a.xsc[64 + b] = a.norm_w ? 1.0f / sqrtf(tot / (float)a.K + a.eps) : 1.0f;
+  }
+  uint8_t *xop = a.xop;
+#pragma unroll 1
+  for (int q = tid; q < nq; q += NTHREADS) {
+    const float4 v = *reinterpret_cast<const float4 *>(row + 4 * q);
+    const float4 g = a.norm_w ? __ldg(reinterpret_cast<const float4 *>(a.norm_w) + q) : make_float4(1.f, 1.f, 1.f, 1.f);
+    const float e[4] = {v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w};
+    if (FMT == FMT_INT8) {
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float r = fminf(fmaxf(e[k] * rs, -127.f), 127.f);
+        // fixed point r 2^21 as a leading part and three balanced base-128 digits
+        int I = __float2int_rn(r * 2097152.f);
+        const int d3 = ((I + 64) & 127) - 64;
+        I = (I - d3) >> 7;
+        const int d2 = ((I + 64) & 127) - 64;
+        I = (I - d2) >> 7;
+        const int d1 = ((I + 64) & 127) - 64;
+        const int a0 = (I - d1) >> 7;
+        w[0] |= ((uint32_t)a0 & 0xffu) << (8 * k);
+        w[1] |= ((uint32_t)d1 & 0xffu) << (8 * k);
+        w[2] |= ((uint32_t)d2 & 0xffu) << (8 * k);
+        w[3] |= ((uint32_t)d3 & 0xffu) << (8 * k);
+      }
+      const int k0 = 4 * q, c = k0 >> 7, kb = k0 & 127;
+#pragma unroll
+      for (int p = 0; p < 4; p++)
+        __stcg(reinterpret_cast<unsigned *>(xop + (size_t)c * N * 128 + tc_sw128(4 * b + p, kb)), w[p]);
+    } else {
+      uint32_t hi[2], lo[2];
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const uint32_t h0 = f32_to_bf16_rn(e[2 * k]), h1 = f32_to_bf16_rn(e[2 * k + 1]);
+        const uint32_t l0 = f32_to_bf16_rn(e[2 * k] - __uint_as_float(h0 << 16));
+        const uint32_t l1 = f32_to_bf16_rn(e[2 * k + 1] - __uint_as_float(h1 << 16));
+        hi[k] = h0 | (h1 << 16);
+        lo[k] = l0 | (l1 << 16);
+      }
+      const int kbyte = 8 * q, c = kbyte >> 7, kb = kbyte & 127;
+      __stcg(reinterpret_cast<uint2 *>(xop + (size_t)c * N * 128 + tc_sw128(2 * b, kb)), make_uint2(hi[0], hi[1]));
+      __stcg(reinterpret_cast<uint2 *>(xop + (size_t)c * N * 128 + tc_sw128(2 * b + 1, kb)), make_uint2(lo[0], lo[1]));
+    }
+  }
+  // the operand is read by other CTAs' bulk copies (async proxy)
+  fence_proxy_async();
 }
 
 // Final value of (row, batch b): 1/rms, row scale, bias, then the epilogue
@@ -2365,56 +2371,118 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
   const V2Plan pl = kc.pring[kc.seq % NDESC];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int P = tc_parts(FMT), Bp = tc_bpad(FMT, B), N = P * Bp, Bh = Bp / 2;
-  const int S = a.S, s = pl.pair, grp = pl.nfill, t0 = pl.t0, nt = pl.nt, kcn = pl.kc;
+  const int S = a.S, s = pl.pair, t0 = pl.t0, nt = pl.nt, kcn = pl.kc;
   const int NKC = a.K / tc_kchunk(FMT);
   const int L = nt * kcn;
-  // operand regions from the first 1024-byte aligned byte of dynamic smem
+  const uint32_t XB = (uint32_t)N * 128u;   // operand bytes per chunk
+  // slot regions from the first 1024-byte aligned byte of dynamic smem
   const uint32_t base_u = smem_u32(smem);
   char *tcb = smem + ((1024u - (base_u & 1023u)) & 1023u);
   char *wring = tcb;
-  char *xreg = tcb + TC_X_OFF;
+  char *xring = tcb + TC_XR_OFF;
   float *s_sx = reinterpret_cast<float *>(smem + TC_SCR_OFF);   // [64]
-  float *s_ss = s_sx + 64;                                      // [64]
-  float *s_inv = s_ss + 64;                                     // [64]
+  float *s_red = s_sx + 64;                                     // [64]
+  float *s_inv = s_red + 64;                                    // [64]
   int *s_flag = reinterpret_cast<int *>(s_inv + 64);            // [4]
   unsigned long long *s_key = reinterpret_cast<unsigned long long *>(s_flag + 4);   // [4][64]
-  if (nt == 0) return;
   const uint64_t pol = a.evict_last ? kc.pol_last : kc.pol_first;
-  const unsigned F0 = kc.tc_issued;   // weight fills of earlier tcgen05 stages (all consumed)
+  const unsigned F0 = kc.tc_issued;   // fills of earlier tcgen05 stages (all consumed)
   const unsigned g0 = kc.tc_waited;   // accumulator uses so far (buffer g & 1 for the g-th)
+  const unsigned ib_target = kc.ibar_target + (unsigned)B;
 
-  // thread 0: bulk copy of fill f (tile t0 + f / kcn, chunk kb + f % kcn) into
-  // slot (F0 + f) % TC_NSLOT once the MMAs that last read the slot are done
-  auto issue = [&](int f) -> bool {
+  // thread 0: fill f (tile t0 + f / kcn, chunk kb + f % kcn) into slot
+  // (F0 + f) % TC_NSLOT once the MMAs that last read the slot are done: the
+  // weight tile now, the operand block now or (first fills) after the prep
+  auto issue_w = [&](int f) -> bool {
     const unsigned F = F0 + (unsigned)f, slot = F % TC_NSLOT, use = F / TC_NSLOT;
     if (use > 0 && !mbar_wait(kc.tcempty + slot, (use - 1) & 1u, WAIT_LIMIT_CYCLES)) {
       raise_err(kc, ERR_MBAR_TIMEOUT, 2000 + f);
       return false;
     }
     const int tile = t0 + f / kcn, chunk = pl.kb + f % kcn;
-    mbar_arrive_expect_tx(kc.tcfull + slot, TC_SLOT_BYTES);
+    mbar_arrive_expect_tx(kc.tcfull + slot, TC_SLOT_BYTES + XB);
     bulk_g2s_hint(wring + slot * TC_SLOT_BYTES, a.wtc + ((size_t)tile * NKC + chunk) * TC_SLOT_BYTES, TC_SLOT_BYTES,
                   kc.tcfull + slot, pol);
     kc.tc_issued = F + 1u;
     return true;
   };
-  if (tid == 0) {
+  auto issue_x = [&](int f) {
+    const unsigned slot = (F0 + (unsigned)f) % TC_NSLOT;
+    const int chunk = pl.kb + f % kcn;
+    bulk_g2s(xring + slot * TC_XSLOT_BYTES, a.xop + (size_t)chunk * XB, XB, kc.tcfull + slot);
+  };
+  // the next tcgen05 stage's weight tiles (this CTA's share) into L2 while
+  // this one runs: its first copies then come from L2 instead of HBM.  Looks
+  // two stages ahead, at descriptors that have landed only.
+  if (tid == 64) {
+    for (unsigned k = 1; k <= 2; k++) {
+      const unsigned nx = kc.seq + k;
+      if (nx >= kc.n_total) break;
+      const int sl = (int)(nx % NDESC);
+      if (!mbar_test(kc.dbars + sl, (nx / NDESC) & 1u)) break;
+      const Stage &ns = kc.dring[sl];
+      if (ns.kind != ST_GEMV) continue;
+      if (ns.g.tc) {
+        const V2Plan &np = kc.pring[sl];
+        const int nkc = ns.g.K / tc_kchunk(ns.g.fmt);
+        for (int ti = 0; ti < np.nt; ti++)
+          prefetch_l2(ns.g.wtc + ((size_t)(np.t0 + ti) * nkc + np.kb) * TC_SLOT_BYTES, (uint32_t)np.kc * TC_SLOT_BYTES);
+      }
+      break;
+    }
+  }
+  const int nfirst = min(TC_NSLOT, L);
+  if (tid == 0 && nt > 0) {
     fence_proxy_async_smem();   // the slots were last written through the generic proxy (other stages)
-    for (int f = 0; f < min(TC_NSLOT, L); f++)
-      if (!issue(f)) break;
+    for (int f = 0; f < nfirst; f++)
+      if (!issue_w(f)) break;
   }
   ckpt(kc, 0);
-  tc_stage_x_f<FMT>(a, B, N, pl.kb * tc_kchunk(FMT), kcn * tc_kchunk(FMT), xreg, s_sx, s_ss);
-  fence_proxy_async_smem();     // the staged operand is read by the tensor cores (async proxy)
-  __syncthreads();
+  // ---- phase 1: this CTA's activation row (the row buffer is the operand
+  // slot region, idle until the operand copies below) ----
+  if ((int)blockIdx.x < B) {
+    tc_prep_row<FMT>(a, blockIdx.x, N, reinterpret_cast<float *>(xring), s_red);
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      atom_add_release_gpu(&kc.ctl->ibar, 1u);
+    }
+  }
   ckpt(kc, 1);
-  // this slice's sums of squares, for the CTAs that finish the tiles
-  if (a.norm_w && S > 1 && tid < B) { __stcg(a.ss_ws + ((size_t)grp * S + s) * 64 + tid, s_ss[tid]); }
-  if (a.norm_w && S == 1 && tid < Bp) s_inv[tid] = (tid < B) ? 1.0f / sqrtf(s_ss[tid] / (float)a.K + a.eps) : 0.f;
-  if (!a.norm_w && tid < 64) s_inv[tid] = 1.0f;
+  // ---- the B rows are in place (bounded wait; warp 1 polls, so thread 0's
+  // weight copies in flight do not hold the poll back) ----
+  if (tid == 32) {
+    const long long w0 = clock64();
+    while ((int)(ld_acquire_gpu(&kc.ctl->ibar) - ib_target) < 0) {
+      if (clock64() - w0 > WAIT_LIMIT_CYCLES || ld_acquire_gpu((const unsigned *)&kc.ctl->err)) {
+        raise_err(kc, ERR_BARRIER_TIMEOUT, 6000 + (int)blockIdx.x);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) kc.ibar_target = ib_target;
+  if (kc.local_err) {
+    // the CTA leaves together; the first fills' operand copies still go out
+    // so that every fill issued completes (the stale operand is never used)
+    if (tid == 0 && nt > 0)
+      for (int f = 0; f < nfirst && F0 + (unsigned)f < kc.tc_issued; f++) issue_x(f);
+    return;
+  }
+  ckpt(kc, 2);
+  if (nt == 0) return;
+  if (tid < Bp) {
+    s_sx[tid] = (tid < B) ? __ldcg(a.xsc + tid) : 0.f;
+    s_inv[tid] = (tid < B) ? __ldcg(a.xsc + 64 + tid) : 0.f;
+  }
+  if (tid == 0) {
+    fence_proxy_async();        // the operand, written by other CTAs, is read by bulk copies
+    fence_proxy_async_smem();   // the row buffer was written through the generic proxy
+    for (int f = 0; f < nfirst; f++) issue_x(f);
+  }
 
   const uint32_t idesc = (FMT == FMT_INT8) ? umma_idesc(2u, 1u, (uint32_t)N) : umma_idesc(1u, 1u, (uint32_t)N);
-  const uint32_t wr_u = smem_u32(wring), xr_u = smem_u32(xreg);
+  const uint32_t wr_u = smem_u32(wring), xr_u = smem_u32(xring);
   // thread 0: the MMAs of tile i into accumulator buffer (g0 + i) & 1
   auto mma_tile = [&](int i) {
     const unsigned g = g0 + (unsigned)i;
@@ -2428,7 +2496,7 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
       }
       kc.tc_done = F + 1u;
       tc_fence_after();
-      const uint32_t ab = wr_u + slot * TC_SLOT_BYTES, bb = xr_u + (uint32_t)(c * N * 128);
+      const uint32_t ab = wr_u + slot * TC_SLOT_BYTES, bb = xr_u + slot * TC_XSLOT_BYTES;
 #pragma unroll
       for (int ks = 0; ks < 4; ks++) {
         const uint64_t ad = umma_desc_sw128(ab + 32u * ks), bd = umma_desc_sw128(bb + 32u * ks);
@@ -2436,18 +2504,20 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
         else umma_bf16(d, ad, bd, idesc, (c | ks) != 0);
       }
       umma_commit(kc.tcempty + slot);
-      if (f >= 1 && f - 1 + TC_NSLOT < L && !issue(f - 1 + TC_NSLOT)) break;
+      if (f + TC_NSLOT < L) {   // refill this slot
+        if (!issue_w(f + TC_NSLOT)) break;
+        issue_x(f + TC_NSLOT);
+      }
     }
     umma_commit(kc.tcacc + (g & 1u));
     kc.tc_committed = g + 1u;
   };
-  __syncthreads();   // s_inv; every warp is past the staging
+  __syncthreads();   // s_sx, s_inv
   if (tid == 0 && !kc.local_err) mma_tile(0);
 
   const int q4 = warp & 3, hh = warp >> 2;
   const int rl = 32 * q4 + lane;   // this thread's row within the tile
   const float c7 = 1.0f / 128.0f, c14 = 1.0f / 16384.0f, c21 = 1.0f / 2097152.0f;
-  const int nb = min(Bh, 32);
   for (int i = 0; i < nt; i++) {
     const int t = t0 + i;
     const unsigned g = g0 + (unsigned)i;
@@ -2460,58 +2530,87 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
     tc_fence_after();
     ckpt(kc, 13);
     if (i < 3) ckpt(kc, 18 + 4 * i);
-    // batch rows [hh * Bh, hh * Bh + Bh) of row rl, 8 (int8) or 16 (bf16) per
-    // 32-column TMEM load
+    // batch rows [hh * Bh, hh * Bh + Bh) of row rl, PER per 32-column TMEM
+    // load: a rolled loop over the loads, each load's values unrolled (this
+    // code runs once per stage, and code that runs once is fetched line by
+    // line into a cold instruction cache)
     constexpr int PER = (FMT == FMT_INT8) ? 8 : 16;
-    float val[32 + PER];
-#pragma unroll
+    const int row = 128 * t + rl;
+    const float rsc = (S == 1 && a.row_scale) ? __ldg(a.row_scale + row) : 1.f;
+    const float bia = (S == 1 && a.bias) ? __ldg(a.bias + row) : 0.f;
+#pragma unroll 1
     for (int j = 0; j < 32 / PER; j++) {
-      const int bb0 = hh * Bh + PER * j;
       if (PER * j >= Bh) break;
+      const int bb0 = hh * Bh + PER * j;
       uint32_t r[32];
       tmem_ld32(kc.tmem + (g & 1u) * (uint32_t)TC_ACC_COLS + ((uint32_t)(32 * q4) << 16) + (uint32_t)(P * bb0), r);
+      float v[PER];
 #pragma unroll
       for (int u = 0; u < PER; u++) {
-        float v;
         if (FMT == FMT_INT8) {
-          v = (((float)(int)r[4 * u + 3] * c21 + (float)(int)r[4 * u + 2] * c14) + (float)(int)r[4 * u + 1] * c7) +
-              (float)(int)r[4 * u];
+          v[u] = (((float)(int)r[4 * u + 3] * c21 + (float)(int)r[4 * u + 2] * c14) + (float)(int)r[4 * u + 1] * c7) +
+                 (float)(int)r[4 * u];
           const int b = bb0 + u;
-          v *= (b < B) ? s_sx[b] : 0.f;
+          v[u] *= (b < B) ? s_sx[b] : 0.f;
         } else {
-          v = __uint_as_float(r[2 * u]) + __uint_as_float(r[2 * u + 1]);
+          v[u] = __uint_as_float(r[2 * u]) + __uint_as_float(r[2 * u + 1]);
         }
-        val[PER * j + u] = v;
+      }
+      const int nu = min(PER, Bh - PER * j);   // this half's rows in the load (a multiple of 4)
+      if (S > 1) {
+        // this slice's partial sums of the tile; added up after the last tile
+        float *wsp = a.ws + (((size_t)t * S + s) * 128 + rl) * Bp + bb0;
+#pragma unroll
+        for (int u = 0; u < PER; u += 4)
+          if (u < nu) __stcg(reinterpret_cast<float4 *>(wsp + u), make_float4(v[u], v[u + 1], v[u + 2], v[u + 3]));
+      } else if (a.epi == EPI_ARGMAX) {
+        // per batch row: this warp's 32 rows now, the four lane quarters below
+#pragma unroll 1
+        for (int u = 0; u < nu; u++) {
+          const int b = bb0 + u;
+          unsigned long long k = 0ull;
+          if (b < B) {
+            float x = v[u] * s_inv[b] * rsc + bia;
+            if (a.gen) x = codec_logit(a.gen, b, row, x);
+            k = amax_key(x, row);
+          }
+#pragma unroll
+          for (int m = 16; m > 0; m >>= 1) {
+            const unsigned long long o = shfl_xor_u64(k, m);
+            k = o > k ? o : k;
+          }
+          if (lane == 0) s_key[q4 * 64 + b] = k;
+        }
+      } else if (a.epi == EPI_SWIGLU) {
+        float *yh = a.y + (row >> 1);
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+          if (u >= nu) break;
+          const int b = bb0 + u;
+          const float x = (v[u] * s_inv[b]) * rsc + bia;
+          const float up = __shfl_xor_sync(0xffffffffu, x, 1);
+          if ((row & 1) == 0 && b < B) __stcg(yh + (size_t)b * a.ldy, __fdividef(x, 1.0f + expf(-x)) * up);
+        }
+      } else if (a.epi == EPI_RESID) {
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+          const int b = bb0 + u;
+          if (u < nu && b < B) {
+            float *yp = a.y + (size_t)b * a.ldy + row;
+            __stcg(yp, __ldcg(yp) + ((v[u] * s_inv[b]) * rsc + bia));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+          const int b = bb0 + u;
+          if (u < nu && b < B) __stcg(a.y + (size_t)b * a.ldy + row, (v[u] * s_inv[b]) * rsc + bia);
+        }
       }
     }
     tc_fence_before();
     if (i < 3) ckpt(kc, 19 + 4 * i);
-    const int row = 128 * t + rl;
-    if (S > 1) {
-      // this slice's partial sums of the tile; added up after the last tile
-      float *wsp = a.ws + (((size_t)t * S + s) * 128 + rl) * Bp + hh * Bh;
-#pragma unroll
-      for (int u = 0; u < 32; u += 4)
-        if (u < nb) __stcg(reinterpret_cast<float4 *>(wsp + u), make_float4(val[u], val[u + 1], val[u + 2], val[u + 3]));
-    } else if (a.epi == EPI_ARGMAX) {
-      // per batch row: this warp's 32 rows, then the four lane quarters
-#pragma unroll
-      for (int u = 0; u < 32; u++) {
-        if (u >= nb) break;
-        const int b = hh * Bh + u;
-        unsigned long long k = 0ull;
-        if (b < B) {
-          float v = val[u] * s_inv[b] * (a.row_scale ? __ldg(a.row_scale + row) : 1.f) + (a.bias ? __ldg(a.bias + row) : 0.f);
-          if (a.gen) v = codec_logit(a.gen, b, row, v);
-          k = amax_key(v, row);
-        }
-#pragma unroll
-        for (int m = 16; m > 0; m >>= 1) {
-          const unsigned long long o = shfl_xor_u64(k, m);
-          k = o > k ? o : k;
-        }
-        if (lane == 0 && b < 64) s_key[q4 * 64 + b] = k;
-      }
+    if (S == 1 && a.epi == EPI_ARGMAX) {
       __syncthreads();
       for (int idx = tid; idx < 8 * B; idx += NTHREADS) {
         const int b = idx % B, sub = idx / B;
@@ -2527,13 +2626,6 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
       }
       __syncthreads();
       if (s_flag[1]) argmax_finish(a, B, kc);
-    } else {
-#pragma unroll
-      for (int u = 0; u < 32; u++) {
-        if (u >= nb) break;
-        const int b = hh * Bh + u;
-        tc_out(a, B, b, row, val[u], s_inv[b]);
-      }
     }
     // this buffer may take tile i + 2
     if (__syncthreads_or(kc.local_err)) return;   // copies and MMAs in flight are drained on the way out
@@ -2569,13 +2661,6 @@ __device__ __noinline__ void gemv_tc_t(const GemvArgs &a, int B, char *smem, KCt
   ckpt(kc, 16);
   if (__syncthreads_or(kc.local_err)) return;
   __threadfence();
-  if (a.norm_w && tid < Bp) {   // 1/rms from every slice of the row group
-    float tot = 0.f;
-    if (tid < B)
-      for (int s2 = 0; s2 < S; s2++) tot += __ldcg(a.ss_ws + ((size_t)grp * S + s2) * 64 + tid);
-    s_inv[tid] = (tid < B) ? 1.0f / sqrtf(tot / (float)a.K + a.eps) : 0.f;
-  }
-  __syncthreads();
   // work items (tile i, sub-tile st of this slice): thread = row r of the
   // sub-tile x batch rows 4 bq .. 4 bq + 3
   const int per_tile = (8 - s + S - 1) / S;   // sub-tiles s, s + S, ... < 8
@@ -4212,6 +4297,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     kc.ctl = ctl;
     kc.stage = 0;
     kc.trace2 = trace ? trace + (size_t)n_iters * n_stages + 1 : nullptr;
+    kc.trace_cta = trace ? ctl->trace_cta : 0;
     kc.gtrace = trace ? reinterpret_cast<unsigned long long *>(trace + (size_t)n_iters * n_stages + 1 +
                                                                (size_t)n_stages * NCKPT)
                       : nullptr;
@@ -4234,6 +4320,7 @@ decode_kernel(const Stage *__restrict__ prog, const V2Plan *__restrict__ plan, i
     kc.tc_done = 0;
     kc.tc_committed = 0;
     kc.tc_waited = 0;
+    kc.ibar_target = 0;
     kc.cl = cl;
     kc.clbars = clbars;
     for (int w = 0; w < NWARPS; w++) {
