@@ -896,7 +896,12 @@ static bool tc_ok(const DMat &m, int B, int fmt) {
 static TcShape tc_choose(int fmt, int rows, int K, int B, int G) {
   const int T = rows / 128, NKC = K * (fmt == FMT_INT8 ? 1 : 2) / 128;
   const int N = tc_parts(fmt) * tc_bpad(fmt, B);
-  const double chunk_us = (TC_SLOT_BYTES + (double)N * 128) / 60e3;
+  static const double sm_gbs = [] {   // QTB_TC_SM_GBS overrides the per-SM stream rate (tuning)
+    const char *v = getenv("QTB_TC_SM_GBS");
+    const double x = v ? atof(v) : 0.0;
+    return x > 0.0 ? x : 60.0;
+  }();
+  const double chunk_us = (TC_SLOT_BYTES + (double)N * 128) / (sm_gbs * 1e3);
   TcShape best;
   double best_cost = 1e30;
   for (int S = 1; S <= std::min(NKC, G); S++) {
