@@ -101,6 +101,7 @@ def lib():
         getattr(L, n).argtypes = [_vp, C.c_int, _vp, _vp, C.c_int, C.c_int]
     L.qtb_session_profile.argtypes = [_vp, C.c_int, _vp, _vp, _vp, C.c_int]
     L.qtb_session_profile_checkpoints.argtypes = [_vp, _vp, C.c_int]
+    L.qtb_session_profile_arrivals.argtypes = [_vp, _vp, C.c_int]
     L.qtb_quantize_int8.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp]
     L.qtb_quantize_q4_0.argtypes = [_vp, C.c_int, C.c_int, _vp]
     L.qtb_quantize_int4g32.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp, _vp]
