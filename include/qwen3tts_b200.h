@@ -139,6 +139,14 @@ int  qtb_session_batch(const qtb_session_t *s);
  * device can co-schedule the cluster and every stage of the program fits it).
  * 0: no such program. */
 int  qtb_session_program_grid(const qtb_session_t *s, int which);
+/* The large-batch (tcgen05) GEMV plan of a rows x cols matrix at `batch` rows
+ * over `grid` CTAs, for CTA `cta` (host arithmetic only, no device needed):
+ * out[0] first 128-row tile, out[1] tile count, out[2] first 128-byte K chunk,
+ * out[3] chunk count, out[4] k-slice, out[5] slices in the plan.  Returns 0,
+ * or QTB_E_UNSUPPORTED when the shape does not take that path (format other
+ * than bf16 / int8, rows % 128 != 0, batch outside 1..64).  Introspection for
+ * tests and tuning; no reference counterpart. */
+int  qtb_tc_plan(int fmt, int rows, int cols, int batch, int grid, int cta, int out[6]);
 int  qtb_session_n_pages(const qtb_session_t *s);
 
 int  qtb_session_max_ctx(const qtb_session_t *s);

@@ -1498,6 +1498,20 @@ fail:
 }
 
 extern "C" int qtb_session_batch(const qtb_session_t *s) { return s ? s->B : 0; }
+extern "C" int qtb_tc_plan(int fmt, int rows, int cols, int batch, int grid, int cta, int out[6]) {
+  if (!out || grid < 1 || cta < 0 || cta >= grid || cols < 1) return set_err(QTB_E_INVALID, "bad argument");
+  if ((fmt != FMT_BF16 && fmt != FMT_INT8) || rows % 128 != 0 || batch < 1 || batch > 64 ||
+      cols % tc_kchunk(fmt) != 0)
+    return set_err(QTB_E_UNSUPPORTED, "not a tcgen05 GEMV shape");
+  GemvArgs g;
+  memset(&g, 0, sizeof g);
+  g.fmt = fmt; g.rows = rows; g.K = cols;
+  const V2Plan p = tc_plan(g, batch, cta, grid);
+  out[0] = p.t0; out[1] = p.nt; out[2] = p.kb; out[3] = p.kc; out[4] = p.pair;
+  out[5] = tc_choose(fmt, rows, cols, batch, grid).S;
+  return 0;
+}
+
 extern "C" int qtb_session_program_grid(const qtb_session_t *s, int which) {
   if (!s || which < 0 || which >= PROG_N || !s->prog[which]) return 0;
   return s->prog_cl[which] ? -s->prog_G[which] : s->prog_G[which];

@@ -90,6 +90,7 @@ def lib():
     L.qtb_session_begin_generation.argtypes = [_vp, _vp, C.c_float]
     L.qtb_prefill.argtypes = [_vp, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp]
     L.qtb_session_program_grid.argtypes = [_vp, C.c_int]
+    L.qtb_tc_plan.argtypes = [C.c_int] * 6 + [_vp]
     L.qtb_session_set_sampling.argtypes = [_vp, C.c_int, C.c_float, C.c_int, C.c_float, C.c_uint32]
     L.qtb_session_get_rng.argtypes = [_vp, _vp]
     L.qtb_codec_sample_host.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp]
@@ -509,6 +510,18 @@ class Session:
         fn = lib().qtb_session_download_cp_kv if cp else lib().qtb_session_download_kv
         check(fn(self.h, b, ptr(k), ptr(v), length, length))
         return k, v
+
+
+def tc_plan(fmt: int, rows: int, cols: int, batch: int, grid: int, cta: int):
+    """qtb_tc_plan: (first tile, tiles, first chunk, chunks, slice, slices) of
+    one CTA in the large-batch GEMV plan, or None when the shape does not take
+    that path."""
+    out = np.zeros(6, np.int32)
+    rc = lib().qtb_tc_plan(int(fmt), int(rows), int(cols), int(batch), int(grid), int(cta), ptr(out))
+    if rc == -5:   # QTB_E_UNSUPPORTED
+        return None
+    check(rc)
+    return tuple(int(v) for v in out)
 
 
 def gemv(fmt: int, q: dict, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
