@@ -49,7 +49,7 @@ class ContinuousBatcher:
     def __init__(self, session: "Q.Session", rep_penalty: float = 1.05):
         self.s = session
         self.B = session.B
-        self.n_pages = Q.lib().qtb_session_n_pages(session.h)
+        self.n_pages = session.n_pages()
         # one scratch page per slot for parking, the rest shared
         self.scratch = list(range(self.B))
         self.free = list(range(self.B, self.n_pages))

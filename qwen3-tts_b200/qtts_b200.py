@@ -387,6 +387,10 @@ class Session:
         except Exception:
             pass
 
+    def n_pages(self):
+        """KV pages in the session's pool (qtb_session_n_pages)."""
+        return lib().qtb_session_n_pages(self.h)
+
     def set_pages(self, b, pages):
         p = np.ascontiguousarray(pages, np.int32)
         check(lib().qtb_session_set_pages(self.h, b, ptr(p), len(p)))
